@@ -1,0 +1,90 @@
+"""ctypes binding of libdflash_b200.so (the C ABI in ``include/dflash_b200.h``).
+
+The shared library is the only compute path: if it is missing or a call
+fails, the caller gets an exception -- there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+from .build import LIB_PATH
+
+_c_int = ctypes.c_int
+_c_size = ctypes.c_size_t
+_vp = ctypes.c_void_p
+
+DFL_OK = 0
+STATUS_NAMES = {
+    0: "DFL_OK",
+    1: "DFL_ERR_NULL_POINTER",
+    2: "DFL_ERR_BAD_SHAPE",
+    3: "DFL_ERR_MISALIGNED",
+    4: "DFL_ERR_WORKSPACE",
+    5: "DFL_ERR_CUDA",
+    6: "DFL_ERR_UNSUPPORTED",
+}
+
+# name -> (restype, argtypes); must match include/dflash_b200.h
+SIGNATURES = {
+    "dfl_status_string": (ctypes.c_char_p, [_c_int]),
+    "dfl_version": (ctypes.c_char_p, []),
+    "dfl_get_device_error": (_c_int, [ctypes.POINTER(_c_int)]),
+    "dfl_verify_qmm_w4g64": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_size, _c_int, _c_int,
+                                      _c_int, _vp]),
+    "dfl_verify_qmm_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class DflashError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, fn: str, status: int):
+        self.status = status
+        name = STATUS_NAMES.get(status, str(status))
+        super().__init__(f"{fn} failed: {name} ({status_string(status)})")
+
+
+def load(path: Path | None = None) -> ctypes.CDLL:
+    """Load (once) and return the library, with argtypes set for every symbol."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"{p.name} is not built ({p}); run __graft_entry__.build() -- "
+                "dflash-b200 has no fallback path")
+        lib = ctypes.CDLL(str(p))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def status_string(status: int) -> str:
+    try:
+        return load().dfl_status_string(int(status)).decode()
+    except Exception:  # pragma: no cover - library missing
+        return STATUS_NAMES.get(status, "unknown")
+
+
+def check(fn: str, status: int) -> None:
+    if status != DFL_OK:
+        raise DflashError(fn, status)
+
+
+def device_error() -> int:
+    """Read and clear the kernels' device error word (synchronises the device)."""
+    v = _c_int(0)
+    check("dfl_get_device_error", load().dfl_get_device_error(ctypes.byref(v)))
+    return int(v.value)

@@ -1,0 +1,33 @@
+// Single translation unit of libdflash_b200.so: the device error word, the
+// generic C-ABI helpers and every kernel family (one TU keeps device
+// symbols private without relocatable device code).
+#include "common.cuh"
+#include "host_common.cuh"
+
+#include "qmm_w4.cu"
+
+extern "C" const char* dfl_status_string(int status) {
+  switch (status) {
+    case DFL_OK: return "ok";
+    case DFL_ERR_NULL_POINTER: return "null pointer";
+    case DFL_ERR_BAD_SHAPE: return "unsupported shape";
+    case DFL_ERR_MISALIGNED: return "misaligned pointer or stride";
+    case DFL_ERR_WORKSPACE: return "workspace missing or too small";
+    case DFL_ERR_CUDA: return "CUDA error";
+    case DFL_ERR_UNSUPPORTED: return "unsupported device or option";
+    default: return "unknown status";
+  }
+}
+
+extern "C" const char* dfl_version(void) { return "dflash-b200 0.1.0 (sm_100a)"; }
+
+extern "C" int dfl_get_device_error(int* device_error) {
+  if (!device_error) return DFL_ERR_NULL_POINTER;
+  int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return DFL_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(&v, dfl::g_device_error, sizeof(int)) != cudaSuccess) return DFL_ERR_CUDA;
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(dfl::g_device_error, &zero, sizeof(int)) != cudaSuccess) return DFL_ERR_CUDA;
+  *device_error = v;
+  return DFL_OK;
+}

@@ -1,0 +1,103 @@
+"""``verify_matmul``: the int4 verify quantized matmul on B200.
+
+Mirrors ``dflash_mlx/verify_qmm.py:905-1022`` (``verify_matmul``) and
+``:15-16`` (``is_enabled``).  Same arguments and weight layout (MLX affine:
+uint32 ``w [N, K/8]`` low nibble first, ``scales`` / ``biases`` ``[N, K/64]``),
+same result up to fp32 summation order.
+
+Differences by design:
+
+* the reference dispatches between Metal variants and falls back to stock
+  ``mx.quantized_matmul`` for anything its verify kernels do not cover; here
+  one sm_100a kernel (``dfl_verify_qmm_w4g64``) serves every row count (rows
+  are processed 32 at a time), so there is no fallback;
+* layouts the kernel does not implement (8-bit, group sizes other than 64,
+  ``transpose=False``, non-bf16 activations) raise ``NotImplementedError``
+  instead of silently taking another path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._runtime import as_u32_bits, require_cuda, stream_ptr, workspace
+from .internal_debug import verify_qmm_enabled
+
+MAX_ROWS_PER_CALL = 32
+
+
+def is_enabled() -> bool:
+    """``DFLASH_VERIFY_QMM == "1"`` (reference ``verify_qmm.py:15-16``).
+
+    Kept for interface parity; the B200 kernel is the only implementation,
+    so the flag does not change which code runs.
+    """
+    return verify_qmm_enabled()
+
+
+def workspace_bytes(m: int, k: int, n: int) -> int:
+    st = ctypes.c_int(0)
+    nbytes = _lib.load().dfl_verify_qmm_workspace_bytes(int(m), int(k), int(n), ctypes.byref(st))
+    _lib.check("dfl_verify_qmm_workspace_bytes", st.value)
+    return int(nbytes)
+
+
+def qmm_w4g64(x2: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x2 [M, K] @ dequant(w_q).T`` through the C ABI -> bf16 ``[M, N]``."""
+    for t, name in ((x2, "x"), (w_q, "w"), (scales, "scales"), (biases, "biases")):
+        require_cuda(t, name)
+    if x2.dtype != torch.bfloat16:
+        raise NotImplementedError(f"activations must be bfloat16, got {x2.dtype}")
+    if scales.dtype != torch.bfloat16 or biases.dtype != torch.bfloat16:
+        raise NotImplementedError("scales and biases must be bfloat16")
+    w_q = as_u32_bits(w_q)
+    x2 = x2.contiguous()
+    scales = scales.contiguous()
+    biases = biases.contiguous()
+    m, k = x2.shape
+    n = w_q.shape[0]
+    if w_q.shape[1] * 8 != k:
+        raise ValueError(f"weight shape {tuple(w_q.shape)} does not match K={k}")
+    if scales.shape != (n, k // 64) or biases.shape != (n, k // 64):
+        raise ValueError("scales/biases must be [N, K/64]")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x2.device)
+    if m == 0 or n == 0:
+        return out
+    lib = _lib.load()
+    with torch.cuda.device(x2.device):
+        sp = stream_ptr(x2.device)
+        for r0 in range(0, m, MAX_ROWS_PER_CALL):
+            r1 = min(m, r0 + MAX_ROWS_PER_CALL)
+            need = workspace_bytes(r1 - r0, k, n)
+            ws = workspace(x2.device, need)
+            xs = x2[r0:r1]
+            ys = out[r0:r1]
+            st = lib.dfl_verify_qmm_w4g64(xs.data_ptr(), w_q.data_ptr(), scales.data_ptr(),
+                                          biases.data_ptr(), ys.data_ptr(), ws.data_ptr(),
+                                          ws.numel(), r1 - r0, k, n, sp)
+            _lib.check("dfl_verify_qmm_w4g64", st)
+    return out
+
+
+def verify_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                  *, transpose: bool = True, group_size: int = 64, bits: int = 4) -> torch.Tensor:
+    """``x @ dequant(w).T`` for MLX affine int4 g64 weights (reference ``verify_qmm.py:905``)."""
+    if bits != 4 or group_size != 64:
+        raise NotImplementedError(
+            f"only bits=4, group_size=64 is implemented (got bits={bits}, group_size={group_size})")
+    if not transpose:
+        raise NotImplementedError("only transpose=True (y = x @ W.T) is implemented")
+    if biases is None:
+        raise ValueError("affine quantization needs biases")
+    orig = x.shape
+    k = orig[-1]
+    m = 1
+    for d in orig[:-1]:
+        m *= int(d)
+    y = qmm_w4g64(x.reshape(m, k), w, scales, biases)
+    return y.reshape(*orig[:-1], w.shape[0])

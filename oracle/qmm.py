@@ -1,0 +1,137 @@
+"""Oracle for the M=16 int4 verify qmm (dense) -- TEST INFRASTRUCTURE ONLY.
+
+Restates the reference's quantized matmul ``y = x @ W.T`` with MLX's affine
+layout, as every verify kernel reads it:
+
+* ``w_q`` is uint32 ``[N, K/8]``; nibble ``ki`` of word ``pack`` sits at bits
+  ``4*ki .. 4*ki+3`` and holds column ``k = 8*pack + ki`` (low nibble first),
+  ``dflash_mlx/verify_qmm.py:243-250`` (also ``:97-115`` for M=4).
+* ``scales`` / ``biases`` are ``[N, K/group_size]`` in the activation dtype;
+  group ``k // group_size``.
+* Dequantisation is ``float(nib) * s + b`` in fp32, then rounded to the
+  activation dtype before the MMA (``verify_qmm.py:249``:
+  ``T(float(nib) * s + b)``).  Accumulation is fp32
+  (``simdgroup_matrix<float>`` accumulators, ``verify_qmm.py:228-232``) and
+  the output is rounded to the activation dtype (``verify_qmm.py:290``).
+
+bf16 tensors are passed as uint16 bit patterns (see ``oracle/bf16.py``).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import bf16
+
+GROUP_SIZE = 64
+BITS = 4
+
+
+def pack_nibbles(q: np.ndarray) -> np.ndarray:
+    """uint8 nibbles ``[N, K]`` (values 0..15) -> uint32 ``[N, K/8]``, low nibble first."""
+    q = np.asarray(q, dtype=np.uint32)
+    n, k = q.shape
+    assert k % 8 == 0
+    q = q.reshape(n, k // 8, 8)
+    out = np.zeros((n, k // 8), dtype=np.uint32)
+    for ki in range(8):
+        out |= (q[:, :, ki] & np.uint32(0xF)) << np.uint32(4 * ki)
+    return out
+
+
+def unpack_nibbles(w_q: np.ndarray) -> np.ndarray:
+    """uint32 ``[N, K/8]`` -> uint8 nibbles ``[N, K]`` (inverse of :func:`pack_nibbles`)."""
+    w_q = np.asarray(w_q, dtype=np.uint32)
+    n, kp = w_q.shape
+    out = np.empty((n, kp, 8), dtype=np.uint8)
+    for ki in range(8):
+        out[:, :, ki] = (w_q >> np.uint32(4 * ki)) & np.uint32(0xF)
+    return out.reshape(n, kp * 8)
+
+
+def dequantize(w_q: np.ndarray, scales: np.ndarray, biases: np.ndarray,
+               group_size: int = GROUP_SIZE) -> np.ndarray:
+    """Dequantised weights as float32 values that are exactly bf16 (``verify_qmm.py:249``)."""
+    nib = unpack_nibbles(w_q).astype(np.float32)
+    n, k = nib.shape
+    s = np.repeat(bf16.to_f32(scales), group_size, axis=1)[:, :k]
+    b = np.repeat(bf16.to_f32(biases), group_size, axis=1)[:, :k]
+    return bf16.round_f32(nib * s + b)
+
+
+def qmm(x: np.ndarray, w_q: np.ndarray, scales: np.ndarray, biases: np.ndarray,
+        group_size: int = GROUP_SIZE, accum=np.float64) -> np.ndarray:
+    """``y = x @ dequant(W).T`` -> bf16 bit patterns ``[M, N]``.
+
+    ``x`` is bf16 bits ``[M, K]``.  ``accum`` selects the accumulation dtype:
+    float64 for golden values, float32 for the timed CPU restatement.
+    """
+    xf = bf16.to_f32(x).astype(accum)
+    n = w_q.shape[0]
+    y = np.empty((xf.shape[0], n), dtype=np.float32)
+    step = 2048
+    for r0 in range(0, n, step):
+        w = dequantize(w_q[r0:r0 + step], scales[r0:r0 + step], biases[r0:r0 + step],
+                       group_size).astype(accum)
+        y[:, r0:r0 + step] = (xf @ w.T).astype(np.float32)
+    return bf16.from_f32(y)
+
+
+def qmm_f32(x: np.ndarray, w_q: np.ndarray, scales: np.ndarray, biases: np.ndarray,
+            group_size: int = GROUP_SIZE) -> np.ndarray:
+    """Unrounded float32 result of :func:`qmm` (float64 accumulation)."""
+    w = dequantize(w_q, scales, biases, group_size).astype(np.float64)
+    return (bf16.to_f32(x).astype(np.float64) @ w.T).astype(np.float32)
+
+
+def affine_quantize(w: np.ndarray, group_size: int = GROUP_SIZE):
+    """Min/max affine 4-bit quantiser used only to build test inputs.
+
+    The reference's parity harness quantises random fp weights with
+    ``mx.quantize`` before calling the kernel
+    (``tests/test_verify_qmm_parity.py:29-30,51-53``).  This is a plain
+    restatement of the published affine scheme (scale = range / 15,
+    bias = group minimum, q = round((w - bias) / scale)); the kernels under
+    test only see its output, so the exact tie rules of MLX's quantiser do
+    not affect parity.  Returns (w_q uint32, scales bf16 bits, biases bf16 bits).
+    """
+    w = np.asarray(w, dtype=np.float32)
+    n, k = w.shape
+    assert k % group_size == 0
+    g = w.reshape(n, k // group_size, group_size)
+    wmin = g.min(axis=2)
+    wmax = g.max(axis=2)
+    scale = np.maximum((wmax - wmin) / 15.0, 1e-7).astype(np.float32)
+    s_bits = bf16.from_f32(scale)
+    b_bits = bf16.from_f32(wmin)
+    s = bf16.to_f32(s_bits)[:, :, None]
+    b = bf16.to_f32(b_bits)[:, :, None]
+    q = np.clip(np.rint((g - b) / s), 0, 15).astype(np.uint8).reshape(n, k)
+    return pack_nibbles(q), s_bits, b_bits
+
+
+def synth_weights(rng: np.random.Generator, n: int, k: int, group_size: int = GROUP_SIZE):
+    """BASELINE config-0 weight distribution.
+
+    q ~ U{0..15}; scales bf16 ~ U(0.004, 0.02) per (row, group);
+    biases = -8*scale + N(0, 0.1*scale).  Returns (w_q, scales, biases).
+    """
+    q = rng.integers(0, 16, size=(n, k), dtype=np.uint8)
+    g = k // group_size
+    s = rng.uniform(0.004, 0.02, size=(n, g)).astype(np.float32)
+    b = (-8.0 * s + rng.standard_normal((n, g)).astype(np.float32) * 0.1 * s).astype(np.float32)
+    return pack_nibbles(q), bf16.from_f32(s), bf16.from_f32(b)
+
+
+def synth_x(rng: np.random.Generator, m: int, k: int) -> np.ndarray:
+    """Activations bf16 ~ N(0, 1) as bit patterns."""
+    return bf16.from_f32(rng.standard_normal((m, k)).astype(np.float32))
+
+
+def max_abs_rel(y: np.ndarray, ref: np.ndarray):
+    """The reference harness metric (``tests/test_verify_qmm_parity.py:68-70``)."""
+    a = bf16.to_f32(y).astype(np.float64)
+    r = bf16.to_f32(ref).astype(np.float64)
+    max_abs = float(np.max(np.abs(a - r))) if a.size else 0.0
+    max_rel = max_abs / (float(np.max(np.abs(r))) + 1e-3) if r.size else 0.0
+    return max_abs, max_rel
