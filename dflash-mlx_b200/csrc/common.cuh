@@ -62,14 +62,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Test for completion of the phase with the given parity.  A waiting thread
+// is suspended (it issues nothing) until the phase completes or the hint of
+// 10 ms runs out; without the hint waiting warps poll and take issue slots
+// from the warps doing the work.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(10000000u)
       : "memory");
   return ok != 0;
 }
@@ -80,15 +84,50 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   unsigned long long t0 = globaltimer_ns();
-  for (uint32_t i = 1;; ++i) {
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0u) {
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        atomicExch(&g_device_error, kDevWaitTimeout);
-        return false;
-      }
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicExch(&g_device_error, kDevWaitTimeout);
+      return false;
     }
   }
+}
+
+// Same, for kernels whose threads also meet at named barriers: leaving a
+// loop early there could strand a barrier, so instead a time-out sets a
+// CTA-wide abort word and every later wait returns false at once.  Threads
+// keep walking the same control flow (skipping the issue of MMAs and copies)
+// and the CTA reaches its teardown.
+__device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity,
+                                                    volatile int* abort_word) {
+  if (mbar_try_wait(bar, parity)) return true;
+  if (*abort_word) return false;
+  unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_word) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicExch(&g_device_error, kDevWaitTimeout);
+      *abort_word = 1;
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- cp.async
+// 16-byte global -> shared copy through L2; src_bytes < 16 zero-fills the
+// rest (0 reads nothing).
+__device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+// Arrive on an mbarrier once all of this thread's prior cp.async copies have
+// landed; the arrival is counted in the barrier's expected count.
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
 }
 
 // ---------------------------------------------------------------- TMA
@@ -227,12 +266,38 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier that also returns the AND of `pred` over all participants.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %3, 0;\n\t"
+      "bar.red.and.pred p, %1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(nthreads), "r"(pred ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "r"(addr));
   return v;
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads (TMA stores, tcgen05.mma operand fetches).
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31u) == 0u; }

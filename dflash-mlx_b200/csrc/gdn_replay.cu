@@ -1,0 +1,217 @@
+// GatedDeltaNet tape-replay rollback (sm_100a).
+//
+// Replaces tape_replay_kernel (dflash_mlx/kernels.py:822-868, Metal body
+// :708-758; mx-op reference _tape_replay_ops :790-820).  For every
+// (sequence b, value head hv) and every step t that is replayed:
+//     S[dv, dk] <- S[dv, dk] * g_t          (g_t scalar per head, or per dk)
+//     S[dv, dk] <- S[dv, dk] + delta_t[dv] * k_t[dk]
+// with k head hk = hv / (Hv / Hk) (kernels.py:712).  Step t of sequence b is
+// replayed when t < steps[b] and mask[b, t] (either may be absent).  The two
+// updates are separately rounded fp32 operations, exactly as the mx-op
+// reference orders them, so results match it bit for bit.
+//
+// Layout: state [B, Hv, Dv, Dk] fp32, tape [B, T, Hv, Dv] fp32,
+// k [B, T, Hk, Dk] (bf16 or fp32), g [B, T, Hv] or [B, T, Hv, Dk] fp32.
+//
+// One CTA per (b, hv) head, 256 threads.  The head's state (Dv x Dk fp32,
+// 64 KB at 128 x 128) is read once with 16-byte coalesced loads into
+// registers, all replayed steps are applied there (the step's k, delta and
+// g sit in shared memory), and it is written back once.  A head with no step
+// to replay is not touched when updating in place.  The kernel is HBM-bound:
+// per replayed head 2 * Dv * Dk * 4 bytes of state plus a * (Dv + Hk/Hv-share
+// of Dk) of tape.
+#include "common.cuh"
+#include "host_common.cuh"
+
+namespace dfl {
+namespace gdn {
+
+constexpr int THREADS = 256;
+constexpr int MAX_CHUNKS = 16;  // float4 state chunks per thread (Dv * Dk <= 16384)
+constexpr int MAX_STEPS = 64;
+// Largest staging area: MAX_STEPS * (Dv + 2 * Dk) floats with Dv * Dk <= 16384.
+constexpr int kMaxSmem = MAX_STEPS * (512 + 2 * 32) * 4 > MAX_STEPS * (64 + 2 * 256) * 4
+                             ? MAX_STEPS * (512 + 2 * 32) * 4
+                             : MAX_STEPS * (64 + 2 * 256) * 4;
+
+struct ReplayParams {
+  const float* tape;
+  const void* k;
+  const float* g;
+  const int32_t* steps;   // [B] or null (= T)
+  const uint8_t* mask;    // [B, T] or null (= all)
+  const float* state_in;
+  float* state_out;
+  int B, T, Hv, Hk, Dv, Dk;
+  int g_vec;
+};
+
+template <typename KT>
+__device__ __forceinline__ float load_k(const KT* p);
+template <>
+__device__ __forceinline__ float load_k<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float load_k<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat162float(*p);
+}
+
+template <typename KT, int DK>
+__global__ void __launch_bounds__(THREADS)
+    tape_replay_kernel(const ReplayParams p) {
+  extern __shared__ float sh[];
+  const int head = blockIdx.x;          // b * Hv + hv
+  const int b = head / p.Hv;
+  const int hv = head - b * p.Hv;
+  const int hk = hv / (p.Hv / p.Hk);
+  const int tid = threadIdx.x;
+
+  int nsteps = p.steps ? p.steps[b] : p.T;
+  nsteps = nsteps < 0 ? 0 : (nsteps > p.T ? p.T : nsteps);
+
+  // Which of the first nsteps steps are replayed (mask), as a bit set.
+  uint64_t active = 0;
+  for (int t = 0; t < nsteps; ++t)
+    if (!p.mask || p.mask[(size_t)b * p.T + t]) active |= (uint64_t(1) << t);
+
+  const int dv_dk = p.Dv * DK;
+  const size_t sbase = (size_t)head * dv_dk;
+  const float4* src = reinterpret_cast<const float4*>(p.state_in + sbase);
+  float4* dst = reinterpret_cast<float4*>(p.state_out + sbase);
+  const int n4 = dv_dk / 4;
+
+  if (active == 0) {
+    if (p.state_in != p.state_out)
+      for (int i = tid; i < n4; i += THREADS) dst[i] = src[i];
+    return;
+  }
+
+  // Stage this head's replayed steps: k [a][DK], g [a] or [a][DK], delta [a][Dv]
+  // (k and vector g first: their rows start on 16-byte boundaries).
+  const int gw = p.g_vec ? DK : 1;
+  float* s_k = sh;
+  float* s_g = s_k + nsteps * DK;
+  float* s_delta = s_g + nsteps * gw;
+  for (int i = tid; i < nsteps * p.Dv; i += THREADS) {
+    const int t = i / p.Dv, dv = i - t * p.Dv;
+    s_delta[i] = p.tape[(((size_t)b * p.T + t) * p.Hv + hv) * p.Dv + dv];
+  }
+  const KT* kp = reinterpret_cast<const KT*>(p.k);
+  for (int i = tid; i < nsteps * DK; i += THREADS) {
+    const int t = i / DK, dk = i - t * DK;
+    s_k[i] = load_k<KT>(kp + (((size_t)b * p.T + t) * p.Hk + hk) * DK + dk);
+  }
+  for (int i = tid; i < nsteps * gw; i += THREADS) {
+    const int t = i / gw, j = i - t * gw;
+    s_g[i] = p.g[(((size_t)b * p.T + t) * p.Hv + hv) * gw + j];
+  }
+
+  // Thread tid owns float4 chunks f = j * THREADS + tid: row dv = 4f / DK,
+  // columns dk0..dk0+3 with dk0 = 4f % DK = (4 * tid) % DK (DK divides 1024).
+  float4 st[MAX_CHUNKS];
+  const int nchunk = (n4 + THREADS - 1) / THREADS;
+#pragma unroll
+  for (int j = 0; j < MAX_CHUNKS; ++j) {
+    const int f = j * THREADS + tid;
+    if (j < nchunk && f < n4) st[j] = __ldcs(src + f);
+  }
+  __syncthreads();
+
+  const int dk0 = (4 * tid) % DK;
+  for (int t = 0; t < nsteps; ++t) {
+    if (!((active >> t) & 1)) continue;
+    const float4 kv = *reinterpret_cast<const float4*>(s_k + t * DK + dk0);
+    float4 gv;
+    if (p.g_vec) {
+      gv = *reinterpret_cast<const float4*>(s_g + t * DK + dk0);
+    } else {
+      const float g0 = s_g[t];
+      gv = make_float4(g0, g0, g0, g0);
+    }
+#pragma unroll
+    for (int j = 0; j < MAX_CHUNKS; ++j) {
+      const int f = j * THREADS + tid;
+      if (j < nchunk && f < n4) {
+        const int dv = (4 * f) / DK;
+        const float d = s_delta[t * p.Dv + dv];
+        float4 s = st[j];
+        s.x = __fadd_rn(__fmul_rn(s.x, gv.x), __fmul_rn(d, kv.x));
+        s.y = __fadd_rn(__fmul_rn(s.y, gv.y), __fmul_rn(d, kv.y));
+        s.z = __fadd_rn(__fmul_rn(s.z, gv.z), __fmul_rn(d, kv.z));
+        s.w = __fadd_rn(__fmul_rn(s.w, gv.w), __fmul_rn(d, kv.w));
+        st[j] = s;
+      }
+    }
+  }
+
+#pragma unroll
+  for (int j = 0; j < MAX_CHUNKS; ++j) {
+    const int f = j * THREADS + tid;
+    if (j < nchunk && f < n4) __stcs(dst + f, st[j]);
+  }
+}
+
+template <typename KT>
+int launch_replay(const ReplayParams& p, cudaStream_t stream) {
+  const int gw = p.g_vec ? p.Dk : 1;
+  const size_t smem = size_t(p.T) * (p.Dv + p.Dk + gw) * sizeof(float);
+  const int grid = p.B * p.Hv;
+  switch (p.Dk) {
+#define DFL_CASE(D)                                                                        \
+  case D: {                                                                                \
+    static std::atomic<uint64_t> done{0};                                                  \
+    int dev = 0;                                                                           \
+    if (cudaGetDevice(&dev) != cudaSuccess) return DFL_ERR_CUDA;                           \
+    int st = host::ensure_smem(tape_replay_kernel<KT, D>, kMaxSmem, dev, done);             \
+    if (st != DFL_OK) return st;                                                           \
+    tape_replay_kernel<KT, D><<<grid, THREADS, smem, stream>>>(p);                         \
+    break;                                                                                 \
+  }
+    DFL_CASE(32)
+    DFL_CASE(64)
+    DFL_CASE(128)
+    DFL_CASE(256)
+#undef DFL_CASE
+    default:
+      return DFL_ERR_BAD_SHAPE;
+  }
+  return host::launch_status();
+}
+
+}  // namespace gdn
+}  // namespace dfl
+
+extern "C" int dfl_gdn_tape_replay(const float* tape, const void* k, int k_is_bf16,
+                                   const float* g, int g_vectorized, const int32_t* steps,
+                                   const uint8_t* mask, const float* state_in, float* state_out,
+                                   int B, int T, int Hv, int Hk, int Dv, int Dk, void* stream) {
+  using namespace dfl;
+  if (B < 0 || T < 0 || Hv < 1 || Hk < 1 || Dv < 1) return DFL_ERR_BAD_SHAPE;
+  if (Hv % Hk != 0) return DFL_ERR_BAD_SHAPE;
+  if (Dk != 32 && Dk != 64 && Dk != 128 && Dk != 256) return DFL_ERR_BAD_SHAPE;
+  if ((long long)Dv * Dk > (long long)gdn::MAX_CHUNKS * gdn::THREADS * 4) return DFL_ERR_BAD_SHAPE;
+  if (T > gdn::MAX_STEPS) return DFL_ERR_BAD_SHAPE;
+  if (B == 0) return DFL_OK;
+  if (!state_in || !state_out) return DFL_ERR_NULL_POINTER;
+  if (T > 0 && (!tape || !k || !g)) return DFL_ERR_NULL_POINTER;
+  if (!host::aligned(state_in, 16) || !host::aligned(state_out, 16)) return DFL_ERR_MISALIGNED;
+  int dev, sms;
+  int st = host::current_device(&dev, &sms);
+  if (st != DFL_OK) return st;
+  gdn::ReplayParams p;
+  p.tape = tape;
+  p.k = k;
+  p.g = g;
+  p.steps = steps;
+  p.mask = mask;
+  p.state_in = state_in;
+  p.state_out = state_out;
+  p.B = B;
+  p.T = T;
+  p.Hv = Hv;
+  p.Hk = Hk;
+  p.Dv = Dv;
+  p.Dk = Dk;
+  p.g_vec = g_vectorized ? 1 : 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return k_is_bf16 ? gdn::launch_replay<__nv_bfloat16>(p, s) : gdn::launch_replay<float>(p, s);
+}

@@ -11,17 +11,30 @@
 // Mapping onto Blackwell (M is tiny, so the MMA is "swapped"):
 //   * a CTA tile is 128 output channels (the UMMA M dimension) x MT tokens
 //     (the UMMA N dimension, MT = 16 or 32);
-//   * TMA streams, per 512-wide K unit, the packed nibbles (2 x [128 x 128 B]
-//     boxes, 128-byte swizzle), the x slice (8 x [MT x 64] bf16 boxes,
-//     128-byte swizzle, directly in the UMMA B layout) and the 8 scales and
-//     8 biases of every row ([128 x 16 B] boxes) into a 3-4 stage ring;
-//   * eight dequant warps unpack nibbles in registers (bf16x2 magic-number
-//     trick + one bf16x2 FMA per pair, exact against the fp32 formula) and
-//     write the bf16 weight tile straight into TMEM with tcgen05.st, one TMEM
-//     lane per output channel, 32 columns per 64-wide quant group;
-//   * one thread issues tcgen05.mma with A from TMEM and B (x) from shared
-//     memory, accumulating fp32 in TMEM (two accumulator buffers);
-//   * four epilogue warps drain the accumulator with tcgen05.ld.
+//   * the pipeline unit is 512 of K (8 quant groups).  TMA streams only the
+//     packed nibbles (2 boxes of [128 rows x 128 B], 128-byte swizzle) into a
+//     4-stage ring: TMA cost scales with the number of box rows, so nothing
+//     with short rows goes through it.  The producer warp's 32 lanes copy the
+//     unit's 8 scales and 8 biases per row with 16-byte cp.async into the
+//     same stage, completing on the stage's mbarrier;
+//   * dequant warps (groups of four, one warp per TMEM lane quadrant, one
+//     thread per output channel) unpack nibbles in registers: one shift + one
+//     LOP3 per bf16 pair gives 128 + n exactly, then one bf16x2 subtract and
+//     one bf16x2 FMA give n * s + b with a single rounding.  The pairs come
+//     out in the within-8 K order 0,4,1,5,2,6,3,7; the tile goes straight
+//     into TMEM with tcgen05.st (one lane per output channel, 32 columns per
+//     quant group, 8 slots = one unit);
+//   * the four epilogue warps also stage x: one unit ahead they load the x
+//     slice from global memory (L2), apply the same within-8 K permutation in
+//     registers and store it into a shared-memory ring in the UMMA
+//     128-byte-swizzled K-major layout;
+//   * four MMA warps each own an accumulator and two of the eight sub-blocks
+//     of a unit.  A thread keeps one tcgen05.mma in flight for ~50-65 cycles
+//     whatever N is, and any dependent scalar work between two MMAs adds to
+//     that, so the issue loops do nothing but wait and issue MMAs with
+//     precomputed descriptors; four issuers keep up with HBM at N = 16;
+//   * the epilogue warps drain and sum the four accumulators (fixed order);
+//     accumulators are double-buffered so the epilogue overlaps the next tile.
 // Work is split "stream-K" style: the (tile, K unit) space is cut into one
 // contiguous range per CTA (grid = min(#SMs, #units)), so every SM streams
 // the same number of bytes whatever N and K are.  Tiles shared by several
@@ -40,35 +53,51 @@ constexpr int UNIT_K = 512;       // K per pipeline stage (8 quant groups)
 constexpr int GS = 64;            // quant group size (one TMEM A slot)
 constexpr int NSUB = UNIT_K / GS; // 8 sub-blocks per stage
 constexpr int A_COLS = 32;        // TMEM columns per A slot (64 bf16 per lane)
-constexpr int NUM_WARPS = 14;
-constexpr int NUM_THREADS = NUM_WARPS * 32;
+constexpr int NUM_MMA_WARPS = 4;  // concurrent tcgen05.mma issuers, one accumulator each
+constexpr int NDG = 4;            // dequant warp groups (4 warps each)
 constexpr int WARP_TMA = 0;
-constexpr int WARP_MMA = 1;
-constexpr int WARP_DQ0 = 2;       // warps 2..9 dequantise
-constexpr int WARP_EPI0 = 10;     // warps 10..13 drain the accumulator
+constexpr int WARP_MMA0 = 1;                           // warps 1..4 issue MMAs
+constexpr int WARP_DQ0 = WARP_MMA0 + NUM_MMA_WARPS;    // dequant warps
+constexpr int WARP_EPI0 = WARP_DQ0 + 4 * NDG;          // 4 x-staging + epilogue warps
+constexpr int NUM_WARPS = WARP_EPI0 + 4;
+constexpr int NUM_THREADS = NUM_WARPS * 32;
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL0 = NSUB * A_COLS;  // 256
+constexpr int SUB_PER_MMA = NSUB / NUM_MMA_WARPS;  // sub-blocks per MMA warp per unit
+constexpr int BAR_ID_EPI = 1;            // named barrier of the epilogue warps
+constexpr int SBC = 4;                   // units per scale/bias chunk (32 groups)
+static_assert(NSUB % NUM_MMA_WARPS == 0, "sub-block split");
 
 template <int MT>
 struct Cfg {
   static constexpr int PACK_BYTES = BN * UNIT_K / 2;  // 32 KB
+  static constexpr int STAGE_BYTES = PACK_BYTES;
+  static constexpr int NSTAGE = 4;
+  // scales / biases: chunks of SBC units (64-byte rows), double-buffered
+  static constexpr int SBC_ROW = SBC * NSUB * 2;      // 64 bytes
+  static constexpr int SBC_HALF = BN * SBC_ROW;       // scales (or biases) of a chunk
+  static constexpr int SBC_BYTES = 2 * SBC_HALF;
+  static constexpr int OFF_SB = NSTAGE * STAGE_BYTES;
   static constexpr int XBLK_BYTES = MT * 128;         // one [MT x 64] bf16 block
-  static constexpr int X_BYTES = MT * UNIT_K * 2;
-  static constexpr int SB_BYTES = BN * 16;            // 8 bf16 per row
-  static constexpr int STAGE_BYTES = PACK_BYTES + X_BYTES + 2 * SB_BYTES;
-  static constexpr int NSTAGE = (MT <= 16) ? 4 : 3;
-  static constexpr int OFF_X = PACK_BYTES;
-  static constexpr int OFF_S = PACK_BYTES + X_BYTES;
-  static constexpr int OFF_B = OFF_S + SB_BYTES;
-  static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = NSTAGE * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr int XSLOT_BYTES = NSUB * XBLK_BYTES;  // one unit of x
+  static constexpr int XS = (MT <= 16) ? 3 : 2;       // x ring depth (units)
+  static constexpr int OFF_XRING = OFF_SB + 2 * SBC_BYTES;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM_BYTES = OFF_XRING + XS * XSLOT_BYTES + BAR_BYTES + 1024;
+  // x chunks (16 bytes = 8 bf16) per unit, and per x-staging thread.
+  static constexpr int X_CHUNKS = NSUB * MT * 8;
+  static constexpr int X_PER_THREAD = X_CHUNKS / 128;
+  static constexpr int NACC = NUM_MMA_WARPS;
+  static constexpr int ACC_COLS = NACC * MT;  // one accumulator buffer
   static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(XBLK_BYTES % 1024 == 0, "x blocks must keep 1024-byte alignment");
-  static_assert(ACC_COL0 + 2 * MT <= TMEM_COLS, "TMEM budget");
+  static_assert(X_CHUNKS % 128 == 0, "x chunks per thread");
+  static_assert(ACC_COL0 + 2 * ACC_COLS <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
 struct Params {
-  const uint16_t* x;       // only used when scales need plain loads
+  const uint16_t* x;       // [M, K]
   const uint16_t* scales;  // [N, K/64]
   const uint16_t* biases;  // [N, K/64]
   uint16_t* y;             // [M, N]
@@ -76,7 +105,7 @@ struct Params {
   int* counters;           // [n_tiles]
   int M, K, N;
   int n_tiles, k_units, total_units, grid;
-  int sb_tma;              // scales/biases via TMA (K % 512 == 0)
+  int sb_tma;              // scales/biases rows are 16-byte multiples (TMA path)
 };
 
 __device__ __forceinline__ int unit_begin(int c, int total, int grid) {
@@ -90,20 +119,19 @@ __device__ __forceinline__ int cta_of_unit(int u, int total, int grid) {
   return int(c);
 }
 
-// Eight nibbles (one packed word, low nibble first) -> four bf16x2 words in
-// natural K order: w = nib * s + b with a single rounding to bf16.
+// Eight nibbles (one packed word, low nibble first) -> four bf16x2 words
+// w = nib * s + b with a single rounding to bf16.  The pairs come out in the
+// K order (0,4), (1,5), (2,6), (3,7): each is one shift + one LOP3 (mask and
+// exponent bits), with no byte permutes.  The x operand gets the same
+// within-8 permutation (permute_x_chunk), so the MMA still sums x_k * w_k.
 __device__ __forceinline__ void dequant8(uint32_t q, __nv_bfloat162 s2, __nv_bfloat162 b2,
                                          uint32_t* out) {
   const uint32_t kMagic = 0x43004300u;  // bf16x2 (128, 128); low mantissa bits carry n
-  const uint32_t a = (q & 0x000F000Fu) | kMagic;          // (n0, n4)
-  const uint32_t b = ((q >> 4) & 0x000F000Fu) | kMagic;   // (n1, n5)
-  const uint32_t c = ((q >> 8) & 0x000F000Fu) | kMagic;   // (n2, n6)
-  const uint32_t d = ((q >> 12) & 0x000F000Fu) | kMagic;  // (n3, n7)
   uint32_t p[4];
-  p[0] = __byte_perm(a, b, 0x5410);  // (n0, n1)
-  p[1] = __byte_perm(c, d, 0x5410);  // (n2, n3)
-  p[2] = __byte_perm(a, b, 0x7632);  // (n4, n5)
-  p[3] = __byte_perm(c, d, 0x7632);  // (n6, n7)
+  p[0] = (q & 0x000F000Fu) | kMagic;          // (n0, n4) + 128
+  p[1] = ((q >> 4) & 0x000F000Fu) | kMagic;   // (n1, n5) + 128
+  p[2] = ((q >> 8) & 0x000F000Fu) | kMagic;   // (n2, n6) + 128
+  p[3] = ((q >> 12) & 0x000F000Fu) | kMagic;  // (n3, n7) + 128
   const __nv_bfloat162 k128 = __halves2bfloat162(__ushort_as_bfloat16(0x4300),
                                                  __ushort_as_bfloat16(0x4300));
 #pragma unroll
@@ -115,42 +143,112 @@ __device__ __forceinline__ void dequant8(uint32_t q, __nv_bfloat162 s2, __nv_bfl
   }
 }
 
+// Reorders the 8 bf16 of a 16-byte x chunk from k = 0..7 to the order the
+// dequantised A operand uses: 0, 4, 1, 5, 2, 6, 3, 7.
+__device__ __forceinline__ uint4 permute_x_chunk(uint4 v) {
+  uint4 r;
+  r.x = __byte_perm(v.x, v.z, 0x5410);  // (x0, x4)
+  r.y = __byte_perm(v.x, v.z, 0x7632);  // (x1, x5)
+  r.z = __byte_perm(v.y, v.w, 0x5410);  // (x2, x6)
+  r.w = __byte_perm(v.y, v.w, 0x7632);  // (x3, x7)
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pick4(const uint32_t (&v)[4], int i) {
+  return i == 0 ? v[0] : i == 1 ? v[1] : i == 2 ? v[2] : v[3];
+}
+
 __device__ __forceinline__ __nv_bfloat162 splat_bf16(uint32_t word, int half) {
   const uint16_t h = half ? uint16_t(word >> 16) : uint16_t(word & 0xFFFFu);
   const __nv_bfloat16 v = __ushort_as_bfloat16(h);
   return __halves2bfloat162(v, v);
 }
 
-template <int MT>
+// Sum the NACC accumulators of one buffer (accumulator a at columns
+// taddr + a * MT) in order a = 0..NACC-1.
+template <int MT, int NACC>
 __device__ __forceinline__ void epilogue_load(uint32_t taddr, float (&acc)[MT]) {
   uint32_t r[16];
 #pragma unroll
   for (int c = 0; c < MT; c += 16) {
-    tmem_ld_32x32b_x16(taddr + c, r);
-    tmem_ld_wait();
 #pragma unroll
-    for (int i = 0; i < 16; ++i) acc[c + i] = __uint_as_float(r[i]);
+    for (int a = 0; a < NACC; ++a) {
+      tmem_ld_32x32b_x16(taddr + a * MT + c, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        acc[c + i] = (a == 0) ? __uint_as_float(r[i]) : acc[c + i] + __uint_as_float(r[i]);
+    }
+  }
+}
+
+// Byte offset of 16-byte chunk c of row r in a [rows x 64 B] tile written by
+// TMA with the 64-byte swizzle (chunk index XOR bits 7-8 of the address).
+__device__ __forceinline__ uint32_t sw64_offset(int r, int c) {
+  return uint32_t(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+}
+
+// The x chunks (16 bytes = 8 bf16) x-staging thread et (0..127) handles for
+// the unit starting at k0: idx = et + 128 * t = (b * MT + r) * 8 + c is
+// chunk c of token row r in K block b.  Rows >= M and columns >= K read 0.
+template <int MT>
+__device__ __forceinline__ void load_x_unit(const Params& p, int k0, int et,
+                                            uint4 (&xr)[Cfg<MT>::X_PER_THREAD]) {
+#pragma unroll
+  for (int t = 0; t < Cfg<MT>::X_PER_THREAD; ++t) {
+    const int idx = et + 128 * t;
+    const int c = idx & 7;
+    const int r = (idx >> 3) % MT;
+    const int b = idx / (MT * 8);
+    const int k = k0 + b * GS + c * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < p.M && k < p.K)
+      v = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)r * p.K + k));
+    xr[t] = v;
+  }
+}
+
+// Permute and store them into a ring slot: block b at b * XBLK_BYTES, UMMA
+// K-major with 128-byte swizzle (chunk c of row r at r*128 + ((c ^ (r&7)) << 4)).
+template <int MT>
+__device__ __forceinline__ void store_x_unit(uint32_t slot, int et,
+                                             const uint4 (&xr)[Cfg<MT>::X_PER_THREAD]) {
+#pragma unroll
+  for (int t = 0; t < Cfg<MT>::X_PER_THREAD; ++t) {
+    const int idx = et + 128 * t;
+    const int c = idx & 7;
+    const int r = (idx >> 3) % MT;
+    const int b = idx / (MT * 8);
+    st_shared_v4(slot + b * Cfg<MT>::XBLK_BYTES + r * 128 + (uint32_t((c ^ (r & 7))) << 4),
+                 permute_x_chunk(xr[t]));
   }
 }
 
 template <int MT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    qmm_w4g64_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_b,
-                     const Params p) {
+    qmm_w4g64_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
+                     const __grid_constant__ CUtensorMap tm_b, const Params p) {
   using C = Cfg<MT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::NSTAGE * C::STAGE_BYTES);
-  uint64_t* full = bars;                       // [NSTAGE]  TMA landed
-  uint64_t* empty = full + C::NSTAGE;          // [NSTAGE]  stage consumed
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_XRING + C::XS * C::XSLOT_BYTES);
+  uint64_t* full = bars;                       // [NSTAGE]  nibbles + scales landed
+  uint64_t* empty = full + C::NSTAGE;          // [NSTAGE]  stage read by the dequant warps
   uint64_t* afull = empty + C::NSTAGE;         // [NSUB]    TMEM A slot written
   uint64_t* aempty = afull + NSUB;             // [NSUB]    TMEM A slot read by MMA
-  uint64_t* accfull = aempty + NSUB;           // [2]
+  uint64_t* xfull = aempty + NSUB;             // [XS]      x slot staged
+  uint64_t* xfree = xfull + C::XS;             // [XS]      x slot read by all MMA warps
+  uint64_t* sbfull = xfree + C::XS;            // [2]       scale/bias chunk landed
+  uint64_t* sbempty = sbfull + 2;              // [2]       chunk read by the dequant warps
+  uint64_t* accfull = sbempty + 2;             // [2]
   uint64_t* accempty = accfull + 2;            // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
   int* flag_slot = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(flag_slot + 1);
+  auto wait = [abort_word](uint64_t* bar, uint32_t parity) {
+    return mbar_wait_abortable(bar, parity, abort_word);
+  };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -161,21 +259,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int ku = p.k_units;
 
   if (threadIdx.x == 0) {
+    *abort_word = 0;
     for (int i = 0; i < C::NSTAGE; ++i) {
-      mbar_init(&full[i], p.sb_tma ? 1 : 2);
-      mbar_init(&empty[i], 8 + 1);
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4 * NDG);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sbfull[i], 1);
+      mbar_init(&sbempty[i], 4 * NDG);
     }
     for (int i = 0; i < NSUB; ++i) {
       mbar_init(&afull[i], 4);
       mbar_init(&aempty[i], 1);
     }
+    for (int i = 0; i < C::XS; ++i) {
+      mbar_init(&xfull[i], 4);
+      mbar_init(&xfree[i], NUM_MMA_WARPS);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&accfull[i], 1);
+      mbar_init(&accfull[i], NUM_MMA_WARPS);
       mbar_init(&accempty[i], 4);
     }
     fence_barrier_init();
   }
-  if (warp == WARP_MMA) {
+  if (warp == WARP_TMA) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
@@ -186,96 +293,127 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp == WARP_TMA) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_w);
-      tma_prefetch_desc(&tm_x);
-      if (p.sb_tma) {
+    // Under full load every instruction of this warp waits for an issue slot
+    // behind the dequant warps, so the loop is kept to a few instructions
+    // per unit: coordinates advance incrementally, one lane issues.
+    if (p.sb_tma) {
+      if (lane == 0) {
+        tma_prefetch_desc(&tm_w);
         tma_prefetch_desc(&tm_s);
         tma_prefetch_desc(&tm_b);
-      }
-    }
-    const int groups = p.K / GS;
-    for (int it = 0; it < n_units; ++it) {
-      const int s = it % C::NSTAGE;
-      const uint32_t ph = (it / C::NSTAGE) & 1;
-      bool ok = true;
-      if (lane == 0) ok = mbar_wait(&empty[s], ph ^ 1);
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      if (!ok) break;
-      const int u = u0 + it;
-      const int tile = u / ku;
-      const int kb = u - tile * ku;
-      const int n0 = tile * BN;
-      const int k0 = kb * UNIT_K;
-      uint8_t* st = smem + s * C::STAGE_BYTES;
-      if (lane == 0) {
-        const uint32_t bytes = C::PACK_BYTES + C::X_BYTES + (p.sb_tma ? 2 * C::SB_BYTES : 0);
-        mbar_arrive_expect_tx(&full[s], bytes);
-        tma_load_2d(st, &tm_w, &full[s], k0 / 8, n0);
-        tma_load_2d(st + C::PACK_BYTES / 2, &tm_w, &full[s], k0 / 8 + 32, n0);
-#pragma unroll
-        for (int b = 0; b < NSUB; ++b)
-          tma_load_2d(st + C::OFF_X + b * C::XBLK_BYTES, &tm_x, &full[s], k0 + b * GS, 0);
-        if (p.sb_tma) {
-          tma_load_2d(st + C::OFF_S, &tm_s, &full[s], k0 / GS, n0);
-          tma_load_2d(st + C::OFF_B, &tm_b, &full[s], k0 / GS, n0);
+        int tile = u0 / ku, kb = u0 - (u0 / ku) * ku;
+        int chunk = -1;
+        for (int it = 0; it < n_units; ++it) {
+          const int n0 = tile * BN;
+          if (it == 0 || kb % SBC == 0) {
+            ++chunk;
+            const int cs = chunk & 1;
+            wait(&sbempty[cs], ((chunk >> 1) & 1) ^ 1);
+            if (*abort_word) break;
+            uint8_t* dst = smem + C::OFF_SB + cs * C::SBC_BYTES;
+            mbar_arrive_expect_tx(&sbfull[cs], C::SBC_BYTES);
+            tma_load_2d(dst, &tm_s, &sbfull[cs], (kb / SBC) * SBC * NSUB, n0);
+            tma_load_2d(dst + C::SBC_HALF, &tm_b, &sbfull[cs], (kb / SBC) * SBC * NSUB, n0);
+          }
+          const int s = it % C::NSTAGE;
+          wait(&empty[s], ((it / C::NSTAGE) & 1) ^ 1);
+          if (*abort_word) break;
+          uint8_t* st = smem + s * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], C::PACK_BYTES);
+          tma_load_2d(st, &tm_w, &full[s], kb * (UNIT_K / 8), n0);
+          tma_load_2d(st + C::PACK_BYTES / 2, &tm_w, &full[s], kb * (UNIT_K / 8) + 32, n0);
+          if (++kb == ku) { kb = 0; ++tile; }
         }
       }
-      if (!p.sb_tma) {
-        // Row strides of scales/biases are not 16-byte multiples: plain loads.
-        uint16_t* ss = reinterpret_cast<uint16_t*>(st + C::OFF_S);
-        uint16_t* sbv = reinterpret_cast<uint16_t*>(st + C::OFF_B);
-        const int g0 = k0 / GS;
-        for (int i = lane; i < BN * 8; i += 32) {
-          const int r = i >> 3, gi = i & 7;
-          const int n = n0 + r, g = g0 + gi;
-          uint16_t sv = 0, bv = 0;
-          if (n < p.N && g < groups) {
-            sv = p.scales[(size_t)n * groups + g];
-            bv = p.biases[(size_t)n * groups + g];
+    } else {
+      // Scale/bias rows are not 16-byte multiples (K % 512 != 0): the warp
+      // fills each chunk with plain loads, in the same swizzled layout.
+      if (lane == 0) tma_prefetch_desc(&tm_w);
+      const int groups = p.K / GS;
+      int tile = u0 / ku, kb = u0 - (u0 / ku) * ku;
+      int chunk = -1;
+      for (int it = 0; it < n_units; ++it) {
+        const int n0 = tile * BN;
+        if (it == 0 || kb % SBC == 0) {
+          ++chunk;
+          const int cs = chunk & 1;
+          if (lane == 0) wait(&sbempty[cs], ((chunk >> 1) & 1) ^ 1);
+          __syncwarp();
+          if (*abort_word) break;
+          uint8_t* dst = smem + C::OFF_SB + cs * C::SBC_BYTES;
+          const int g0 = (kb / SBC) * SBC * NSUB;
+          for (int i = lane; i < BN * SBC * NSUB; i += 32) {
+            const int r = i / (SBC * NSUB), gi = i - r * (SBC * NSUB);
+            const int n = n0 + r, g = g0 + gi;
+            uint16_t sv = 0, bv = 0;
+            if (n < p.N && g < groups) {
+              sv = p.scales[(size_t)n * groups + g];
+              bv = p.biases[(size_t)n * groups + g];
+            }
+            const uint32_t off = sw64_offset(r, gi >> 3) + (gi & 7) * 2;
+            *reinterpret_cast<uint16_t*>(dst + off) = sv;
+            *reinterpret_cast<uint16_t*>(dst + C::SBC_HALF + off) = bv;
           }
-          ss[i] = sv;
-          sbv[i] = bv;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sbfull[cs]);
+        }
+        const int s = it % C::NSTAGE;
+        if (lane == 0) {
+          wait(&empty[s], ((it / C::NSTAGE) & 1) ^ 1);
+          if (!*abort_word) {
+            uint8_t* st = smem + s * C::STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[s], C::PACK_BYTES);
+            tma_load_2d(st, &tm_w, &full[s], kb * (UNIT_K / 8), n0);
+            tma_load_2d(st + C::PACK_BYTES / 2, &tm_w, &full[s], kb * (UNIT_K / 8) + 32, n0);
+          }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full[s]);
+        if (*abort_word) break;
+        if (++kb == ku) { kb = 0; ++tile; }
       }
     }
-  } else if (warp == WARP_MMA) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp < WARP_DQ0) {
+    // ------------------------------------------------------------ MMA issuers
+    // Warp j issues the MMAs of sub-blocks j, j + 4 into accumulator j.  The
+    // loop body is only waits and MMAs: everything else is precomputed.
+    const int j = warp - WARP_MMA0;
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_bf16(BN, MT);
+      const uint64_t ring_desc = make_sw128_desc(smem_u32(smem + C::OFF_XRING));
+      constexpr uint64_t kSlotDesc = uint64_t(C::XSLOT_BYTES >> 4);
+      constexpr uint64_t kBlkDesc = uint64_t(C::XBLK_BYTES >> 4);
       int acc_it = 0;
       uint32_t buf = 0;
-      for (int it = 0; it < n_units; ++it) {
-        const int s = it % C::NSTAGE;
-        const uint32_t ph = (it / C::NSTAGE) & 1;
-        const int kb = (u0 + it) % ku;
+      int kb = u0 % ku;
+      for (int it = 0; it < n_units; ++it, kb = (kb + 1 == ku) ? 0 : kb + 1) {
         const bool seg_start = (it == 0) || (kb == 0);
         const bool seg_end = (it == n_units - 1) || (kb == ku - 1);
+        const int xs = it % C::XS;
         if (seg_start) {
           buf = acc_it & 1;
-          if (!mbar_wait(&accempty[buf], ((acc_it >> 1) & 1) ^ 1)) break;
-          tc_fence_after();
+          wait(&accempty[buf], ((acc_it >> 1) & 1) ^ 1);
         }
-        if (!mbar_wait(&full[s], ph)) break;
-        const uint32_t xbase = smem_u32(smem + s * C::STAGE_BYTES + C::OFF_X);
-        const uint32_t d_tmem = tmem_base + ACC_COL0 + buf * MT;
-        bool ok = true;
-        for (int sb = 0; sb < NSUB; ++sb) {
-          if (!mbar_wait(&afull[sb], it & 1)) { ok = false; break; }
-          tc_fence_after();
+        wait(&xfull[xs], (it / C::XS) & 1);
+        const uint32_t d_tmem = tmem_base + ACC_COL0 + buf * C::ACC_COLS + j * MT;
+        const uint64_t slot_desc = ring_desc + kSlotDesc * xs;
+        uint32_t acc0 = seg_start ? 0u : 1u;
 #pragma unroll
-          for (int k4 = 0; k4 < GS / 16; ++k4) {
-            const uint32_t a_tmem = tmem_base + sb * A_COLS + k4 * 8;
-            const uint64_t bdesc = make_sw128_desc(xbase + sb * C::XBLK_BYTES + k4 * 32);
-            const uint32_t accum = (seg_start && sb == 0 && k4 == 0) ? 0u : 1u;
-            mma_bf16_ts(d_tmem, a_tmem, bdesc, idesc, accum);
+        for (int i = 0; i < SUB_PER_MMA; ++i) {
+          const int sb = j + i * NUM_MMA_WARPS;
+          wait(&afull[sb], it & 1);
+          tc_fence_after();
+          if (!*abort_word) {
+            const uint32_t a_tmem = tmem_base + sb * A_COLS;
+            const uint64_t bdesc = slot_desc + kBlkDesc * sb;
+            mma_bf16_ts(d_tmem, a_tmem, bdesc, idesc, acc0);
+            mma_bf16_ts(d_tmem, a_tmem + 8, bdesc + 2, idesc, 1u);
+            mma_bf16_ts(d_tmem, a_tmem + 16, bdesc + 4, idesc, 1u);
+            mma_bf16_ts(d_tmem, a_tmem + 24, bdesc + 6, idesc, 1u);
           }
+          acc0 = 1u;
           tc_commit(&aempty[sb]);
         }
-        if (!ok) break;
-        tc_commit(&empty[s]);
+        tc_commit(&xfree[xs]);
         if (seg_end) {
           tc_commit(&accfull[buf]);
           ++acc_it;
@@ -286,70 +424,104 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp < WARP_EPI0) {
     // ------------------------------------------------------------ dequant
     const int dw = warp - WARP_DQ0;
-    const int grp = dw >> 2;              // handles sub-blocks with sb % 2 == grp
+    const int grp = dw >> 2;              // handles sub-blocks with sb % NDG == grp
     const int quad = warp & 3;            // TMEM lane quadrant of this warp
     const int r = quad * 32 + lane;       // output channel within the tile
     const uint32_t lane_base = tmem_base + (uint32_t(quad * 32) << 16);
-    for (int it = 0; it < n_units; ++it) {
+    int kb = u0 % ku;
+    int chunk = -1;
+    for (int it = 0; it < n_units; ++it, kb = (kb + 1 == ku) ? 0 : kb + 1) {
+      if (it == 0 || kb % SBC == 0) {
+        if (chunk >= 0) {  // done with the previous scale/bias chunk
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sbempty[chunk & 1]);
+        }
+        ++chunk;
+        wait(&sbfull[chunk & 1], (chunk >> 1) & 1);
+      }
       const int s = it % C::NSTAGE;
       const uint32_t ph = (it / C::NSTAGE) & 1;
-      if (!mbar_wait(&full[s], ph)) break;
+      wait(&full[s], ph);
       const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
-      const uint4 sv = ld_shared_v4(st + C::OFF_S + r * 16);
-      const uint4 bv = ld_shared_v4(st + C::OFF_B + r * 16);
+      const uint32_t sbc = smem_u32(smem + C::OFF_SB + (chunk & 1) * C::SBC_BYTES) +
+                           sw64_offset(r, kb % SBC);
+      const uint4 sv = ld_shared_v4(sbc);
+      const uint4 bv = ld_shared_v4(sbc + C::SBC_HALF);
       const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
       const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-      bool ok = true;
 #pragma unroll
-      for (int j = 0; j < NSUB / 2; ++j) {
-        const int sb = 2 * j + grp;
-        if (!mbar_wait(&aempty[sb], (it & 1) ^ 1)) { ok = false; break; }
+      for (int jj = 0; jj < (NSUB + NDG - 1) / NDG; ++jj) {
+        const int sb = NDG * jj + grp;
+        if (sb >= NSUB) break;
+        wait(&aempty[sb], (it & 1) ^ 1);
         tc_fence_after();
         const int box = sb >> 2;
         const int c0 = 2 * (sb & 3);
         const uint32_t rowb = st + box * (C::PACK_BYTES / 2) + r * 128;
         const uint4 q0 = ld_shared_v4(rowb + (uint32_t((c0 ^ (r & 7))) << 4));
         const uint4 q1 = ld_shared_v4(rowb + (uint32_t(((c0 + 1) ^ (r & 7))) << 4));
-        // group sb = 2j + grp lives in word j, half grp
-        const __nv_bfloat162 s2 = splat_bf16(sw[j], grp);
-        const __nv_bfloat162 b2 = splat_bf16(bw[j], grp);
+        // group sb lives in scale word sb / 2, half sb % 2
+        const __nv_bfloat162 sc = splat_bf16(pick4(sw, sb >> 1), sb & 1);
+        const __nv_bfloat162 bc = splat_bf16(pick4(bw, sb >> 1), sb & 1);
         uint32_t w[32];
-        dequant8(q0.x, s2, b2, &w[0]);
-        dequant8(q0.y, s2, b2, &w[4]);
-        dequant8(q0.z, s2, b2, &w[8]);
-        dequant8(q0.w, s2, b2, &w[12]);
-        dequant8(q1.x, s2, b2, &w[16]);
-        dequant8(q1.y, s2, b2, &w[20]);
-        dequant8(q1.z, s2, b2, &w[24]);
-        dequant8(q1.w, s2, b2, &w[28]);
+        dequant8(q0.x, sc, bc, &w[0]);
+        dequant8(q0.y, sc, bc, &w[4]);
+        dequant8(q0.z, sc, bc, &w[8]);
+        dequant8(q0.w, sc, bc, &w[12]);
+        dequant8(q1.x, sc, bc, &w[16]);
+        dequant8(q1.y, sc, bc, &w[20]);
+        dequant8(q1.z, sc, bc, &w[24]);
+        dequant8(q1.w, sc, bc, &w[28]);
         tmem_st_32x32b_x32(lane_base + sb * A_COLS, w);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&afull[sb]);
       }
-      if (!ok) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
   } else {
-    // ------------------------------------------------------------ epilogue
+    // ------------------------------------------------- x staging + epilogue
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int et = threadIdx.x - WARP_EPI0 * 32;  // 0..127
     const uint32_t lane_base = tmem_base + (uint32_t(quad * 32) << 16);
+    const uint32_t ring = smem_u32(smem + C::OFF_XRING);
+    uint4 xr[C::X_PER_THREAD];
+    // x for unit `ix` goes into slot ix % XS once the MMAs of unit ix - XS
+    // have read that slot.
+    auto stage_x = [&](int ix) {
+      const int xs = ix % C::XS;
+      if (ix >= C::XS) wait(&xfree[xs], ((ix / C::XS) - 1) & 1);
+      store_x_unit<MT>(ring + xs * C::XSLOT_BYTES, et, xr);
+      if (ix + 1 < n_units) load_x_unit<MT>(p, ((u0 + ix + 1) % ku) * UNIT_K, et, xr);
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xfull[xs]);
+    };
+    int staged = 0;  // units of x staged so far
     if (n_units > 0) {
+      load_x_unit<MT>(p, (u0 % ku) * UNIT_K, et, xr);
+      for (; staged < n_units && staged < C::XS; ++staged) stage_x(staged);
       const int t_first = u0 / ku;
       const int t_last = (u1 - 1) / ku;
       int acc_it = 0;
       for (int t = t_first; t <= t_last; ++t) {
         const int kb0 = (t == t_first) ? (u0 - t * ku) : 0;
         const int kb1 = (t == t_last) ? (u1 - t * ku) : ku;
+        // Stage x through this segment's last unit (its MMAs need it) and up
+        // to XS - 1 units beyond: staging unit ix waits for the MMAs of unit
+        // ix - XS, which is then still inside this segment, so those waits
+        // never depend on this segment's epilogue.
+        const int seg_last = t * ku + kb1 - 1 - u0;
+        for (; staged < n_units && staged <= seg_last + C::XS - 1; ++staged) stage_x(staged);
         const uint32_t buf = acc_it & 1;
-        if (!mbar_wait(&accfull[buf], (acc_it >> 1) & 1)) break;
+        // all four epilogue warps agree before leaving (they share BAR_ID_EPI)
+        if (!named_bar_and(BAR_ID_EPI, 128, wait(&accfull[buf], (acc_it >> 1) & 1))) break;
         tc_fence_after();
         float acc[MT];
-        epilogue_load<MT>(lane_base + ACC_COL0 + buf * MT, acc);
+        epilogue_load<MT, C::NACC>(lane_base + ACC_COL0 + buf * C::ACC_COLS, acc);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&accempty[buf]);
@@ -371,7 +543,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int m = 0; m < MT; ++m) mine[m * BN + r] = acc[m];
         __threadfence();
-        named_bar_sync(1, 128);
+        named_bar_sync(BAR_ID_EPI, 128);
         if (et == 0) {
           const int c_lo = cta_of_unit(t * ku, p.total_units, p.grid);
           const int c_hi = cta_of_unit(t * ku + ku - 1, p.total_units, p.grid);
@@ -379,7 +551,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int prev = atomicAdd(&p.counters[t], 1);
           *flag_slot = (prev == expected - 1) ? 1 : 0;
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(BAR_ID_EPI, 128);
         if (*flag_slot) {
           __threadfence();
           const int c_lo = cta_of_unit(t * ku, p.total_units, p.grid);
@@ -400,7 +572,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           if (et == 0) p.counters[t] = 0;
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(BAR_ID_EPI, 128);
       }
     }
   }
@@ -408,7 +580,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == WARP_MMA) tmem_dealloc(tmem_base, TMEM_COLS);
+  if (warp == WARP_TMA) tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
 }  // namespace qmm
@@ -421,8 +593,14 @@ namespace qmm {
 
 inline int choose_mt(int M) { return M <= 16 ? 16 : 32; }
 
+// Zero-invariant counter area at the start of every workspace (one int per
+// 128-row tile): N <= kMaxTiles * 128.
+constexpr size_t kCounterBytes = 64 * 1024;
+constexpr int kMaxTiles = int(kCounterBytes / sizeof(int));
+
 inline void geometry(int M, int K, int N, int num_sms, int* n_tiles, int* k_units, int* total,
                      int* grid) {
+  (void)M;
   *n_tiles = (N + BN - 1) / BN;
   *k_units = (K + UNIT_K - 1) / UNIT_K;
   *total = *n_tiles * *k_units;
@@ -433,9 +611,7 @@ inline size_t workspace_bytes_for(int M, int K, int N, int num_sms) {
   int n_tiles, k_units, total, grid;
   geometry(M, K, N, num_sms, &n_tiles, &k_units, &total, &grid);
   const int mt = choose_mt(M);
-  const size_t part = size_t(grid) * 2 * mt * BN * sizeof(float);
-  const size_t cnt = ((size_t(n_tiles) * sizeof(int)) + 255) & ~size_t(255);
-  return part + cnt;
+  return kCounterBytes + size_t(grid) * 2 * mt * BN * sizeof(float);
 }
 
 template <int MT>
@@ -456,30 +632,32 @@ int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const
   p.K = K;
   p.N = N;
   geometry(M, K, N, num_sms, &p.n_tiles, &p.k_units, &p.total_units, &p.grid);
-  p.partials = reinterpret_cast<float*>(ws);
-  p.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) +
-                                      size_t(p.grid) * 2 * MT * BN * sizeof(float));
+  // Workspace layout: [tile counters, fixed size][fp32 partials].  The
+  // counters sit at a fixed offset so that no call's partials ever overlap
+  // another call's counters; every kernel leaves its counters at zero.
+  p.counters = reinterpret_cast<int*>(ws);
+  p.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes);
+  // TMA of scale/bias rows needs 16-byte multiples: K % 512 == 0.
   p.sb_tma = (K % UNIT_K == 0) && host::aligned(scales, 16) && host::aligned(biases, 16);
 
-  CUtensorMap tm_w, tm_x, tm_s, tm_b;
+  CUtensorMap tm_w, tm_s, tm_b;
   st = host::make_tmap_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w_q, uint64_t(K / 8), uint64_t(N),
                           uint64_t(K / 2), 32, BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != DFL_OK) return st;
-  st = host::make_tmap_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, uint64_t(K), uint64_t(M),
-                          uint64_t(K) * 2, GS, MT, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (st != DFL_OK) return st;
   if (p.sb_tma) {
     st = host::make_tmap_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scales, uint64_t(K / GS),
-                            uint64_t(N), uint64_t(K / GS) * 2, 8, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+                            uint64_t(N), uint64_t(K / GS) * 2, SBC * NSUB, BN,
+                            CU_TENSOR_MAP_SWIZZLE_64B);
     if (st != DFL_OK) return st;
     st = host::make_tmap_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, biases, uint64_t(K / GS),
-                            uint64_t(N), uint64_t(K / GS) * 2, 8, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+                            uint64_t(N), uint64_t(K / GS) * 2, SBC * NSUB, BN,
+                            CU_TENSOR_MAP_SWIZZLE_64B);
     if (st != DFL_OK) return st;
   } else {
     std::memset(&tm_s, 0, sizeof(tm_s));
     std::memset(&tm_b, 0, sizeof(tm_b));
   }
-  qmm_w4g64_kernel<MT><<<p.grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_x, tm_s, tm_b, p);
+  qmm_w4g64_kernel<MT><<<p.grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_s, tm_b, p);
   return host::launch_status();
 }
 
@@ -489,7 +667,8 @@ int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const
 extern "C" size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status) {
   int dummy;
   int* st = status ? status : &dummy;
-  if (M < 1 || M > 32 || K < 64 || K % 64 != 0 || N < 1) {
+  if (M < 1 || M > 32 || K < 64 || K % 64 != 0 || N < 1 ||
+      N > dfl::qmm::kMaxTiles * dfl::qmm::BN) {
     *st = DFL_ERR_BAD_SHAPE;
     return 0;
   }
@@ -502,7 +681,9 @@ extern "C" size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* statu
 extern "C" int dfl_verify_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
                                     const uint16_t* biases, uint16_t* y, void* workspace,
                                     size_t workspace_bytes, int M, int K, int N, void* stream) {
-  if (M < 1 || M > 32 || K < 64 || K % 64 != 0 || N < 1) return DFL_ERR_BAD_SHAPE;
+  if (M < 1 || M > 32 || K < 64 || K % 64 != 0 || N < 1 ||
+      N > dfl::qmm::kMaxTiles * dfl::qmm::BN)
+    return DFL_ERR_BAD_SHAPE;
   if (!x || !w_q || !scales || !biases || !y) return DFL_ERR_NULL_POINTER;
   if (!dfl::host::aligned(x, 16) || !dfl::host::aligned(w_q, 16) ||
       !dfl::host::aligned(scales, 2) || !dfl::host::aligned(biases, 2) ||

@@ -57,11 +57,13 @@ int dfl_get_device_error(int* device_error);
  *   w_q     uint32 [N, K/8], nibble i of word p = column 8p+i (low first), 16-byte aligned
  *   scales  bf16 [N, K/64];  biases bf16 [N, K/64]  (w = nib * scale + bias)
  *   y       bf16 [M, N], row-major
- * Constraints: 1 <= M <= 32, K % 64 == 0, K >= 64, N >= 1.
+ * Constraints: 1 <= M <= 32, K % 64 == 0, K >= 64, 1 <= N <= 2097152.
  * workspace: at least dfl_verify_qmm_workspace_bytes(M, K, N) bytes of
- * device memory, zero-filled once before first use; the kernel leaves it
- * zero again.  One workspace must not be shared by calls that may run
- * concurrently.
+ * device memory, 16-byte aligned.  Its first 64 KB hold split-K tile
+ * counters that must be zero before the first call (zero-fill the buffer
+ * once); every call leaves them zero again, so one buffer serves any
+ * sequence of calls in stream order.  The rest is fp32 partial sums.  One
+ * workspace must not be shared by calls that may run concurrently.
  * Replaces verify_matmul (dflash_mlx/verify_qmm.py:905-1022) and the
  * VerifyQuantizedLinear dispatch closure (dflash_mlx/verify_linear.py:118-309).
  * ---------------------------------------------------------------------- */
