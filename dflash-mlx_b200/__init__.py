@@ -5,11 +5,18 @@ Public surface (mirrors the reference's names):
 * ``verify_matmul``, ``is_enabled``                      (dflash_mlx/verify_qmm.py)
 * ``QuantizedLinear``, ``VerifyQuantizedLinear``, ``is_verify_eligible``,
   ``install_verify_linears``, ``prewarm_verify_kernels`` (dflash_mlx/verify_linear.py)
+* ``tape_replay_kernel`` (dflash_mlx/kernels.py), ``RecurrentRollbackCache``
+  (dflash_mlx/recurrent_rollback_cache.py), ``restore_after_acceptance``
+  (dflash_mlx/engine/target_qwen_gdn.py)
 
 Every op runs hand-written sm_100a CUDA from ``libdflash_b200.so`` through
 its C ABI (``include/dflash_b200.h``); there is no CPU fallback.
 """
 
+from . import kernels, lm_head
+from .lm_head import lm_head_argmax_keys, lm_head_verify, match_acceptance_length, verify_accept
+from .kernels import tape_replay_kernel, tape_replay_
+from .recurrent_rollback_cache import RecurrentRollbackCache, restore_after_acceptance
 from .verify_qmm import is_enabled, verify_matmul, qmm_w4g64
 from .verify_linear import (
     QuantizedLinear,
@@ -20,6 +27,14 @@ from .verify_linear import (
 )
 
 __all__ = [
+    "lm_head_argmax_keys",
+    "lm_head_verify",
+    "match_acceptance_length",
+    "verify_accept",
+    "tape_replay_kernel",
+    "tape_replay_",
+    "RecurrentRollbackCache",
+    "restore_after_acceptance",
     "is_enabled",
     "verify_matmul",
     "qmm_w4g64",

@@ -35,6 +35,13 @@ SIGNATURES = {
     "dfl_verify_qmm_w4g64": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_size, _c_int, _c_int,
                                       _c_int, _vp]),
     "dfl_verify_qmm_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
+    "dfl_gdn_tape_replay": (_c_int, [_vp, _vp, _c_int, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int,
+                                     _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
+    "dfl_lmhead_argmax": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
+                                   _c_size, _vp]),
+    "dfl_lmhead_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
+    "dfl_lmhead_accept": (_c_int, [_vp, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp]),
+    "dfl_match_acceptance": (_c_int, [_vp, _vp, _c_int, _c_int, _vp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -5,6 +5,8 @@
 #include "host_common.cuh"
 
 #include "qmm_w4.cu"
+#include "gdn_replay.cu"
+#include "lmhead.cu"
 
 extern "C" const char* dfl_status_string(int status) {
   switch (status) {

@@ -75,6 +75,71 @@ int dfl_verify_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t*
  * device; 0 with *status != DFL_OK on error. */
 size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status);
 
+/* ------------------------------------------------------------------------
+ * GatedDeltaNet tape-replay rollback.
+ *
+ * For every sequence b, value head hv and replayed step t:
+ *     S[dv, dk] <- S[dv, dk] * g_t  (g_t per head, or per dk when g_vectorized)
+ *     S[dv, dk] <- S[dv, dk] + tape_t[dv] * k_t[dk]
+ * each a separately rounded fp32 operation; k head hk = hv / (Hv / Hk).
+ * Step t of sequence b is replayed when t < steps[b] (steps NULL: all T) and
+ * mask[b, t] != 0 (mask NULL: all).  state_out may equal state_in (in place;
+ * heads with no replayed step are then not touched).
+ *   tape   fp32 [B, T, Hv, Dv]          k  [B, T, Hk, Dk], bf16 (k_is_bf16) or fp32
+ *   g      fp32 [B, T, Hv] or [B, T, Hv, Dk]
+ *   steps  int32 [B] or NULL            mask uint8 [B, T] or NULL
+ *   state  fp32 [B, Hv, Dv, Dk], 16-byte aligned
+ * Constraints: Dk in {32, 64, 128, 256}, Dv * Dk <= 16384, Hv % Hk == 0, T <= 64.
+ * Replaces tape_replay_kernel (dflash_mlx/kernels.py:822-868) as called by
+ * RecurrentRollbackCache.rollback (dflash_mlx/recurrent_rollback_cache.py:142-165).
+ * ---------------------------------------------------------------------- */
+int dfl_gdn_tape_replay(const float* tape, const void* k, int k_is_bf16, const float* g,
+                        int g_vectorized, const int32_t* steps, const uint8_t* mask,
+                        const float* state_in, float* state_out, int B, int T, int Hv, int Hk,
+                        int Dv, int Dk, void* stream);
+
+/* ------------------------------------------------------------------------
+ * lm_head verify epilogue.
+ *
+ * dfl_lmhead_argmax: for the R = B * T hidden rows h (bf16 [R, D]) and one
+ * vocabulary shard w (bf16 [V, D], global ids v_begin .. v_begin + V - 1),
+ * computes each row's bf16 logits h . w_v (fp32 accumulation, rounded to
+ * bf16 like the reference's bf16 logits), replaces suppressed ids
+ * (suppress[v_begin + v] != 0; suppress may be NULL) by the bf16 value of
+ * -1e9, and writes one 64-bit key per row: high 32 bits an order-preserving
+ * image of the winning logit, low 32 bits 0xFFFFFFFF - id.  The largest key
+ * is the largest logit with ties to the lowest id (argmax's first index),
+ * so keys of several shards combine with max.  Logits are never written.
+ * Constraints: 1 <= R <= 4096, D % 8 == 0, h and w 16-byte aligned.
+ * workspace: dfl_lmhead_workspace_bytes(R, D, V) bytes, first 256 bytes
+ * zero before the first call (left zero).
+ * Replaces logits_from_hidden (dflash_mlx/engine/target_qwen_gdn.py:774-778)
+ * + greedy_tokens_with_mask (dflash_mlx/engine/sampling.py:47-55).
+ * ---------------------------------------------------------------------- */
+int dfl_lmhead_argmax(const uint16_t* h, const uint16_t* w, int R, int D, int V, int v_begin,
+                      const uint8_t* suppress, uint64_t* keys, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+size_t dfl_lmhead_workspace_bytes(int R, int D, int V, int* status);
+
+/* dfl_lmhead_accept: reduces the keys of G shards (keys [G][B*T]), writes the
+ * posterior ids [B, T], and with verify_ids [B, T] (verify_ids[b, 0] the staged
+ * token, verify_ids[b, 1:] the drafts) the acceptance length
+ * sum_i prod_{j<=i} [verify_ids[b, j+1] == posterior[b, j]] (0 .. T-1) and the
+ * next staged token posterior[b, acceptance].  verify_ids, acceptance,
+ * next_token and max_logit (the winning bf16 logit as fp32) may be NULL.
+ * Replaces match_acceptance_length (dflash_mlx/engine/acceptance.py:9-16) as
+ * composed at dflash_mlx/engine/spec_epoch.py:2067-2072,2129. */
+int dfl_lmhead_accept(const uint64_t* keys, int G, const int32_t* verify_ids, int B, int T,
+                      int32_t* posterior, int32_t* acceptance, int32_t* next_token,
+                      float* max_logit, void* stream);
+
+/* dfl_match_acceptance: acceptance[b] = length of the common prefix of
+ * drafted[b, :L] and posterior[b, :L] (int32 [B, L] each).
+ * Replaces match_acceptance_length (dflash_mlx/engine/acceptance.py:9-16). */
+int dfl_match_acceptance(const int32_t* drafted, const int32_t* posterior, int B, int L,
+                         int32_t* acceptance, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
