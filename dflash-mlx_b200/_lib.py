@@ -42,6 +42,13 @@ SIGNATURES = {
     "dfl_lmhead_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
     "dfl_lmhead_accept": (_c_int, [_vp, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp]),
     "dfl_match_acceptance": (_c_int, [_vp, _vp, _c_int, _c_int, _vp, _vp]),
+    "dfl_moe_route": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp]),
+    "dfl_moe_route_table_ints": (_c_size, [_c_int]),
+    "dfl_moe_qmm_w4g64": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                   _c_int, _vp, _c_size, _vp]),
+    "dfl_moe_qmm_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
+    "dfl_silu_mul_bf16": (_c_int, [_vp, _vp, _vp, _c_int, _vp]),
+    "dfl_moe_combine": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
 }
 
 _lock = threading.Lock()

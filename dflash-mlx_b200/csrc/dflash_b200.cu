@@ -7,6 +7,7 @@
 #include "qmm_w4.cu"
 #include "gdn_replay.cu"
 #include "lmhead.cu"
+#include "moe.cu"
 
 extern "C" const char* dfl_status_string(int status) {
   switch (status) {

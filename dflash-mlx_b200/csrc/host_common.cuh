@@ -19,6 +19,11 @@ namespace host {
 
 constexpr int kMaxDevices = 64;
 
+// Every workspace starts with this many bytes of counters that are zero
+// between calls (each kernel resets what it uses); kernels put their other
+// scratch data after it, so one buffer can serve any sequence of calls.
+constexpr size_t kWorkspaceCounterBytes = 64 * 1024;
+
 struct DeviceInfo {
   std::atomic<int> num_sms{0};
   std::atomic<int> cc_major{0};
@@ -84,6 +89,26 @@ inline int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void*
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DFL_OK : DFL_ERR_CUDA;
+}
+
+// 3-D tensor map: dims {inner, outer, depth}, strides in bytes for the two
+// outer dims, box {box_inner, box_outer, 1}.  Out-of-range elements read as 0.
+inline int make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                        uint64_t inner, uint64_t outer, uint64_t depth, uint64_t outer_stride_bytes,
+                        uint64_t depth_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return DFL_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return DFL_ERR_MISALIGNED;
+  if (outer_stride_bytes % 16 != 0 || depth_stride_bytes % 16 != 0) return DFL_ERR_MISALIGNED;
+  cuuint64_t dims[3] = {inner, outer, depth};
+  cuuint64_t strides[2] = {outer_stride_bytes, depth_stride_bytes};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? DFL_OK : DFL_ERR_CUDA;

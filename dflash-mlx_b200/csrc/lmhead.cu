@@ -38,7 +38,7 @@ constexpr int BK = 64;         // K per stage (one 128-byte swizzle atom)
 constexpr int NUM_THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
 constexpr int WARP_EPI0 = 2;
 constexpr int MAX_ROWS = 4096;    // hidden rows per call (running keys in shared memory)
-constexpr size_t kCounterBytes = 256;
+constexpr size_t kCounterBytes = host::kWorkspaceCounterBytes;
 
 template <int RT>
 struct Cfg {

@@ -1,0 +1,161 @@
+// MoE verify helpers around the grouped int4 qmm (qmm_w4.cu):
+//   * routing: top-k experts per token by router logit (ties to the lower
+//     expert id), softmax over the k kept logits (equal to softmax over all
+//     experts followed by renormalisation of the kept probabilities), and a
+//     route table listing the active experts with their tokens;
+//   * silu(gate) * up in fp32, rounded to bf16;
+//   * the weighted combine y_t = sum_j w[t, j] * out[t*k + j] (+ shared expert).
+// The expert block restated here is mlx-lm's SwitchGLU (third party, not in
+// the reference tree), reached from dflash_mlx/engine/target_qwen_gdn.py:863-865.
+#include "common.cuh"
+#include "host_common.cuh"
+
+namespace dfl {
+namespace moe {
+
+constexpr int MAX_TOKENS = 16;   // tokens per verify block (rows per expert problem <= 16)
+constexpr int MAX_K = 16;
+
+// One CTA.  Table layout (int32): [0] = P (active experts); [1 .. E] active
+// expert ids in increasing order; [1+E .. 1+2E) rows per problem;
+// [1+2E ..) token of row m of problem pi at (pi * 16 + m); then E * 16 pair
+// rows (t * k + j) in the same order.
+__global__ void route_kernel(const float* logits, int T, int E, int k, int32_t* table,
+                             float* weights, int32_t* topk) {
+  extern __shared__ int sh[];
+  int* cnt = sh;                 // [E]
+  int* start = cnt + E;          // [E]
+  int* ids = start + E;          // [T * k]
+  const int tid = threadIdx.x;
+  for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  // top-k per token: one warp per token
+  const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
+  for (int t = warp; t < T; t += nwarps) {
+    const float* row = logits + (size_t)t * E;
+    float kept[MAX_K];
+    int kept_id[MAX_K];
+    for (int j = 0; j < k; ++j) {
+      // best not-yet-taken (value desc, id asc)
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int e = lane; e < E; e += 32) {
+        bool taken = false;
+        for (int q = 0; q < j; ++q) taken |= (kept_id[q] == e);
+        if (taken) continue;
+        const float v = row[e];
+        if (v > bv || (v == bv && e < bi)) { bv = v; bi = e; }
+      }
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      kept[j] = bv;
+      kept_id[j] = bi;
+    }
+    if (lane == 0) {
+      float mx = kept[0];
+      double den = 0.0;
+      for (int j = 0; j < k; ++j) den += exp((double)kept[j] - mx);
+      for (int j = 0; j < k; ++j) {
+        weights[t * k + j] = float(exp((double)kept[j] - mx) / den);
+        topk[t * k + j] = kept_id[j];
+        ids[t * k + j] = kept_id[j];
+        atomicAdd(&cnt[kept_id[j]], 1);
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int P = 0;
+    for (int e = 0; e < E; ++e) {
+      if (cnt[e] > 0) {
+        start[e] = P;
+        table[1 + P] = e;
+        table[1 + E + P] = 0;
+        ++P;
+      } else {
+        start[e] = -1;
+      }
+    }
+    table[0] = P;
+    // rows in token order (t ascending, then slot), deterministic
+    for (int pr = 0; pr < T * k; ++pr) {
+      const int e = ids[pr];
+      const int pi = start[e];
+      const int m = table[1 + E + pi]++;
+      table[1 + 2 * E + pi * 16 + m] = pr / k;          // token row
+      table[1 + 2 * E + 16 * E + pi * 16 + m] = pr;     // pair row
+    }
+  }
+}
+
+__global__ void silu_mul_kernel(const uint16_t* gate, const uint16_t* up, uint16_t* out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float g = __bfloat162float(__ushort_as_bfloat16(gate[i]));
+  const float u = __bfloat162float(__ushort_as_bfloat16(up[i]));
+  const float s = g / (1.0f + expf(-g));
+  out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(s * u));
+}
+
+// y[t, c] = bf16( sum_j w[t, j] * pair_out[t * k + j, c]  (+ shared[t, c]) ), fp32 in slot order
+__global__ void combine_kernel(const uint16_t* pair_out, const float* weights, const uint16_t* shared,
+                               uint16_t* y, int T, int k, int H) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * H) return;
+  const int t = i / H, c = i - t * H;
+  float acc = 0.f;
+  for (int j = 0; j < k; ++j) {
+    const float v = __bfloat162float(__ushort_as_bfloat16(pair_out[((size_t)t * k + j) * H + c]));
+    acc = __fadd_rn(acc, __fmul_rn(weights[t * k + j], v));
+  }
+  if (shared) acc = __fadd_rn(acc, __bfloat162float(__ushort_as_bfloat16(shared[i])));
+  y[i] = __bfloat16_as_ushort(__float2bfloat16_rn(acc));
+}
+
+}  // namespace moe
+}  // namespace dfl
+
+extern "C" int dfl_moe_route(const float* logits, int T, int E, int top_k, int32_t* route_table,
+                             float* weights, int32_t* topk_ids, void* stream) {
+  using namespace dfl;
+  if (T < 1 || T > moe::MAX_TOKENS || E < 1 || E > 4096 || top_k < 1 || top_k > moe::MAX_K ||
+      top_k > E)
+    return DFL_ERR_BAD_SHAPE;
+  if (!logits || !route_table || !weights || !topk_ids) return DFL_ERR_NULL_POINTER;
+  int dev, sms;
+  int st = host::current_device(&dev, &sms);
+  if (st != DFL_OK) return st;
+  const size_t smem = (2 * size_t(E) + size_t(T) * top_k) * sizeof(int);
+  moe::route_kernel<<<1, 512, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      logits, T, E, top_k, route_table, weights, topk_ids);
+  return host::launch_status();
+}
+
+extern "C" size_t dfl_moe_route_table_ints(int E) { return 1 + 2 * size_t(E) + 32 * size_t(E); }
+
+extern "C" int dfl_silu_mul_bf16(const uint16_t* gate, const uint16_t* up, uint16_t* out, int n,
+                                 void* stream) {
+  using namespace dfl;
+  if (n < 0) return DFL_ERR_BAD_SHAPE;
+  if (n == 0) return DFL_OK;
+  if (!gate || !up || !out) return DFL_ERR_NULL_POINTER;
+  moe::silu_mul_kernel<<<(n + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      gate, up, out, n);
+  return host::launch_status();
+}
+
+extern "C" int dfl_moe_combine(const uint16_t* pair_out, const float* weights,
+                               const uint16_t* shared, uint16_t* y, int T, int top_k, int H,
+                               void* stream) {
+  using namespace dfl;
+  if (T < 0 || top_k < 1 || H < 1) return DFL_ERR_BAD_SHAPE;
+  if (T == 0) return DFL_OK;
+  if (!pair_out || !weights || !y) return DFL_ERR_NULL_POINTER;
+  const int n = T * H;
+  moe::combine_kernel<<<(n + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      pair_out, weights, shared, y, T, top_k, H);
+  return host::launch_status();
+}

@@ -106,6 +106,16 @@ struct Params {
   int M, K, N;
   int n_tiles, k_units, total_units, grid;
   int sb_tma;              // scales/biases rows are 16-byte multiples (TMA path)
+  // Grouped (MoE expert) mode: problem pi multiplies g_m[pi] <= 16 rows of x,
+  // gathered through g_rows[pi][*], with expert g_expert[pi]'s weights and
+  // scatters them to rows g_out[pi][*] of y.  The problem count lives in
+  // device memory (g_count) so routing never needs a host round trip.
+  const int* g_count;
+  const int* g_expert;
+  const int* g_m;
+  const int* g_rows;       // [P][16]
+  const int* g_out;        // [P][16]
+  int tpp;                 // 128-row tiles per problem (all tiles when dense)
 };
 
 __device__ __forceinline__ int unit_begin(int c, int total, int grid) {
@@ -191,9 +201,10 @@ __device__ __forceinline__ uint32_t sw64_offset(int r, int c) {
 // The x chunks (16 bytes = 8 bf16) x-staging thread et (0..127) handles for
 // the unit starting at k0: idx = et + 128 * t = (b * MT + r) * 8 + c is
 // chunk c of token row r in K block b.  Rows >= M and columns >= K read 0.
-template <int MT>
-__device__ __forceinline__ void load_x_unit(const Params& p, int k0, int et,
+template <int MT, bool GROUPED>
+__device__ __forceinline__ void load_x_unit(const Params& p, int k0, int pi, int et,
                                             uint4 (&xr)[Cfg<MT>::X_PER_THREAD]) {
+  const int rows = GROUPED ? p.g_m[pi] : p.M;
 #pragma unroll
   for (int t = 0; t < Cfg<MT>::X_PER_THREAD; ++t) {
     const int idx = et + 128 * t;
@@ -202,8 +213,10 @@ __device__ __forceinline__ void load_x_unit(const Params& p, int k0, int et,
     const int b = idx / (MT * 8);
     const int k = k0 + b * GS + c * 8;
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < p.M && k < p.K)
-      v = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)r * p.K + k));
+    if (r < rows && k < p.K) {
+      const int xrow = GROUPED ? p.g_rows[pi * 16 + r] : r;
+      v = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)xrow * p.K + k));
+    }
     xr[t] = v;
   }
 }
@@ -224,7 +237,7 @@ __device__ __forceinline__ void store_x_unit(uint32_t slot, int et,
   }
 }
 
-template <int MT>
+template <int MT, bool GROUPED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     qmm_w4g64_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
                      const __grid_constant__ CUtensorMap tm_b, const Params p) {
@@ -253,10 +266,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
-  const int u0 = unit_begin(cta, p.total_units, p.grid);
-  const int u1 = unit_begin(cta + 1, p.total_units, p.grid);
-  const int n_units = u1 - u0;
   const int ku = p.k_units;
+  const int tpp = p.tpp;
+  const int total = GROUPED ? (*p.g_count) * tpp * ku : p.total_units;
+  const int u0 = unit_begin(cta, total, p.grid);
+  const int u1 = unit_begin(cta + 1, total, p.grid);
+  const int n_units = u1 - u0;
 
   if (threadIdx.x == 0) {
     *abort_word = 0;
@@ -302,6 +317,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tma_prefetch_desc(&tm_s);
         tma_prefetch_desc(&tm_b);
         int tile = u0 / ku, kb = u0 - (u0 / ku) * ku;
+        int pi = tile / tpp;
+        tile -= pi * tpp;
+        int e = (GROUPED && n_units > 0) ? p.g_expert[pi] : 0;
         int chunk = -1;
         for (int it = 0; it < n_units; ++it) {
           const int n0 = tile * BN;
@@ -312,17 +330,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (*abort_word) break;
             uint8_t* dst = smem + C::OFF_SB + cs * C::SBC_BYTES;
             mbar_arrive_expect_tx(&sbfull[cs], C::SBC_BYTES);
-            tma_load_2d(dst, &tm_s, &sbfull[cs], (kb / SBC) * SBC * NSUB, n0);
-            tma_load_2d(dst + C::SBC_HALF, &tm_b, &sbfull[cs], (kb / SBC) * SBC * NSUB, n0);
+            tma_load_3d(dst, &tm_s, &sbfull[cs], (kb / SBC) * SBC * NSUB, n0, e);
+            tma_load_3d(dst + C::SBC_HALF, &tm_b, &sbfull[cs], (kb / SBC) * SBC * NSUB, n0, e);
           }
           const int s = it % C::NSTAGE;
           wait(&empty[s], ((it / C::NSTAGE) & 1) ^ 1);
           if (*abort_word) break;
           uint8_t* st = smem + s * C::STAGE_BYTES;
           mbar_arrive_expect_tx(&full[s], C::PACK_BYTES);
-          tma_load_2d(st, &tm_w, &full[s], kb * (UNIT_K / 8), n0);
-          tma_load_2d(st + C::PACK_BYTES / 2, &tm_w, &full[s], kb * (UNIT_K / 8) + 32, n0);
-          if (++kb == ku) { kb = 0; ++tile; }
+          tma_load_3d(st, &tm_w, &full[s], kb * (UNIT_K / 8), n0, e);
+          tma_load_3d(st + C::PACK_BYTES / 2, &tm_w, &full[s], kb * (UNIT_K / 8) + 32, n0, e);
+          if (++kb == ku) {
+            kb = 0;
+            if (++tile == tpp) {
+              tile = 0;
+              ++pi;
+              if (GROUPED && it + 1 < n_units) e = p.g_expert[pi];
+            }
+          }
         }
       }
     } else {
@@ -331,6 +356,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) tma_prefetch_desc(&tm_w);
       const int groups = p.K / GS;
       int tile = u0 / ku, kb = u0 - (u0 / ku) * ku;
+      int pi = tile / tpp;
+      tile -= pi * tpp;
+      int e = (GROUPED && n_units > 0) ? p.g_expert[pi] : 0;
       int chunk = -1;
       for (int it = 0; it < n_units; ++it) {
         const int n0 = tile * BN;
@@ -347,8 +375,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int n = n0 + r, g = g0 + gi;
             uint16_t sv = 0, bv = 0;
             if (n < p.N && g < groups) {
-              sv = p.scales[(size_t)n * groups + g];
-              bv = p.biases[(size_t)n * groups + g];
+              const size_t idx = ((size_t)e * p.N + n) * groups + g;
+              sv = p.scales[idx];
+              bv = p.biases[idx];
             }
             const uint32_t off = sw64_offset(r, gi >> 3) + (gi & 7) * 2;
             *reinterpret_cast<uint16_t*>(dst + off) = sv;
@@ -363,13 +392,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!*abort_word) {
             uint8_t* st = smem + s * C::STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s], C::PACK_BYTES);
-            tma_load_2d(st, &tm_w, &full[s], kb * (UNIT_K / 8), n0);
-            tma_load_2d(st + C::PACK_BYTES / 2, &tm_w, &full[s], kb * (UNIT_K / 8) + 32, n0);
+            tma_load_3d(st, &tm_w, &full[s], kb * (UNIT_K / 8), n0, e);
+            tma_load_3d(st + C::PACK_BYTES / 2, &tm_w, &full[s], kb * (UNIT_K / 8) + 32, n0, e);
           }
         }
         __syncwarp();
         if (*abort_word) break;
-        if (++kb == ku) { kb = 0; ++tile; }
+        if (++kb == ku) {
+          kb = 0;
+          if (++tile == tpp) {
+            tile = 0;
+            ++pi;
+            if (GROUPED && it + 1 < n_units) e = p.g_expert[pi];
+          }
+        }
       }
     }
   } else if (warp < WARP_DQ0) {
@@ -495,14 +531,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int xs = ix % C::XS;
       if (ix >= C::XS) wait(&xfree[xs], ((ix / C::XS) - 1) & 1);
       store_x_unit<MT>(ring + xs * C::XSLOT_BYTES, et, xr);
-      if (ix + 1 < n_units) load_x_unit<MT>(p, ((u0 + ix + 1) % ku) * UNIT_K, et, xr);
+      if (ix + 1 < n_units) {
+        const int un = u0 + ix + 1;
+        load_x_unit<MT, GROUPED>(p, (un % ku) * UNIT_K, un / (ku * tpp), et, xr);
+      }
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(&xfull[xs]);
     };
     int staged = 0;  // units of x staged so far
     if (n_units > 0) {
-      load_x_unit<MT>(p, (u0 % ku) * UNIT_K, et, xr);
+      load_x_unit<MT, GROUPED>(p, (u0 % ku) * UNIT_K, u0 / (ku * tpp), et, xr);
       for (; staged < n_units && staged < C::XS; ++staged) stage_x(staged);
       const int t_first = u0 / ku;
       const int t_last = (u1 - 1) / ku;
@@ -527,13 +566,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) mbar_arrive(&accempty[buf]);
         ++acc_it;
 
-        const int n = t * BN + r;
+        const int pi = t / tpp;
+        const int n = (t - pi * tpp) * BN + r;
+        const int rows = GROUPED ? p.g_m[pi] : p.M;
+        const int* outrow = GROUPED ? p.g_out + pi * 16 : nullptr;
         const bool full_tile = (kb0 == 0) && (kb1 == ku);
         if (full_tile) {
           if (n < p.N) {
 #pragma unroll
             for (int m = 0; m < MT; ++m)
-              if (m < p.M) p.y[(size_t)m * p.N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[m]));
+              if (m < rows)
+                p.y[(size_t)(GROUPED ? outrow[m] : m) * p.N + n] =
+                    __bfloat16_as_ushort(__float2bfloat16_rn(acc[m]));
           }
           continue;
         }
@@ -545,8 +589,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         __threadfence();
         named_bar_sync(BAR_ID_EPI, 128);
         if (et == 0) {
-          const int c_lo = cta_of_unit(t * ku, p.total_units, p.grid);
-          const int c_hi = cta_of_unit(t * ku + ku - 1, p.total_units, p.grid);
+          const int c_lo = cta_of_unit(t * ku, total, p.grid);
+          const int c_hi = cta_of_unit(t * ku + ku - 1, total, p.grid);
           const int expected = c_hi - c_lo + 1;
           const int prev = atomicAdd(&p.counters[t], 1);
           *flag_slot = (prev == expected - 1) ? 1 : 0;
@@ -554,13 +598,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         named_bar_sync(BAR_ID_EPI, 128);
         if (*flag_slot) {
           __threadfence();
-          const int c_lo = cta_of_unit(t * ku, p.total_units, p.grid);
-          const int c_hi = cta_of_unit(t * ku + ku - 1, p.total_units, p.grid);
+          const int c_lo = cta_of_unit(t * ku, total, p.grid);
+          const int c_hi = cta_of_unit(t * ku + ku - 1, total, p.grid);
           float sum[MT];
 #pragma unroll
           for (int m = 0; m < MT; ++m) sum[m] = 0.f;
           for (int c = c_lo; c <= c_hi; ++c) {
-            const int cs = (unit_begin(c, p.total_units, p.grid) >= t * ku) ? 0 : 1;
+            const int cs = (unit_begin(c, total, p.grid) >= t * ku) ? 0 : 1;
             const float* src = p.partials + ((size_t)(c * 2 + cs) * MT) * BN;
 #pragma unroll
             for (int m = 0; m < MT; ++m) sum[m] += __ldcg(src + m * BN + r);
@@ -568,7 +612,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (n < p.N) {
 #pragma unroll
             for (int m = 0; m < MT; ++m)
-              if (m < p.M) p.y[(size_t)m * p.N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(sum[m]));
+              if (m < rows)
+                p.y[(size_t)(GROUPED ? outrow[m] : m) * p.N + n] =
+                    __bfloat16_as_ushort(__float2bfloat16_rn(sum[m]));
           }
           if (et == 0) p.counters[t] = 0;
         }
@@ -595,7 +641,7 @@ inline int choose_mt(int M) { return M <= 16 ? 16 : 32; }
 
 // Zero-invariant counter area at the start of every workspace (one int per
 // 128-row tile): N <= kMaxTiles * 128.
-constexpr size_t kCounterBytes = 64 * 1024;
+constexpr size_t kCounterBytes = host::kWorkspaceCounterBytes;
 constexpr int kMaxTiles = int(kCounterBytes / sizeof(int));
 
 inline void geometry(int M, int K, int N, int num_sms, int* n_tiles, int* k_units, int* total,
@@ -614,16 +660,50 @@ inline size_t workspace_bytes_for(int M, int K, int N, int num_sms) {
   return kCounterBytes + size_t(grid) * 2 * mt * BN * sizeof(float);
 }
 
+// Weight / scale / bias tensor maps over [E, N, K/8] and [E, N, K/64]
+// (E = 1 for a dense layer).  Scales and biases go through TMA only when their
+// rows are 16-byte multiples (K % 512 == 0).
+inline int make_weight_maps(const uint32_t* w_q, const uint16_t* scales, const uint16_t* biases,
+                            int E, int K, int N, bool sb_tma, CUtensorMap* tm_w, CUtensorMap* tm_s,
+                            CUtensorMap* tm_b) {
+  int st = host::make_tmap_3d(tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w_q, uint64_t(K / 8),
+                              uint64_t(N), uint64_t(E), uint64_t(K / 2), uint64_t(N) * (K / 2), 32,
+                              BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != DFL_OK) return st;
+  if (sb_tma) {
+    const uint64_t row = uint64_t(K / GS) * 2;
+    st = host::make_tmap_3d(tm_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scales, uint64_t(K / GS),
+                            uint64_t(N), uint64_t(E), row, row * N, SBC * NSUB, BN,
+                            CU_TENSOR_MAP_SWIZZLE_64B);
+    if (st != DFL_OK) return st;
+    st = host::make_tmap_3d(tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, biases, uint64_t(K / GS),
+                            uint64_t(N), uint64_t(E), row, row * N, SBC * NSUB, BN,
+                            CU_TENSOR_MAP_SWIZZLE_64B);
+    if (st != DFL_OK) return st;
+  } else {
+    std::memset(tm_s, 0, sizeof(*tm_s));
+    std::memset(tm_b, 0, sizeof(*tm_b));
+  }
+  return DFL_OK;
+}
+
+template <int MT, bool GROUPED>
+int launch_kernel(const CUtensorMap& tm_w, const CUtensorMap& tm_s, const CUtensorMap& tm_b,
+                  const Params& p, int dev, cudaStream_t stream) {
+  using C = Cfg<MT>;
+  static std::atomic<uint64_t> smem_done{0};
+  int st = host::ensure_smem(qmm_w4g64_kernel<MT, GROUPED>, C::SMEM_BYTES, dev, smem_done);
+  if (st != DFL_OK) return st;
+  qmm_w4g64_kernel<MT, GROUPED><<<p.grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_s, tm_b, p);
+  return host::launch_status();
+}
+
 template <int MT>
 int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const uint16_t* biases,
            uint16_t* y, void* ws, int M, int K, int N, int num_sms, int dev,
            cudaStream_t stream) {
-  using C = Cfg<MT>;
-  static std::atomic<uint64_t> smem_done{0};
-  int st = host::ensure_smem(qmm_w4g64_kernel<MT>, C::SMEM_BYTES, dev, smem_done);
-  if (st != DFL_OK) return st;
-
   Params p;
+  std::memset(&p, 0, sizeof(p));
   p.x = x;
   p.scales = scales;
   p.biases = biases;
@@ -632,6 +712,7 @@ int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const
   p.K = K;
   p.N = N;
   geometry(M, K, N, num_sms, &p.n_tiles, &p.k_units, &p.total_units, &p.grid);
+  p.tpp = p.n_tiles;
   // Workspace layout: [tile counters, fixed size][fp32 partials].  The
   // counters sit at a fixed offset so that no call's partials ever overlap
   // another call's counters; every kernel leaves its counters at zero.
@@ -639,26 +720,10 @@ int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const
   p.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes);
   // TMA of scale/bias rows needs 16-byte multiples: K % 512 == 0.
   p.sb_tma = (K % UNIT_K == 0) && host::aligned(scales, 16) && host::aligned(biases, 16);
-
   CUtensorMap tm_w, tm_s, tm_b;
-  st = host::make_tmap_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, w_q, uint64_t(K / 8), uint64_t(N),
-                          uint64_t(K / 2), 32, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  int st = make_weight_maps(w_q, scales, biases, 1, K, N, p.sb_tma != 0, &tm_w, &tm_s, &tm_b);
   if (st != DFL_OK) return st;
-  if (p.sb_tma) {
-    st = host::make_tmap_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, scales, uint64_t(K / GS),
-                            uint64_t(N), uint64_t(K / GS) * 2, SBC * NSUB, BN,
-                            CU_TENSOR_MAP_SWIZZLE_64B);
-    if (st != DFL_OK) return st;
-    st = host::make_tmap_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, biases, uint64_t(K / GS),
-                            uint64_t(N), uint64_t(K / GS) * 2, SBC * NSUB, BN,
-                            CU_TENSOR_MAP_SWIZZLE_64B);
-    if (st != DFL_OK) return st;
-  } else {
-    std::memset(&tm_s, 0, sizeof(tm_s));
-    std::memset(&tm_b, 0, sizeof(tm_b));
-  }
-  qmm_w4g64_kernel<MT><<<p.grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_s, tm_b, p);
-  return host::launch_status();
+  return launch_kernel<MT, false>(tm_w, tm_s, tm_b, p, dev, stream);
 }
 
 }  // namespace qmm
@@ -699,4 +764,83 @@ extern "C" int dfl_verify_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, cons
   if (dfl::qmm::choose_mt(M) == 16)
     return dfl::qmm::launch<16>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
   return dfl::qmm::launch<32>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
+}
+
+// ------------------------------------------------------------------ MoE
+namespace dfl {
+namespace qmm {
+
+inline void grouped_geometry(int max_problems, int K, int N, int num_sms, int* tpp, int* ku,
+                             int* grid) {
+  *tpp = (N + BN - 1) / BN;
+  *ku = (K + UNIT_K - 1) / UNIT_K;
+  const long long units = (long long)max_problems * *tpp * *ku;
+  *grid = units < num_sms ? int(units) : num_sms;
+}
+
+inline size_t grouped_workspace_bytes(int max_problems, int K, int N, int num_sms) {
+  int tpp, ku, grid;
+  grouped_geometry(max_problems, K, N, num_sms, &tpp, &ku, &grid);
+  return kCounterBytes + size_t(grid) * 2 * 16 * BN * sizeof(float);
+}
+
+}  // namespace qmm
+}  // namespace dfl
+
+extern "C" size_t dfl_moe_qmm_workspace_bytes(int max_problems, int K, int N, int* status) {
+  int dummy;
+  int* st = status ? status : &dummy;
+  if (max_problems < 1 || K < 64 || K % 64 != 0 || N < 1 ||
+      (long long)max_problems * ((N + 127) / 128) > dfl::qmm::kMaxTiles) {
+    *st = DFL_ERR_BAD_SHAPE;
+    return 0;
+  }
+  int dev, sms;
+  *st = dfl::host::current_device(&dev, &sms);
+  if (*st != DFL_OK) return 0;
+  return dfl::qmm::grouped_workspace_bytes(max_problems, K, N, sms);
+}
+
+extern "C" int dfl_moe_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
+                                 const uint16_t* biases, uint16_t* y, const int32_t* route,
+                                 int gather_by_pair, int max_problems, int E, int K, int N,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace dfl;
+  if (max_problems < 1 || max_problems > E || E < 1 || K < 64 || K % 64 != 0 || N < 1 ||
+      (long long)max_problems * ((N + 127) / 128) > qmm::kMaxTiles)
+    return DFL_ERR_BAD_SHAPE;
+  if (!x || !w_q || !scales || !biases || !y || !route) return DFL_ERR_NULL_POINTER;
+  if (!host::aligned(x, 16) || !host::aligned(w_q, 16) || !host::aligned(route, 4))
+    return DFL_ERR_MISALIGNED;
+  int dev, sms;
+  int st = host::current_device(&dev, &sms);
+  if (st != DFL_OK) return st;
+  if (!workspace || workspace_bytes < qmm::grouped_workspace_bytes(max_problems, K, N, sms))
+    return DFL_ERR_WORKSPACE;
+  if (!host::aligned(workspace, 16)) return DFL_ERR_MISALIGNED;
+  qmm::Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.x = x;
+  p.scales = scales;
+  p.biases = biases;
+  p.y = y;
+  p.M = 16;
+  p.K = K;
+  p.N = N;
+  qmm::grouped_geometry(max_problems, K, N, sms, &p.tpp, &p.k_units, &p.grid);
+  p.n_tiles = max_problems * p.tpp;
+  p.counters = reinterpret_cast<int*>(workspace);
+  p.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + qmm::kCounterBytes);
+  p.sb_tma = (K % qmm::UNIT_K == 0) && host::aligned(scales, 16) && host::aligned(biases, 16);
+  // route table layout (int32): [0] problem count P, then E expert ids,
+  // E row counts, E x 16 token rows, E x 16 pair rows (see dfl_moe_route)
+  p.g_count = route;
+  p.g_expert = route + 1;
+  p.g_m = route + 1 + E;
+  p.g_rows = gather_by_pair ? route + 1 + 2 * E + 16 * E : route + 1 + 2 * E;
+  p.g_out = route + 1 + 2 * E + 16 * E;
+  CUtensorMap tm_w, tm_s, tm_b;
+  st = qmm::make_weight_maps(w_q, scales, biases, E, K, N, p.sb_tma != 0, &tm_w, &tm_s, &tm_b);
+  if (st != DFL_OK) return st;
+  return qmm::launch_kernel<16, true>(tm_w, tm_s, tm_b, p, dev, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -1,0 +1,139 @@
+"""MoE verify expert block on B200 (routed experts + shared expert).
+
+Restates mlx-lm's ``SwitchGLU`` / ``SwitchLinear`` -> ``mx.gather_qmm`` path
+(third party: mlx-lm >= 0.31.0, not vendored in the reference) that the
+reference reaches from the decoder layers at
+``dflash_mlx/engine/target_qwen_gdn.py:863-865``:
+
+1. ``route``: top-k experts per token by router logit, softmax over the k kept
+   logits (= softmax over all experts, then renormalised), and a device-side
+   route table of the active experts and their tokens;
+2. ``gate``/``up`` = grouped int4 qmm over the active experts (each expert's
+   weights are read once), ``h = silu(gate) * up``;
+3. ``down`` = grouped int4 qmm on the (token, slot) rows of h;
+4. ``y_t = sum_j w[t, j] * down[t, j] + shared_expert(x_t)``.
+
+Every intermediate is rounded to bf16 as the MLX ops return it; the combine
+accumulates in fp32 in slot order.  Nothing is synchronised with the host.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._runtime import require_cuda, stream_ptr, workspace
+from .verify_qmm import qmm_w4g64
+
+
+@dataclass
+class QuantWeight:
+    """One affine int4 g64 weight: ``q`` uint32 ``[.., N, K/8]``, bf16 ``s``/``b`` ``[.., N, K/64]``."""
+
+    q: torch.Tensor
+    s: torch.Tensor
+    b: torch.Tensor
+
+    @property
+    def n(self) -> int:
+        return int(self.q.shape[-2])
+
+    @property
+    def k(self) -> int:
+        return int(self.q.shape[-1]) * 8
+
+
+def _moe_ws_bytes(max_problems: int, k: int, n: int) -> int:
+    st = ctypes.c_int(0)
+    nb = _lib.load().dfl_moe_qmm_workspace_bytes(int(max_problems), int(k), int(n), ctypes.byref(st))
+    _lib.check("dfl_moe_qmm_workspace_bytes", st.value)
+    return int(nb)
+
+
+def route(router_logits: torch.Tensor, top_k: int = 8):
+    """Returns (route_table int32, weights fp32 [T, k], topk_ids int32 [T, k])."""
+    require_cuda(router_logits, "router_logits")
+    lg = router_logits.to(torch.float32).contiguous()
+    t, e = lg.shape
+    dev = lg.device
+    table = torch.empty(int(_lib.load().dfl_moe_route_table_ints(e)), dtype=torch.int32, device=dev)
+    w = torch.empty((t, top_k), dtype=torch.float32, device=dev)
+    ids = torch.empty((t, top_k), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        st = _lib.load().dfl_moe_route(lg.data_ptr(), t, e, int(top_k), table.data_ptr(),
+                                       w.data_ptr(), ids.data_ptr(), stream_ptr(dev))
+    _lib.check("dfl_moe_route", st)
+    return table, w, ids
+
+
+def gather_qmm(x: torch.Tensor, weight: QuantWeight, table: torch.Tensor, *, rows_out: int,
+               gather_by_pair: bool, max_problems: Optional[int] = None,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Grouped int4 qmm over the route table's active experts -> bf16 ``[rows_out, N]``."""
+    e = int(weight.q.shape[0])
+    k, n = weight.k, weight.n
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty((rows_out, n), dtype=torch.bfloat16, device=x.device)
+    mp = e if max_problems is None else int(max_problems)
+    with torch.cuda.device(x.device):
+        ws = workspace(x.device, _moe_ws_bytes(mp, k, n))
+        st = _lib.load().dfl_moe_qmm_w4g64(
+            x.data_ptr(), weight.q.data_ptr(), weight.s.data_ptr(), weight.b.data_ptr(),
+            out.data_ptr(), table.data_ptr(), 1 if gather_by_pair else 0, mp, e, k, n,
+            ws.data_ptr(), ws.numel(), stream_ptr(x.device))
+    _lib.check("dfl_moe_qmm_w4g64", st)
+    return out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    out = torch.empty_like(gate)
+    with torch.cuda.device(gate.device):
+        st = _lib.load().dfl_silu_mul_bf16(gate.data_ptr(), up.contiguous().data_ptr(), out.data_ptr(),
+                                           gate.numel(), stream_ptr(gate.device))
+    _lib.check("dfl_silu_mul_bf16", st)
+    return out
+
+
+def combine(pair_out: torch.Tensor, weights: torch.Tensor, shared: Optional[torch.Tensor]) -> torch.Tensor:
+    t, k = weights.shape
+    h = pair_out.shape[-1]
+    y = torch.empty((t, h), dtype=torch.bfloat16, device=pair_out.device)
+    with torch.cuda.device(y.device):
+        st = _lib.load().dfl_moe_combine(pair_out.data_ptr(), weights.contiguous().data_ptr(),
+                                         None if shared is None else shared.contiguous().data_ptr(),
+                                         y.data_ptr(), t, k, h, stream_ptr(y.device))
+    _lib.check("dfl_moe_combine", st)
+    return y
+
+
+def dense_mlp(x: torch.Tensor, gate: QuantWeight, up: QuantWeight, down: QuantWeight) -> torch.Tensor:
+    g = qmm_w4g64(x, gate.q, gate.s, gate.b)
+    u = qmm_w4g64(x, up.q, up.s, up.b)
+    return qmm_w4g64(silu_mul(g, u), down.q, down.s, down.b)
+
+
+def moe_layer(x: torch.Tensor, router_logits: torch.Tensor, experts: dict, shared: Optional[dict],
+              top_k: int = 8) -> torch.Tensor:
+    """One MoE verify layer: ``x`` bf16 ``[T, H]`` -> bf16 ``[T, H]``.
+
+    ``experts``: QuantWeight stacks ``gate`` / ``up`` ``[E, I, H/8]`` and
+    ``down`` ``[E, H, I/8]``; ``shared``: unstacked QuantWeights (or None).
+    """
+    require_cuda(x, "x")
+    t = x.shape[0]
+    table, w, _ = route(router_logits, top_k)
+    e = int(experts["gate"].q.shape[0])
+    mp = min(e, t * top_k)
+    g = gather_qmm(x, experts["gate"], table, rows_out=t * top_k, gather_by_pair=False, max_problems=mp)
+    u = gather_qmm(x, experts["up"], table, rows_out=t * top_k, gather_by_pair=False, max_problems=mp)
+    h = silu_mul(g, u)
+    d = gather_qmm(h, experts["down"], table, rows_out=t * top_k, gather_by_pair=True, max_problems=mp)
+    so = None
+    if shared is not None:
+        so = dense_mlp(x, shared["gate"], shared["up"], shared["down"])
+    return combine(d, w, so)

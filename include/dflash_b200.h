@@ -111,8 +111,9 @@ int dfl_gdn_tape_replay(const float* tape, const void* k, int k_is_bf16, const f
  * is the largest logit with ties to the lowest id (argmax's first index),
  * so keys of several shards combine with max.  Logits are never written.
  * Constraints: 1 <= R <= 4096, D % 8 == 0, h and w 16-byte aligned.
- * workspace: dfl_lmhead_workspace_bytes(R, D, V) bytes, first 256 bytes
- * zero before the first call (left zero).
+ * workspace: dfl_lmhead_workspace_bytes(R, D, V) bytes; the same convention
+ * as every workspace here: the first 64 KB are counters that must be zero
+ * before the first call and are left zero, scratch data follows.
  * Replaces logits_from_hidden (dflash_mlx/engine/target_qwen_gdn.py:774-778)
  * + greedy_tokens_with_mask (dflash_mlx/engine/sampling.py:47-55).
  * ---------------------------------------------------------------------- */
@@ -139,6 +140,47 @@ int dfl_lmhead_accept(const uint64_t* keys, int G, const int32_t* verify_ids, in
  * Replaces match_acceptance_length (dflash_mlx/engine/acceptance.py:9-16). */
 int dfl_match_acceptance(const int32_t* drafted, const int32_t* posterior, int B, int L,
                          int32_t* acceptance, void* stream);
+
+/* ------------------------------------------------------------------------
+ * MoE expert path (routed experts of one verify block).
+ *
+ * dfl_moe_route: router logits fp32 [T, E] (T <= 16 tokens) -> top_k experts
+ * per token (largest logit first, ties to the lower id), their softmax
+ * weights renormalised over the k kept experts (fp32 [T, top_k]), expert ids
+ * (int32 [T, top_k]) and a route table of dfl_moe_route_table_ints(E) int32:
+ * [0] number P of active experts, [1..E] their ids (ascending), [1+E..]
+ * rows per active expert, then per active expert 16 token rows and 16 pair
+ * rows (pair = t * top_k + j).  Everything stays on the device.
+ *
+ * dfl_moe_qmm_w4g64: for every active expert e (P read from the route table
+ * on the device), y[pair rows] = x[rows] @ dequant(W_e)^T with W as for
+ * dfl_verify_qmm_w4g64 but stacked per expert: w_q uint32 [E, N, K/8],
+ * scales / biases bf16 [E, N, K/64].  x rows are the table's token rows
+ * (gather_by_pair = 0; x is [T, K]) or its pair rows (gather_by_pair = 1; x is
+ * [T * top_k, K]); y is [T * top_k, N].  Each active expert's weights are read
+ * once.  max_problems bounds P (grid size); workspace as for the dense qmm
+ * with dfl_moe_qmm_workspace_bytes.
+ *
+ * dfl_silu_mul_bf16: out = bf16(silu(gate) * up), fp32 math.
+ * dfl_moe_combine: y[t] = bf16(sum_j weights[t, j] * pair_out[t * top_k + j]
+ * (+ shared[t])), fp32 in slot order.
+ *
+ * Replaces the mlx-lm SwitchGLU -> mx.gather_qmm expert block (third party,
+ * not in the reference tree) that the reference reaches from the decoder
+ * layers at dflash_mlx/engine/target_qwen_gdn.py:863-865.
+ * ---------------------------------------------------------------------- */
+int dfl_moe_route(const float* logits, int T, int E, int top_k, int32_t* route_table,
+                  float* weights, int32_t* topk_ids, void* stream);
+size_t dfl_moe_route_table_ints(int E);
+int dfl_moe_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
+                      const uint16_t* biases, uint16_t* y, const int32_t* route,
+                      int gather_by_pair, int max_problems, int E, int K, int N, void* workspace,
+                      size_t workspace_bytes, void* stream);
+size_t dfl_moe_qmm_workspace_bytes(int max_problems, int K, int N, int* status);
+int dfl_silu_mul_bf16(const uint16_t* gate, const uint16_t* up, uint16_t* out, int n,
+                      void* stream);
+int dfl_moe_combine(const uint16_t* pair_out, const float* weights, const uint16_t* shared,
+                    uint16_t* y, int T, int top_k, int H, void* stream);
 
 #ifdef __cplusplus
 }
