@@ -1,0 +1,206 @@
+"""Synthetic target-verify step on B200 (the path the benchmark times).
+
+One verify cycle of the reference's decode loop
+(``dflash_mlx/engine/spec_epoch.py:2022-2106``) restricted to its hot path,
+for ``requests`` independent requests of 16 verify tokens on this GPU:
+
+1. the int4 g64 verify projections of every decoder layer at M = 16 per
+   request (q, k, v, o, gate, up, down; ``verify_linear.py`` ->
+   ``verify_qmm.py``), with SiLU * up feeding down;
+2. the lm_head argmax + greedy acceptance epilogue (``spec_epoch.py:2067-2072``)
+   on a vocabulary shard, keys all-gathered across ranks when the vocabulary
+   is split;
+3. GatedDeltaNet tape-replay rollback of every GDN layer with the accepted
+   step counts straight from step 2 (``recurrent_rollback_cache.py:142-165``:
+   ``accepted + 1`` steps), so no value is read back to the host.
+
+Weights are random with BASELINE's distributions (no checkpoints offline).
+The per-request qmm stack runs the same x through every layer (no attention
+or residual stream: those are outside the hot path).  Each device-side part
+is captured once in a CUDA graph and replayed; NCCL collectives (vocabulary
+split across ranks) run between the graphs.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import lm_head as _lm
+from .kernels import tape_replay_
+from .moe import QuantWeight, silu_mul
+from .verify_qmm import qmm_w4g64
+
+
+@dataclass
+class StackShape:
+    hidden: int = 5120
+    layers: int = 64
+    q_out: int = 6144
+    kv_out: int = 1024
+    inter: int = 17408
+    vocab: int = 248320
+    gdn_layers: int = 48
+    gdn_heads: int = 48
+    gdn_dk: int = 128
+    gdn_dv: int = 128
+    block: int = 16
+
+    def projections(self):
+        """(name, out_features N, in_features K) of one decoder layer."""
+        h = self.hidden
+        return [("q", self.q_out, h), ("k", self.kv_out, h), ("v", self.kv_out, h),
+                ("o", h, self.q_out), ("gate", self.inter, h), ("up", self.inter, h),
+                ("down", h, self.inter)]
+
+    def qmm_bytes_per_request(self) -> int:
+        """Algorithmic bytes of one request's projection stack: packed weights +
+        bf16 scales and biases + bf16 activations in and out."""
+        total = 0
+        for _, n, k in self.projections():
+            total += n * k // 2 + 2 * 2 * n * (k // 64) + 2 * self.block * (k + n)
+        return total * self.layers
+
+    def qmm_flops_per_request(self) -> int:
+        return 2 * self.block * sum(n * k for _, n, k in self.projections()) * self.layers
+
+
+def _quant_weight(gen, dev, n, k):
+    q = torch.randint(-2**31, 2**31 - 1, (n, k // 8), dtype=torch.int64, generator=gen,
+                      device=dev).to(torch.int32)
+    s = torch.rand((n, k // 64), generator=gen, device=dev) * 0.016 + 0.004
+    b = -8 * s + torch.randn((n, k // 64), generator=gen, device=dev) * 0.1 * s
+    return QuantWeight(q, s.to(torch.bfloat16), b.to(torch.bfloat16))
+
+
+class VerifyStep:
+    """Owns the synthetic weights and state of one GPU and runs verify steps."""
+
+    def __init__(self, device: torch.device, *, requests: int = 1, shape: Optional[StackShape] = None,
+                 rank: int = 0, world: int = 1, group=None, seed: int = 0):
+        self.dev = torch.device(device)
+        self.shape = shape or StackShape()
+        self.requests = int(requests)
+        self.rank, self.world, self.group = rank, world, group
+        sh = self.shape
+        gen = torch.Generator(device=self.dev).manual_seed(seed)
+        # replicated decoder weights (identical on every rank: same seed)
+        self.layers = [{name: _quant_weight(gen, self.dev, n, k) for name, n, k in sh.projections()}
+                       for _ in range(sh.layers)]
+        # this rank's vocabulary shard of the bf16 lm_head, N(0, 0.02)
+        per = (sh.vocab + world - 1) // world
+        self.v_begin = rank * per
+        v_len = max(0, min(sh.vocab, self.v_begin + per) - self.v_begin)
+        wgen = torch.Generator(device=self.dev).manual_seed(seed + 1000 + rank)
+        self.lm_w = (torch.randn((v_len, sh.hidden), generator=wgen, device=self.dev) * 0.02).to(torch.bfloat16)
+        # GDN rollback state and tapes: [layer][B, Hv, Dv, Dk] fp32 ~ N(0, 0.05)
+        b, t, hv, dk, dv = self.requests, sh.block, sh.gdn_heads, sh.gdn_dk, sh.gdn_dv
+        sgen = torch.Generator(device=self.dev).manual_seed(seed + 2000 + rank)
+        self.gdn_state = torch.randn((sh.gdn_layers, b, hv, dv, dk), generator=sgen, device=self.dev) * 0.05
+        self.tape = torch.randn((sh.gdn_layers, b, t, hv, dv), generator=sgen, device=self.dev) * 0.3
+        kk = torch.randn((sh.gdn_layers, b, t, hv, dk), generator=sgen, device=self.dev)
+        self.tape_k = (kk / kk.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+        self.tape_g = torch.exp(-torch.nn.functional.softplus(
+            torch.randn((sh.gdn_layers, b, t, hv), generator=sgen, device=self.dev)))
+        # step inputs / outputs (static buffers for graph replay)
+        self.x = torch.empty((b * sh.block, sh.hidden), dtype=torch.bfloat16, device=self.dev)
+        self.verify_ids = torch.zeros((b, sh.block), dtype=torch.int32, device=self.dev)
+        self.stream = torch.cuda.Stream(self.dev)
+        self.graphs = None
+        self.ev = None
+
+    # -------------------------------------------------------------- parts
+    def _qmm_stack(self):
+        sh = self.shape
+        for r in range(self.requests):
+            x = self.x[r * sh.block:(r + 1) * sh.block]
+            for lw in self.layers:
+                q = qmm_w4g64(x, lw["q"].q, lw["q"].s, lw["q"].b)
+                qmm_w4g64(x, lw["k"].q, lw["k"].s, lw["k"].b)
+                qmm_w4g64(x, lw["v"].q, lw["v"].s, lw["v"].b)
+                qmm_w4g64(q, lw["o"].q, lw["o"].s, lw["o"].b)
+                g = qmm_w4g64(x, lw["gate"].q, lw["gate"].s, lw["gate"].b)
+                u = qmm_w4g64(x, lw["up"].q, lw["up"].s, lw["up"].b)
+                self.last_down = qmm_w4g64(silu_mul(g, u), lw["down"].q, lw["down"].s, lw["down"].b)
+
+    def _keys(self, hidden_all):
+        self.keys = _lm.lm_head_argmax_keys(hidden_all, self.lm_w, v_begin=self.v_begin)
+
+    def _accept_and_rollback(self, keys_all, ids_all):
+        post, acc, nxt, _ = _lm.verify_accept(keys_all, ids_all, block=self.shape.block)
+        b0 = self.rank * self.requests
+        self.posterior = post[b0:b0 + self.requests]
+        self.acceptance = acc[b0:b0 + self.requests]
+        self.next_token = nxt[b0:b0 + self.requests]
+        steps = self.acceptance + 1       # recurrent_rollback_cache.py:154
+        for layer in range(self.shape.gdn_layers):
+            tape_replay_(self.gdn_state[layer], self.tape[layer], self.tape_k[layer],
+                         self.tape_g[layer], steps)
+
+    # -------------------------------------------------------------- driving
+    def capture(self):
+        """Warm up once eagerly, then capture the three device parts in CUDA
+        graphs: A = qmm stack, B = lm_head keys, C = accept + rollback.  With
+        several ranks the hidden rows, verify ids and keys are all-gathered
+        between the graphs."""
+        sh = self.shape
+        rows = self.requests * sh.block
+        with torch.cuda.device(self.dev), torch.cuda.stream(self.stream):
+            if self.world == 1:
+                self.x_all, self.ids_all = self.x, self.verify_ids
+            else:
+                self.x_all = torch.empty((self.world * rows, sh.hidden), dtype=torch.bfloat16,
+                                         device=self.dev)
+                self.ids_all = torch.empty((self.world * self.requests, sh.block), dtype=torch.int32,
+                                           device=self.dev)
+            self.keys_all = torch.empty((self.world, self.world * rows), dtype=torch.int64,
+                                        device=self.dev)
+            self._qmm_stack()
+            self._keys(self.x_all)
+            self._accept_and_rollback(self.keys_all, self.ids_all)
+            self.stream.synchronize()
+            ga, gb, gc = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ga, stream=self.stream):
+                self._qmm_stack()
+            with torch.cuda.graph(gb, stream=self.stream):
+                self._keys(self.x_all)
+            with torch.cuda.graph(gc, stream=self.stream):
+                self._accept_and_rollback(self.keys_all, self.ids_all)
+            self.graphs = [ga, gb, gc]
+        torch.cuda.synchronize(self.dev)
+
+    def run_step(self, ev_qmm: Optional[tuple] = None):
+        """One verify step on self.stream (graphs must be captured).  With
+        ``ev_qmm = (start, end)`` the qmm stack is bracketed by those events."""
+        with torch.cuda.device(self.dev), torch.cuda.stream(self.stream):
+            if ev_qmm is not None:
+                ev_qmm[0].record(self.stream)
+            self.graphs[0].replay()
+            if ev_qmm is not None:
+                ev_qmm[1].record(self.stream)
+            if self.world > 1:
+                import torch.distributed as dist
+
+                dist.all_gather_into_tensor(self.x_all, self.x, group=self.group)
+                dist.all_gather_into_tensor(self.ids_all, self.verify_ids, group=self.group)
+                self.graphs[1].replay()
+                dist.all_gather_into_tensor(self.keys_all.view(-1), self.keys, group=self.group)
+            else:
+                self.graphs[1].replay()
+                self.keys_all.view(-1).copy_(self.keys)
+            self.graphs[2].replay()
+
+    def verify(self, x_host: torch.Tensor, verify_ids_host: torch.Tensor):
+        """End-to-end call: copy this rank's inputs from (pinned) host memory,
+        run one step, return (posterior, acceptance, next_token) on the host."""
+        with torch.cuda.stream(self.stream):
+            self.x.copy_(x_host, non_blocking=True)
+            self.verify_ids.copy_(verify_ids_host, non_blocking=True)
+        self.run_step()
+        with torch.cuda.stream(self.stream):
+            out = torch.cat([self.posterior.reshape(-1), self.acceptance, self.next_token]).to(
+                "cpu", non_blocking=True)
+        self.stream.synchronize()
+        return out
