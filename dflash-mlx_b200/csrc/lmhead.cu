@@ -64,7 +64,10 @@ struct Params {
 };
 
 // Order-preserving image of a float in 32 bits (larger float -> larger word).
+// -0 is folded into +0 first (x + 0 is +0 for both zeros under round-to-
+// nearest), so equal logits always tie and the lower id wins, as in argmax.
 __host__ __device__ __forceinline__ uint32_t ordered_bits(float v) {
+  v = v + 0.0f;
 #ifdef __CUDA_ARCH__
   const uint32_t u = __float_as_uint(v);
 #else

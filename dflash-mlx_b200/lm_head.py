@@ -111,13 +111,61 @@ def lm_head_verify(hidden: torch.Tensor, weight: torch.Tensor, verify_ids: Optio
     keys = lm_head_argmax_keys(hidden, weight, v_begin=v_begin,
                                suppress_token_mask=suppress_token_mask)
     if group is not None:
-        import torch.distributed as dist
-
-        world = dist.get_world_size(group)
-        gathered = torch.empty((world, keys.numel()), dtype=keys.dtype, device=keys.device)
-        dist.all_gather_into_tensor(gathered, keys, group=group)
-        keys = gathered
+        keys = gather_keys(keys, group)
     return verify_accept(keys, verify_ids, block=block)
+
+
+# ------------------------------------------------- vocabulary split (host side)
+def vocab_shard(vocab: int, rank: int, world: int):
+    """``(v_begin, v_len)`` of rank ``rank``'s contiguous lm_head row range when
+    ``vocab`` rows are split over ``world`` ranks (ceil-sized shards; the last
+    ones may be shorter or empty)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    per = (int(vocab) + world - 1) // world
+    begin = min(int(vocab), rank * per)
+    return begin, min(int(vocab), begin + per) - begin
+
+
+def gather_keys(keys: torch.Tensor, group) -> torch.Tensor:
+    """All-gather one shard's row keys ``[R]`` into ``[world, R]`` (rank order)."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    keys = keys.reshape(-1).contiguous()
+    gathered = torch.empty((world, keys.numel()), dtype=keys.dtype, device=keys.device)
+    dist.all_gather_into_tensor(gathered.view(-1), keys, group=group)
+    return gathered
+
+
+_SIGN64 = -(1 << 63)
+
+
+def make_keys(values: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+    """The kernels' 64-bit row key, as int64 bits: high word an order-preserving
+    image of the fp32 ``values``, low word ``0xFFFFFFFF - ids``.  The unsigned
+    maximum of keys is the largest value with ties to the lowest id (-0 is
+    folded into +0 so that equal values tie)."""
+    v = values.to(torch.float32) + 0.0
+    u = v.contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    ordered = torch.where(u >= (1 << 31), (~u) & 0xFFFFFFFF, u | (1 << 31))
+    low = 0xFFFFFFFF - (ids.to(torch.int64) & 0xFFFFFFFF)
+    # (ordered << 32) as unsigned bits, built without signed overflow
+    return (((ordered - (1 << 31)) << 32) | low) ^ _SIGN64
+
+
+def reduce_keys(keys: torch.Tensor) -> torch.Tensor:
+    """Unsigned maximum over the leading (shard) axis of int64-held keys."""
+    return (keys ^ _SIGN64).amax(dim=0) ^ _SIGN64
+
+
+def decode_keys(keys: torch.Tensor):
+    """``(values fp32, ids int32)`` of row keys (inverse of :func:`make_keys`)."""
+    hi = (keys >> 32) & 0xFFFFFFFF
+    u = torch.where(hi >= (1 << 31), hi & 0x7FFFFFFF, (~hi) & 0xFFFFFFFF)
+    values = (u - ((u >= (1 << 31)).to(torch.int64) << 32)).to(torch.int32).view(torch.float32)
+    ids = (0xFFFFFFFF - (keys & 0xFFFFFFFF)).to(torch.int32)
+    return values, ids
 
 
 def match_acceptance_length(drafted_tokens: torch.Tensor, posterior_tokens: torch.Tensor) -> torch.Tensor:

@@ -90,9 +90,7 @@ class VerifyStep:
         self.layers = [{name: _quant_weight(gen, self.dev, n, k) for name, n, k in sh.projections()}
                        for _ in range(sh.layers)]
         # this rank's vocabulary shard of the bf16 lm_head, N(0, 0.02)
-        per = (sh.vocab + world - 1) // world
-        self.v_begin = rank * per
-        v_len = max(0, min(sh.vocab, self.v_begin + per) - self.v_begin)
+        self.v_begin, v_len = _lm.vocab_shard(sh.vocab, rank, world)
         wgen = torch.Generator(device=self.dev).manual_seed(seed + 1000 + rank)
         self.lm_w = (torch.randn((v_len, sh.hidden), generator=wgen, device=self.dev) * 0.02).to(torch.bfloat16)
         # GDN rollback state and tapes: [layer][B, Hv, Dv, Dk] fp32 ~ N(0, 0.05)

@@ -88,7 +88,13 @@ def test_vocab_shards_combine_to_global_argmax(pkg, dev):
     post_sh, _, _, mx_sh = pkg.verify_accept(shards, None)
     assert torch.equal(post_full, post_sh)
     assert torch.equal(mx_full, mx_sh)
-    assert torch.equal(shards.max(dim=0).values, full)
+    lm = pkg.lm_head
+    assert torch.equal(lm.reduce_keys(shards), full)
+    # the host-side key helpers use the kernels' exact key format
+    vals, ids = lm.decode_keys(full)
+    assert torch.equal(lm.make_keys(vals, ids), full)
+    assert torch.equal(ids.cpu().long(), torch.from_numpy(_decode(full)))
+    assert torch.equal(vals.reshape(-1, 16), mx_full)
 
 
 def test_verify_accept_scan(pkg, dev):
