@@ -25,6 +25,7 @@ STATUS_NAMES = {
     4: "DFL_ERR_WORKSPACE",
     5: "DFL_ERR_CUDA",
     6: "DFL_ERR_UNSUPPORTED",
+    7: "DFL_ERR_SCRATCH_LIMIT",
 }
 
 # name -> (restype, argtypes); must match include/dflash_b200.h
@@ -35,6 +36,8 @@ SIGNATURES = {
     "dfl_verify_qmm_w4g64": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_size, _c_int, _c_int,
                                       _c_int, _vp]),
     "dfl_verify_qmm_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
+    "dfl_verify_qmm_w4g64_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
+                                              _vp]),
     "dfl_gdn_tape_replay": (_c_int, [_vp, _vp, _c_int, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int,
                                      _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
     "dfl_lmhead_argmax": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,

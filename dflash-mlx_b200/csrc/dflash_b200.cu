@@ -5,6 +5,7 @@
 #include "host_common.cuh"
 
 #include "qmm_w4.cu"
+#include "qmm_noalloc.cu"
 #include "gdn_replay.cu"
 #include "lmhead.cu"
 #include "moe.cu"
@@ -18,6 +19,7 @@ extern "C" const char* dfl_status_string(int status) {
     case DFL_ERR_WORKSPACE: return "workspace missing or too small";
     case DFL_ERR_CUDA: return "CUDA error";
     case DFL_ERR_UNSUPPORTED: return "unsupported device or option";
+    case DFL_ERR_SCRATCH_LIMIT: return "shape needs more scratch than the fixed no-allocation array";
     default: return "unknown status";
   }
 }

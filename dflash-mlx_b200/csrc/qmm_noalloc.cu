@@ -1,0 +1,85 @@
+// Dense int4 g64 verify qmm for callers that cannot allocate device memory.
+//
+// Same kernel and arguments as dfl_verify_qmm_w4g64, but the split-K scratch
+// (tile counters + fp32 partial sums) lives in one fixed file-scope device
+// array instead of a caller workspace:
+//   * kScratchBytes (8 MiB) is the limit; a call whose scratch need
+//     (dfl_verify_qmm_workspace_bytes for its shape) is larger returns
+//     DFL_ERR_SCRATCH_LIMIT.  For M <= 32 the need is 64 KB + 32 KB per SM,
+//     which fits for any part with at most 254 SMs (B200: 148 -> 4.8 MB).
+//   * The first call on a device resolves the array's address on that
+//     device (cudaGetSymbolAddress, with that device current); make it
+//     before any stream capture on that device.
+//   * Every call on a device shares the one array.  Each call clears the
+//     tile counters (which must start at zero) on its stream before the
+//     kernel, so calls in stream order are safe; calls that may overlap in
+//     time (different streams or host threads) race on the array.
+// Nothing here calls cudaMalloc / cudaFree or any allocating routine.
+
+namespace dfl {
+namespace qmm_noalloc {
+
+constexpr size_t kScratchBytes = size_t(8) << 20;
+
+static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
+
+struct DeviceScratch {
+  std::atomic<void*> ptr{nullptr};
+};
+
+inline DeviceScratch& scratch_slot(int dev) {
+  static DeviceScratch slots[host::kMaxDevices];
+  return slots[dev];
+}
+
+// Device address of g_scratch on `dev` (the current device); resolved once.
+inline int scratch_for_device(int dev, void** out) {
+  DeviceScratch& slot = scratch_slot(dev);
+  void* p = slot.ptr.load(std::memory_order_acquire);
+  if (!p) {
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    p = slot.ptr.load(std::memory_order_acquire);
+    if (!p) {
+      if (cudaGetSymbolAddress(&p, g_scratch) != cudaSuccess || p == nullptr) {
+        cudaGetLastError();
+        return DFL_ERR_CUDA;
+      }
+      slot.ptr.store(p, std::memory_order_release);
+    }
+  }
+  *out = p;
+  return DFL_OK;
+}
+
+}  // namespace qmm_noalloc
+}  // namespace dfl
+
+extern "C" int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q,
+                                            const uint16_t* scales, const uint16_t* biases,
+                                            uint16_t* y, int M, int K, int N, void* stream) {
+  using namespace dfl;
+  if (M < 1 || M > 32 || K < 64 || K % 64 != 0 || N < 1 || N > qmm::kMaxTiles * qmm::BN)
+    return DFL_ERR_BAD_SHAPE;
+  if (!x || !w_q || !scales || !biases || !y) return DFL_ERR_NULL_POINTER;
+  if (!host::aligned(x, 16) || !host::aligned(w_q, 16) || !host::aligned(scales, 2) ||
+      !host::aligned(biases, 2) || !host::aligned(y, 2))
+    return DFL_ERR_MISALIGNED;
+  int dev, sms;
+  int st = host::current_device(&dev, &sms);
+  if (st != DFL_OK) return st;
+  if (qmm::workspace_bytes_for(M, K, N, sms) > qmm_noalloc::kScratchBytes)
+    return DFL_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  st = qmm_noalloc::scratch_for_device(dev, &scratch);
+  if (st != DFL_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t counter_bytes = size_t((N + qmm::BN - 1) / qmm::BN) * sizeof(int);
+  if (cudaMemsetAsync(scratch, 0, counter_bytes, s) != cudaSuccess) {
+    cudaGetLastError();
+    return DFL_ERR_CUDA;
+  }
+  if (qmm::choose_mt(M) == 16)
+    return qmm::launch<16>(x, w_q, scales, biases, y, scratch, M, K, N, sms, dev, s);
+  return qmm::launch<32>(x, w_q, scales, biases, y, scratch, M, K, N, sms, dev, s);
+}

@@ -36,7 +36,8 @@ enum {
   DFL_ERR_MISALIGNED = 3,    /* a pointer or row stride breaks an alignment rule */
   DFL_ERR_WORKSPACE = 4,     /* workspace missing or too small */
   DFL_ERR_CUDA = 5,          /* a CUDA runtime / driver call failed */
-  DFL_ERR_UNSUPPORTED = 6    /* no sm_100 device, or an unsupported option */
+  DFL_ERR_UNSUPPORTED = 6,   /* no sm_100 device, or an unsupported option */
+  DFL_ERR_SCRATCH_LIMIT = 7  /* needs more scratch than the fixed no-allocation array */
 };
 
 /* Human-readable text for a status code (static storage). */
@@ -74,6 +75,22 @@ int dfl_verify_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t*
 /* Workspace bytes dfl_verify_qmm_w4g64 needs for this shape on the current
  * device; 0 with *status != DFL_OK on error. */
 size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status);
+
+/* dfl_verify_qmm_w4g64 without a workspace argument, for callers that cannot
+ * allocate device memory.  No counterpart in the reference (MLX allocates
+ * its own buffers).  Same x / w_q / scales / biases / y / shape rules and the
+ * same results.  Split-K scratch is a fixed 8 MiB device array inside the
+ * library, shared by every call on a device:
+ *   - a shape whose dfl_verify_qmm_workspace_bytes exceeds 8 MiB returns
+ *     DFL_ERR_SCRATCH_LIMIT (never for M <= 32 on parts with <= 254 SMs);
+ *   - the first call on a device looks the array up on that device (make it
+ *     before any stream capture there);
+ *   - each call zeroes the counters it uses on `stream` first, so calls in
+ *     stream order are safe; calls that can overlap in time race.
+ * Allocates nothing. */
+int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
+                                 const uint16_t* biases, uint16_t* y, int M, int K, int N,
+                                 void* stream);
 
 /* ------------------------------------------------------------------------
  * GatedDeltaNet tape-replay rollback.
