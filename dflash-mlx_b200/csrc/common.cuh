@@ -114,6 +114,21 @@ __device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t pari
   }
 }
 
+// ------------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel in the stream is still running.  griddep_wait() blocks
+// until that kernel has completed and its memory is visible; everything that
+// reads the previous kernel's outputs (or writes what it may still read) must
+// come after it.  griddep_launch_dependents() lets the next such kernel start
+// early.  Both are no-ops for a normal launch.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- cp.async
 // 16-byte global -> shared copy through L2; src_bytes < 16 zero-fills the
 // rest (0 reads nothing).
@@ -121,6 +136,58 @@ __device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void* src, 
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src),
                "r"(src_bytes)
                : "memory");
+}
+
+// Untiled bulk copy global -> this CTA's shared memory, completing bytes on
+// an mbarrier.  Both addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst_smem), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Orders this thread's earlier generic-proxy observations of global memory
+// before its later async-proxy (bulk copy / TMA) reads of it.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Release-add on a global counter (no return value): writes this thread
+// observed before it (including other threads' writes ordered by a barrier)
+// are visible to whoever acquires the new value.
+__device__ __forceinline__ void red_release_add(int* addr, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire(const int* addr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// Spin until *addr >= target (acquire).  Gives up like mbar_wait_abortable:
+// after kWaitLimitNs, or at once when the CTA abort word is set.
+__device__ __forceinline__ bool spin_acquire_geq(const int* addr, int target,
+                                                 volatile int* abort_word) {
+  if (ld_acquire(addr) >= target) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+    __nanosleep(64);
+    if (ld_acquire(addr) >= target) return true;
+    if (*abort_word) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicExch(&g_device_error, kDevWaitTimeout);
+      *abort_word = 1;
+      return false;
+    }
+  }
+}
+
+// Wait until all of this thread's prior cp.async copies have landed.
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // Arrive on an mbarrier once all of this thread's prior cp.async copies have

@@ -11,6 +11,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "../../include/dflash_b200.h"
 
@@ -123,6 +124,30 @@ inline int ensure_smem(Kernel kernel, int bytes, int dev, std::atomic<uint64_t>&
       cudaSuccess)
     return DFL_ERR_CUDA;
   done_mask.fetch_or(bit, std::memory_order_acq_rel);
+  return DFL_OK;
+}
+
+// Launch with programmatic stream serialization: the kernel may begin (its
+// prologue and its weight loads) while the previous kernel in the stream is
+// still running; it calls griddep_wait() before touching that kernel's outputs.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), int grid, int block, size_t smem,
+                      cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) != cudaSuccess) {
+    cudaGetLastError();
+    return DFL_ERR_CUDA;
+  }
   return DFL_OK;
 }
 

@@ -256,9 +256,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* sbempty = sbfull + 2;              // [2]       chunk read by the dequant warps
   uint64_t* accfull = sbempty + 2;             // [2]
   uint64_t* accempty = accfull + 2;            // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
-  int* flag_slot = reinterpret_cast<int*>(tmem_slot + 1);
-  volatile int* abort_word = reinterpret_cast<volatile int*>(flag_slot + 1);
+  uint64_t* redbar = accempty + 2;             // [1]       split-K partials landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(redbar + 1);
+  int* red_ok = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(red_ok + 1);
   auto wait = [abort_word](uint64_t* bar, uint32_t parity) {
     return mbar_wait_abortable(bar, parity, abort_word);
   };
@@ -268,13 +269,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int cta = blockIdx.x;
   const int ku = p.k_units;
   const int tpp = p.tpp;
+  // Launched with programmatic serialization: the route table of grouped
+  // mode may be written by the kernel just before, so grouped CTAs wait for
+  // it first.  Dense CTAs only wait in the warps that read x and write y or
+  // the workspace; weight loads and dequant start at once.
+  if (GROUPED) griddep_wait();
   const int total = GROUPED ? (*p.g_count) * tpp * ku : p.total_units;
   const int u0 = unit_begin(cta, total, p.grid);
   const int u1 = unit_begin(cta + 1, total, p.grid);
   const int n_units = u1 - u0;
 
   if (threadIdx.x == 0) {
+    // descriptor fetches overlap the set-up below
+    tma_prefetch_desc(&tm_w);
+    if (p.sb_tma) {
+      tma_prefetch_desc(&tm_s);
+      tma_prefetch_desc(&tm_b);
+    }
     *abort_word = 0;
+    mbar_init(redbar, 1);
     for (int i = 0; i < C::NSTAGE; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 4 * NDG);
@@ -305,6 +318,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_launch_dependents();
 
   if (warp == WARP_TMA) {
     // ------------------------------------------------------------ producer
@@ -313,9 +327,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // per unit: coordinates advance incrementally, one lane issues.
     if (p.sb_tma) {
       if (lane == 0) {
-        tma_prefetch_desc(&tm_w);
-        tma_prefetch_desc(&tm_s);
-        tma_prefetch_desc(&tm_b);
         int tile = u0 / ku, kb = u0 - (u0 / ku) * ku;
         int pi = tile / tpp;
         tile -= pi * tpp;
@@ -353,7 +364,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else {
       // Scale/bias rows are not 16-byte multiples (K % 512 != 0): the warp
       // fills each chunk with plain loads, in the same swizzled layout.
-      if (lane == 0) tma_prefetch_desc(&tm_w);
       const int groups = p.K / GS;
       int tile = u0 / ku, kb = u0 - (u0 / ku) * ku;
       int pi = tile / tpp;
@@ -540,6 +550,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) mbar_arrive(&xfull[xs]);
     };
     int staged = 0;  // units of x staged so far
+    griddep_wait();
     if (n_units > 0) {
       load_x_unit<MT, GROUPED>(p, (u0 % ku) * UNIT_K, u0 / (ku * tpp), et, xr);
       for (; staged < n_units && staged < C::XS; ++staged) stage_x(staged);
@@ -581,44 +592,68 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           continue;
         }
-        // Partial tile: publish fp32 partial, last arriver reduces.
-        const int slot = (u0 >= t * ku) ? 0 : 1;
-        float* mine = p.partials + ((size_t)(cta * 2 + slot) * MT) * BN;
+        // Partial tile, split over CTAs c_lo..c_hi.  The tile is the last one
+        // of c_lo's range and the first (or only) one of every other
+        // contributor's.  Contributors publish their fp32 partial and count it
+        // with a release-add (the named barrier orders the four warps' stores
+        // before it); c_lo reduces once it has finished its own part, which
+        // is also the end of its range, so its weight ring is free to receive
+        // the others' partials by bulk copy.  Sources are summed in CTA order,
+        // so the result is bit-reproducible.
+        const int c_lo = cta_of_unit(t * ku, total, p.grid);
+        if (cta != c_lo) {
+          float* mine = p.partials + ((size_t)(cta * 2) * MT) * BN;
 #pragma unroll
-        for (int m = 0; m < MT; ++m) mine[m * BN + r] = acc[m];
-        __threadfence();
-        named_bar_sync(BAR_ID_EPI, 128);
+          for (int m = 0; m < MT; ++m) __stcg(mine + m * BN + r, acc[m]);
+          named_bar_sync(BAR_ID_EPI, 128);
+          if (et == 0) red_release_add(&p.counters[t], 1);
+          continue;
+        }
+        const int c_hi = cta_of_unit(t * ku + ku - 1, total, p.grid);
         if (et == 0) {
-          const int c_lo = cta_of_unit(t * ku, total, p.grid);
-          const int c_hi = cta_of_unit(t * ku + ku - 1, total, p.grid);
-          const int expected = c_hi - c_lo + 1;
-          const int prev = atomicAdd(&p.counters[t], 1);
-          *flag_slot = (prev == expected - 1) ? 1 : 0;
+          const bool ok = spin_acquire_geq(&p.counters[t], c_hi - c_lo, abort_word);
+          fence_proxy_async_global();
+          *red_ok = ok ? 1 : 0;
         }
         named_bar_sync(BAR_ID_EPI, 128);
-        if (*flag_slot) {
-          __threadfence();
-          const int c_lo = cta_of_unit(t * ku, total, p.grid);
-          const int c_hi = cta_of_unit(t * ku + ku - 1, total, p.grid);
-          float sum[MT];
+        if (!*red_ok) break;
+        constexpr int SRC_BYTES = MT * BN * 4;
+        constexpr int NB = (C::NSTAGE * C::STAGE_BYTES) / SRC_BYTES;  // sources per batch
+        const uint32_t ring0 = smem_u32(smem);
+        float sum[MT];
 #pragma unroll
-          for (int m = 0; m < MT; ++m) sum[m] = 0.f;
-          for (int c = c_lo; c <= c_hi; ++c) {
-            const int cs = (unit_begin(c, total, p.grid) >= t * ku) ? 0 : 1;
-            const float* src = p.partials + ((size_t)(c * 2 + cs) * MT) * BN;
-#pragma unroll
-            for (int m = 0; m < MT; ++m) sum[m] += __ldcg(src + m * BN + r);
+        for (int m = 0; m < MT; ++m) sum[m] = acc[m];
+        uint32_t red_phase = 0;
+        bool red_done = true;
+        for (int c0 = c_lo + 1; c0 <= c_hi; c0 += NB) {
+          const int nb = (c_hi - c0 + 1) < NB ? (c_hi - c0 + 1) : NB;
+          if (et == 0) {
+            mbar_arrive_expect_tx(redbar, uint32_t(nb * SRC_BYTES));
+            for (int q = 0; q < nb; ++q)
+              bulk_load(ring0 + q * SRC_BYTES, p.partials + ((size_t)((c0 + q) * 2) * MT) * BN,
+                        SRC_BYTES, redbar);
           }
-          if (n < p.N) {
-#pragma unroll
-            for (int m = 0; m < MT; ++m)
-              if (m < rows)
-                p.y[(size_t)(GROUPED ? outrow[m] : m) * p.N + n] =
-                    __bfloat16_as_ushort(__float2bfloat16_rn(sum[m]));
+          if (!named_bar_and(BAR_ID_EPI, 128, wait(redbar, red_phase))) {
+            red_done = false;
+            break;
           }
-          if (et == 0) p.counters[t] = 0;
+          red_phase ^= 1;
+          for (int q = 0; q < nb; ++q) {
+            const float* sp = reinterpret_cast<const float*>(smem + q * SRC_BYTES);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) sum[m] += sp[m * BN + r];
+          }
+          named_bar_sync(BAR_ID_EPI, 128);  // batch read before the next overwrites it
         }
-        named_bar_sync(BAR_ID_EPI, 128);
+        if (!red_done) break;
+        if (n < p.N) {
+#pragma unroll
+          for (int m = 0; m < MT; ++m)
+            if (m < rows)
+              p.y[(size_t)(GROUPED ? outrow[m] : m) * p.N + n] =
+                  __bfloat16_as_ushort(__float2bfloat16_rn(sum[m]));
+        }
+        if (et == 0) p.counters[t] = 0;
       }
     }
   }
@@ -694,8 +729,8 @@ int launch_kernel(const CUtensorMap& tm_w, const CUtensorMap& tm_s, const CUtens
   static std::atomic<uint64_t> smem_done{0};
   int st = host::ensure_smem(qmm_w4g64_kernel<MT, GROUPED>, C::SMEM_BYTES, dev, smem_done);
   if (st != DFL_OK) return st;
-  qmm_w4g64_kernel<MT, GROUPED><<<p.grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(tm_w, tm_s, tm_b, p);
-  return host::launch_status();
+  return host::launch_pdl(qmm_w4g64_kernel<MT, GROUPED>, p.grid, NUM_THREADS, C::SMEM_BYTES, stream,
+                          tm_w, tm_s, tm_b, p);
 }
 
 template <int MT>
