@@ -240,7 +240,8 @@ __device__ __forceinline__ void store_x_unit(uint32_t slot, int et,
 template <int MT, bool GROUPED>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     qmm_w4g64_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
-                     const __grid_constant__ CUtensorMap tm_b, const Params p) {
+                     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_x,
+                     const Params p) {
   using C = Cfg<MT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -252,7 +253,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* aempty = afull + NSUB;             // [NSUB]    TMEM A slot read by MMA
   uint64_t* xfull = aempty + NSUB;             // [XS]      x slot staged
   uint64_t* xfree = xfull + C::XS;             // [XS]      x slot read by all MMA warps
-  uint64_t* sbfull = xfree + C::XS;            // [2]       scale/bias chunk landed
+  uint64_t* xtma = xfree + C::XS;              // [XS]      x slot landed (dense: TMA)
+  uint64_t* sbfull = xtma + C::XS;             // [2]       scale/bias chunk landed
   uint64_t* sbempty = sbfull + 2;              // [2]       chunk read by the dequant warps
   uint64_t* accfull = sbempty + 2;             // [2]
   uint64_t* accempty = accfull + 2;            // [2]
@@ -282,6 +284,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     // descriptor fetches overlap the set-up below
     tma_prefetch_desc(&tm_w);
+    if (!GROUPED) tma_prefetch_desc(&tm_x);
     if (p.sb_tma) {
       tma_prefetch_desc(&tm_s);
       tma_prefetch_desc(&tm_b);
@@ -303,6 +306,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int i = 0; i < C::XS; ++i) {
       mbar_init(&xfull[i], 4);
       mbar_init(&xfree[i], NUM_MMA_WARPS);
+      mbar_init(&xtma[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accfull[i], NUM_MMA_WARPS);
@@ -322,70 +326,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp == WARP_TMA) {
     // ------------------------------------------------------------ producer
-    // Under full load every instruction of this warp waits for an issue slot
-    // behind the dequant warps, so the loop is kept to a few instructions
-    // per unit: coordinates advance incrementally, one lane issues.
-    if (p.sb_tma) {
-      if (lane == 0) {
-        int tile = u0 / ku, kb = u0 - (u0 / ku) * ku;
-        int pi = tile / tpp;
-        tile -= pi * tpp;
-        int e = (GROUPED && n_units > 0) ? p.g_expert[pi] : 0;
-        int chunk = -1;
-        for (int it = 0; it < n_units; ++it) {
-          const int n0 = tile * BN;
-          if (it == 0 || kb % SBC == 0) {
-            ++chunk;
-            const int cs = chunk & 1;
-            wait(&sbempty[cs], ((chunk >> 1) & 1) ^ 1);
-            if (*abort_word) break;
-            uint8_t* dst = smem + C::OFF_SB + cs * C::SBC_BYTES;
+    // Two streams: packed weights (+ scale/bias chunks) into the stage ring
+    // and, in dense mode, x into the x ring.  Weights do not depend on the
+    // previous kernel, so the first NSTAGE units are requested before
+    // griddep_wait(); x (possibly the previous kernel's output) only after.
+    // x runs XD = XS - 1 units ahead of the MMAs and weights NSTAGE units
+    // ahead of the dequant warps, interleaved so neither stream waits on the
+    // other.  Lane 0 waits and issues; the other lanes only help with
+    // scale/bias rows that are not 16-byte multiples (K % 512 != 0).
+    int w_tile = u0 / ku, w_kb = u0 - (u0 / ku) * ku;
+    int w_pi = w_tile / tpp;
+    w_tile -= w_pi * tpp;
+    int w_e = (GROUPED && n_units > 0) ? p.g_expert[w_pi] : 0;
+    int chunk = -1;
+    const int groups = p.K / GS;
+    auto issue_w = [&](int it) -> bool {
+      const int n0 = w_tile * BN;
+      if (it == 0 || w_kb % SBC == 0) {
+        ++chunk;
+        const int cs = chunk & 1;
+        if (lane == 0) wait(&sbempty[cs], ((chunk >> 1) & 1) ^ 1);
+        __syncwarp();
+        if (*abort_word) return false;
+        uint8_t* dst = smem + C::OFF_SB + cs * C::SBC_BYTES;
+        const int g0 = (w_kb / SBC) * SBC * NSUB;
+        if (p.sb_tma) {
+          if (lane == 0) {
             mbar_arrive_expect_tx(&sbfull[cs], C::SBC_BYTES);
-            tma_load_3d(dst, &tm_s, &sbfull[cs], (kb / SBC) * SBC * NSUB, n0, e);
-            tma_load_3d(dst + C::SBC_HALF, &tm_b, &sbfull[cs], (kb / SBC) * SBC * NSUB, n0, e);
+            tma_load_3d(dst, &tm_s, &sbfull[cs], g0, n0, w_e);
+            tma_load_3d(dst + C::SBC_HALF, &tm_b, &sbfull[cs], g0, n0, w_e);
           }
-          const int s = it % C::NSTAGE;
-          wait(&empty[s], ((it / C::NSTAGE) & 1) ^ 1);
-          if (*abort_word) break;
-          uint8_t* st = smem + s * C::STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[s], C::PACK_BYTES);
-          tma_load_3d(st, &tm_w, &full[s], kb * (UNIT_K / 8), n0, e);
-          tma_load_3d(st + C::PACK_BYTES / 2, &tm_w, &full[s], kb * (UNIT_K / 8) + 32, n0, e);
-          if (++kb == ku) {
-            kb = 0;
-            if (++tile == tpp) {
-              tile = 0;
-              ++pi;
-              if (GROUPED && it + 1 < n_units) e = p.g_expert[pi];
-            }
-          }
-        }
-      }
-    } else {
-      // Scale/bias rows are not 16-byte multiples (K % 512 != 0): the warp
-      // fills each chunk with plain loads, in the same swizzled layout.
-      const int groups = p.K / GS;
-      int tile = u0 / ku, kb = u0 - (u0 / ku) * ku;
-      int pi = tile / tpp;
-      tile -= pi * tpp;
-      int e = (GROUPED && n_units > 0) ? p.g_expert[pi] : 0;
-      int chunk = -1;
-      for (int it = 0; it < n_units; ++it) {
-        const int n0 = tile * BN;
-        if (it == 0 || kb % SBC == 0) {
-          ++chunk;
-          const int cs = chunk & 1;
-          if (lane == 0) wait(&sbempty[cs], ((chunk >> 1) & 1) ^ 1);
-          __syncwarp();
-          if (*abort_word) break;
-          uint8_t* dst = smem + C::OFF_SB + cs * C::SBC_BYTES;
-          const int g0 = (kb / SBC) * SBC * NSUB;
+        } else {
           for (int i = lane; i < BN * SBC * NSUB; i += 32) {
             const int r = i / (SBC * NSUB), gi = i - r * (SBC * NSUB);
             const int n = n0 + r, g = g0 + gi;
             uint16_t sv = 0, bv = 0;
             if (n < p.N && g < groups) {
-              const size_t idx = ((size_t)e * p.N + n) * groups + g;
+              const size_t idx = ((size_t)w_e * p.N + n) * groups + g;
               sv = p.scales[idx];
               bv = p.biases[idx];
             }
@@ -396,27 +373,58 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&sbfull[cs]);
         }
-        const int s = it % C::NSTAGE;
-        if (lane == 0) {
-          wait(&empty[s], ((it / C::NSTAGE) & 1) ^ 1);
-          if (!*abort_word) {
-            uint8_t* st = smem + s * C::STAGE_BYTES;
-            mbar_arrive_expect_tx(&full[s], C::PACK_BYTES);
-            tma_load_3d(st, &tm_w, &full[s], kb * (UNIT_K / 8), n0, e);
-            tma_load_3d(st + C::PACK_BYTES / 2, &tm_w, &full[s], kb * (UNIT_K / 8) + 32, n0, e);
-          }
-        }
-        __syncwarp();
-        if (*abort_word) break;
-        if (++kb == ku) {
-          kb = 0;
-          if (++tile == tpp) {
-            tile = 0;
-            ++pi;
-            if (GROUPED && it + 1 < n_units) e = p.g_expert[pi];
-          }
+      }
+      const int s = it % C::NSTAGE;
+      if (lane == 0) {
+        wait(&empty[s], ((it / C::NSTAGE) & 1) ^ 1);
+        if (!*abort_word) {
+          uint8_t* st = smem + s * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], C::PACK_BYTES);
+          tma_load_3d(st, &tm_w, &full[s], w_kb * (UNIT_K / 8), n0, w_e);
+          tma_load_3d(st + C::PACK_BYTES / 2, &tm_w, &full[s], w_kb * (UNIT_K / 8) + 32, n0, w_e);
         }
       }
+      __syncwarp();
+      if (*abort_word) return false;
+      if (++w_kb == ku) {
+        w_kb = 0;
+        if (++w_tile == tpp) {
+          w_tile = 0;
+          ++w_pi;
+          if (GROUPED && it + 1 < n_units) w_e = p.g_expert[w_pi];
+        }
+      }
+      return true;
+    };
+    // x unit ix -> slot ix % XS as NSUB boxes of [64 K x MT rows] (rows >= M
+    // and columns >= K read as zero), once the MMAs of unit ix - XS are done.
+    auto issue_x = [&](int ix) -> bool {
+      const int xs = ix % C::XS;
+      if (lane == 0) {
+        if (ix >= C::XS) wait(&xfree[xs], ((ix / C::XS) - 1) & 1);
+        if (!*abort_word) {
+          const int k0 = ((u0 + ix) % ku) * UNIT_K;
+          uint8_t* dst = smem + C::OFF_XRING + xs * C::XSLOT_BYTES;
+          mbar_arrive_expect_tx(&xtma[xs], C::XSLOT_BYTES);
+#pragma unroll
+          for (int b = 0; b < NSUB; ++b)
+            tma_load_2d(dst + b * C::XBLK_BYTES, &tm_x, &xtma[xs], k0 + b * GS, 0);
+        }
+      }
+      __syncwarp();
+      return !*abort_word;
+    };
+    constexpr int XD = C::XS - 1;
+    const int pro = n_units < C::NSTAGE ? n_units : C::NSTAGE;
+    bool ok = true;
+    for (int it = 0; ok && it < pro; ++it) ok = issue_w(it);
+    if (!GROUPED) {
+      griddep_wait();
+      for (int ix = 0; ok && ix < XD && ix < n_units; ++ix) ok = issue_x(ix);
+    }
+    for (int i = 0; ok && i < n_units; ++i) {
+      if (!GROUPED && i + XD < n_units) ok = issue_x(i + XD);
+      if (ok && i + C::NSTAGE < n_units) ok = issue_w(i + C::NSTAGE);
     }
   } else if (warp < WARP_DQ0) {
     // ------------------------------------------------------------ MMA issuers
@@ -534,16 +542,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int et = threadIdx.x - WARP_EPI0 * 32;  // 0..127
     const uint32_t lane_base = tmem_base + (uint32_t(quad * 32) << 16);
     const uint32_t ring = smem_u32(smem + C::OFF_XRING);
-    uint4 xr[C::X_PER_THREAD];
+    uint4 xr[GROUPED ? C::X_PER_THREAD : 1];
     // x for unit `ix` goes into slot ix % XS once the MMAs of unit ix - XS
-    // have read that slot.
+    // have read that slot.  Dense: the producer's TMA brought it in natural
+    // K order and it is permuted in place here (the permutation stays inside
+    // each 16-byte chunk, so the swizzle does not matter).  Grouped: rows are
+    // gathered through the route table with plain loads, one unit ahead.
     auto stage_x = [&](int ix) {
       const int xs = ix % C::XS;
-      if (ix >= C::XS) wait(&xfree[xs], ((ix / C::XS) - 1) & 1);
-      store_x_unit<MT>(ring + xs * C::XSLOT_BYTES, et, xr);
-      if (ix + 1 < n_units) {
-        const int un = u0 + ix + 1;
-        load_x_unit<MT, GROUPED>(p, (un % ku) * UNIT_K, un / (ku * tpp), et, xr);
+      if constexpr (GROUPED) {
+        if (ix >= C::XS) wait(&xfree[xs], ((ix / C::XS) - 1) & 1);
+        store_x_unit<MT>(ring + xs * C::XSLOT_BYTES, et, xr);
+        if (ix + 1 < n_units) {
+          const int un = u0 + ix + 1;
+          load_x_unit<MT, GROUPED>(p, (un % ku) * UNIT_K, un / (ku * tpp), et, xr);
+        }
+      } else {
+        wait(&xtma[xs], (ix / C::XS) & 1);
+        const uint32_t slot = ring + xs * C::XSLOT_BYTES;
+#pragma unroll
+        for (int t = 0; t < C::X_PER_THREAD; ++t) {
+          const uint32_t a = slot + uint32_t(et + 128 * t) * 16u;
+          st_shared_v4(a, permute_x_chunk(ld_shared_v4(a)));
+        }
       }
       fence_proxy_async_shared();
       __syncwarp();
@@ -552,7 +573,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int staged = 0;  // units of x staged so far
     griddep_wait();
     if (n_units > 0) {
-      load_x_unit<MT, GROUPED>(p, (u0 % ku) * UNIT_K, u0 / (ku * tpp), et, xr);
+      if constexpr (GROUPED)
+        load_x_unit<MT, GROUPED>(p, (u0 % ku) * UNIT_K, u0 / (ku * tpp), et, xr);
       for (; staged < n_units && staged < C::XS; ++staged) stage_x(staged);
       const int t_first = u0 / ku;
       const int t_last = (u1 - 1) / ku;
@@ -724,13 +746,14 @@ inline int make_weight_maps(const uint32_t* w_q, const uint16_t* scales, const u
 
 template <int MT, bool GROUPED>
 int launch_kernel(const CUtensorMap& tm_w, const CUtensorMap& tm_s, const CUtensorMap& tm_b,
+                  const CUtensorMap& tm_x,
                   const Params& p, int dev, cudaStream_t stream) {
   using C = Cfg<MT>;
   static std::atomic<uint64_t> smem_done{0};
   int st = host::ensure_smem(qmm_w4g64_kernel<MT, GROUPED>, C::SMEM_BYTES, dev, smem_done);
   if (st != DFL_OK) return st;
   return host::launch_pdl(qmm_w4g64_kernel<MT, GROUPED>, p.grid, NUM_THREADS, C::SMEM_BYTES, stream,
-                          tm_w, tm_s, tm_b, p);
+                          tm_w, tm_s, tm_b, tm_x, p);
 }
 
 template <int MT>
@@ -755,10 +778,15 @@ int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const
   p.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes);
   // TMA of scale/bias rows needs 16-byte multiples: K % 512 == 0.
   p.sb_tma = (K % UNIT_K == 0) && host::aligned(scales, 16) && host::aligned(biases, 16);
-  CUtensorMap tm_w, tm_s, tm_b;
+  CUtensorMap tm_w, tm_s, tm_b, tm_x;
   int st = make_weight_maps(w_q, scales, biases, 1, K, N, p.sb_tma != 0, &tm_w, &tm_s, &tm_b);
   if (st != DFL_OK) return st;
-  return launch_kernel<MT, false>(tm_w, tm_s, tm_b, p, dev, stream);
+  // x [M, K] bf16 in boxes of [64 K x MT rows], 128-byte swizzle (the UMMA
+  // K-major layout); rows >= M read as zero.
+  st = host::make_tmap_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, uint64_t(K), uint64_t(M),
+                          uint64_t(K) * 2, GS, MT, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != DFL_OK) return st;
+  return launch_kernel<MT, false>(tm_w, tm_s, tm_b, tm_x, p, dev, stream);
 }
 
 }  // namespace qmm
@@ -874,8 +902,10 @@ extern "C" int dfl_moe_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const u
   p.g_m = route + 1 + E;
   p.g_rows = gather_by_pair ? route + 1 + 2 * E + 16 * E : route + 1 + 2 * E;
   p.g_out = route + 1 + 2 * E + 16 * E;
-  CUtensorMap tm_w, tm_s, tm_b;
+  CUtensorMap tm_w, tm_s, tm_b, tm_x;
+  std::memset(&tm_x, 0, sizeof(tm_x));  // grouped mode gathers x rows with plain loads
   st = qmm::make_weight_maps(w_q, scales, biases, E, K, N, p.sb_tma != 0, &tm_w, &tm_s, &tm_b);
   if (st != DFL_OK) return st;
-  return qmm::launch_kernel<16, true>(tm_w, tm_s, tm_b, p, dev, reinterpret_cast<cudaStream_t>(stream));
+  return qmm::launch_kernel<16, true>(tm_w, tm_s, tm_b, tm_x, p, dev,
+                                      reinterpret_cast<cudaStream_t>(stream));
 }
