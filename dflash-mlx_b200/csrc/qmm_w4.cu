@@ -326,14 +326,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp == WARP_TMA) {
     // ------------------------------------------------------------ producer
-    // Two streams: packed weights (+ scale/bias chunks) into the stage ring
-    // and, in dense mode, x into the x ring.  Weights do not depend on the
-    // previous kernel, so the first NSTAGE units are requested before
-    // griddep_wait(); x (possibly the previous kernel's output) only after.
-    // x runs XD = XS - 1 units ahead of the MMAs and weights NSTAGE units
-    // ahead of the dequant warps, interleaved so neither stream waits on the
-    // other.  Lane 0 waits and issues; the other lanes only help with
-    // scale/bias rows that are not 16-byte multiples (K % 512 != 0).
+    // Packed weights (+ scale/bias chunks) into the stage ring, NSTAGE units
+    // ahead of the dequant warps.  Weights do not depend on the previous
+    // kernel, so this warp never waits for it.  It waits only on dequant
+    // progress (stage and chunk release), never on the MMAs: x, whose slots
+    // the MMAs release, is requested by the x warps.  Lane 0 waits and
+    // issues; the other lanes only help with scale/bias rows that are not
+    // 16-byte multiples (K % 512 != 0).
     int w_tile = u0 / ku, w_kb = u0 - (u0 / ku) * ku;
     int w_pi = w_tile / tpp;
     w_tile -= w_pi * tpp;
@@ -396,36 +395,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       return true;
     };
-    // x unit ix -> slot ix % XS as NSUB boxes of [64 K x MT rows] (rows >= M
-    // and columns >= K read as zero), once the MMAs of unit ix - XS are done.
-    auto issue_x = [&](int ix) -> bool {
-      const int xs = ix % C::XS;
-      if (lane == 0) {
-        if (ix >= C::XS) wait(&xfree[xs], ((ix / C::XS) - 1) & 1);
-        if (!*abort_word) {
-          const int k0 = ((u0 + ix) % ku) * UNIT_K;
-          uint8_t* dst = smem + C::OFF_XRING + xs * C::XSLOT_BYTES;
-          mbar_arrive_expect_tx(&xtma[xs], C::XSLOT_BYTES);
-#pragma unroll
-          for (int b = 0; b < NSUB; ++b)
-            tma_load_2d(dst + b * C::XBLK_BYTES, &tm_x, &xtma[xs], k0 + b * GS, 0);
-        }
-      }
-      __syncwarp();
-      return !*abort_word;
-    };
-    constexpr int XD = C::XS - 1;
-    const int pro = n_units < C::NSTAGE ? n_units : C::NSTAGE;
-    bool ok = true;
-    for (int it = 0; ok && it < pro; ++it) ok = issue_w(it);
-    if (!GROUPED) {
-      griddep_wait();
-      for (int ix = 0; ok && ix < XD && ix < n_units; ++ix) ok = issue_x(ix);
-    }
-    for (int i = 0; ok && i < n_units; ++i) {
-      if (!GROUPED && i + XD < n_units) ok = issue_x(i + XD);
-      if (ok && i + C::NSTAGE < n_units) ok = issue_w(i + C::NSTAGE);
-    }
+    for (int it = 0; it < n_units; ++it)
+      if (!issue_w(it)) break;
   } else if (warp < WARP_DQ0) {
     // ------------------------------------------------------------ MMA issuers
     // Warp j issues the MMAs of sub-blocks j, j + 4 into accumulator j.  The
@@ -548,6 +519,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // K order and it is permuted in place here (the permutation stays inside
     // each 16-byte chunk, so the swizzle does not matter).  Grouped: rows are
     // gathered through the route table with plain loads, one unit ahead.
+    // Dense: one thread requests x for unit ix (slot ix % XS) as NSUB boxes
+    // of [64 K x MT rows] (rows >= M and columns >= K read as zero) once the
+    // MMAs of unit ix - XS have released the slot, XD = XS - 1 units ahead
+    // of the permutation.
+    constexpr int XD = C::XS - 1;
+    auto issue_x = [&](int ix) {
+      const int xs = ix % C::XS;
+      if (ix >= C::XS) wait(&xfree[xs], ((ix / C::XS) - 1) & 1);
+      if (!*abort_word) {
+        const int k0 = ((u0 + ix) % ku) * UNIT_K;
+        uint8_t* dst = smem + C::OFF_XRING + xs * C::XSLOT_BYTES;
+        mbar_arrive_expect_tx(&xtma[xs], C::XSLOT_BYTES);
+#pragma unroll
+        for (int b = 0; b < NSUB; ++b)
+          tma_load_2d(dst + b * C::XBLK_BYTES, &tm_x, &xtma[xs], k0 + b * GS, 0);
+      }
+    };
     auto stage_x = [&](int ix) {
       const int xs = ix % C::XS;
       if constexpr (GROUPED) {
@@ -569,12 +557,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(&xfull[xs]);
+      if constexpr (!GROUPED) {
+        if (et == 0 && ix + XD < n_units) issue_x(ix + XD);
+        __syncwarp();
+      }
     };
     int staged = 0;  // units of x staged so far
     griddep_wait();
     if (n_units > 0) {
-      if constexpr (GROUPED)
+      if constexpr (GROUPED) {
         load_x_unit<MT, GROUPED>(p, (u0 % ku) * UNIT_K, u0 / (ku * tpp), et, xr);
+      } else {
+        if (et == 0)
+          for (int ix = 0; ix < XD && ix < n_units; ++ix) issue_x(ix);
+        __syncwarp();
+      }
       for (; staged < n_units && staged < C::XS; ++staged) stage_x(staged);
       const int t_first = u0 / ku;
       const int t_last = (u1 - 1) / ku;

@@ -122,6 +122,12 @@ def test_real_mlp_shapes_reference_harness(pkg, dev, name, M, K, N):
     (1, 64, 8),          # smallest K
     (3, 8192, 136),      # long K, many stream-K segments per tile
     (16, 512, 128 * 300),  # many tiles, one unit per tile (no split)
+    # several units per CTA where every unit (K = 512) or every fifth unit
+    # (K = 2560) starts a new scale/bias chunk: the producer runs far ahead
+    # of the dequant warps and must never wait on the MMAs
+    (16, 512, 128 * 740),
+    (16, 2560, 128 * 160),
+    (32, 512, 128 * 600),
 ])
 def test_edge_shapes(pkg, dev, M, K, N):
     rng = np.random.default_rng(M * 131 + K * 7 + N)
