@@ -185,6 +185,17 @@ __device__ __forceinline__ bool spin_acquire_geq(const int* addr, int target,
   }
 }
 
+// Close the current cp.async group / wait until at most N of this thread's
+// most recent groups are still in flight.
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Wait until all of this thread's prior cp.async copies have landed.
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
@@ -375,6 +386,28 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
 // async-proxy reads (TMA stores, tcgen05.mma operand fetches).
 __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Warp-wide forms: every lane of the warp executes the call (so the operands
+// stay warp-uniform) and one elected lane issues the instruction.
+__device__ __forceinline__ void mma_bf16_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31u) == 0u; }

@@ -62,7 +62,6 @@ constexpr int WARP_EPI0 = WARP_DQ0 + 4 * NDG;          // 4 x-staging + epilogue
 constexpr int NUM_WARPS = WARP_EPI0 + 4;
 constexpr int NUM_THREADS = NUM_WARPS * 32;
 constexpr int TMEM_COLS = 512;
-constexpr int ACC_COL0 = NSUB * A_COLS;  // 256
 constexpr int SUB_PER_MMA = NSUB / NUM_MMA_WARPS;  // sub-blocks per MMA warp per unit
 constexpr int BAR_ID_EPI = 1;            // named barrier of the epilogue warps
 constexpr int SBC = 4;                   // units per scale/bias chunk (32 groups)
@@ -89,10 +88,15 @@ struct Cfg {
   static constexpr int X_PER_THREAD = X_CHUNKS / 128;
   static constexpr int NACC = NUM_MMA_WARPS;
   static constexpr int ACC_COLS = NACC * MT;  // one accumulator buffer
+  // TMEM A slots (one quant group of the dequantised tile each): 1.5 units
+  // when the accumulators leave room, so dequant can run ahead of the MMAs.
+  static constexpr int NASLOT = (MT <= 16) ? 12 : 8;
+  static constexpr int ACC_COL0 = NASLOT * A_COLS;
   static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(XBLK_BYTES % 1024 == 0, "x blocks must keep 1024-byte alignment");
   static_assert(X_CHUNKS % 128 == 0, "x chunks per thread");
   static_assert(ACC_COL0 + 2 * ACC_COLS <= TMEM_COLS, "TMEM budget");
+  static_assert(NASLOT % NDG == 0 && NASLOT % NUM_MMA_WARPS == 0 && NASLOT >= NSUB, "A slots");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -136,21 +140,30 @@ __device__ __forceinline__ int cta_of_unit(int u, int total, int grid) {
 // within-8 permutation (permute_x_chunk), so the MMA still sums x_k * w_k.
 __device__ __forceinline__ void dequant8(uint32_t q, __nv_bfloat162 s2, __nv_bfloat162 b2,
                                          uint32_t* out) {
-  const uint32_t kMagic = 0x43004300u;  // bf16x2 (128, 128); low mantissa bits carry n
-  uint32_t p[4];
-  p[0] = (q & 0x000F000Fu) | kMagic;          // (n0, n4) + 128
-  p[1] = ((q >> 4) & 0x000F000Fu) | kMagic;   // (n1, n5) + 128
-  p[2] = ((q >> 8) & 0x000F000Fu) | kMagic;   // (n2, n6) + 128
-  p[3] = ((q >> 12) & 0x000F000Fu) | kMagic;  // (n3, n7) + 128
-  const __nv_bfloat162 k128 = __halves2bfloat162(__ushort_as_bfloat16(0x4300),
-                                                 __ushort_as_bfloat16(0x4300));
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&p[i]);
-    v = __hsub2(v, k128);            // exact: integer n in bf16
-    v = __hfma2(v, s2, b2);          // n * s + b, one rounding
-    out[i] = *reinterpret_cast<const uint32_t*>(&v);
-  }
+  // Written in PTX so that each step is exactly one instruction: 3 shifts
+  // and 4 LOP3 (mask | exponent bits 0x4300 = 128.0) on the integer pipe,
+  // then per pair an exact bf16x2 FMA (v * 1 - 128 = n) and the scale/bias
+  // FMA with a single rounding.
+  const uint32_t s = *reinterpret_cast<const uint32_t*>(&s2);
+  const uint32_t b = *reinterpret_cast<const uint32_t*>(&b2);
+  asm("{\n\t.reg .b32 h1, h2, h3, t0, t1, t2, t3;\n\t"
+      "shr.b32 h1, %4, 4;\n\t"
+      "shr.b32 h2, %4, 8;\n\t"
+      "shr.b32 h3, %4, 12;\n\t"
+      "lop3.b32 t0, %4, 0x000F000F, 0x43004300, 0xEA;\n\t"
+      "lop3.b32 t1, h1, 0x000F000F, 0x43004300, 0xEA;\n\t"
+      "lop3.b32 t2, h2, 0x000F000F, 0x43004300, 0xEA;\n\t"
+      "lop3.b32 t3, h3, 0x000F000F, 0x43004300, 0xEA;\n\t"
+      "fma.rn.bf16x2 t0, t0, %7, %8;\n\t"
+      "fma.rn.bf16x2 t1, t1, %7, %8;\n\t"
+      "fma.rn.bf16x2 t2, t2, %7, %8;\n\t"
+      "fma.rn.bf16x2 t3, t3, %7, %8;\n\t"
+      "fma.rn.bf16x2 %0, t0, %5, %6;\n\t"
+      "fma.rn.bf16x2 %1, t1, %5, %6;\n\t"
+      "fma.rn.bf16x2 %2, t2, %5, %6;\n\t"
+      "fma.rn.bf16x2 %3, t3, %5, %6;\n\t}"
+      : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
+      : "r"(q), "r"(s), "r"(b), "r"(0x3F803F80u), "r"(0xC300C300u));
 }
 
 // Reorders the 8 bf16 of a 16-byte x chunk from k = 0..7 to the order the
@@ -249,9 +262,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_XRING + C::XS * C::XSLOT_BYTES);
   uint64_t* full = bars;                       // [NSTAGE]  nibbles + scales landed
   uint64_t* empty = full + C::NSTAGE;          // [NSTAGE]  stage read by the dequant warps
-  uint64_t* afull = empty + C::NSTAGE;         // [NSUB]    TMEM A slot written
-  uint64_t* aempty = afull + NSUB;             // [NSUB]    TMEM A slot read by MMA
-  uint64_t* xfull = aempty + NSUB;             // [XS]      x slot staged
+  uint64_t* afull = empty + C::NSTAGE;         // [NASLOT]  TMEM A slot written
+  uint64_t* aempty = afull + C::NASLOT;        // [NASLOT]  TMEM A slot read by MMA
+  uint64_t* xfull = aempty + C::NASLOT;        // [XS]      x slot staged
   uint64_t* xfree = xfull + C::XS;             // [XS]      x slot read by all MMA warps
   uint64_t* xtma = xfree + C::XS;              // [XS]      x slot landed (dense: TMA)
   uint64_t* sbfull = xtma + C::XS;             // [2]       scale/bias chunk landed
@@ -299,7 +312,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&sbfull[i], 1);
       mbar_init(&sbempty[i], 4 * NDG);
     }
-    for (int i = 0; i < NSUB; ++i) {
+    for (int i = 0; i < C::NASLOT; ++i) {
       mbar_init(&afull[i], 4);
       mbar_init(&aempty[i], 1);
     }
@@ -400,9 +413,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp < WARP_DQ0) {
     // ------------------------------------------------------------ MMA issuers
     // Warp j issues the MMAs of sub-blocks j, j + 4 into accumulator j.  The
-    // loop body is only waits and MMAs: everything else is precomputed.
+    // whole warp runs the loop (waits, descriptors stay warp-uniform) and one
+    // elected lane issues each MMA and commit; the loop body is only waits
+    // and MMAs, everything else is precomputed.
     const int j = warp - WARP_MMA0;
-    if (lane == 0) {
+    {
       constexpr uint32_t idesc = make_idesc_bf16(BN, MT);
       const uint64_t ring_desc = make_sw128_desc(smem_u32(smem + C::OFF_XRING));
       constexpr uint64_t kSlotDesc = uint64_t(C::XSLOT_BYTES >> 4);
@@ -419,33 +434,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           wait(&accempty[buf], ((acc_it >> 1) & 1) ^ 1);
         }
         wait(&xfull[xs], (it / C::XS) & 1);
-        const uint32_t d_tmem = tmem_base + ACC_COL0 + buf * C::ACC_COLS + j * MT;
+        const uint32_t d_tmem = tmem_base + C::ACC_COL0 + buf * C::ACC_COLS + j * MT;
         const uint64_t slot_desc = ring_desc + kSlotDesc * xs;
         uint32_t acc0 = seg_start ? 0u : 1u;
 #pragma unroll
         for (int i = 0; i < SUB_PER_MMA; ++i) {
           const int sb = j + i * NUM_MMA_WARPS;
-          wait(&afull[sb], it & 1);
+          const int g = it * NSUB + sb;  // sub-block sequence number -> A slot
+          const int slot = g % C::NASLOT;
+          wait(&afull[slot], (g / C::NASLOT) & 1);
           tc_fence_after();
           if (!*abort_word) {
-            const uint32_t a_tmem = tmem_base + sb * A_COLS;
+            const uint32_t a_tmem = tmem_base + slot * A_COLS;
             const uint64_t bdesc = slot_desc + kBlkDesc * sb;
-            mma_bf16_ts(d_tmem, a_tmem, bdesc, idesc, acc0);
-            mma_bf16_ts(d_tmem, a_tmem + 8, bdesc + 2, idesc, 1u);
-            mma_bf16_ts(d_tmem, a_tmem + 16, bdesc + 4, idesc, 1u);
-            mma_bf16_ts(d_tmem, a_tmem + 24, bdesc + 6, idesc, 1u);
+            mma_bf16_ts_warp(d_tmem, a_tmem, bdesc, idesc, acc0);
+            mma_bf16_ts_warp(d_tmem, a_tmem + 8, bdesc + 2, idesc, 1u);
+            mma_bf16_ts_warp(d_tmem, a_tmem + 16, bdesc + 4, idesc, 1u);
+            mma_bf16_ts_warp(d_tmem, a_tmem + 24, bdesc + 6, idesc, 1u);
           }
           acc0 = 1u;
-          tc_commit(&aempty[sb]);
+          tc_commit_warp(&aempty[slot]);
         }
-        tc_commit(&xfree[xs]);
+        tc_commit_warp(&xfree[xs]);
         if (seg_end) {
-          tc_commit(&accfull[buf]);
+          tc_commit_warp(&accfull[buf]);
           ++acc_it;
         }
       }
     }
-    __syncwarp();
   } else if (warp < WARP_EPI0) {
     // ------------------------------------------------------------ dequant
     const int dw = warp - WARP_DQ0;
@@ -474,17 +490,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint4 bv = ld_shared_v4(sbc + C::SBC_HALF);
       const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
       const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+      // This warp's packed words of the unit (its sub-blocks grp, grp + 4)
+      // go to registers at once, so the stage is released before any
+      // dequant work and the producer can refill it while this unit is
+      // still being converted.
+      constexpr int SPW = NSUB / NDG;  // sub-blocks per dequant warp per unit
+      static_assert(NSUB % NDG == 0, "sub-blocks per dequant warp");
+      uint4 qv[SPW][2];
 #pragma unroll
-      for (int jj = 0; jj < (NSUB + NDG - 1) / NDG; ++jj) {
+      for (int jj = 0; jj < SPW; ++jj) {
         const int sb = NDG * jj + grp;
-        if (sb >= NSUB) break;
-        wait(&aempty[sb], (it & 1) ^ 1);
-        tc_fence_after();
-        const int box = sb >> 2;
         const int c0 = 2 * (sb & 3);
-        const uint32_t rowb = st + box * (C::PACK_BYTES / 2) + r * 128;
-        const uint4 q0 = ld_shared_v4(rowb + (uint32_t((c0 ^ (r & 7))) << 4));
-        const uint4 q1 = ld_shared_v4(rowb + (uint32_t(((c0 + 1) ^ (r & 7))) << 4));
+        const uint32_t rowb = st + (sb >> 2) * (C::PACK_BYTES / 2) + r * 128;
+        qv[jj][0] = ld_shared_v4(rowb + (uint32_t((c0 ^ (r & 7))) << 4));
+        qv[jj][1] = ld_shared_v4(rowb + (uint32_t(((c0 + 1) ^ (r & 7))) << 4));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+      for (int jj = 0; jj < SPW; ++jj) {
+        const int sb = NDG * jj + grp;
+        const int g = it * NSUB + sb;  // sub-block sequence number -> A slot
+        const int slot = g % C::NASLOT;
+        wait(&aempty[slot], ((g / C::NASLOT) & 1) ^ 1);
+        tc_fence_after();
+        const uint4 q0 = qv[jj][0];
+        const uint4 q1 = qv[jj][1];
         // group sb lives in scale word sb / 2, half sb % 2
         const __nv_bfloat162 sc = splat_bf16(pick4(sw, sb >> 1), sb & 1);
         const __nv_bfloat162 bc = splat_bf16(pick4(bw, sb >> 1), sb & 1);
@@ -497,14 +528,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         dequant8(q1.y, sc, bc, &w[20]);
         dequant8(q1.z, sc, bc, &w[24]);
         dequant8(q1.w, sc, bc, &w[28]);
-        tmem_st_32x32b_x32(lane_base + sb * A_COLS, w);
+        tmem_st_32x32b_x32(lane_base + slot * A_COLS, w);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[sb]);
+        if (lane == 0) mbar_arrive(&afull[slot]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
     }
   } else {
     // ------------------------------------------------- x staging + epilogue
@@ -590,7 +619,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!named_bar_and(BAR_ID_EPI, 128, wait(&accfull[buf], (acc_it >> 1) & 1))) break;
         tc_fence_after();
         float acc[MT];
-        epilogue_load<MT, C::NACC>(lane_base + ACC_COL0 + buf * C::ACC_COLS, acc);
+        epilogue_load<MT, C::NACC>(lane_base + C::ACC_COL0 + buf * C::ACC_COLS, acc);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&accempty[buf]);
