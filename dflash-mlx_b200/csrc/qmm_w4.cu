@@ -138,14 +138,11 @@ __device__ __forceinline__ int cta_of_unit(int u, int total, int grid) {
 // K order (0,4), (1,5), (2,6), (3,7): each is one shift + one LOP3 (mask and
 // exponent bits), with no byte permutes.  The x operand gets the same
 // within-8 permutation (permute_x_chunk), so the MMA still sums x_k * w_k.
-__device__ __forceinline__ void dequant8(uint32_t q, __nv_bfloat162 s2, __nv_bfloat162 b2,
-                                         uint32_t* out) {
+__device__ __forceinline__ void dequant8(uint32_t q, uint32_t s, uint32_t b, uint32_t* out) {
   // Written in PTX so that each step is exactly one instruction: 3 shifts
   // and 4 LOP3 (mask | exponent bits 0x4300 = 128.0) on the integer pipe,
   // then per pair an exact bf16x2 FMA (v * 1 - 128 = n) and the scale/bias
   // FMA with a single rounding.
-  const uint32_t s = *reinterpret_cast<const uint32_t*>(&s2);
-  const uint32_t b = *reinterpret_cast<const uint32_t*>(&b2);
   asm("{\n\t.reg .b32 h1, h2, h3, t0, t1, t2, t3;\n\t"
       "shr.b32 h1, %4, 4;\n\t"
       "shr.b32 h2, %4, 8;\n\t"
@@ -175,16 +172,6 @@ __device__ __forceinline__ uint4 permute_x_chunk(uint4 v) {
   r.z = __byte_perm(v.y, v.w, 0x5410);  // (x2, x6)
   r.w = __byte_perm(v.y, v.w, 0x7632);  // (x3, x7)
   return r;
-}
-
-__device__ __forceinline__ uint32_t pick4(const uint32_t (&v)[4], int i) {
-  return i == 0 ? v[0] : i == 1 ? v[1] : i == 2 ? v[2] : v[3];
-}
-
-__device__ __forceinline__ __nv_bfloat162 splat_bf16(uint32_t word, int half) {
-  const uint16_t h = half ? uint16_t(word >> 16) : uint16_t(word & 0xFFFFu);
-  const __nv_bfloat16 v = __ushort_as_bfloat16(h);
-  return __halves2bfloat162(v, v);
 }
 
 // Sum the NACC accumulators of one buffer (accumulator a at columns
@@ -469,6 +456,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int quad = warp & 3;            // TMEM lane quadrant of this warp
     const int r = quad * 32 + lane;       // output channel within the tile
     const uint32_t lane_base = tmem_base + (uint32_t(quad * 32) << 16);
+    const uint32_t half_sel = (grp & 1) ? 0x3232u : 0x1010u;  // bf16 half -> both halves
     int kb = u0 % ku;
     int chunk = -1;
     for (int it = 0; it < n_units; ++it, kb = (kb + 1 == ku) ? 0 : kb + 1) {
@@ -484,18 +472,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t ph = (it / C::NSTAGE) & 1;
       wait(&full[s], ph);
       const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
+      // This warp's sub-blocks of the unit are grp and grp + 4 (quant groups
+      // of the same numbers); their scales/biases are halves (grp & 1) of
+      // words grp / 2 and grp / 2 + 2 of the unit's 16-byte scale row.
       const uint32_t sbc = smem_u32(smem + C::OFF_SB + (chunk & 1) * C::SBC_BYTES) +
-                           sw64_offset(r, kb % SBC);
-      const uint4 sv = ld_shared_v4(sbc);
-      const uint4 bv = ld_shared_v4(sbc + C::SBC_HALF);
-      const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
-      const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-      // This warp's packed words of the unit (its sub-blocks grp, grp + 4)
-      // go to registers at once, so the stage is released before any
-      // dequant work and the producer can refill it while this unit is
-      // still being converted.
+                           sw64_offset(r, kb % SBC) + (grp >> 1) * 4;
+      const uint32_t s_w0 = ld_shared_u32(sbc), s_w1 = ld_shared_u32(sbc + 8);
+      const uint32_t b_w0 = ld_shared_u32(sbc + C::SBC_HALF), b_w1 = ld_shared_u32(sbc + C::SBC_HALF + 8);
+      // This warp's packed words of the unit go to registers at once, so the
+      // stage is released before any dequant work and the producer can
+      // refill it while this unit is still being converted.
       constexpr int SPW = NSUB / NDG;  // sub-blocks per dequant warp per unit
-      static_assert(NSUB % NDG == 0, "sub-blocks per dequant warp");
+      static_assert(NSUB % NDG == 0 && SPW == 2, "two sub-blocks per dequant warp");
       uint4 qv[SPW][2];
 #pragma unroll
       for (int jj = 0; jj < SPW; ++jj) {
@@ -507,32 +495,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
+      // Both sub-blocks are converted and stored before one wait for the
+      // stores, so the second conversion overlaps the first store.
+      int slots[SPW];
 #pragma unroll
       for (int jj = 0; jj < SPW; ++jj) {
         const int sb = NDG * jj + grp;
         const int g = it * NSUB + sb;  // sub-block sequence number -> A slot
         const int slot = g % C::NASLOT;
+        slots[jj] = slot;
         wait(&aempty[slot], ((g / C::NASLOT) & 1) ^ 1);
         tc_fence_after();
         const uint4 q0 = qv[jj][0];
         const uint4 q1 = qv[jj][1];
-        // group sb lives in scale word sb / 2, half sb % 2
-        const __nv_bfloat162 sc = splat_bf16(pick4(sw, sb >> 1), sb & 1);
-        const __nv_bfloat162 bc = splat_bf16(pick4(bw, sb >> 1), sb & 1);
+        const uint32_t s2 = __byte_perm(jj ? s_w1 : s_w0, 0, half_sel);
+        const uint32_t b2 = __byte_perm(jj ? b_w1 : b_w0, 0, half_sel);
         uint32_t w[32];
-        dequant8(q0.x, sc, bc, &w[0]);
-        dequant8(q0.y, sc, bc, &w[4]);
-        dequant8(q0.z, sc, bc, &w[8]);
-        dequant8(q0.w, sc, bc, &w[12]);
-        dequant8(q1.x, sc, bc, &w[16]);
-        dequant8(q1.y, sc, bc, &w[20]);
-        dequant8(q1.z, sc, bc, &w[24]);
-        dequant8(q1.w, sc, bc, &w[28]);
+        dequant8(q0.x, s2, b2, &w[0]);
+        dequant8(q0.y, s2, b2, &w[4]);
+        dequant8(q0.z, s2, b2, &w[8]);
+        dequant8(q0.w, s2, b2, &w[12]);
+        dequant8(q1.x, s2, b2, &w[16]);
+        dequant8(q1.y, s2, b2, &w[20]);
+        dequant8(q1.z, s2, b2, &w[24]);
+        dequant8(q1.w, s2, b2, &w[28]);
         tmem_st_32x32b_x32(lane_base + slot * A_COLS, w);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[slot]);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+#pragma unroll
+        for (int jj = 0; jj < SPW; ++jj) mbar_arrive(&afull[slots[jj]]);
       }
     }
   } else {
