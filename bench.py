@@ -3,7 +3,8 @@
 One step = one synthetic verify cycle per request (BASELINE configs 1 + 3 + 4):
 the 64-layer int4 g64 verify projection stack at M = 16 tokens per request
 (hidden 5120: q 5120->6144, k/v 5120->1024, o 6144->5120, gate/up
-5120->17408, down 17408->5120), the lm_head (248320 x 5120 bf16) argmax +
+5120->17408, down 17408->5120; same-input projections stored concatenated and
+run as one launch each: q|k|v, o, gate|up, down), the lm_head (248320 x 5120 bf16) argmax +
 greedy acceptance of 16 verify ids, and the GatedDeltaNet tape-replay
 rollback of 48 layers (48 heads, 128 x 128 fp32 state) with the accepted
 step counts.  Requests are data-parallel across GPUs (weak scaling:
@@ -266,7 +267,7 @@ def run_ours(args):
 
     # roofline of the dominant kernel (the int4 verify qmm)
     peak, peak_kind = _peaks()
-    launches = 7 * sh.layers * b
+    launches = len(sh.launches()) * sh.layers * b
     bytes_per_step = sh.qmm_bytes_per_request() * b
     achieved = bytes_per_step / (t_qmm / args.steps) / 1e9
     traffic, _ = _traffic_per_launch()
@@ -297,10 +298,11 @@ def run_ours(args):
                          "frac": achieved / peak, "traffic": traffic,
                          "kernel": "qmm_w4g64 (int4 verify qmm, M=16)",
                          "peak_source": peak_kind,
-                         "note": "achieved = algorithmic bytes of the 448 qmm launches of a step / "
-                                 "their CUDA-event time inside the timed region"},
-            # ours per step: 448 qmm + 64 SiLU*up per request, lm_head argmax, accept,
-            # one tape replay per GDN layer
+                         "note": "achieved = algorithmic bytes of the qmm launches of a step (4 per "
+                                 "layer: q|k|v, o, gate|up, down) / their CUDA-event time inside "
+                                 "the timed region"},
+            # ours per step: 4 qmm + 1 SiLU*up per layer and request, lm_head argmax,
+            # accept, one tape replay per GDN layer
             "gpu_launches": args.steps * (launches + sh.layers * b + 2 + sh.gdn_layers),
             "e2e": {"value": world * b / t_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},

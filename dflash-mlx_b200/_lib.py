@@ -51,6 +51,7 @@ SIGNATURES = {
                                    _c_int, _vp, _c_size, _vp]),
     "dfl_moe_qmm_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
     "dfl_silu_mul_bf16": (_c_int, [_vp, _vp, _vp, _c_int, _vp]),
+    "dfl_silu_mul_rows_bf16": (_c_int, [_vp, _vp, _c_int, _vp, _c_int, _c_int, _vp]),
     "dfl_moe_combine": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
 }
 

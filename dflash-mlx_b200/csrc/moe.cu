@@ -100,6 +100,20 @@ __global__ void silu_mul_kernel(const uint16_t* gate, const uint16_t* up, uint16
   out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(s * u));
 }
 
+// Same on row-strided inputs: out[r, c] (contiguous) from gate/up rows of
+// stride ld, e.g. the two halves of a fused gate|up projection output.
+__global__ void silu_mul_rows_kernel(const uint16_t* gate, const uint16_t* up, int ld, uint16_t* out,
+                                     int rows, int cols) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * cols) return;
+  const int r = i / cols, c = i - r * cols;
+  const size_t j = (size_t)r * ld + c;
+  const float g = __bfloat162float(__ushort_as_bfloat16(gate[j]));
+  const float u = __bfloat162float(__ushort_as_bfloat16(up[j]));
+  const float s = g / (1.0f + expf(-g));
+  out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(s * u));
+}
+
 // y[t, c] = bf16( sum_j w[t, j] * pair_out[t * k + j, c]  (+ shared[t, c]) ), fp32 in slot order
 __global__ void combine_kernel(const uint16_t* pair_out, const float* weights, const uint16_t* shared,
                                uint16_t* y, int T, int k, int H) {
@@ -144,6 +158,19 @@ extern "C" int dfl_silu_mul_bf16(const uint16_t* gate, const uint16_t* up, uint1
   if (!gate || !up || !out) return DFL_ERR_NULL_POINTER;
   moe::silu_mul_kernel<<<(n + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       gate, up, out, n);
+  return host::launch_status();
+}
+
+extern "C" int dfl_silu_mul_rows_bf16(const uint16_t* gate, const uint16_t* up, int ld,
+                                      uint16_t* out, int rows, int cols, void* stream) {
+  using namespace dfl;
+  if (rows < 0 || cols < 0 || ld < cols) return DFL_ERR_BAD_SHAPE;
+  if ((long long)rows * cols > 0x7fffffffLL) return DFL_ERR_BAD_SHAPE;
+  if (rows == 0 || cols == 0) return DFL_OK;
+  if (!gate || !up || !out) return DFL_ERR_NULL_POINTER;
+  const int n = rows * cols;
+  moe::silu_mul_rows_kernel<<<(n + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      gate, up, ld, out, rows, cols);
   return host::launch_status();
 }
 

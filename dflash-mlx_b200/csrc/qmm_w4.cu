@@ -538,25 +538,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t ring = smem_u32(smem + C::OFF_XRING);
     uint4 xr[GROUPED ? C::X_PER_THREAD : 1];
     // x for unit `ix` goes into slot ix % XS once the MMAs of unit ix - XS
-    // have read that slot.  Dense: the producer's TMA brought it in natural
-    // K order and it is permuted in place here (the permutation stays inside
-    // each 16-byte chunk, so the swizzle does not matter).  Grouped: rows are
-    // gathered through the route table with plain loads, one unit ahead.
-    // Dense: one thread requests x for unit ix (slot ix % XS) as NSUB boxes
-    // of [64 K x MT rows] (rows >= M and columns >= K read as zero) once the
-    // MMAs of unit ix - XS have released the slot, XD = XS - 1 units ahead
-    // of the permutation.
+    // have read that slot, XD = XS - 1 units ahead of its permutation, in
+    // the UMMA K-major 128-byte-swizzled layout (rows >= M and columns >= K
+    // zero).  Dense x arrives in natural K order and each 16-byte chunk is
+    // permuted in place (the K permutation stays inside a chunk):
+    //   * M <= 16 (X_CP): every thread copies its own chunks with cp.async,
+    //     one commit group per unit; these go through L1/L2 and do not queue
+    //     behind the weight boxes the producer keeps in the TMA unit;
+    //   * M <= 32: one thread requests NSUB TMA boxes of [64 K x MT rows]
+    //     (twice the bytes; per-thread copies would cost more issue slots).
+    // Grouped: rows are gathered through the route table with plain loads,
+    // one unit ahead.
     constexpr int XD = C::XS - 1;
-    auto issue_x = [&](int ix) {
+    constexpr bool X_CP = (MT <= 16);
+    auto x_chunk = [&](int t, int& b, int& rr, int& c) {
+      const int idx = et + 128 * t;
+      c = idx & 7;
+      rr = (idx >> 3) % MT;
+      b = idx / (MT * 8);
+    };
+    auto issue_x = [&](int ix) {  // X_CP: all x threads; else one thread
       const int xs = ix % C::XS;
       if (ix >= C::XS) wait(&xfree[xs], ((ix / C::XS) - 1) & 1);
-      if (!*abort_word) {
-        const int k0 = ((u0 + ix) % ku) * UNIT_K;
-        uint8_t* dst = smem + C::OFF_XRING + xs * C::XSLOT_BYTES;
-        mbar_arrive_expect_tx(&xtma[xs], C::XSLOT_BYTES);
+      const int k0 = ((u0 + ix) % ku) * UNIT_K;
+      if constexpr (X_CP) {
+        const uint32_t slot = ring + xs * C::XSLOT_BYTES;
 #pragma unroll
-        for (int b = 0; b < NSUB; ++b)
-          tma_load_2d(dst + b * C::XBLK_BYTES, &tm_x, &xtma[xs], k0 + b * GS, 0);
+        for (int t = 0; t < C::X_PER_THREAD; ++t) {
+          int b, rr, c;
+          x_chunk(t, b, rr, c);
+          const int k = k0 + b * GS + c * 8;
+          const bool in = rr < p.M && k < p.K;
+          cp_async_16(slot + b * C::XBLK_BYTES + rr * 128 + (uint32_t((c ^ (rr & 7))) << 4),
+                      in ? p.x + (size_t)rr * p.K + k : p.x, in ? 16u : 0u);
+        }
+        cp_async_commit();
+      } else {
+        if (!*abort_word) {
+          uint8_t* dst = smem + C::OFF_XRING + xs * C::XSLOT_BYTES;
+          mbar_arrive_expect_tx(&xtma[xs], C::XSLOT_BYTES);
+#pragma unroll
+          for (int b = 0; b < NSUB; ++b)
+            tma_load_2d(dst + b * C::XBLK_BYTES, &tm_x, &xtma[xs], k0 + b * GS, 0);
+        }
       }
     };
     auto stage_x = [&](int ix) {
@@ -569,19 +593,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           load_x_unit<MT, GROUPED>(p, (un % ku) * UNIT_K, un / (ku * tpp), et, xr);
         }
       } else {
-        wait(&xtma[xs], (ix / C::XS) & 1);
         const uint32_t slot = ring + xs * C::XSLOT_BYTES;
+        if constexpr (X_CP) {
+          // groups committed so far: units 0 .. min(ix + XD, n) - 1
+          if (ix + XD <= n_units)
+            cp_async_wait_group<XD - 1>();
+          else
+            cp_async_wait_all();
 #pragma unroll
-        for (int t = 0; t < C::X_PER_THREAD; ++t) {
-          const uint32_t a = slot + uint32_t(et + 128 * t) * 16u;
-          st_shared_v4(a, permute_x_chunk(ld_shared_v4(a)));
+          for (int t = 0; t < C::X_PER_THREAD; ++t) {
+            int b, rr, c;
+            x_chunk(t, b, rr, c);
+            const uint32_t a = slot + b * C::XBLK_BYTES + rr * 128 + (uint32_t((c ^ (rr & 7))) << 4);
+            st_shared_v4(a, permute_x_chunk(ld_shared_v4(a)));
+          }
+        } else {
+          wait(&xtma[xs], (ix / C::XS) & 1);
+#pragma unroll
+          for (int t = 0; t < C::X_PER_THREAD; ++t) {
+            const uint32_t a = slot + uint32_t(et + 128 * t) * 16u;
+            st_shared_v4(a, permute_x_chunk(ld_shared_v4(a)));
+          }
         }
       }
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(&xfull[xs]);
       if constexpr (!GROUPED) {
-        if (et == 0 && ix + XD < n_units) issue_x(ix + XD);
+        if (ix + XD < n_units) {
+          if (X_CP || et == 0) issue_x(ix + XD);
+        }
         __syncwarp();
       }
     };
@@ -591,7 +632,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if constexpr (GROUPED) {
         load_x_unit<MT, GROUPED>(p, (u0 % ku) * UNIT_K, u0 / (ku * tpp), et, xr);
       } else {
-        if (et == 0)
+        if (X_CP || et == 0)
           for (int ix = 0; ix < XD && ix < n_units; ++ix) issue_x(ix);
         __syncwarp();
       }

@@ -91,6 +91,21 @@ def gather_qmm(x: torch.Tensor, weight: QuantWeight, table: torch.Tensor, *, row
 
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """``bf16(silu(gate) * up)`` (fp32 math).  2-D ``gate``/``up`` may be
+    row-strided views with the same row stride (e.g. the two halves of a
+    fused gate|up projection output); the result is contiguous."""
+    if gate.shape != up.shape:
+        raise ValueError(f"gate {tuple(gate.shape)} and up {tuple(up.shape)} differ")
+    if (gate.dim() == 2 and gate.stride() == up.stride() and gate.stride(1) == 1
+            and not (gate.is_contiguous() and up.is_contiguous())):
+        rows, cols = gate.shape
+        out = torch.empty((rows, cols), dtype=gate.dtype, device=gate.device)
+        with torch.cuda.device(gate.device):
+            st = _lib.load().dfl_silu_mul_rows_bf16(gate.data_ptr(), up.data_ptr(), gate.stride(0),
+                                                    out.data_ptr(), rows, cols, stream_ptr(gate.device))
+        _lib.check("dfl_silu_mul_rows_bf16", st)
+        return out
+    gate = gate.contiguous()
     out = torch.empty_like(gate)
     with torch.cuda.device(gate.device):
         st = _lib.load().dfl_silu_mul_bf16(gate.data_ptr(), up.contiguous().data_ptr(), out.data_ptr(),

@@ -6,7 +6,9 @@ for ``requests`` independent requests of 16 verify tokens on this GPU:
 
 1. the int4 g64 verify projections of every decoder layer at M = 16 per
    request (q, k, v, o, gate, up, down; ``verify_linear.py`` ->
-   ``verify_qmm.py``), with SiLU * up feeding down;
+   ``verify_qmm.py``), with SiLU * up feeding down.  Projections that read
+   the same input are stored concatenated (q|k|v, gate|up) and run as one
+   launch each, 4 launches per layer;
 2. the lm_head argmax + greedy acceptance epilogue (``spec_epoch.py:2067-2072``)
    on a vocabulary shard, keys all-gathered across ranks when the vocabulary
    is split;
@@ -55,11 +57,19 @@ class StackShape:
                 ("o", h, self.q_out), ("gate", self.inter, h), ("up", self.inter, h),
                 ("down", h, self.inter)]
 
+    def launches(self):
+        """(name, N, K) of the qmm launches of one layer.  Projections that
+        read the same input are stored concatenated along N, as fused-
+        projection checkpoints do (q|k|v, gate|up), and run as one launch."""
+        h = self.hidden
+        return [("qkv", self.q_out + 2 * self.kv_out, h), ("o", h, self.q_out),
+                ("gate_up", 2 * self.inter, h), ("down", h, self.inter)]
+
     def qmm_bytes_per_request(self) -> int:
         """Algorithmic bytes of one request's projection stack: packed weights +
-        bf16 scales and biases + bf16 activations in and out."""
+        bf16 scales and biases + bf16 activations in and out, per launch."""
         total = 0
-        for _, n, k in self.projections():
+        for _, n, k in self.launches():
             total += n * k // 2 + 2 * 2 * n * (k // 64) + 2 * self.block * (k + n)
         return total * self.layers
 
@@ -86,8 +96,9 @@ class VerifyStep:
         self.rank, self.world, self.group = rank, world, group
         sh = self.shape
         gen = torch.Generator(device=self.dev).manual_seed(seed)
-        # replicated decoder weights (identical on every rank: same seed)
-        self.layers = [{name: _quant_weight(gen, self.dev, n, k) for name, n, k in sh.projections()}
+        # replicated decoder weights (identical on every rank: same seed), in
+        # the fused launch layout (q|k|v and gate|up concatenated along N)
+        self.layers = [{name: _quant_weight(gen, self.dev, n, k) for name, n, k in sh.launches()}
                        for _ in range(sh.layers)]
         # this rank's vocabulary shard of the bf16 lm_head, N(0, 0.02)
         self.v_begin, v_len = _lm.vocab_shard(sh.vocab, rank, world)
@@ -104,6 +115,10 @@ class VerifyStep:
             torch.randn((sh.gdn_layers, b, t, hv), generator=sgen, device=self.dev)))
         # step inputs / outputs (static buffers for graph replay)
         self.x = torch.empty((b * sh.block, sh.hidden), dtype=torch.bfloat16, device=self.dev)
+        # stand-in for the attention output feeding o_proj (produced outside
+        # the verify hot path; fixed random rows)
+        self.attn_out = (torch.randn((b * sh.block, sh.q_out), generator=sgen, device=self.dev)
+                         * 0.5).to(torch.bfloat16)
         self.verify_ids = torch.zeros((b, sh.block), dtype=torch.int32, device=self.dev)
         self.stream = torch.cuda.Stream(self.dev)
         self.graphs = None
@@ -114,14 +129,13 @@ class VerifyStep:
         sh = self.shape
         for r in range(self.requests):
             x = self.x[r * sh.block:(r + 1) * sh.block]
+            a = self.attn_out[r * sh.block:(r + 1) * sh.block]
             for lw in self.layers:
-                q = qmm_w4g64(x, lw["q"].q, lw["q"].s, lw["q"].b)
-                qmm_w4g64(x, lw["k"].q, lw["k"].s, lw["k"].b)
-                qmm_w4g64(x, lw["v"].q, lw["v"].s, lw["v"].b)
-                qmm_w4g64(q, lw["o"].q, lw["o"].s, lw["o"].b)
-                g = qmm_w4g64(x, lw["gate"].q, lw["gate"].s, lw["gate"].b)
-                u = qmm_w4g64(x, lw["up"].q, lw["up"].s, lw["up"].b)
-                self.last_down = qmm_w4g64(silu_mul(g, u), lw["down"].q, lw["down"].s, lw["down"].b)
+                self.last_qkv = qmm_w4g64(x, lw["qkv"].q, lw["qkv"].s, lw["qkv"].b)
+                qmm_w4g64(a, lw["o"].q, lw["o"].s, lw["o"].b)
+                gu = qmm_w4g64(x, lw["gate_up"].q, lw["gate_up"].s, lw["gate_up"].b)
+                h = silu_mul(gu[:, :sh.inter], gu[:, sh.inter:])
+                self.last_down = qmm_w4g64(h, lw["down"].q, lw["down"].s, lw["down"].b)
 
     def _keys(self, hidden_all):
         self.keys = _lm.lm_head_argmax_keys(hidden_all, self.lm_w, v_begin=self.v_begin)

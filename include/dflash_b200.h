@@ -196,6 +196,13 @@ int dfl_moe_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t* sc
 size_t dfl_moe_qmm_workspace_bytes(int max_problems, int K, int N, int* status);
 int dfl_silu_mul_bf16(const uint16_t* gate, const uint16_t* up, uint16_t* out, int n,
                       void* stream);
+
+/* dfl_silu_mul_rows_bf16: out[r, c] = bf16(silu(gate[r * ld + c]) * up[r * ld + c])
+ * for r < rows, c < cols (out contiguous [rows, cols], ld >= cols): the SiLU
+ * gate of a fused gate|up projection output read in place.  Same math as
+ * dfl_silu_mul_bf16 (mlx-lm SwitchGLU / dense MLP activation). */
+int dfl_silu_mul_rows_bf16(const uint16_t* gate, const uint16_t* up, int ld, uint16_t* out,
+                           int rows, int cols, void* stream);
 int dfl_moe_combine(const uint16_t* pair_out, const float* weights, const uint16_t* shared,
                     uint16_t* y, int T, int top_k, int H, void* stream);
 
