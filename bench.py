@@ -44,8 +44,9 @@ def _peaks():
 
 
 def _traffic_per_launch():
-    """DRAM bytes per qmm launch from the committed ncu summary, if present."""
-    f = ROOT / "profiles" / "qmm_w4g64_gate_16x5120x17408.md"
+    """DRAM bytes per qmm launch (mean over the four launch kinds of a layer)
+    from the committed ncu summary, if present."""
+    f = ROOT / "profiles" / "qmm_w4g64_verify_layer_launches.md"
     try:
         for line in f.read_text().splitlines():
             if line.startswith("dram_bytes_per_launch:"):
@@ -200,7 +201,11 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
         group = dist.group.WORLD
 
-    step = VerifyStep(dev, requests=args.requests_per_gpu, rank=rank, world=world, group=group)
+    from dflash_mlx_b200.verify_step import StackShape
+
+    shape = StackShape(layers=args.layers)
+    step = VerifyStep(dev, requests=args.requests_per_gpu, shape=shape, rank=rank, world=world,
+                      group=group)
     sh = step.shape
     b = args.requests_per_gpu
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -285,9 +290,9 @@ def run_ours(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random weights with BASELINE distributions; no checkpoints offline)",
             "config": {
-                "workload": "verify step = config1 (64-layer int4 g64 qmm stack, hidden 5120, M=16 per "
-                            "request) + config3 (lm_head 248320x5120 bf16, vocab split over ranks) + "
-                            "config4 (48-layer GDN tape-replay rollback)",
+                "workload": f"verify step = config1 ({sh.layers}-layer int4 g64 qmm stack, hidden 5120, "
+                            "M=16 per request) + config3 (lm_head 248320x5120 bf16, vocab split over "
+                            "ranks) + config4 (48-layer GDN tape-replay rollback)",
                 "requests_per_gpu": b, "tokens_per_request": sh.block,
                 "parallelism": f"request-DP x{world}, lm_head vocab split x{world}",
                 "l2": "inputs larger than L2 (12.3 GB of packed weights per step)",
@@ -325,6 +330,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--requests-per-gpu", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=64,
+                    help="decoder layers of the qmm stack (64 = the benchmark; fewer only for "
+                         "profiling small cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -12,7 +12,7 @@
  *                             VerifyQuantizedLinear.__call__ dflash_mlx/verify_linear.py:115-116,266-286
  *                             (stock mx.quantized_matmul(transpose=True) for other M)
  *   dfl_gdn_tape_replay    <- tape_replay_kernel       dflash_mlx/kernels.py:822-868
- *   dfl_lmhead_argmax_partial + dfl_lmhead_accept
+ *   dfl_lmhead_argmax + dfl_lmhead_accept
  *                          <- logits_from_hidden       dflash_mlx/engine/target_qwen_gdn.py:774-778
  *                             greedy_tokens_with_mask  dflash_mlx/engine/sampling.py:47-55
  *                             match_acceptance_length  dflash_mlx/engine/acceptance.py:9-16
