@@ -16,7 +16,13 @@ its C ABI (``include/dflash_b200.h``); there is no CPU fallback.
 from . import kernels, lm_head, moe
 from .lm_head import lm_head_argmax_keys, lm_head_verify, match_acceptance_length, verify_accept
 from .kernels import tape_replay_kernel, tape_replay_
-from .recurrent_rollback_cache import RecurrentRollbackCache, restore_after_acceptance
+from .recurrent_rollback_cache import (
+    RecurrentRollbackCache,
+    arm_rollback,
+    cleanup_generation_caches,
+    clear_rollback_state,
+    restore_after_acceptance,
+)
 from .verify_qmm import is_enabled, verify_matmul, qmm_w4g64
 from .verify_linear import (
     QuantizedLinear,

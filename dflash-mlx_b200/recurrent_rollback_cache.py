@@ -20,6 +20,8 @@ not touched by the kernel.
 
 from __future__ import annotations
 
+import time
+
 from typing import Any, Optional, Sequence, Union
 
 import torch
@@ -109,25 +111,62 @@ class RecurrentRollbackCache:
         self.clear_transients()
 
 
+def arm_rollback(cache_entries, *, prefix_len: int) -> None:
+    """``target_qwen_gdn.py:1003-1006``: arm every entry that supports rollback."""
+    for entry in cache_entries:
+        if hasattr(entry, "arm_rollback"):
+            entry.arm_rollback(prefix_len=int(prefix_len))
+
+
+def clear_rollback_state(entry) -> None:
+    """``target_qwen_gdn.py:1008-1023``: drop an entry's tape and snapshot."""
+    if hasattr(entry, "clear_transients"):
+        entry.clear_transients()
+        return
+    for name in ("_tape", "_tape_k", "_tape_g", "_tape_qkv", "_snapshot"):
+        if hasattr(entry, name):
+            setattr(entry, name, None)
+    if hasattr(entry, "_armed"):
+        entry._armed = False
+
+
 def restore_after_acceptance(cache_entries, *, target_len: int, acceptance_length: int,
-                             drafted_tokens: int = 0) -> None:
-    """``target_qwen_gdn.py:1025-1055`` for the recurrent entries: full
-    acceptance clears the transients without replaying; otherwise roll back.
-    Attention caches (``trim`` / ``offset`` / ``crop``) are handled as there."""
+                             drafted_tokens: int = 0) -> int:
+    """``target_qwen_gdn.py:1025-1055``: full acceptance clears the recurrent
+    entries' transients without replaying; otherwise they roll back to
+    ``acceptance_length`` accepted drafts.  Attention caches (``trim`` /
+    ``offset`` / ``crop``) are cut back to ``target_len``.  Returns the host
+    time spent in rollback and trim calls, in ns (the replays themselves are
+    asynchronous GPU work)."""
+    replay_ns = 0
     fully_accepted = acceptance_length == drafted_tokens
     for entry in cache_entries:
         if hasattr(entry, "rollback"):
             if fully_accepted:
-                entry.clear_transients()
+                clear_rollback_state(entry)
                 continue
+            t0 = time.perf_counter_ns()
             entry.rollback(acceptance_length)
+            replay_ns += time.perf_counter_ns() - t0
         elif hasattr(entry, "trim"):
             offset = int(getattr(entry, "offset", 0) or 0)
             if offset > target_len:
+                t0 = time.perf_counter_ns()
                 entry.trim(offset - target_len)
+                replay_ns += time.perf_counter_ns() - t0
         elif hasattr(entry, "offset"):
             offset = int(getattr(entry, "offset", 0) or 0)
             if offset > target_len:
                 entry.offset = target_len
         elif hasattr(entry, "crop"):
             entry.crop(target_len)
+    return replay_ns
+
+
+def cleanup_generation_caches(target_cache: list, draft_cache: list) -> None:
+    """``target_qwen_gdn.py:1057-1066``: drop transients, empty both lists."""
+    for entry in target_cache:
+        if hasattr(entry, "clear_transients"):
+            entry.clear_transients()
+    draft_cache.clear()
+    target_cache.clear()

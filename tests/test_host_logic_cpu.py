@@ -1,0 +1,215 @@
+"""Host-side logic on CPU, checked against the reference's own test data.
+
+* ``tests/golden/reference_cases.json`` (read from the dflash-mlx test sources
+  by ``tests/golden/make_golden.py``): the acceptance table, the qmm parity
+  harness's shapes and random-shape rule, the verify-linear eligibility shapes;
+* rollback control (``engine/target_qwen_gdn.py:1003-1066``) with the fake
+  cache entries of ``tests/test_engine_rollback.py``;
+* verify-linear eligibility and installation (``verify_linear.py:54-87,
+  338-361``) on CPU-held modules (no kernel runs).
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+from torch import nn
+
+import __graft_entry__
+from oracle import lmhead as olm
+
+GOLDEN = json.loads((Path(__file__).resolve().parent / "golden" / "reference_cases.json").read_text())
+
+
+@pytest.fixture(scope="module")
+def pkg():
+    return __graft_entry__.load_package()
+
+
+# ------------------------------------------------------------ golden data
+@pytest.mark.parametrize("case", GOLDEN["acceptance_cases"])
+def test_acceptance_table_from_reference_tests(case):
+    got = olm.match_acceptance_length(np.array(case["drafted"], np.uint32),
+                                      np.array(case["posterior"], np.uint32))
+    assert got == case["expected"]
+
+
+def test_qmm_random_shapes_follow_reference_rule():
+    """The GPU parity suite's random shapes are the reference harness's."""
+    from test_qmm_gpu import _gen_random_shapes
+
+    rule = GOLDEN["qmm_random_shapes"]
+    rng = np.random.default_rng(rule["seed"])
+    gs = GOLDEN["qmm_group_size"]
+    expected = []
+    for i in range(rule["n"]):
+        m = rule["m_levels"][i % len(rule["m_levels"])]
+        k = int(rng.integers(*rule["k_blocks_range"])) * gs
+        n = int(rng.integers(*rule["n_blocks_range"])) * 8
+        expected.append((f"rnd{i:02d}", m, k, n))
+    assert _gen_random_shapes(rule["n"], rule["seed"]) == expected
+
+
+def test_qmm_real_shapes_cover_reference_lists():
+    from test_qmm_gpu import REAL_SHAPES, REAL_M4_SHAPES
+
+    ours = {(m, k, n) for _, m, k, n in REAL_SHAPES + REAL_M4_SHAPES}
+    for _, m, k, n in GOLDEN["qmm_real_mlp_shapes"] + GOLDEN["qmm_real_mlp_m4_shapes"]:
+        assert (m, k, n) in ours
+
+
+# ------------------------------------------------------------ rollback control
+class _ArmableCache:
+    def __init__(self):
+        self.armed_at: list[int] = []
+        self.rolled_back_to: list[int] = []
+        self._tape, self._tape_k, self._tape_g, self._tape_qkv = "x", "y", "z", "q"
+        self._snapshot = "s"
+        self._armed = True
+
+    def arm_rollback(self, *, prefix_len: int) -> None:
+        self.armed_at.append(int(prefix_len))
+
+    def rollback(self, accepted: int) -> None:
+        self.rolled_back_to.append(int(accepted))
+
+    def clear_transients(self) -> None:
+        self._tape = self._tape_k = self._tape_g = self._tape_qkv = self._snapshot = None
+        self._armed = False
+
+
+class _OffsetCache:
+    def __init__(self, offset: int):
+        self.offset = int(offset)
+        self.trim_calls: list[int] = []
+
+    def trim(self, n: int) -> None:
+        self.trim_calls.append(int(n))
+        self.offset -= int(n)
+
+
+class _CropCache:
+    def __init__(self):
+        self.crop_calls: list[int] = []
+
+    def crop(self, target_len: int) -> None:
+        self.crop_calls.append(int(target_len))
+
+
+def test_arm_calls_arm_rollback_with_int_prefix(pkg):
+    a, b = _ArmableCache(), _ArmableCache()
+    pkg.arm_rollback([a, b, "not_armable"], prefix_len=42)
+    assert a.armed_at == [42] and b.armed_at == [42]
+
+
+def test_clear_rollback_state_uses_clear_transients(pkg):
+    c = _ArmableCache()
+    pkg.clear_rollback_state(c)
+    assert c._armed is False and c._tape is None and c._tape_k is None and c._snapshot is None
+
+
+def test_full_acceptance_skips_replay(pkg):
+    c = _ArmableCache()
+    ns = pkg.restore_after_acceptance([c], target_len=100, acceptance_length=4, drafted_tokens=4)
+    assert c.rolled_back_to == [] and c._tape is None and ns == 0
+
+
+def test_partial_acceptance_rolls_back_to_acceptance_length(pkg):
+    c = _ArmableCache()
+    ns = pkg.restore_after_acceptance([c], target_len=100, acceptance_length=2, drafted_tokens=4)
+    assert c.rolled_back_to == [2] and ns >= 0
+
+
+def test_offset_caches_trim_to_target(pkg):
+    over, under = _OffsetCache(110), _OffsetCache(80)
+    pkg.restore_after_acceptance([over, under], target_len=100, acceptance_length=0,
+                                 drafted_tokens=0)
+    assert over.trim_calls == [10] and under.trim_calls == []
+
+
+def test_crop_fallback(pkg):
+    c = _CropCache()
+    pkg.restore_after_acceptance([c], target_len=64, acceptance_length=0, drafted_tokens=0)
+    assert c.crop_calls == [64]
+
+
+def test_cleanup_clears_transients_and_empties_lists(pkg):
+    c = _ArmableCache()
+    target, draft = [c], ["draft_entry"]
+    pkg.cleanup_generation_caches(target, draft)
+    assert target == [] and draft == [] and c._tape is None
+
+
+def test_rollback_cache_without_tape_restores_snapshot(pkg):
+    """Rollback with no recorded tape restores the armed snapshot (CPU tensors,
+    no replay kernel involved) and clears the transients."""
+    cache = pkg.RecurrentRollbackCache(2)
+    cache[0] = torch.ones(2, 3)
+    cache[1] = torch.zeros(2, 4)
+    cache.arm_rollback(prefix_len=5)
+    cache[0] = torch.full((2, 3), 7.0)
+    cache.rollback(1)
+    assert torch.equal(cache[0], torch.ones(2, 3))
+    assert cache._tape is None and cache._snapshot is None
+
+
+# ------------------------------------------------------------ verify linears
+def _ql(pkg, n, k, *, bits=4, group_size=64, mode="affine"):
+    w = torch.zeros((n, k * bits // 32), dtype=torch.int32)
+    s = torch.ones((n, k // group_size), dtype=torch.bfloat16)
+    return pkg.QuantizedLinear(w, s, s.clone(), group_size=group_size, bits=bits, mode=mode)
+
+
+def test_eligibility_basic_and_large_n(pkg):
+    small = GOLDEN["linear_small"]
+    assert pkg.is_verify_eligible(_ql(pkg, small["out_dims"], small["in_dims"]))
+    assert not pkg.is_verify_eligible(_ql(pkg, GOLDEN["linear_large_n"], small["in_dims"]))
+
+
+def test_eligibility_rejects_layouts_without_a_kernel(pkg):
+    assert not pkg.is_verify_eligible(_ql(pkg, 64, 512, bits=8))
+    assert not pkg.is_verify_eligible(_ql(pkg, 64, 512, group_size=32))
+    assert not pkg.is_verify_eligible(_ql(pkg, 64, 512, mode="mxfp4"))
+    assert not pkg.is_verify_eligible(nn.Linear(8, 8))
+
+
+def test_eligibility_include_filter(pkg, monkeypatch):
+    ql = _ql(pkg, 64, 512)
+    monkeypatch.setenv("DFLASH_VERIFY_INCLUDE", "mlp")
+    assert pkg.is_verify_eligible(ql, path="model.layers.0.mlp.gate_proj")
+    assert not pkg.is_verify_eligible(ql, path="model.layers.0.self_attn.q_proj")
+    monkeypatch.setenv("DFLASH_VERIFY_INCLUDE", "attn_q,gdn")
+    assert pkg.is_verify_eligible(ql, path="model.layers.0.self_attn.q_proj")
+    assert pkg.is_verify_eligible(ql, path="model.layers.3.linear_attn.out_proj")
+    assert not pkg.is_verify_eligible(ql, path="model.layers.0.self_attn.k_proj")
+    monkeypatch.setenv("DFLASH_VERIFY_MAX_N", "32")
+    assert not pkg.is_verify_eligible(ql, path="model.layers.0.self_attn.q_proj")
+
+
+def test_install_swaps_eligible_modules_once(pkg):
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.gate_proj = _ql(pkg, 128, 512)
+            self.down_proj = _ql(pkg, 512, 128)
+            self.wide = _ql(pkg, 64, 512, bits=8)              # no kernel: stays
+
+    model = nn.Module()
+    model.mlp = Block()
+    model.head = nn.Linear(4, 4)
+    w_ptr = model.mlp.gate_proj.weight.data_ptr()
+    n = pkg.install_verify_linears(model)
+    assert n == 2
+    assert isinstance(model.mlp.gate_proj, pkg.VerifyQuantizedLinear)
+    assert isinstance(model.mlp.down_proj, pkg.VerifyQuantizedLinear)
+    assert not isinstance(model.mlp.wide, pkg.VerifyQuantizedLinear)
+    assert pkg.install_verify_linears(model) == 0
+    # the wrapper shares the original (already contiguous) tensors
+    assert model.mlp.gate_proj.weight.data_ptr() == w_ptr
+    only_down = nn.Module()
+    only_down.mlp = Block()
+    assert pkg.install_verify_linears(only_down, predicate=lambda path, m: path.endswith("down_proj")) == 1

@@ -60,6 +60,22 @@ REAL_SHAPES = [
 ]
 
 
+# tests/test_verify_qmm_parity.py:23-27 (the reference's M = 4 verify shapes)
+REAL_M4_SHAPES = [
+    ("gate_proj_m4", 4, 5120, 17408),
+    ("down_proj_m4", 4, 17408, 5120),
+]
+
+
+@pytest.mark.parametrize("name,M,K,N", REAL_M4_SHAPES)
+def test_real_shapes_m4_reference_harness(pkg, dev, name, M, K, N):
+    x, w_q, s, b = _ref_style_case(name, M, K, N)
+    y = _run(pkg, dev, x, w_q, s, b)
+    max_abs, max_rel = oqmm.max_abs_rel(y, oqmm.qmm(x, w_q, s, b, accum=np.float32))
+    assert y.shape == (M, N)
+    assert max_abs <= 8e-3 and max_rel <= 2e-2, (name, max_abs, max_rel)
+
+
 @pytest.mark.parametrize("name,M,K,N", REAL_SHAPES)
 def test_real_shapes_baseline_distribution(pkg, dev, name, M, K, N):
     rng = np.random.default_rng(abs(hash(name)) & 0xFFFF)
@@ -168,3 +184,21 @@ def test_dequant_is_exact(pkg, dev):
     y = _run(pkg, dev, x, w_q, s, b)
     w = oqmm.dequantize(w_q, s, b)
     assert np.array_equal(obf16.to_f32(y), w[:, cols].T)
+
+
+def test_verify_linear_matches_direct_call(pkg, dev):
+    """VerifyQuantizedLinear(x) is bit-identical to verify_matmul on the same
+    weights (reference tests/test_verify_linear_parity.py:53-63), for M = 16
+    and for other row counts (which the reference sends to stock qmm)."""
+    import torch
+
+    rng = np.random.default_rng(21)
+    w_q, s, b = oqmm.synth_weights(rng, 1024, 512)
+    ql = pkg.QuantizedLinear(to_dev_u32(w_q, dev), to_dev_bf16(s, dev), to_dev_bf16(b, dev))
+    verify = pkg.VerifyQuantizedLinear.from_quantized(ql)
+    for m in (16, 1, 8, 32, 40):
+        x = to_dev_bf16(oqmm.synth_x(rng, m, 512), dev)
+        direct = pkg.verify_matmul(x, ql.weight, ql.scales, ql.biases, transpose=True,
+                                   group_size=64, bits=4)
+        assert torch.equal(verify(x), direct)
+        assert torch.equal(ql(x), direct)
