@@ -15,7 +15,7 @@ its C ABI (``include/dflash_b200.h``); there is no CPU fallback.
 
 from . import kernels, lm_head, moe
 from .lm_head import lm_head_argmax_keys, lm_head_verify, match_acceptance_length, verify_accept
-from .kernels import tape_replay_kernel, tape_replay_
+from .kernels import gated_delta_kernel_with_tape, tape_replay_kernel, tape_replay_
 from .recurrent_rollback_cache import (
     RecurrentRollbackCache,
     arm_rollback,

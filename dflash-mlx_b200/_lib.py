@@ -40,6 +40,8 @@ SIGNATURES = {
                                               _vp]),
     "dfl_gdn_tape_replay": (_c_int, [_vp, _vp, _c_int, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int,
                                      _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
+    "dfl_gdn_forward_tape": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _vp, _vp,
+                                      _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
     "dfl_lmhead_argmax": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
                                    _c_size, _vp]),
     "dfl_lmhead_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),

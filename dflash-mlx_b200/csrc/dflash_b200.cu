@@ -7,6 +7,7 @@
 #include "qmm_w4.cu"
 #include "qmm_noalloc.cu"
 #include "gdn_replay.cu"
+#include "gdn_forward.cu"
 #include "lmhead.cu"
 #include "moe.cu"
 

@@ -1,0 +1,250 @@
+// GatedDeltaNet verify forward that records the innovation tape (sm_100a).
+//
+// Replaces gated_delta_kernel_with_tape (dflash_mlx/kernels.py:169-219, Metal
+// body :28-101; mx-op reference _gated_delta_ops_with_tape :125-167).  For
+// every sequence b, value head hv (k/q head hk = hv / (Hv / Hk)) and step t
+// with mask[b, t] (mask absent: all steps):
+//     S'      = S * g_t                    (g_t scalar per head, or per dk)
+//     kv[dv]  = sum_dk S'[dv, dk] * k_t[dk]
+//     delta   = (v_t[dv] - kv[dv]) * beta_t
+//     S       = S' + k_t[dk] * delta[dv]
+//     y_t[dv] = sum_dk S[dv, dk] * q_t[dk]          (bf16 out)
+//     tape_t[dv] = delta[dv]                         (fp32)
+// A masked-out step leaves S unchanged and writes tape = 0, y = 0.  The two
+// state updates are separately rounded fp32 operations in the mx-op
+// reference's order -- the same ones tape_replay_kernel applies -- so
+// replaying this kernel's tape over the first a steps reproduces its state
+// after a steps exactly.
+//
+// Layout: q, k [B, T, Hk, Dk] bf16; v [B, T, Hv, Dv] bf16; g [B, T, Hv] or
+// [B, T, Hv, Dk] fp32; beta [B, T, Hv] fp32; state [B, Hv, Dv, Dk] fp32;
+// y [B, T, Hv, Dv] bf16; tape [B, T, Hv, Dv] fp32.
+//
+// Mapping: a CTA of 8 warps owns 32 value rows of one head; a warp owns 4
+// rows and lane l holds elements [l * Dk/32, (l+1) * Dk/32) of each, so the
+// two dot products per row are Dk/32 FMAs per lane plus a butterfly (the four
+// rows' reductions interleave).  The head's k, q and the CTA's v, g, beta for
+// all T steps are staged in shared memory first, so the sequential step loop
+// touches no global memory.  The state is read once and written once: the
+// kernel is HBM-bound at B x Hv x Dv x Dk x 8 bytes of state traffic.
+
+namespace dfl {
+namespace gdnf {
+
+constexpr int THREADS = 256;
+constexpr int WARPS = THREADS / 32;
+constexpr int ROWS_PER_WARP = 4;
+constexpr int ROWS = WARPS * ROWS_PER_WARP;  // value rows per CTA
+constexpr int MAX_STEPS = 64;
+
+struct FwdParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const float* g;
+  const float* beta;
+  const uint8_t* mask;  // [B, T] or null
+  const float* state_in;
+  float* state_out;
+  __nv_bfloat16* y;
+  float* tape;
+  int B, T, Hv, Hk, Dv, Dk;
+  int g_vec;
+};
+
+__host__ __device__ constexpr size_t smem_bytes(int T, int Dk, int g_vec) {
+  // k and q as float [T][Dk], g [T][Dk] or [T], beta [T], v [T][ROWS], mask [T]
+  return size_t(T) * Dk * 4 * 2 + size_t(T) * (g_vec ? Dk : 1) * 4 + size_t(T) * 4 +
+         size_t(T) * ROWS * 4 + size_t(T) * 4;
+}
+
+template <int NPL>
+__device__ __forceinline__ void load_row(const float* src, float (&r)[NPL]) {
+  if constexpr (NPL % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < NPL; i += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(src + i);
+      r[i] = v.x; r[i + 1] = v.y; r[i + 2] = v.z; r[i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) r[i] = src[i];
+  }
+}
+
+template <int NPL>
+__device__ __forceinline__ void store_row(float* dst, const float (&r)[NPL]) {
+  if constexpr (NPL % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < NPL; i += 4)
+      *reinterpret_cast<float4*>(dst + i) = make_float4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) dst[i] = r[i];
+  }
+}
+
+template <int DK>
+__global__ void __launch_bounds__(THREADS) gdn_forward_tape_kernel(const FwdParams p) {
+  constexpr int NPL = DK / 32;  // state elements of a row per lane
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int T = p.T;
+  float* k_s = reinterpret_cast<float*>(smem_raw);          // [T][DK]
+  float* q_s = k_s + T * DK;                                // [T][DK]
+  float* g_s = q_s + T * DK;                                // [T][DK] or [T]
+  float* b_s = g_s + T * (p.g_vec ? DK : 1);                // [T]
+  float* v_s = b_s + T;                                     // [T][ROWS]
+  int* m_s = reinterpret_cast<int*>(v_s + T * ROWS);        // [T]
+
+  const int blocks_per_head = p.Dv / ROWS;
+  const int n = blockIdx.x / blocks_per_head;  // b * Hv + hv
+  const int row0 = (blockIdx.x - n * blocks_per_head) * ROWS;
+  const int b = n / p.Hv;
+  const int hv = n - b * p.Hv;
+  const int hk = hv / (p.Hv / p.Hk);
+
+  // ---- stage the head's per-step inputs
+  for (int i = threadIdx.x; i < T * DK; i += THREADS) {
+    const int t = i / DK, d = i - t * DK;
+    const size_t kq = (((size_t)b * T + t) * p.Hk + hk) * DK + d;
+    k_s[i] = __bfloat162float(p.k[kq]);
+    q_s[i] = __bfloat162float(p.q[kq]);
+    if (p.g_vec) g_s[i] = p.g[(((size_t)b * T + t) * p.Hv + hv) * DK + d];
+  }
+  for (int i = threadIdx.x; i < T * ROWS; i += THREADS) {
+    const int t = i / ROWS, r = i - t * ROWS;
+    v_s[i] = __bfloat162float(p.v[(((size_t)b * T + t) * p.Hv + hv) * p.Dv + row0 + r]);
+  }
+  for (int t = threadIdx.x; t < T; t += THREADS) {
+    const size_t bt = ((size_t)b * T + t) * p.Hv + hv;
+    if (!p.g_vec) g_s[t] = p.g[bt];
+    b_s[t] = p.beta[bt];
+    m_s[t] = p.mask ? (p.mask[(size_t)b * T + t] != 0) : 1;
+  }
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int c0 = lane * NPL;  // this lane's first dk
+  float s[ROWS_PER_WARP][NPL];
+  const size_t head_off = (size_t)n * p.Dv * DK;
+#pragma unroll
+  for (int j = 0; j < ROWS_PER_WARP; ++j)
+    load_row<NPL>(p.state_in + head_off + (size_t)(row0 + warp * ROWS_PER_WARP + j) * DK + c0, s[j]);
+  __syncthreads();
+
+  for (int t = 0; t < T; ++t) {
+    const float* kt = k_s + t * DK + c0;
+    const float* qt = q_s + t * DK + c0;
+    const size_t out_off = (((size_t)b * T + t) * p.Hv + hv) * p.Dv + row0 + warp * ROWS_PER_WARP;
+    if (!m_s[t]) {
+      if (lane < ROWS_PER_WARP) {
+        p.tape[out_off + lane] = 0.f;
+        p.y[out_off + lane] = __float2bfloat16_rn(0.f);
+      }
+      continue;
+    }
+    float kv[ROWS_PER_WARP];
+#pragma unroll
+    for (int j = 0; j < ROWS_PER_WARP; ++j) {
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) {
+        const float gd = p.g_vec ? g_s[t * DK + c0 + i] : g_s[t];
+        s[j][i] = __fmul_rn(s[j][i], gd);
+        acc = __fmaf_rn(s[j][i], kt[i], acc);
+      }
+      kv[j] = acc;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int j = 0; j < ROWS_PER_WARP; ++j) kv[j] += __shfl_xor_sync(0xffffffffu, kv[j], off);
+    float delta[ROWS_PER_WARP], out[ROWS_PER_WARP];
+#pragma unroll
+    for (int j = 0; j < ROWS_PER_WARP; ++j) {
+      delta[j] = __fmul_rn(__fsub_rn(v_s[t * ROWS + warp * ROWS_PER_WARP + j], kv[j]), b_s[t]);
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) {
+        s[j][i] = __fadd_rn(s[j][i], __fmul_rn(kt[i], delta[j]));
+        acc = __fmaf_rn(s[j][i], qt[i], acc);
+      }
+      out[j] = acc;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int j = 0; j < ROWS_PER_WARP; ++j) out[j] += __shfl_xor_sync(0xffffffffu, out[j], off);
+    if (lane < ROWS_PER_WARP) {
+      // lane j writes row j (values are uniform across the warp after the butterfly)
+      float dj = delta[0], oj = out[0];
+#pragma unroll
+      for (int j = 1; j < ROWS_PER_WARP; ++j)
+        if (lane == j) { dj = delta[j]; oj = out[j]; }
+      p.tape[out_off + lane] = dj;
+      p.y[out_off + lane] = __float2bfloat16_rn(oj);
+    }
+  }
+
+#pragma unroll
+  for (int j = 0; j < ROWS_PER_WARP; ++j)
+    store_row<NPL>(p.state_out + head_off + (size_t)(row0 + warp * ROWS_PER_WARP + j) * DK + c0, s[j]);
+}
+
+template <int DK>
+int launch_forward(const FwdParams& p, cudaStream_t stream) {
+  static std::atomic<uint64_t> smem_done{0};
+  const size_t smem = smem_bytes(p.T, DK, p.g_vec);
+  int dev, sms;
+  int st = host::current_device(&dev, &sms);
+  if (st != DFL_OK) return st;
+  st = host::ensure_smem(gdn_forward_tape_kernel<DK>, int(smem_bytes(MAX_STEPS, DK, 1)), dev,
+                         smem_done);
+  if (st != DFL_OK) return st;
+  const int grid = p.B * p.Hv * (p.Dv / ROWS);
+  gdn_forward_tape_kernel<DK><<<grid, THREADS, smem, stream>>>(p);
+  return host::launch_status();
+}
+
+}  // namespace gdnf
+}  // namespace dfl
+
+extern "C" int dfl_gdn_forward_tape(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                    const float* g, int g_vectorized, const float* beta,
+                                    const uint8_t* mask, const float* state_in, float* state_out,
+                                    uint16_t* y, float* tape, int B, int T, int Hv, int Hk, int Dv,
+                                    int Dk, void* stream) {
+  using namespace dfl;
+  if (B < 0 || T < 0 || Hv < 1 || Hk < 1 || Dv < 1 || Hv % Hk != 0) return DFL_ERR_BAD_SHAPE;
+  if (Dk != 32 && Dk != 64 && Dk != 128 && Dk != 256) return DFL_ERR_BAD_SHAPE;
+  if (Dv % gdnf::ROWS != 0 || T > gdnf::MAX_STEPS) return DFL_ERR_BAD_SHAPE;
+  if (B == 0) return DFL_OK;
+  if (!state_in || !state_out) return DFL_ERR_NULL_POINTER;
+  if (T > 0 && (!q || !k || !v || !g || !beta || !y || !tape)) return DFL_ERR_NULL_POINTER;
+  if (!host::aligned(state_in, 16) || !host::aligned(state_out, 16)) return DFL_ERR_MISALIGNED;
+  gdnf::FwdParams p;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  p.k = reinterpret_cast<const __nv_bfloat16*>(k);
+  p.v = reinterpret_cast<const __nv_bfloat16*>(v);
+  p.g = g;
+  p.beta = beta;
+  p.mask = mask;
+  p.state_in = state_in;
+  p.state_out = state_out;
+  p.y = reinterpret_cast<__nv_bfloat16*>(y);
+  p.tape = tape;
+  p.B = B;
+  p.T = T;
+  p.Hv = Hv;
+  p.Hk = Hk;
+  p.Dv = Dv;
+  p.Dk = Dk;
+  p.g_vec = g_vectorized ? 1 : 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (Dk) {
+    case 32: return gdnf::launch_forward<32>(p, s);
+    case 64: return gdnf::launch_forward<64>(p, s);
+    case 128: return gdnf::launch_forward<128>(p, s);
+    default: return gdnf::launch_forward<256>(p, s);
+  }
+}

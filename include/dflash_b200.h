@@ -12,6 +12,7 @@
  *                             VerifyQuantizedLinear.__call__ dflash_mlx/verify_linear.py:115-116,266-286
  *                             (stock mx.quantized_matmul(transpose=True) for other M)
  *   dfl_gdn_tape_replay    <- tape_replay_kernel       dflash_mlx/kernels.py:822-868
+ *   dfl_gdn_forward_tape   <- gated_delta_kernel_with_tape dflash_mlx/kernels.py:169-219
  *   dfl_lmhead_argmax + dfl_lmhead_accept
  *                          <- logits_from_hidden       dflash_mlx/engine/target_qwen_gdn.py:774-778
  *                             greedy_tokens_with_mask  dflash_mlx/engine/sampling.py:47-55
@@ -114,6 +115,27 @@ int dfl_gdn_tape_replay(const float* tape, const void* k, int k_is_bf16, const f
                         int g_vectorized, const int32_t* steps, const uint8_t* mask,
                         const float* state_in, float* state_out, int B, int T, int Hv, int Hk,
                         int Dv, int Dk, void* stream);
+
+/* GatedDeltaNet verify forward that records the innovation tape.
+ *
+ * For every sequence b, value head hv (q/k head hk = hv / (Hv / Hk)) and step t
+ * with mask[b, t] != 0 (mask NULL: all steps):
+ *     S' = S * g_t;  kv = S' k_t;  delta = (v_t - kv) * beta_t;
+ *     S = S' + delta (x) k_t;  y_t = S q_t;  tape_t = delta
+ * (state updates separately rounded fp32, in tape-replay order, so replaying
+ * the tape over the first a steps reproduces the state after a steps exactly).
+ * A masked-out step leaves S and writes tape = 0, y = 0.
+ *   q, k   bf16 [B, T, Hk, Dk]      v bf16 [B, T, Hv, Dv]
+ *   g      fp32 [B, T, Hv] or [B, T, Hv, Dk] (g_vectorized)    beta fp32 [B, T, Hv]
+ *   state  fp32 [B, Hv, Dv, Dk], 16-byte aligned (state_out may equal state_in)
+ *   y      bf16 [B, T, Hv, Dv]      tape fp32 [B, T, Hv, Dv]
+ * Constraints: Dk in {32, 64, 128, 256}, Dv % 32 == 0, Hv % Hk == 0, T <= 64.
+ * Replaces gated_delta_kernel_with_tape (dflash_mlx/kernels.py:169-219; Metal
+ * body :28-101; mx-op reference _gated_delta_ops_with_tape :125-167). */
+int dfl_gdn_forward_tape(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,
+                         int g_vectorized, const float* beta, const uint8_t* mask,
+                         const float* state_in, float* state_out, uint16_t* y, float* tape,
+                         int B, int T, int Hv, int Hk, int Dv, int Dk, void* stream);
 
 /* ------------------------------------------------------------------------
  * lm_head verify epilogue.
