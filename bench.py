@@ -307,8 +307,8 @@ def run_ours(args):
                                  "layer: q|k|v, o, gate|up, down) / their CUDA-event time inside "
                                  "the timed region"},
             # ours per step: 4 qmm + 1 SiLU*up per layer and request, lm_head argmax,
-            # accept, one tape replay per GDN layer
-            "gpu_launches": args.steps * (launches + sh.layers * b + 2 + sh.gdn_layers),
+            # accept, one tape replay over all GDN layers
+            "gpu_launches": args.steps * (launches + sh.layers * b + 2 + 1),
             "e2e": {"value": world * b / t_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "clocks": clk,

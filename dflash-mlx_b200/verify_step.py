@@ -14,7 +14,8 @@ for ``requests`` independent requests of 16 verify tokens on this GPU:
    is split;
 3. GatedDeltaNet tape-replay rollback of every GDN layer with the accepted
    step counts straight from step 2 (``recurrent_rollback_cache.py:142-165``:
-   ``accepted + 1`` steps), so no value is read back to the host.
+   ``accepted + 1`` steps), so no value is read back to the host; all layers'
+   states share one arena and roll back in one launch.
 
 Weights are random with BASELINE's distributions (no checkpoints offline).
 The per-request qmm stack runs the same x through every layer (no attention
@@ -31,7 +32,7 @@ from typing import Optional
 import torch
 
 from . import lm_head as _lm
-from .kernels import tape_replay_
+from .kernels import gated_delta_kernel_with_tape, tape_replay_
 from .moe import QuantWeight, silu_mul
 from .verify_qmm import qmm_w4g64
 
@@ -104,15 +105,29 @@ class VerifyStep:
         self.v_begin, v_len = _lm.vocab_shard(sh.vocab, rank, world)
         wgen = torch.Generator(device=self.dev).manual_seed(seed + 1000 + rank)
         self.lm_w = (torch.randn((v_len, sh.hidden), generator=wgen, device=self.dev) * 0.02).to(torch.bfloat16)
-        # GDN rollback state and tapes: [layer][B, Hv, Dv, Dk] fp32 ~ N(0, 0.05)
+        # GDN rollback snapshot states [layer, B, Hv, Dv, Dk] fp32 ~ N(0, 0.05)
+        # and the tapes of one verify block, recorded by the verify forward
+        # (gated_delta_kernel_with_tape) from BASELINE config 4's inputs:
+        # q, k, v bf16 ~ N(0, 1) (q, k L2-normalised), beta = sigmoid(N),
+        # g = exp(-softplus(N)).
         b, t, hv, dk, dv = self.requests, sh.block, sh.gdn_heads, sh.gdn_dk, sh.gdn_dv
         sgen = torch.Generator(device=self.dev).manual_seed(seed + 2000 + rank)
         self.gdn_state = torch.randn((sh.gdn_layers, b, hv, dv, dk), generator=sgen, device=self.dev) * 0.05
-        self.tape = torch.randn((sh.gdn_layers, b, t, hv, dv), generator=sgen, device=self.dev) * 0.3
-        kk = torch.randn((sh.gdn_layers, b, t, hv, dk), generator=sgen, device=self.dev)
-        self.tape_k = (kk / kk.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+
+        def _unit(shape):
+            a = torch.randn(shape, generator=sgen, device=self.dev)
+            return (a / a.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+
+        self.tape_k = _unit((sh.gdn_layers, b, t, hv, dk))
         self.tape_g = torch.exp(-torch.nn.functional.softplus(
             torch.randn((sh.gdn_layers, b, t, hv), generator=sgen, device=self.dev)))
+        self.tape = torch.empty((sh.gdn_layers, b, t, hv, dv), device=self.dev)
+        for layer in range(sh.gdn_layers):
+            q = _unit((b, t, hv, dk))
+            v = torch.randn((b, t, hv, dv), generator=sgen, device=self.dev).to(torch.bfloat16)
+            beta = torch.sigmoid(torch.randn((b, t, hv), generator=sgen, device=self.dev))
+            _, _, self.tape[layer] = gated_delta_kernel_with_tape(
+                q, self.tape_k[layer], v, self.tape_g[layer], beta, self.gdn_state[layer])
         # step inputs / outputs (static buffers for graph replay)
         self.x = torch.empty((b * sh.block, sh.hidden), dtype=torch.bfloat16, device=self.dev)
         # stand-in for the attention output feeding o_proj (produced outside
@@ -147,9 +162,16 @@ class VerifyStep:
         self.acceptance = acc[b0:b0 + self.requests]
         self.next_token = nxt[b0:b0 + self.requests]
         steps = self.acceptance + 1       # recurrent_rollback_cache.py:154
-        for layer in range(self.shape.gdn_layers):
-            tape_replay_(self.gdn_state[layer], self.tape[layer], self.tape_k[layer],
-                         self.tape_g[layer], steps)
+        # The GDN states of all layers live in one [L, B, Hv, Dv, Dk] arena, so
+        # the rollback of every layer is a single launch with the layer folded
+        # into the batch (sequence i of layer l is batch entry l * B + i).
+        sh = self.shape
+        lb = sh.gdn_layers * self.requests
+        tape_replay_(self.gdn_state.view(lb, *self.gdn_state.shape[2:]),
+                     self.tape.view(lb, *self.tape.shape[2:]),
+                     self.tape_k.view(lb, *self.tape_k.shape[2:]),
+                     self.tape_g.view(lb, *self.tape_g.shape[2:]),
+                     steps.repeat(sh.gdn_layers))
 
     # -------------------------------------------------------------- driving
     def capture(self):
