@@ -35,6 +35,8 @@ SIGNATURES = {
     "dfl_get_device_error": (_c_int, [ctypes.POINTER(_c_int)]),
     "dfl_verify_qmm_w4g64": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_size, _c_int, _c_int,
                                       _c_int, _vp]),
+    "dfl_verify_qmm_w4g64_f16": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_size, _c_int, _c_int,
+                                          _c_int, _vp]),
     "dfl_verify_qmm_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
     "dfl_verify_qmm_w4g64_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
                                               _vp]),

@@ -295,6 +295,16 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, ui
 
 // Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both
 // K-major, shape M x N.
+// Instruction descriptor for kind::f16 with fp32 accumulation and A, B both
+// fp16 (f16 = true) or both bf16.
+__host__ __device__ constexpr uint32_t make_idesc_16(int m, int n, bool f16) {
+  return (1u << 4)                                  // D format f32
+         | ((f16 ? 0u : 1u) << 7)                   // A format f16 / bf16
+         | ((f16 ? 0u : 1u) << 10)                  // B format f16 / bf16
+         | (uint32_t(n >> 3) << 17)                 // N / 8
+         | (uint32_t(m >> 4) << 24);                // M / 16
+}
+
 __host__ __device__ constexpr uint32_t make_idesc_bf16(int m, int n) {
   return (1u << 4)                               // D format f32
          | (1u << 7)                             // A format bf16

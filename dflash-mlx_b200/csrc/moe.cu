@@ -102,8 +102,13 @@ __global__ void silu_mul_kernel(const uint16_t* gate, const uint16_t* up, uint16
 
 // Same on row-strided inputs: out[r, c] (contiguous) from gate/up rows of
 // stride ld, e.g. the two halves of a fused gate|up projection output.
+// Launched with programmatic stream serialization, like the qmm it sits
+// between: it lets the next launch start its weight prefetch at once and
+// waits for the previous launch's output before reading it.
 __global__ void silu_mul_rows_kernel(const uint16_t* gate, const uint16_t* up, int ld, uint16_t* out,
                                      int rows, int cols) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * cols) return;
   const int r = i / cols, c = i - r * cols;
@@ -169,9 +174,8 @@ extern "C" int dfl_silu_mul_rows_bf16(const uint16_t* gate, const uint16_t* up, 
   if (rows == 0 || cols == 0) return DFL_OK;
   if (!gate || !up || !out) return DFL_ERR_NULL_POINTER;
   const int n = rows * cols;
-  moe::silu_mul_rows_kernel<<<(n + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      gate, up, ld, out, rows, cols);
-  return host::launch_status();
+  return host::launch_pdl(moe::silu_mul_rows_kernel, (n + 255) / 256, 256, 0,
+                          reinterpret_cast<cudaStream_t>(stream), gate, up, ld, out, rows, cols);
 }
 
 extern "C" int dfl_moe_combine(const uint16_t* pair_out, const float* weights,

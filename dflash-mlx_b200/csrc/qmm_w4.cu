@@ -138,29 +138,60 @@ __device__ __forceinline__ int cta_of_unit(int u, int total, int grid) {
 // K order (0,4), (1,5), (2,6), (3,7): each is one shift + one LOP3 (mask and
 // exponent bits), with no byte permutes.  The x operand gets the same
 // within-8 permutation (permute_x_chunk), so the MMA still sums x_k * w_k.
+template <bool F16>
 __device__ __forceinline__ void dequant8(uint32_t q, uint32_t s, uint32_t b, uint32_t* out) {
   // Written in PTX so that each step is exactly one instruction: 3 shifts
-  // and 4 LOP3 (mask | exponent bits 0x4300 = 128.0) on the integer pipe,
-  // then per pair an exact bf16x2 FMA (v * 1 - 128 = n) and the scale/bias
-  // FMA with a single rounding.
-  asm("{\n\t.reg .b32 h1, h2, h3, t0, t1, t2, t3;\n\t"
-      "shr.b32 h1, %4, 4;\n\t"
-      "shr.b32 h2, %4, 8;\n\t"
-      "shr.b32 h3, %4, 12;\n\t"
-      "lop3.b32 t0, %4, 0x000F000F, 0x43004300, 0xEA;\n\t"
-      "lop3.b32 t1, h1, 0x000F000F, 0x43004300, 0xEA;\n\t"
-      "lop3.b32 t2, h2, 0x000F000F, 0x43004300, 0xEA;\n\t"
-      "lop3.b32 t3, h3, 0x000F000F, 0x43004300, 0xEA;\n\t"
-      "fma.rn.bf16x2 t0, t0, %7, %8;\n\t"
-      "fma.rn.bf16x2 t1, t1, %7, %8;\n\t"
-      "fma.rn.bf16x2 t2, t2, %7, %8;\n\t"
-      "fma.rn.bf16x2 t3, t3, %7, %8;\n\t"
-      "fma.rn.bf16x2 %0, t0, %5, %6;\n\t"
-      "fma.rn.bf16x2 %1, t1, %5, %6;\n\t"
-      "fma.rn.bf16x2 %2, t2, %5, %6;\n\t"
-      "fma.rn.bf16x2 %3, t3, %5, %6;\n\t}"
-      : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
-      : "r"(q), "r"(s), "r"(b), "r"(0x3F803F80u), "r"(0xC300C300u));
+  // and 4 LOP3 (mask | exponent bits of the magic value: bf16 0x4300 = 128.0,
+  // fp16 0x6400 = 1024.0) on the integer pipe, then per pair an exact x2 FMA
+  // (v * 1 - magic = n) and the scale/bias FMA with a single rounding.
+  if constexpr (F16) {
+    asm("{\n\t.reg .b32 h1, h2, h3, t0, t1, t2, t3;\n\t"
+        "shr.b32 h1, %4, 4;\n\t"
+        "shr.b32 h2, %4, 8;\n\t"
+        "shr.b32 h3, %4, 12;\n\t"
+        "lop3.b32 t0, %4, 0x000F000F, 0x64006400, 0xEA;\n\t"
+        "lop3.b32 t1, h1, 0x000F000F, 0x64006400, 0xEA;\n\t"
+        "lop3.b32 t2, h2, 0x000F000F, 0x64006400, 0xEA;\n\t"
+        "lop3.b32 t3, h3, 0x000F000F, 0x64006400, 0xEA;\n\t"
+        "fma.rn.f16x2 t0, t0, %7, %8;\n\t"
+        "fma.rn.f16x2 t1, t1, %7, %8;\n\t"
+        "fma.rn.f16x2 t2, t2, %7, %8;\n\t"
+        "fma.rn.f16x2 t3, t3, %7, %8;\n\t"
+        "fma.rn.f16x2 %0, t0, %5, %6;\n\t"
+        "fma.rn.f16x2 %1, t1, %5, %6;\n\t"
+        "fma.rn.f16x2 %2, t2, %5, %6;\n\t"
+        "fma.rn.f16x2 %3, t3, %5, %6;\n\t}"
+        : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
+        : "r"(q), "r"(s), "r"(b), "r"(0x3C003C00u), "r"(0xE400E400u));
+  } else {
+    asm("{\n\t.reg .b32 h1, h2, h3, t0, t1, t2, t3;\n\t"
+        "shr.b32 h1, %4, 4;\n\t"
+        "shr.b32 h2, %4, 8;\n\t"
+        "shr.b32 h3, %4, 12;\n\t"
+        "lop3.b32 t0, %4, 0x000F000F, 0x43004300, 0xEA;\n\t"
+        "lop3.b32 t1, h1, 0x000F000F, 0x43004300, 0xEA;\n\t"
+        "lop3.b32 t2, h2, 0x000F000F, 0x43004300, 0xEA;\n\t"
+        "lop3.b32 t3, h3, 0x000F000F, 0x43004300, 0xEA;\n\t"
+        "fma.rn.bf16x2 t0, t0, %7, %8;\n\t"
+        "fma.rn.bf16x2 t1, t1, %7, %8;\n\t"
+        "fma.rn.bf16x2 t2, t2, %7, %8;\n\t"
+        "fma.rn.bf16x2 t3, t3, %7, %8;\n\t"
+        "fma.rn.bf16x2 %0, t0, %5, %6;\n\t"
+        "fma.rn.bf16x2 %1, t1, %5, %6;\n\t"
+        "fma.rn.bf16x2 %2, t2, %5, %6;\n\t"
+        "fma.rn.bf16x2 %3, t3, %5, %6;\n\t}"
+        : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
+        : "r"(q), "r"(s), "r"(b), "r"(0x3F803F80u), "r"(0xC300C300u));
+  }
+}
+
+// fp32 accumulator -> the activation dtype's bits.
+template <bool F16>
+__device__ __forceinline__ uint16_t to_out16(float v) {
+  if constexpr (F16)
+    return __half_as_ushort(__float2half_rn(v));
+  else
+    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
 }
 
 // Reorders the 8 bf16 of a 16-byte x chunk from k = 0..7 to the order the
@@ -237,7 +268,7 @@ __device__ __forceinline__ void store_x_unit(uint32_t slot, int et,
   }
 }
 
-template <int MT, bool GROUPED>
+template <int MT, bool GROUPED, bool F16 = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     qmm_w4g64_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
                      const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_x,
@@ -405,7 +436,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // and MMAs, everything else is precomputed.
     const int j = warp - WARP_MMA0;
     {
-      constexpr uint32_t idesc = make_idesc_bf16(BN, MT);
+      constexpr uint32_t idesc = make_idesc_16(BN, MT, F16);
       const uint64_t ring_desc = make_sw128_desc(smem_u32(smem + C::OFF_XRING));
       constexpr uint64_t kSlotDesc = uint64_t(C::XSLOT_BYTES >> 4);
       constexpr uint64_t kBlkDesc = uint64_t(C::XBLK_BYTES >> 4);
@@ -511,14 +542,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t s2 = __byte_perm(jj ? s_w1 : s_w0, 0, half_sel);
         const uint32_t b2 = __byte_perm(jj ? b_w1 : b_w0, 0, half_sel);
         uint32_t w[32];
-        dequant8(q0.x, s2, b2, &w[0]);
-        dequant8(q0.y, s2, b2, &w[4]);
-        dequant8(q0.z, s2, b2, &w[8]);
-        dequant8(q0.w, s2, b2, &w[12]);
-        dequant8(q1.x, s2, b2, &w[16]);
-        dequant8(q1.y, s2, b2, &w[20]);
-        dequant8(q1.z, s2, b2, &w[24]);
-        dequant8(q1.w, s2, b2, &w[28]);
+        dequant8<F16>(q0.x, s2, b2, &w[0]);
+        dequant8<F16>(q0.y, s2, b2, &w[4]);
+        dequant8<F16>(q0.z, s2, b2, &w[8]);
+        dequant8<F16>(q0.w, s2, b2, &w[12]);
+        dequant8<F16>(q1.x, s2, b2, &w[16]);
+        dequant8<F16>(q1.y, s2, b2, &w[20]);
+        dequant8<F16>(q1.z, s2, b2, &w[24]);
+        dequant8<F16>(q1.w, s2, b2, &w[28]);
         tmem_st_32x32b_x32(lane_base + slot * A_COLS, w);
       }
       tmem_st_wait();
@@ -671,7 +702,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int m = 0; m < MT; ++m)
               if (m < rows)
                 p.y[(size_t)(GROUPED ? outrow[m] : m) * p.N + n] =
-                    __bfloat16_as_ushort(__float2bfloat16_rn(acc[m]));
+                    to_out16<F16>(acc[m]);
           }
           continue;
         }
@@ -734,7 +765,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int m = 0; m < MT; ++m)
             if (m < rows)
               p.y[(size_t)(GROUPED ? outrow[m] : m) * p.N + n] =
-                  __bfloat16_as_ushort(__float2bfloat16_rn(sum[m]));
+                  to_out16<F16>(sum[m]);
         }
         if (et == 0) p.counters[t] = 0;
       }
@@ -805,19 +836,19 @@ inline int make_weight_maps(const uint32_t* w_q, const uint16_t* scales, const u
   return DFL_OK;
 }
 
-template <int MT, bool GROUPED>
+template <int MT, bool GROUPED, bool F16 = false>
 int launch_kernel(const CUtensorMap& tm_w, const CUtensorMap& tm_s, const CUtensorMap& tm_b,
                   const CUtensorMap& tm_x,
                   const Params& p, int dev, cudaStream_t stream) {
   using C = Cfg<MT>;
   static std::atomic<uint64_t> smem_done{0};
-  int st = host::ensure_smem(qmm_w4g64_kernel<MT, GROUPED>, C::SMEM_BYTES, dev, smem_done);
+  int st = host::ensure_smem(qmm_w4g64_kernel<MT, GROUPED, F16>, C::SMEM_BYTES, dev, smem_done);
   if (st != DFL_OK) return st;
-  return host::launch_pdl(qmm_w4g64_kernel<MT, GROUPED>, p.grid, NUM_THREADS, C::SMEM_BYTES, stream,
+  return host::launch_pdl(qmm_w4g64_kernel<MT, GROUPED, F16>, p.grid, NUM_THREADS, C::SMEM_BYTES, stream,
                           tm_w, tm_s, tm_b, tm_x, p);
 }
 
-template <int MT>
+template <int MT, bool F16 = false>
 int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const uint16_t* biases,
            uint16_t* y, void* ws, int M, int K, int N, int num_sms, int dev,
            cudaStream_t stream) {
@@ -844,10 +875,11 @@ int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const
   if (st != DFL_OK) return st;
   // x [M, K] bf16 in boxes of [64 K x MT rows], 128-byte swizzle (the UMMA
   // K-major layout); rows >= M read as zero.
-  st = host::make_tmap_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, uint64_t(K), uint64_t(M),
+  st = host::make_tmap_2d(&tm_x, F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                          x, uint64_t(K), uint64_t(M),
                           uint64_t(K) * 2, GS, MT, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != DFL_OK) return st;
-  return launch_kernel<MT, false>(tm_w, tm_s, tm_b, tm_x, p, dev, stream);
+  return launch_kernel<MT, false, F16>(tm_w, tm_s, tm_b, tm_x, p, dev, stream);
 }
 
 }  // namespace qmm
@@ -867,27 +899,45 @@ extern "C" size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* statu
   return dfl::qmm::workspace_bytes_for(M, K, N, sms);
 }
 
+namespace dfl {
+namespace qmm {
+template <bool F16>
+int verify_entry(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
+                 const uint16_t* biases, uint16_t* y, void* workspace, size_t workspace_bytes,
+                 int M, int K, int N, void* stream) {
+  if (M < 1 || M > 32 || K < 64 || K % 64 != 0 || N < 1 || N > kMaxTiles * BN)
+    return DFL_ERR_BAD_SHAPE;
+  if (!x || !w_q || !scales || !biases || !y) return DFL_ERR_NULL_POINTER;
+  if (!host::aligned(x, 16) || !host::aligned(w_q, 16) || !host::aligned(scales, 2) ||
+      !host::aligned(biases, 2) || !host::aligned(y, 2))
+    return DFL_ERR_MISALIGNED;
+  int dev, sms;
+  int st = host::current_device(&dev, &sms);
+  if (st != DFL_OK) return st;
+  const size_t need = workspace_bytes_for(M, K, N, sms);
+  if (!workspace || workspace_bytes < need) return DFL_ERR_WORKSPACE;
+  if (!host::aligned(workspace, 16)) return DFL_ERR_MISALIGNED;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (choose_mt(M) == 16)
+    return launch<16, F16>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
+  return launch<32, F16>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
+}
+}  // namespace qmm
+}  // namespace dfl
+
 extern "C" int dfl_verify_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
                                     const uint16_t* biases, uint16_t* y, void* workspace,
                                     size_t workspace_bytes, int M, int K, int N, void* stream) {
-  if (M < 1 || M > 32 || K < 64 || K % 64 != 0 || N < 1 ||
-      N > dfl::qmm::kMaxTiles * dfl::qmm::BN)
-    return DFL_ERR_BAD_SHAPE;
-  if (!x || !w_q || !scales || !biases || !y) return DFL_ERR_NULL_POINTER;
-  if (!dfl::host::aligned(x, 16) || !dfl::host::aligned(w_q, 16) ||
-      !dfl::host::aligned(scales, 2) || !dfl::host::aligned(biases, 2) ||
-      !dfl::host::aligned(y, 2))
-    return DFL_ERR_MISALIGNED;
-  int dev, sms;
-  int st = dfl::host::current_device(&dev, &sms);
-  if (st != DFL_OK) return st;
-  const size_t need = dfl::qmm::workspace_bytes_for(M, K, N, sms);
-  if (!workspace || workspace_bytes < need) return DFL_ERR_WORKSPACE;
-  if (!dfl::host::aligned(workspace, 16)) return DFL_ERR_MISALIGNED;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (dfl::qmm::choose_mt(M) == 16)
-    return dfl::qmm::launch<16>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
-  return dfl::qmm::launch<32>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
+  return dfl::qmm::verify_entry<false>(x, w_q, scales, biases, y, workspace, workspace_bytes, M, K,
+                                       N, stream);
+}
+
+extern "C" int dfl_verify_qmm_w4g64_f16(const uint16_t* x, const uint32_t* w_q,
+                                        const uint16_t* scales, const uint16_t* biases,
+                                        uint16_t* y, void* workspace, size_t workspace_bytes,
+                                        int M, int K, int N, void* stream) {
+  return dfl::qmm::verify_entry<true>(x, w_q, scales, biases, y, workspace, workspace_bytes, M, K,
+                                      N, stream);
 }
 
 // ------------------------------------------------------------------ MoE

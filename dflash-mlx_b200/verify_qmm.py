@@ -45,15 +45,24 @@ def workspace_bytes(m: int, k: int, n: int) -> int:
     return int(nbytes)
 
 
+_ENTRY_BY_DTYPE = {torch.bfloat16: "dfl_verify_qmm_w4g64",
+                   torch.float16: "dfl_verify_qmm_w4g64_f16"}
+
+
 def qmm_w4g64(x2: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
               out: torch.Tensor | None = None) -> torch.Tensor:
-    """``x2 [M, K] @ dequant(w_q).T`` through the C ABI -> bf16 ``[M, N]``."""
+    """``x2 [M, K] @ dequant(w_q).T`` through the C ABI -> ``[M, N]`` in x's dtype.
+
+    Activations, scales and biases are all bfloat16 or all float16 (the two
+    kernel instantiations of the reference, ``verify_linear.py:163-164``)."""
     for t, name in ((x2, "x"), (w_q, "w"), (scales, "scales"), (biases, "biases")):
         require_cuda(t, name)
-    if x2.dtype != torch.bfloat16:
-        raise NotImplementedError(f"activations must be bfloat16, got {x2.dtype}")
-    if scales.dtype != torch.bfloat16 or biases.dtype != torch.bfloat16:
-        raise NotImplementedError("scales and biases must be bfloat16")
+    entry = _ENTRY_BY_DTYPE.get(x2.dtype)
+    if entry is None:
+        raise NotImplementedError(f"activations must be bfloat16 or float16, got {x2.dtype}")
+    if scales.dtype != x2.dtype or biases.dtype != x2.dtype:
+        raise NotImplementedError(
+            f"scales/biases ({scales.dtype}, {biases.dtype}) must match the activations' {x2.dtype}")
     w_q = as_u32_bits(w_q)
     x2 = x2.contiguous()
     scales = scales.contiguous()
@@ -65,10 +74,10 @@ def qmm_w4g64(x2: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases:
     if scales.shape != (n, k // 64) or biases.shape != (n, k // 64):
         raise ValueError("scales/biases must be [N, K/64]")
     if out is None:
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=x2.device)
+        out = torch.empty((m, n), dtype=x2.dtype, device=x2.device)
     if m == 0 or n == 0:
         return out
-    lib = _lib.load()
+    fn = getattr(_lib.load(), entry)
     with torch.cuda.device(x2.device):
         sp = stream_ptr(x2.device)
         for r0 in range(0, m, MAX_ROWS_PER_CALL):
@@ -77,10 +86,9 @@ def qmm_w4g64(x2: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases:
             ws = workspace(x2.device, need)
             xs = x2[r0:r1]
             ys = out[r0:r1]
-            st = lib.dfl_verify_qmm_w4g64(xs.data_ptr(), w_q.data_ptr(), scales.data_ptr(),
-                                          biases.data_ptr(), ys.data_ptr(), ws.data_ptr(),
-                                          ws.numel(), r1 - r0, k, n, sp)
-            _lib.check("dfl_verify_qmm_w4g64", st)
+            st = fn(xs.data_ptr(), w_q.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                    ys.data_ptr(), ws.data_ptr(), ws.numel(), r1 - r0, k, n, sp)
+            _lib.check(entry, st)
     return out
 
 

@@ -73,6 +73,14 @@ int dfl_verify_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t*
                          const uint16_t* biases, uint16_t* y, void* workspace,
                          size_t workspace_bytes, int M, int K, int N, void* stream);
 
+/* The same contract with x, scales, biases and y all fp16 (the reference
+ * builds a bf16 and an fp16 kernel per layer, dflash_mlx/verify_linear.py:
+ * 163-164, and dispatches on x.dtype, verify_linear.py:241-247).  Uses the
+ * same workspace size and the same counter rules. */
+int dfl_verify_qmm_w4g64_f16(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
+                             const uint16_t* biases, uint16_t* y, void* workspace,
+                             size_t workspace_bytes, int M, int K, int N, void* stream);
+
 /* Workspace bytes dfl_verify_qmm_w4g64 needs for this shape on the current
  * device; 0 with *status != DFL_OK on error. */
 size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status);

@@ -49,32 +49,53 @@ def unpack_nibbles(w_q: np.ndarray) -> np.ndarray:
     return out.reshape(n, kp * 8)
 
 
+def _to_f32(bits: np.ndarray, dtype: str) -> np.ndarray:
+    if dtype == "bf16":
+        return bf16.to_f32(bits)
+    return np.asarray(bits, np.uint16).view(np.float16).astype(np.float32)
+
+
+def _round(x: np.ndarray, dtype: str) -> np.ndarray:
+    if dtype == "bf16":
+        return bf16.round_f32(x)
+    return np.asarray(x, np.float32).astype(np.float16).astype(np.float32)
+
+
+def _from_f32(x: np.ndarray, dtype: str) -> np.ndarray:
+    if dtype == "bf16":
+        return bf16.from_f32(x)
+    return np.asarray(x, np.float32).astype(np.float16).view(np.uint16)
+
+
 def dequantize(w_q: np.ndarray, scales: np.ndarray, biases: np.ndarray,
-               group_size: int = GROUP_SIZE) -> np.ndarray:
-    """Dequantised weights as float32 values that are exactly bf16 (``verify_qmm.py:249``)."""
+               group_size: int = GROUP_SIZE, dtype: str = "bf16") -> np.ndarray:
+    """Dequantised weights ``float(nib) * s + b`` rounded to the activation
+    dtype (``verify_qmm.py:249``), as float32 values.  ``scales`` / ``biases``
+    are bit patterns of that dtype ("bf16" or "f16")."""
     nib = unpack_nibbles(w_q).astype(np.float32)
     n, k = nib.shape
-    s = np.repeat(bf16.to_f32(scales), group_size, axis=1)[:, :k]
-    b = np.repeat(bf16.to_f32(biases), group_size, axis=1)[:, :k]
-    return bf16.round_f32(nib * s + b)
+    s = np.repeat(_to_f32(scales, dtype), group_size, axis=1)[:, :k]
+    b = np.repeat(_to_f32(biases, dtype), group_size, axis=1)[:, :k]
+    return _round(nib * s + b, dtype)
 
 
 def qmm(x: np.ndarray, w_q: np.ndarray, scales: np.ndarray, biases: np.ndarray,
-        group_size: int = GROUP_SIZE, accum=np.float64) -> np.ndarray:
-    """``y = x @ dequant(W).T`` -> bf16 bit patterns ``[M, N]``.
+        group_size: int = GROUP_SIZE, accum=np.float64, dtype: str = "bf16") -> np.ndarray:
+    """``y = x @ dequant(W).T`` -> bit patterns ``[M, N]`` of ``dtype``.
 
-    ``x`` is bf16 bits ``[M, K]``.  ``accum`` selects the accumulation dtype:
-    float64 for golden values, float32 for the timed CPU restatement.
+    ``x`` holds bits of ``dtype`` ("bf16" or "f16") ``[M, K]``.  ``accum``
+    selects the accumulation dtype: float64 for golden values, float32 for the
+    timed CPU restatement.
     """
-    xf = bf16.to_f32(x).astype(accum)
+    xf = _to_f32(x, dtype).astype(accum)
     n = w_q.shape[0]
     y = np.empty((xf.shape[0], n), dtype=np.float32)
     step = 2048
     for r0 in range(0, n, step):
         w = dequantize(w_q[r0:r0 + step], scales[r0:r0 + step], biases[r0:r0 + step],
-                       group_size).astype(accum)
+                       group_size, dtype).astype(accum)
         y[:, r0:r0 + step] = (xf @ w.T).astype(np.float32)
-    return bf16.from_f32(y)
+    return _from_f32(y, dtype)
 
 
 def qmm_f32(x: np.ndarray, w_q: np.ndarray, scales: np.ndarray, biases: np.ndarray,
@@ -84,7 +105,7 @@ def qmm_f32(x: np.ndarray, w_q: np.ndarray, scales: np.ndarray, biases: np.ndarr
     return (bf16.to_f32(x).astype(np.float64) @ w.T).astype(np.float32)
 
 
-def affine_quantize(w: np.ndarray, group_size: int = GROUP_SIZE):
+def affine_quantize(w: np.ndarray, group_size: int = GROUP_SIZE, dtype: str = "bf16"):
     """Min/max affine 4-bit quantiser used only to build test inputs.
 
     The reference's parity harness quantises random fp weights with
@@ -93,7 +114,8 @@ def affine_quantize(w: np.ndarray, group_size: int = GROUP_SIZE):
     restatement of the published affine scheme (scale = range / 15,
     bias = group minimum, q = round((w - bias) / scale)); the kernels under
     test only see its output, so the exact tie rules of MLX's quantiser do
-    not affect parity.  Returns (w_q uint32, scales bf16 bits, biases bf16 bits).
+    not affect parity.  Returns (w_q uint32, scales bits, biases bits) with
+    scales/biases in ``dtype`` ("bf16" or "f16").
     """
     w = np.asarray(w, dtype=np.float32)
     n, k = w.shape
@@ -102,15 +124,16 @@ def affine_quantize(w: np.ndarray, group_size: int = GROUP_SIZE):
     wmin = g.min(axis=2)
     wmax = g.max(axis=2)
     scale = np.maximum((wmax - wmin) / 15.0, 1e-7).astype(np.float32)
-    s_bits = bf16.from_f32(scale)
-    b_bits = bf16.from_f32(wmin)
-    s = bf16.to_f32(s_bits)[:, :, None]
-    b = bf16.to_f32(b_bits)[:, :, None]
+    s_bits = _from_f32(scale, dtype)
+    b_bits = _from_f32(wmin, dtype)
+    s = _to_f32(s_bits, dtype)[:, :, None]
+    b = _to_f32(b_bits, dtype)[:, :, None]
     q = np.clip(np.rint((g - b) / s), 0, 15).astype(np.uint8).reshape(n, k)
     return pack_nibbles(q), s_bits, b_bits
 
 
-def synth_weights(rng: np.random.Generator, n: int, k: int, group_size: int = GROUP_SIZE):
+def synth_weights(rng: np.random.Generator, n: int, k: int, group_size: int = GROUP_SIZE,
+                  dtype: str = "bf16"):
     """BASELINE config-0 weight distribution.
 
     q ~ U{0..15}; scales bf16 ~ U(0.004, 0.02) per (row, group);
@@ -120,18 +143,18 @@ def synth_weights(rng: np.random.Generator, n: int, k: int, group_size: int = GR
     g = k // group_size
     s = rng.uniform(0.004, 0.02, size=(n, g)).astype(np.float32)
     b = (-8.0 * s + rng.standard_normal((n, g)).astype(np.float32) * 0.1 * s).astype(np.float32)
-    return pack_nibbles(q), bf16.from_f32(s), bf16.from_f32(b)
+    return pack_nibbles(q), _from_f32(s, dtype), _from_f32(b, dtype)
 
 
-def synth_x(rng: np.random.Generator, m: int, k: int) -> np.ndarray:
-    """Activations bf16 ~ N(0, 1) as bit patterns."""
-    return bf16.from_f32(rng.standard_normal((m, k)).astype(np.float32))
+def synth_x(rng: np.random.Generator, m: int, k: int, dtype: str = "bf16") -> np.ndarray:
+    """Activations ~ N(0, 1) as bit patterns of ``dtype``."""
+    return _from_f32(rng.standard_normal((m, k)).astype(np.float32), dtype)
 
 
-def max_abs_rel(y: np.ndarray, ref: np.ndarray):
+def max_abs_rel(y: np.ndarray, ref: np.ndarray, dtype: str = "bf16"):
     """The reference harness metric (``tests/test_verify_qmm_parity.py:68-70``)."""
-    a = bf16.to_f32(y).astype(np.float64)
-    r = bf16.to_f32(ref).astype(np.float64)
+    a = _to_f32(y, dtype).astype(np.float64)
+    r = _to_f32(ref, dtype).astype(np.float64)
     max_abs = float(np.max(np.abs(a - r))) if a.size else 0.0
     max_rel = max_abs / (float(np.max(np.abs(r))) + 1e-3) if r.size else 0.0
     return max_abs, max_rel
