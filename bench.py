@@ -205,7 +205,7 @@ def run_ours(args):
 
     shape = StackShape(layers=args.layers)
     step = VerifyStep(dev, requests=args.requests_per_gpu, shape=shape, rank=rank, world=world,
-                      group=group)
+                      group=group, weight_layout=args.weight_layout)
     sh = step.shape
     b = args.requests_per_gpu
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -294,6 +294,7 @@ def run_ours(args):
                             "M=16 per request) + config3 (lm_head 248320x5120 bf16, vocab split over "
                             "ranks) + config4 (48-layer GDN tape-replay rollback)",
                 "requests_per_gpu": b, "tokens_per_request": sh.block,
+                "weight_layout": args.weight_layout,
                 "parallelism": f"request-DP x{world}, lm_head vocab split x{world}",
                 "l2": "inputs larger than L2 (12.3 GB of packed weights per step)",
                 "qmm_ms_per_step": t_qmm / args.steps * 1e3,
@@ -333,6 +334,9 @@ def main():
     ap.add_argument("--layers", type=int, default=64,
                     help="decoder layers of the qmm stack (64 = the benchmark; fewer only for "
                          "profiling small cases)")
+    ap.add_argument("--weight-layout", choices=["mlx", "pairs"], default="pairs",
+                    help="int4 nibble order of the stack's weights: the reference's MLX packing, "
+                         "or repacked once at load into the kernel's pair-packed order")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -23,7 +23,7 @@ from .recurrent_rollback_cache import (
     clear_rollback_state,
     restore_after_acceptance,
 )
-from .verify_qmm import is_enabled, verify_matmul, qmm_w4g64
+from .verify_qmm import is_enabled, verify_matmul, qmm_w4g64, repack_pairs
 from .verify_linear import (
     QuantizedLinear,
     VerifyQuantizedLinear,
@@ -44,6 +44,7 @@ __all__ = [
     "is_enabled",
     "verify_matmul",
     "qmm_w4g64",
+    "repack_pairs",
     "QuantizedLinear",
     "VerifyQuantizedLinear",
     "install_verify_linears",

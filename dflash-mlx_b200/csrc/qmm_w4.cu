@@ -49,6 +49,7 @@ namespace dfl {
 namespace qmm {
 
 constexpr int BN = 128;           // output channels per tile (UMMA M)
+constexpr int kMaxGrid = 160;     // CTAs of a dense launch (one per SM; B200 has 148)
 constexpr int UNIT_K = 512;       // K per pipeline stage (8 quant groups)
 constexpr int GS = 64;            // quant group size (one TMEM A slot)
 constexpr int NSUB = UNIT_K / GS; // 8 sub-blocks per stage
@@ -67,7 +68,7 @@ constexpr int BAR_ID_EPI = 1;            // named barrier of the epilogue warps
 constexpr int SBC = 4;                   // units per scale/bias chunk (32 groups)
 static_assert(NSUB % NUM_MMA_WARPS == 0, "sub-block split");
 
-template <int MT>
+template <int MT, bool PW = false>
 struct Cfg {
   static constexpr int PACK_BYTES = BN * UNIT_K / 2;  // 32 KB
   static constexpr int STAGE_BYTES = PACK_BYTES;
@@ -79,7 +80,9 @@ struct Cfg {
   static constexpr int OFF_SB = NSTAGE * STAGE_BYTES;
   static constexpr int XBLK_BYTES = MT * 128;         // one [MT x 64] bf16 block
   static constexpr int XSLOT_BYTES = NSUB * XBLK_BYTES;  // one unit of x
-  static constexpr int XS = (MT <= 16) ? 3 : 2;       // x ring depth (units)
+  // x ring depth (units); pair-packed weights have no permute step and
+  // use the smem it leaves for one more slot at MT = 16
+  static constexpr int XS = (MT <= 16) ? (PW ? 4 : 3) : 2;
   static constexpr int OFF_XRING = OFF_SB + 2 * SBC_BYTES;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM_BYTES = OFF_XRING + XS * XSLOT_BYTES + BAR_BYTES + 1024;
@@ -120,17 +123,33 @@ struct Params {
   const int* g_rows;       // [P][16]
   const int* g_out;        // [P][16]
   int tpp;                 // 128-row tiles per problem (all tiles when dense)
+  // Dense: first unit of every CTA's stream-K range, ubeg[grid] = total
+  // (computed on the host, see split_ranges).  Grouped launches know their
+  // unit count only on the device and split evenly.
+  int ubeg[kMaxGrid + 1];
 };
 
-__device__ __forceinline__ int unit_begin(int c, int total, int grid) {
-  return int((long long)c * total / grid);
+__device__ __forceinline__ int unit_begin(const Params& p, bool grouped, int c, int total) {
+  if (grouped) return int((long long)c * total / p.grid);
+  return p.ubeg[c];
 }
 
-// First CTA whose unit range contains unit u.
-__device__ __forceinline__ int cta_of_unit(int u, int total, int grid) {
-  // largest c with floor(c * total / grid) <= u
-  long long c = ((long long)(u + 1) * grid + total - 1) / total - 1;
-  return int(c);
+// The CTA whose (non-empty) unit range contains unit u: the largest c with
+// unit_begin(c) <= u.
+__device__ __forceinline__ int cta_of_unit(const Params& p, bool grouped, int u, int total) {
+  if (grouped) {
+    const long long c = ((long long)(u + 1) * p.grid + total - 1) / total - 1;
+    return int(c);
+  }
+  int lo = 0, hi = p.grid - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.ubeg[mid] <= u)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
 }
 
 // Eight nibbles (one packed word, low nibble first) -> four bf16x2 words
@@ -268,12 +287,13 @@ __device__ __forceinline__ void store_x_unit(uint32_t slot, int et,
   }
 }
 
-template <int MT, bool GROUPED, bool F16 = false>
+template <int MT, bool GROUPED, bool F16 = false, bool PW = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     qmm_w4g64_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
                      const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_x,
-                     const Params p) {
-  using C = Cfg<MT>;
+                     const __grid_constant__ Params p) {
+  static_assert(!(PW && GROUPED), "pair-packed weights: dense layers only");
+  using C = Cfg<MT, PW>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -308,8 +328,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // the workspace; weight loads and dequant start at once.
   if (GROUPED) griddep_wait();
   const int total = GROUPED ? (*p.g_count) * tpp * ku : p.total_units;
-  const int u0 = unit_begin(cta, total, p.grid);
-  const int u1 = unit_begin(cta + 1, total, p.grid);
+  const int u0 = unit_begin(p, GROUPED, cta, total);
+  const int u1 = unit_begin(p, GROUPED, cta + 1, total);
   const int n_units = u1 - u0;
 
   if (threadIdx.x == 0) {
@@ -451,7 +471,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           buf = acc_it & 1;
           wait(&accempty[buf], ((acc_it >> 1) & 1) ^ 1);
         }
-        wait(&xfull[xs], (it / C::XS) & 1);
+        wait(PW ? &xtma[xs] : &xfull[xs], (it / C::XS) & 1);
         const uint32_t d_tmem = tmem_base + C::ACC_COL0 + buf * C::ACC_COLS + j * MT;
         const uint64_t slot_desc = ring_desc + kSlotDesc * xs;
         uint32_t acc0 = seg_start ? 0u : 1u;
@@ -580,8 +600,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     //     (twice the bytes; per-thread copies would cost more issue slots).
     // Grouped: rows are gathered through the route table with plain loads,
     // one unit ahead.
+    // Pair-packed weights (PW) dequantise to natural K order: x then goes by
+    // TMA straight into its slot, XS units ahead, and the MMAs wait on the
+    // copy itself (no permutation, no xfull hand-off).
     constexpr int XD = C::XS - 1;
-    constexpr bool X_CP = (MT <= 16);
+    constexpr bool X_CP = (MT <= 16) && !PW;
     auto x_chunk = [&](int t, int& b, int& rr, int& c) {
       const int idx = et + 128 * t;
       c = idx & 7;
@@ -615,6 +638,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     };
     auto stage_x = [&](int ix) {
+      if constexpr (PW) {
+        if (et == 0) issue_x(ix);
+        __syncwarp();
+        return;
+      }
       const int xs = ix % C::XS;
       if constexpr (GROUPED) {
         if (ix >= C::XS) wait(&xfree[xs], ((ix / C::XS) - 1) & 1);
@@ -660,7 +688,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int staged = 0;  // units of x staged so far
     griddep_wait();
     if (n_units > 0) {
-      if constexpr (GROUPED) {
+      if constexpr (PW) {
+        // stage_x only issues: nothing to prefetch ahead of it
+      } else if constexpr (GROUPED) {
         load_x_unit<MT, GROUPED>(p, (u0 % ku) * UNIT_K, u0 / (ku * tpp), et, xr);
       } else {
         if (X_CP || et == 0)
@@ -714,7 +744,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // is also the end of its range, so its weight ring is free to receive
         // the others' partials by bulk copy.  Sources are summed in CTA order,
         // so the result is bit-reproducible.
-        const int c_lo = cta_of_unit(t * ku, total, p.grid);
+        const int c_lo = cta_of_unit(p, GROUPED, t * ku, total);
         if (cta != c_lo) {
           float* mine = p.partials + ((size_t)(cta * 2) * MT) * BN;
 #pragma unroll
@@ -723,7 +753,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (et == 0) red_release_add(&p.counters[t], 1);
           continue;
         }
-        const int c_hi = cta_of_unit(t * ku + ku - 1, total, p.grid);
+        const int c_hi = cta_of_unit(p, GROUPED, t * ku + ku - 1, total);
         if (et == 0) {
           const bool ok = spin_acquire_geq(&p.counters[t], c_hi - c_lo, abort_word);
           fence_proxy_async_global();
@@ -792,6 +822,36 @@ inline int choose_mt(int M) { return M <= 16 ? 16 : 32; }
 // 128-row tile): N <= kMaxTiles * 128.
 constexpr size_t kCounterBytes = host::kWorkspaceCounterBytes;
 constexpr int kMaxTiles = int(kCounterBytes / sizeof(int));
+// Stream-K split skew of the dense launches (see split_weight).
+constexpr int kSplitSkew = 64;
+
+// Largest skew <= want (in steps of 8) that still leaves the last CTA a
+// share of at least two units, so that every CTA's range is non-empty (the
+// split-K reduction counts one contribution per CTA between the tile's first
+// and last CTA).  The mean weight is 1 - skew / 1024 and the last CTA's
+// 1 - skew / 256.
+inline int clamp_skew(int want, int total, int grid) {
+  const double avg = double(total) / grid;
+  int skew = want;
+  while (skew > 0 && avg * (1.0 - skew / 256.0) / (1.0 - skew / 1024.0) < 2.0) skew -= 8;
+  return skew > 0 ? skew : 0;
+}
+
+// Stream-K ranges: CTA c takes units [ubeg[c], ubeg[c + 1]).  The first half
+// of the CTAs weigh 1 each; from there the weight falls linearly to
+// 1 - skew / 256 at the last CTA.  Under programmatic dependent launch the
+// CTAs with the highest indices start last (they go to the SMs the previous
+// kernel frees last) and their first weights land after the others', so they
+// may take fewer units.  skew = 0 is the even split floor(c * total / grid).
+inline void split_ranges(int total, int grid, int skew, int* ubeg) {
+  const long long h = grid / 2, L = grid - h;
+  auto weight = [&](long long c) {
+    const long long d = c > h ? c - h : 0;
+    return 512LL * L * c - (long long)skew * d * (d + 1);
+  };
+  const long long wsum = weight(grid);
+  for (int c = 0; c <= grid; ++c) ubeg[c] = int((long long)total * weight(c) / wsum);
+}
 
 inline void geometry(int M, int K, int N, int num_sms, int* n_tiles, int* k_units, int* total,
                      int* grid) {
@@ -799,7 +859,8 @@ inline void geometry(int M, int K, int N, int num_sms, int* n_tiles, int* k_unit
   *n_tiles = (N + BN - 1) / BN;
   *k_units = (K + UNIT_K - 1) / UNIT_K;
   *total = *n_tiles * *k_units;
-  *grid = *total < num_sms ? *total : num_sms;
+  const int cap = num_sms < kMaxGrid ? num_sms : kMaxGrid;
+  *grid = *total < cap ? *total : cap;
 }
 
 inline size_t workspace_bytes_for(int M, int K, int N, int num_sms) {
@@ -836,19 +897,20 @@ inline int make_weight_maps(const uint32_t* w_q, const uint16_t* scales, const u
   return DFL_OK;
 }
 
-template <int MT, bool GROUPED, bool F16 = false>
+template <int MT, bool GROUPED, bool F16 = false, bool PW = false>
 int launch_kernel(const CUtensorMap& tm_w, const CUtensorMap& tm_s, const CUtensorMap& tm_b,
                   const CUtensorMap& tm_x,
                   const Params& p, int dev, cudaStream_t stream) {
-  using C = Cfg<MT>;
+  using C = Cfg<MT, PW>;
   static std::atomic<uint64_t> smem_done{0};
-  int st = host::ensure_smem(qmm_w4g64_kernel<MT, GROUPED, F16>, C::SMEM_BYTES, dev, smem_done);
+  int st = host::ensure_smem(qmm_w4g64_kernel<MT, GROUPED, F16, PW>, C::SMEM_BYTES, dev, smem_done);
   if (st != DFL_OK) return st;
-  return host::launch_pdl(qmm_w4g64_kernel<MT, GROUPED, F16>, p.grid, NUM_THREADS, C::SMEM_BYTES, stream,
+  return host::launch_pdl(qmm_w4g64_kernel<MT, GROUPED, F16, PW>, p.grid,
+                          NUM_THREADS, C::SMEM_BYTES, stream,
                           tm_w, tm_s, tm_b, tm_x, p);
 }
 
-template <int MT, bool F16 = false>
+template <int MT, bool F16 = false, bool PW = false>
 int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const uint16_t* biases,
            uint16_t* y, void* ws, int M, int K, int N, int num_sms, int dev,
            cudaStream_t stream) {
@@ -863,6 +925,7 @@ int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const
   p.N = N;
   geometry(M, K, N, num_sms, &p.n_tiles, &p.k_units, &p.total_units, &p.grid);
   p.tpp = p.n_tiles;
+  split_ranges(p.total_units, p.grid, clamp_skew(kSplitSkew, p.total_units, p.grid), p.ubeg);
   // Workspace layout: [tile counters, fixed size][fp32 partials].  The
   // counters sit at a fixed offset so that no call's partials ever overlap
   // another call's counters; every kernel leaves its counters at zero.
@@ -879,7 +942,7 @@ int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const
                           x, uint64_t(K), uint64_t(M),
                           uint64_t(K) * 2, GS, MT, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != DFL_OK) return st;
-  return launch_kernel<MT, false, F16>(tm_w, tm_s, tm_b, tm_x, p, dev, stream);
+  return launch_kernel<MT, false, F16, PW>(tm_w, tm_s, tm_b, tm_x, p, dev, stream);
 }
 
 }  // namespace qmm
@@ -901,7 +964,7 @@ extern "C" size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* statu
 
 namespace dfl {
 namespace qmm {
-template <bool F16>
+template <bool F16, bool PW = false>
 int verify_entry(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
                  const uint16_t* biases, uint16_t* y, void* workspace, size_t workspace_bytes,
                  int M, int K, int N, void* stream) {
@@ -919,11 +982,73 @@ int verify_entry(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
   if (!host::aligned(workspace, 16)) return DFL_ERR_MISALIGNED;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (choose_mt(M) == 16)
-    return launch<16, F16>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
-  return launch<32, F16>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
+    return launch<16, F16, PW>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
+  return launch<32, F16, PW>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
+}
+
+// Pair-packed nibble order: word p of a row holds columns 8p..8p+7 with
+// nibble j (bits 4j..4j+3) = column 8p + 2j and nibble 4 + j = column
+// 8p + 2j + 1 (j = 0..3).  The dequantiser's shift/mask sequence then yields
+// bf16 pairs in natural K order.  Each word maps to itself, so the repack
+// may run in place.
+__device__ __forceinline__ uint32_t pair_pack_word(uint32_t q) {
+  uint32_t r = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    r |= ((q >> (8 * j)) & 0xFu) << (4 * j);             // column 2j     -> nibble j
+    r |= ((q >> (8 * j + 4)) & 0xFu) << (4 * (j + 4));   // column 2j + 1 -> nibble 4 + j
+  }
+  return r;
+}
+
+__global__ void repack_pairs_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                    size_t n_vec) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n_vec;
+       i += size_t(gridDim.x) * blockDim.x) {
+    uint4 v = src[i];
+    v.x = pair_pack_word(v.x);
+    v.y = pair_pack_word(v.y);
+    v.z = pair_pack_word(v.z);
+    v.w = pair_pack_word(v.w);
+    dst[i] = v;
+  }
 }
 }  // namespace qmm
 }  // namespace dfl
+
+extern "C" int dfl_repack_w4_pairs(const uint32_t* src, uint32_t* dst, size_t n_words,
+                                   void* stream) {
+  if (n_words == 0) return DFL_OK;
+  if (!src || !dst) return DFL_ERR_NULL_POINTER;
+  if (n_words % 4 != 0) return DFL_ERR_BAD_SHAPE;
+  if (!dfl::host::aligned(src, 16) || !dfl::host::aligned(dst, 16)) return DFL_ERR_MISALIGNED;
+  int dev, sms;
+  int st = dfl::host::current_device(&dev, &sms);
+  if (st != DFL_OK) return st;
+  const size_t n_vec = n_words / 4;
+  const size_t want = (n_vec + 255) / 256;
+  const int blocks = int(want < size_t(sms) * 8 ? (want ? want : 1) : size_t(sms) * 8);
+  dfl::qmm::repack_pairs_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), n_vec);
+  return dfl::host::launch_status();
+}
+
+extern "C" int dfl_verify_qmm_w4g64_pairs(const uint16_t* x, const uint32_t* w_q,
+                                          const uint16_t* scales, const uint16_t* biases,
+                                          uint16_t* y, void* workspace, size_t workspace_bytes,
+                                          int M, int K, int N, void* stream) {
+  return dfl::qmm::verify_entry<false, true>(x, w_q, scales, biases, y, workspace,
+                                             workspace_bytes, M, K, N, stream);
+}
+
+extern "C" int dfl_verify_qmm_w4g64_pairs_f16(const uint16_t* x, const uint32_t* w_q,
+                                              const uint16_t* scales, const uint16_t* biases,
+                                              uint16_t* y, void* workspace,
+                                              size_t workspace_bytes, int M, int K, int N,
+                                              void* stream) {
+  return dfl::qmm::verify_entry<true, true>(x, w_q, scales, biases, y, workspace,
+                                            workspace_bytes, M, K, N, stream);
+}
 
 extern "C" int dfl_verify_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
                                     const uint16_t* biases, uint16_t* y, void* workspace,

@@ -45,19 +45,48 @@ def workspace_bytes(m: int, k: int, n: int) -> int:
     return int(nbytes)
 
 
-_ENTRY_BY_DTYPE = {torch.bfloat16: "dfl_verify_qmm_w4g64",
-                   torch.float16: "dfl_verify_qmm_w4g64_f16"}
+_ENTRY = {("mlx", torch.bfloat16): "dfl_verify_qmm_w4g64",
+          ("mlx", torch.float16): "dfl_verify_qmm_w4g64_f16",
+          ("pairs", torch.bfloat16): "dfl_verify_qmm_w4g64_pairs",
+          ("pairs", torch.float16): "dfl_verify_qmm_w4g64_pairs_f16"}
+
+
+def repack_pairs(w_q: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """MLX-packed int4 weights -> the pair-packed order (``out`` may be ``w_q``).
+
+    In the pair-packed order nibble ``j`` of each uint32 holds column
+    ``8p + 2j`` and nibble ``4 + j`` column ``8p + 2j + 1``; the qmm then
+    dequantises straight to natural K order and streams x without a
+    permutation step.  A load-time layout, like concatenating projections
+    that share an input: done once per weight, never per call.
+    """
+    require_cuda(w_q, "w")
+    src = as_u32_bits(w_q)
+    if not src.is_contiguous():
+        raise ValueError("weights must be contiguous")
+    dst = torch.empty_like(src) if out is None else as_u32_bits(out)
+    if dst.shape != src.shape or not dst.is_contiguous():
+        raise ValueError("out must be a contiguous tensor of the weights' shape")
+    with torch.cuda.device(src.device):
+        st = _lib.load().dfl_repack_w4_pairs(src.data_ptr(), dst.data_ptr(), src.numel(),
+                                             stream_ptr(src.device))
+    _lib.check("dfl_repack_w4_pairs", st)
+    return dst if out is None else out
 
 
 def qmm_w4g64(x2: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
-              out: torch.Tensor | None = None) -> torch.Tensor:
+              out: torch.Tensor | None = None, *, layout: str = "mlx") -> torch.Tensor:
     """``x2 [M, K] @ dequant(w_q).T`` through the C ABI -> ``[M, N]`` in x's dtype.
 
     Activations, scales and biases are all bfloat16 or all float16 (the two
-    kernel instantiations of the reference, ``verify_linear.py:163-164``)."""
+    kernel instantiations of the reference, ``verify_linear.py:163-164``).
+    ``layout`` is ``"mlx"`` (the reference's packing) or ``"pairs"``
+    (weights passed through :func:`repack_pairs`)."""
     for t, name in ((x2, "x"), (w_q, "w"), (scales, "scales"), (biases, "biases")):
         require_cuda(t, name)
-    entry = _ENTRY_BY_DTYPE.get(x2.dtype)
+    if layout not in ("mlx", "pairs"):
+        raise ValueError(f"unknown weight layout {layout!r}")
+    entry = _ENTRY.get((layout, x2.dtype))
     if entry is None:
         raise NotImplementedError(f"activations must be bfloat16 or float16, got {x2.dtype}")
     if scales.dtype != x2.dtype or biases.dtype != x2.dtype:

@@ -34,7 +34,7 @@ import torch
 from . import lm_head as _lm
 from .kernels import gated_delta_kernel_with_tape, tape_replay_
 from .moe import QuantWeight, silu_mul
-from .verify_qmm import qmm_w4g64
+from .verify_qmm import qmm_w4g64, repack_pairs
 
 
 @dataclass
@@ -90,8 +90,12 @@ class VerifyStep:
     """Owns the synthetic weights and state of one GPU and runs verify steps."""
 
     def __init__(self, device: torch.device, *, requests: int = 1, shape: Optional[StackShape] = None,
-                 rank: int = 0, world: int = 1, group=None, seed: int = 0):
+                 rank: int = 0, world: int = 1, group=None, seed: int = 0,
+                 weight_layout: str = "mlx"):
         self.dev = torch.device(device)
+        if weight_layout not in ("mlx", "pairs"):
+            raise ValueError(f"unknown weight layout {weight_layout!r}")
+        self.weight_layout = weight_layout
         self.shape = shape or StackShape()
         self.requests = int(requests)
         self.rank, self.world, self.group = rank, world, group
@@ -101,6 +105,11 @@ class VerifyStep:
         # the fused launch layout (q|k|v and gate|up concatenated along N)
         self.layers = [{name: _quant_weight(gen, self.dev, n, k) for name, n, k in sh.launches()}
                        for _ in range(sh.layers)]
+        if weight_layout == "pairs":
+            # load-time repack into the pair-packed nibble order (in place)
+            for lw in self.layers:
+                for qw in lw.values():
+                    repack_pairs(qw.q, out=qw.q)
         # this rank's vocabulary shard of the bf16 lm_head, N(0, 0.02)
         self.v_begin, v_len = _lm.vocab_shard(sh.vocab, rank, world)
         wgen = torch.Generator(device=self.dev).manual_seed(seed + 1000 + rank)
@@ -145,12 +154,13 @@ class VerifyStep:
         for r in range(self.requests):
             x = self.x[r * sh.block:(r + 1) * sh.block]
             a = self.attn_out[r * sh.block:(r + 1) * sh.block]
+            lay = self.weight_layout
             for lw in self.layers:
-                self.last_qkv = qmm_w4g64(x, lw["qkv"].q, lw["qkv"].s, lw["qkv"].b)
-                qmm_w4g64(a, lw["o"].q, lw["o"].s, lw["o"].b)
-                gu = qmm_w4g64(x, lw["gate_up"].q, lw["gate_up"].s, lw["gate_up"].b)
+                self.last_qkv = qmm_w4g64(x, lw["qkv"].q, lw["qkv"].s, lw["qkv"].b, layout=lay)
+                qmm_w4g64(a, lw["o"].q, lw["o"].s, lw["o"].b, layout=lay)
+                gu = qmm_w4g64(x, lw["gate_up"].q, lw["gate_up"].s, lw["gate_up"].b, layout=lay)
                 h = silu_mul(gu[:, :sh.inter], gu[:, sh.inter:])
-                self.last_down = qmm_w4g64(h, lw["down"].q, lw["down"].s, lw["down"].b)
+                self.last_down = qmm_w4g64(h, lw["down"].q, lw["down"].s, lw["down"].b, layout=lay)
 
     def _keys(self, hidden_all):
         self.keys = _lm.lm_head_argmax_keys(hidden_all, self.lm_w, v_begin=self.v_begin)

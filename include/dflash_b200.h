@@ -81,6 +81,25 @@ int dfl_verify_qmm_w4g64_f16(const uint16_t* x, const uint32_t* w_q, const uint1
                              const uint16_t* biases, uint16_t* y, void* workspace,
                              size_t workspace_bytes, int M, int K, int N, void* stream);
 
+/* Pair-packed weight order.  dfl_repack_w4_pairs rewrites MLX-packed int4
+ * words so that nibble j of word p holds column 8p + 2j and nibble 4 + j
+ * column 8p + 2j + 1 (j = 0..3); dst may equal src (each word maps to
+ * itself).  n_words % 4 == 0, both pointers 16-byte aligned.  A load-time
+ * layout of this library, not a reference format: the reference keeps MLX
+ * order and its kernels take that layout directly (verify_qmm.py:905).
+ * dfl_verify_qmm_w4g64_pairs / _pairs_f16 are dfl_verify_qmm_w4g64 / _f16
+ * on repacked weights (same arguments, workspace and results up to fp32
+ * summation order): the dequantiser then yields natural K order and x goes
+ * to shared memory by TMA without a permutation step. */
+int dfl_repack_w4_pairs(const uint32_t* src, uint32_t* dst, size_t n_words, void* stream);
+int dfl_verify_qmm_w4g64_pairs(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
+                               const uint16_t* biases, uint16_t* y, void* workspace,
+                               size_t workspace_bytes, int M, int K, int N, void* stream);
+int dfl_verify_qmm_w4g64_pairs_f16(const uint16_t* x, const uint32_t* w_q,
+                                   const uint16_t* scales, const uint16_t* biases, uint16_t* y,
+                                   void* workspace, size_t workspace_bytes, int M, int K, int N,
+                                   void* stream);
+
 /* Workspace bytes dfl_verify_qmm_w4g64 needs for this shape on the current
  * device; 0 with *status != DFL_OK on error. */
 size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status);

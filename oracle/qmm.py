@@ -49,6 +49,21 @@ def unpack_nibbles(w_q: np.ndarray) -> np.ndarray:
     return out.reshape(n, kp * 8)
 
 
+def pair_pack(w_q: np.ndarray) -> np.ndarray:
+    """MLX-packed uint32 ``[N, K/8]`` -> the kernel's pair-packed order.
+
+    Not a reference format: a load-time layout of this build in which nibble
+    ``j`` of word ``p`` holds column ``8p + 2j`` and nibble ``4 + j`` column
+    ``8p + 2j + 1`` (j = 0..3), so that the kernel's mask/shift dequantiser
+    emits columns in natural order.  Used only to check the repack kernel.
+    """
+    nib = unpack_nibbles(w_q)
+    n, k = nib.shape
+    g = nib.reshape(n, k // 8, 8)
+    order = np.array([0, 2, 4, 6, 1, 3, 5, 7])  # nibble slot -> column within 8
+    return pack_nibbles(g[:, :, order].reshape(n, k))
+
+
 def _to_f32(bits: np.ndarray, dtype: str) -> np.ndarray:
     if dtype == "bf16":
         return bf16.to_f32(bits)
