@@ -154,6 +154,24 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// Relaxed (gpu scope, L2-coherent) 32-bit global load / store.  Each aligned
+// 32-bit access is single-copy atomic, so a word that carries its own
+// validity bit can be polled without a separate flag.
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_relaxed_u32(uint32_t* addr, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+// Arrive at named barrier `id` of `count` threads without waiting for it.
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Release-add on a global counter (no return value): writes this thread
 // observed before it (including other threads' writes ordered by a barrier)
 // are visible to whoever acquires the new value.

@@ -1,19 +1,20 @@
 // Dense int4 g64 verify qmm for callers that cannot allocate device memory.
 //
 // Same kernel and arguments as dfl_verify_qmm_w4g64, but the split-K scratch
-// (tile counters + fp32 partial sums) lives in one fixed file-scope device
+// (fp32 partial sums) lives in one fixed file-scope device
 // array instead of a caller workspace:
 //   * kScratchBytes (8 MiB) is the limit; a call whose scratch need
 //     (dfl_verify_qmm_workspace_bytes for its shape) is larger returns
-//     DFL_ERR_SCRATCH_LIMIT.  For M <= 32 the need is 64 KB + 32 KB per SM,
-//     which fits for any part with at most 254 SMs (B200: 148 -> 4.8 MB).
+//     DFL_ERR_SCRATCH_LIMIT.  For M <= 32 the need is 64 KB + 16 KB per CTA
+//     (at most 160 CTAs), at most 2.6 MB (B200: 148 CTAs -> 2.4 MB).
 //   * The first call on a device resolves the array's address on that
 //     device (cudaGetSymbolAddress, with that device current); make it
 //     before any stream capture on that device.
-//   * Every call on a device shares the one array.  Each call clears the
-//     tile counters (which must start at zero) on its stream before the
-//     kernel, so calls in stream order are safe; calls that may overlap in
-//     time (different streams or host threads) race on the array.
+//   * Every call on a device shares the one array.  The first call on a
+//     device zero-fills it on its stream; each kernel clears the partial
+//     slots it consumes, so the array is zero again for the next call and
+//     calls in stream order are safe; calls that may overlap in time
+//     (different streams or host threads) race on the array.
 // Nothing here calls cudaMalloc / cudaFree or any allocating routine.
 
 namespace dfl {
@@ -32,8 +33,9 @@ inline DeviceScratch& scratch_slot(int dev) {
   return slots[dev];
 }
 
-// Device address of g_scratch on `dev` (the current device); resolved once.
-inline int scratch_for_device(int dev, void** out) {
+// Device address of g_scratch on `dev` (the current device); resolved once,
+// and zero-filled on `stream` by the first call.
+inline int scratch_for_device(int dev, cudaStream_t stream, void** out) {
   DeviceScratch& slot = scratch_slot(dev);
   void* p = slot.ptr.load(std::memory_order_acquire);
   if (!p) {
@@ -42,6 +44,10 @@ inline int scratch_for_device(int dev, void** out) {
     p = slot.ptr.load(std::memory_order_acquire);
     if (!p) {
       if (cudaGetSymbolAddress(&p, g_scratch) != cudaSuccess || p == nullptr) {
+        cudaGetLastError();
+        return DFL_ERR_CUDA;
+      }
+      if (cudaMemsetAsync(p, 0, kScratchBytes, stream) != cudaSuccess) {
         cudaGetLastError();
         return DFL_ERR_CUDA;
       }
@@ -70,15 +76,10 @@ extern "C" int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w
   if (st != DFL_OK) return st;
   if (qmm::workspace_bytes_for(M, K, N, sms) > qmm_noalloc::kScratchBytes)
     return DFL_ERR_SCRATCH_LIMIT;
-  void* scratch = nullptr;
-  st = qmm_noalloc::scratch_for_device(dev, &scratch);
-  if (st != DFL_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const size_t counter_bytes = size_t((N + qmm::BN - 1) / qmm::BN) * sizeof(int);
-  if (cudaMemsetAsync(scratch, 0, counter_bytes, s) != cudaSuccess) {
-    cudaGetLastError();
-    return DFL_ERR_CUDA;
-  }
+  void* scratch = nullptr;
+  st = qmm_noalloc::scratch_for_device(dev, s, &scratch);
+  if (st != DFL_OK) return st;
   if (qmm::choose_mt(M) == 16)
     return qmm::launch<16>(x, w_q, scales, biases, y, scratch, M, K, N, sms, dev, s);
   return qmm::launch<32>(x, w_q, scales, biases, y, scratch, M, K, N, sms, dev, s);

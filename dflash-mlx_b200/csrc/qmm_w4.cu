@@ -65,6 +65,8 @@ constexpr int NUM_THREADS = NUM_WARPS * 32;
 constexpr int TMEM_COLS = 512;
 constexpr int SUB_PER_MMA = NSUB / NUM_MMA_WARPS;  // sub-blocks per MMA warp per unit
 constexpr int BAR_ID_EPI = 1;            // named barrier of the epilogue warps
+constexpr int BAR_ID_RED = 2;            // dequant warps hand the split-K sum to the epilogue
+constexpr int BAR_ID_DQ = 3;             // the dequant warps among themselves
 constexpr int SBC = 4;                   // units per scale/bias chunk (32 groups)
 static_assert(NSUB % NUM_MMA_WARPS == 0, "sub-block split");
 
@@ -108,8 +110,7 @@ struct Params {
   const uint16_t* scales;  // [N, K/64]
   const uint16_t* biases;  // [N, K/64]
   uint16_t* y;             // [M, N]
-  float* partials;         // [grid][2][MT][BN]
-  int* counters;           // [n_tiles]
+  float* partials;         // [grid][MT][BN], low mantissa bit = valid
   int M, K, N;
   int n_tiles, k_units, total_units, grid;
   int sb_tma;              // scales/biases rows are 16-byte multiples (TMA path)
@@ -287,6 +288,62 @@ __device__ __forceinline__ void store_x_unit(uint32_t slot, int et,
   }
 }
 
+// Sum, in CTA order, of the split-K partials of CTAs c_first..c_last (the
+// contributors of the tile the calling CTA reduces), element tid + 512 j of
+// the [MT][BN] tile for j < EPT.  A partial word is valid once its lowest bit
+// is set (contributors tag what they store; a consumed slot is cleared to 0
+// here for the next call), so each word is polled until valid, bounded like
+// every other wait: past kWaitLimitNs it records kDevWaitTimeout and sets
+// the CTA abort word.
+template <int MT>
+__device__ __forceinline__ void reduce_partials(const Params& p, int c_first, int c_last, int tid,
+                                                volatile int* abort_word,
+                                                float (&sum)[MT * BN / (32 * 4 * NDG)]) {
+  constexpr int NT = 32 * 4 * NDG;
+  constexpr int EPT = MT * BN / NT;
+  constexpr int QB = 16 / EPT;  // sources per batch: 16 words in flight per thread
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) sum[j] = 0.f;
+  uint32_t* base = reinterpret_cast<uint32_t*>(p.partials);
+  for (int c0 = c_first; c0 <= c_last; c0 += QB) {
+    if (*abort_word) return;
+    const int nq = (c_last - c0 + 1) < QB ? (c_last - c0 + 1) : QB;
+    uint32_t v[QB][EPT];
+#pragma unroll
+    for (int q = 0; q < QB; ++q)
+#pragma unroll
+      for (int j = 0; j < EPT; ++j)
+        v[q][j] = q < nq ? ld_relaxed_u32(base + size_t(c0 + q) * MT * BN + tid + NT * j) : 1u;
+    const unsigned long long t0 = globaltimer_ns();
+    for (;;) {
+      bool all = true;
+#pragma unroll
+      for (int q = 0; q < QB; ++q)
+#pragma unroll
+        for (int j = 0; j < EPT; ++j)
+          if (!(v[q][j] & 1u)) {
+            all = false;
+            v[q][j] = ld_relaxed_u32(base + size_t(c0 + q) * MT * BN + tid + NT * j);
+          }
+      if (all) break;
+      if (*abort_word) return;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicExch(&g_device_error, kDevWaitTimeout);
+        *abort_word = 1;
+        return;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < QB; ++q)
+#pragma unroll
+      for (int j = 0; j < EPT; ++j)
+        if (q < nq) {
+          sum[j] += __uint_as_float(v[q][j]);
+          st_relaxed_u32(base + size_t(c0 + q) * MT * BN + tid + NT * j, 0u);
+        }
+  }
+}
+
 template <int MT, bool GROUPED, bool F16 = false, bool PW = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     qmm_w4g64_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
@@ -309,10 +366,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* sbempty = sbfull + 2;              // [2]       chunk read by the dequant warps
   uint64_t* accfull = sbempty + 2;             // [2]
   uint64_t* accempty = accfull + 2;            // [2]
-  uint64_t* redbar = accempty + 2;             // [1]       split-K partials landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(redbar + 1);
-  int* red_ok = reinterpret_cast<int*>(tmem_slot + 1);
-  volatile int* abort_word = reinterpret_cast<volatile int*>(red_ok + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto wait = [abort_word](uint64_t* bar, uint32_t parity) {
     return mbar_wait_abortable(bar, parity, abort_word);
   };
@@ -341,7 +396,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tm_b);
     }
     *abort_word = 0;
-    mbar_init(redbar, 1);
     for (int i = 0; i < C::NSTAGE; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 4 * NDG);
@@ -580,6 +634,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int jj = 0; jj < SPW; ++jj) mbar_arrive(&afull[slots[jj]]);
       }
     }
+    // The split-K sum of the tile this CTA reduces (the last of its range):
+    // the other CTAs' partials, polled and summed here while this CTA's last
+    // MMAs drain, handed to the epilogue through shared memory.
+    if (n_units > 0) {
+      const int t = (u1 - 1) / ku;
+      const int kb0 = (t == u0 / ku) ? (u0 - t * ku) : 0;
+      const int kb1 = u1 - t * ku;
+      if (!(kb0 == 0 && kb1 == ku) && cta_of_unit(p, GROUPED, t * ku, total) == cta) {
+        const int c_hi = cta_of_unit(p, GROUPED, t * ku + ku - 1, total);
+        constexpr int NT = 32 * 4 * NDG;
+        constexpr int EPT = MT * BN / NT;  // partial-sum elements per dequant thread
+        float sum[EPT];
+        reduce_partials<MT>(p, cta + 1, c_hi, threadIdx.x - WARP_DQ0 * 32, abort_word, sum);
+        named_bar_sync(BAR_ID_DQ, NT);  // every dequant warp is done with the stage ring
+        float* red = reinterpret_cast<float*>(smem);
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) red[threadIdx.x - WARP_DQ0 * 32 + NT * j] = sum[j];
+        named_bar_arrive(BAR_ID_RED, 128 + NT);
+      }
+    }
   } else {
     // ------------------------------------------------- x staging + epilogue
     const int quad = warp & 3;
@@ -738,66 +812,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         // Partial tile, split over CTAs c_lo..c_hi.  The tile is the last one
         // of c_lo's range and the first (or only) one of every other
-        // contributor's.  Contributors publish their fp32 partial and count it
-        // with a release-add (the named barrier orders the four warps' stores
-        // before it); c_lo reduces once it has finished its own part, which
-        // is also the end of its range, so its weight ring is free to receive
-        // the others' partials by bulk copy.  Sources are summed in CTA order,
-        // so the result is bit-reproducible.
+        // contributor's.  Contributors store their fp32 partial with the
+        // lowest mantissa bit set as a validity tag (a cleared slot reads 0,
+        // so no flag or fence round trip is needed); c_lo's dequant warps,
+        // idle once its range is converted, poll and sum the other CTAs'
+        // partials in CTA order while its own MMAs drain (reduce_partials),
+        // and clear the slots for the next call.  The epilogue adds its own
+        // accumulator to that sum, so the result is bit-reproducible.
         const int c_lo = cta_of_unit(p, GROUPED, t * ku, total);
         if (cta != c_lo) {
-          float* mine = p.partials + ((size_t)(cta * 2) * MT) * BN;
+          uint32_t* mine = reinterpret_cast<uint32_t*>(p.partials) + size_t(cta) * MT * BN;
 #pragma unroll
-          for (int m = 0; m < MT; ++m) __stcg(mine + m * BN + r, acc[m]);
-          named_bar_sync(BAR_ID_EPI, 128);
-          if (et == 0) red_release_add(&p.counters[t], 1);
+          for (int m = 0; m < MT; ++m) st_relaxed_u32(mine + m * BN + r, __float_as_uint(acc[m]) | 1u);
           continue;
         }
-        const int c_hi = cta_of_unit(p, GROUPED, t * ku + ku - 1, total);
-        if (et == 0) {
-          const bool ok = spin_acquire_geq(&p.counters[t], c_hi - c_lo, abort_word);
-          fence_proxy_async_global();
-          *red_ok = ok ? 1 : 0;
-        }
-        named_bar_sync(BAR_ID_EPI, 128);
-        if (!*red_ok) break;
-        constexpr int SRC_BYTES = MT * BN * 4;
-        constexpr int NB = (C::NSTAGE * C::STAGE_BYTES) / SRC_BYTES;  // sources per batch
-        const uint32_t ring0 = smem_u32(smem);
-        float sum[MT];
-#pragma unroll
-        for (int m = 0; m < MT; ++m) sum[m] = acc[m];
-        uint32_t red_phase = 0;
-        bool red_done = true;
-        for (int c0 = c_lo + 1; c0 <= c_hi; c0 += NB) {
-          const int nb = (c_hi - c0 + 1) < NB ? (c_hi - c0 + 1) : NB;
-          if (et == 0) {
-            mbar_arrive_expect_tx(redbar, uint32_t(nb * SRC_BYTES));
-            for (int q = 0; q < nb; ++q)
-              bulk_load(ring0 + q * SRC_BYTES, p.partials + ((size_t)((c0 + q) * 2) * MT) * BN,
-                        SRC_BYTES, redbar);
-          }
-          if (!named_bar_and(BAR_ID_EPI, 128, wait(redbar, red_phase))) {
-            red_done = false;
-            break;
-          }
-          red_phase ^= 1;
-          for (int q = 0; q < nb; ++q) {
-            const float* sp = reinterpret_cast<const float*>(smem + q * SRC_BYTES);
-#pragma unroll
-            for (int m = 0; m < MT; ++m) sum[m] += sp[m * BN + r];
-          }
-          named_bar_sync(BAR_ID_EPI, 128);  // batch read before the next overwrites it
-        }
-        if (!red_done) break;
+        named_bar_sync(BAR_ID_RED, 128 + 32 * 4 * NDG);
+        if (*abort_word) break;
+        const float* red = reinterpret_cast<const float*>(smem);
         if (n < p.N) {
 #pragma unroll
           for (int m = 0; m < MT; ++m)
             if (m < rows)
               p.y[(size_t)(GROUPED ? outrow[m] : m) * p.N + n] =
-                  to_out16<F16>(sum[m]);
+                  to_out16<F16>(acc[m] + red[m * BN + r]);
         }
-        if (et == 0) p.counters[t] = 0;
       }
     }
   }
@@ -867,7 +905,7 @@ inline size_t workspace_bytes_for(int M, int K, int N, int num_sms) {
   int n_tiles, k_units, total, grid;
   geometry(M, K, N, num_sms, &n_tiles, &k_units, &total, &grid);
   const int mt = choose_mt(M);
-  return kCounterBytes + size_t(grid) * 2 * mt * BN * sizeof(float);
+  return kCounterBytes + size_t(grid) * mt * BN * sizeof(float);
 }
 
 // Weight / scale / bias tensor maps over [E, N, K/8] and [E, N, K/64]
@@ -926,10 +964,8 @@ int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const
   geometry(M, K, N, num_sms, &p.n_tiles, &p.k_units, &p.total_units, &p.grid);
   p.tpp = p.n_tiles;
   split_ranges(p.total_units, p.grid, clamp_skew(kSplitSkew, p.total_units, p.grid), p.ubeg);
-  // Workspace layout: [tile counters, fixed size][fp32 partials].  The
-  // counters sit at a fixed offset so that no call's partials ever overlap
-  // another call's counters; every kernel leaves its counters at zero.
-  p.counters = reinterpret_cast<int*>(ws);
+  // Workspace layout: [64 KB header, unused by this kernel][one tagged fp32
+  // partial slot of MT x BN per CTA]; every kernel leaves the slots zero.
   p.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes);
   // TMA of scale/bias rows needs 16-byte multiples: K % 512 == 0.
   p.sb_tma = (K % UNIT_K == 0) && host::aligned(scales, 16) && host::aligned(biases, 16);
@@ -1080,7 +1116,7 @@ inline void grouped_geometry(int max_problems, int K, int N, int num_sms, int* t
 inline size_t grouped_workspace_bytes(int max_problems, int K, int N, int num_sms) {
   int tpp, ku, grid;
   grouped_geometry(max_problems, K, N, num_sms, &tpp, &ku, &grid);
-  return kCounterBytes + size_t(grid) * 2 * 16 * BN * sizeof(float);
+  return kCounterBytes + size_t(grid) * 16 * BN * sizeof(float);
 }
 
 }  // namespace qmm
@@ -1128,7 +1164,6 @@ extern "C" int dfl_moe_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const u
   p.N = N;
   qmm::grouped_geometry(max_problems, K, N, sms, &p.tpp, &p.k_units, &p.grid);
   p.n_tiles = max_problems * p.tpp;
-  p.counters = reinterpret_cast<int*>(workspace);
   p.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + qmm::kCounterBytes);
   p.sb_tma = (K % qmm::UNIT_K == 0) && host::aligned(scales, 16) && host::aligned(biases, 16);
   // route table layout (int32): [0] problem count P, then E expert ids,

@@ -61,10 +61,11 @@ int dfl_get_device_error(int* device_error);
  *   y       bf16 [M, N], row-major
  * Constraints: 1 <= M <= 32, K % 64 == 0, K >= 64, 1 <= N <= 2097152.
  * workspace: at least dfl_verify_qmm_workspace_bytes(M, K, N) bytes of
- * device memory, 16-byte aligned.  Its first 64 KB hold split-K tile
- * counters that must be zero before the first call (zero-fill the buffer
- * once); every call leaves them zero again, so one buffer serves any
- * sequence of calls in stream order.  The rest is fp32 partial sums.  One
+ * device memory, 16-byte aligned, zero before the first call (zero-fill it
+ * once): it holds split-K partial sums whose words carry a validity bit,
+ * and every call clears what it consumed, so one buffer serves any
+ * sequence of calls in stream order.  After a call that reported a device
+ * error (dfl_get_device_error) the buffer must be zero-filled again.  One
  * workspace must not be shared by calls that may run concurrently.
  * Replaces verify_matmul (dflash_mlx/verify_qmm.py:905-1022) and the
  * VerifyQuantizedLinear dispatch closure (dflash_mlx/verify_linear.py:118-309).
@@ -76,7 +77,7 @@ int dfl_verify_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t*
 /* The same contract with x, scales, biases and y all fp16 (the reference
  * builds a bf16 and an fp16 kernel per layer, dflash_mlx/verify_linear.py:
  * 163-164, and dispatches on x.dtype, verify_linear.py:241-247).  Uses the
- * same workspace size and the same counter rules. */
+ * same workspace size and the same workspace rules. */
 int dfl_verify_qmm_w4g64_f16(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
                              const uint16_t* biases, uint16_t* y, void* workspace,
                              size_t workspace_bytes, int M, int K, int N, void* stream);
@@ -110,11 +111,12 @@ size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status);
  * same results.  Split-K scratch is a fixed 8 MiB device array inside the
  * library, shared by every call on a device:
  *   - a shape whose dfl_verify_qmm_workspace_bytes exceeds 8 MiB returns
- *     DFL_ERR_SCRATCH_LIMIT (never for M <= 32 on parts with <= 254 SMs);
+ *     DFL_ERR_SCRATCH_LIMIT (never for M <= 32: the need is at most 2.6 MB);
  *   - the first call on a device looks the array up on that device (make it
  *     before any stream capture there);
- *   - each call zeroes the counters it uses on `stream` first, so calls in
- *     stream order are safe; calls that can overlap in time race.
+ *   - the first call on a device zero-fills the array on `stream`; every
+ *     call leaves it zero again, so calls in stream order are safe; calls
+ *     that can overlap in time race.
  * Allocates nothing. */
 int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
                                  const uint16_t* biases, uint16_t* y, int M, int K, int N,
