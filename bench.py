@@ -205,7 +205,8 @@ def run_ours(args):
 
     shape = StackShape(layers=args.layers)
     step = VerifyStep(dev, requests=args.requests_per_gpu, shape=shape, rank=rank, world=world,
-                      group=group, weight_layout=args.weight_layout)
+                      group=group, weight_layout=args.weight_layout,
+                      fuse_silu=args.weight_layout == "pairs" and not args.no_fuse_silu)
     sh = step.shape
     b = args.requests_per_gpu
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -273,7 +274,7 @@ def run_ours(args):
     # roofline of the dominant kernel (the int4 verify qmm)
     peak, peak_kind = _peaks()
     launches = len(sh.launches()) * sh.layers * b
-    bytes_per_step = sh.qmm_bytes_per_request() * b
+    bytes_per_step = sh.qmm_bytes_per_request(silu_fused=step.fuse_silu) * b
     achieved = bytes_per_step / (t_qmm / args.steps) / 1e9
     traffic, _ = _traffic_per_launch()
 
@@ -295,6 +296,7 @@ def run_ours(args):
                             "ranks) + config4 (48-layer GDN tape-replay rollback)",
                 "requests_per_gpu": b, "tokens_per_request": sh.block,
                 "weight_layout": args.weight_layout,
+                "mlp_silu_fused": step.fuse_silu,
                 "parallelism": f"request-DP x{world}, lm_head vocab split x{world}",
                 "l2": "inputs larger than L2 (12.3 GB of packed weights per step)",
                 "qmm_ms_per_step": t_qmm / args.steps * 1e3,
@@ -307,9 +309,11 @@ def run_ours(args):
                          "note": "achieved = algorithmic bytes of the qmm launches of a step (4 per "
                                  "layer: q|k|v, o, gate|up, down) / their CUDA-event time inside "
                                  "the timed region"},
-            # ours per step: 4 qmm + 1 SiLU*up per layer and request, lm_head argmax,
-            # accept, one tape replay over all GDN layers
-            "gpu_launches": args.steps * (launches + sh.layers * b + 2 + 1),
+            # ours per step: 4 qmm per layer and request (+ 1 SiLU*up launch unless it
+            # is fused into the gate|up epilogue), lm_head argmax, accept, one tape
+            # replay over all GDN layers
+            "gpu_launches": args.steps * (launches + (0 if step.fuse_silu else sh.layers * b)
+                                          + 2 + 1),
             "e2e": {"value": world * b / t_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "clocks": clk,
@@ -337,6 +341,8 @@ def main():
     ap.add_argument("--weight-layout", choices=["mlx", "pairs"], default="pairs",
                     help="int4 nibble order of the stack's weights: the reference's MLX packing, "
                          "or repacked once at load into the kernel's pair-packed order")
+    ap.add_argument("--no-fuse-silu", action="store_true",
+                    help="run SiLU*up as its own launch after the gate|up projection")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -23,7 +23,8 @@ from .recurrent_rollback_cache import (
     clear_rollback_state,
     restore_after_acceptance,
 )
-from .verify_qmm import is_enabled, verify_matmul, qmm_w4g64, repack_pairs
+from .verify_qmm import (is_enabled, verify_matmul, qmm_w4g64, repack_pairs, interleave_gate_up,
+                         gate_up_silu)
 from .verify_linear import (
     QuantizedLinear,
     VerifyQuantizedLinear,
@@ -45,6 +46,8 @@ __all__ = [
     "verify_matmul",
     "qmm_w4g64",
     "repack_pairs",
+    "interleave_gate_up",
+    "gate_up_silu",
     "QuantizedLinear",
     "VerifyQuantizedLinear",
     "install_verify_linears",

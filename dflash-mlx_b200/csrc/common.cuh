@@ -154,6 +154,25 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// bf16 / fp16 bits of silu(g) * u computed in fp32 from the bits of g and u
+// (the one definition every SiLU*up in this library uses).
+template <bool F16>
+__device__ __forceinline__ uint16_t silu_mul_bits(uint16_t gb, uint16_t ub) {
+  float g, u;
+  if constexpr (F16) {
+    g = __half2float(__ushort_as_half(gb));
+    u = __half2float(__ushort_as_half(ub));
+  } else {
+    g = __bfloat162float(__ushort_as_bfloat16(gb));
+    u = __bfloat162float(__ushort_as_bfloat16(ub));
+  }
+  const float s = g / (1.0f + expf(-g));
+  if constexpr (F16)
+    return __half_as_ushort(__float2half_rn(s * u));
+  else
+    return __bfloat16_as_ushort(__float2bfloat16_rn(s * u));
+}
+
 // Relaxed (gpu scope, L2-coherent) 32-bit global load / store.  Each aligned
 // 32-bit access is single-copy atomic, so a word that carries its own
 // validity bit can be polled without a separate flag.

@@ -94,10 +94,7 @@ __global__ void route_kernel(const float* logits, int T, int E, int k, int32_t* 
 __global__ void silu_mul_kernel(const uint16_t* gate, const uint16_t* up, uint16_t* out, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  const float g = __bfloat162float(__ushort_as_bfloat16(gate[i]));
-  const float u = __bfloat162float(__ushort_as_bfloat16(up[i]));
-  const float s = g / (1.0f + expf(-g));
-  out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(s * u));
+  out[i] = silu_mul_bits<false>(gate[i], up[i]);
 }
 
 // Same on row-strided inputs: out[r, c] (contiguous) from gate/up rows of
@@ -113,10 +110,7 @@ __global__ void silu_mul_rows_kernel(const uint16_t* gate, const uint16_t* up, i
   if (i >= rows * cols) return;
   const int r = i / cols, c = i - r * cols;
   const size_t j = (size_t)r * ld + c;
-  const float g = __bfloat162float(__ushort_as_bfloat16(gate[j]));
-  const float u = __bfloat162float(__ushort_as_bfloat16(up[j]));
-  const float s = g / (1.0f + expf(-g));
-  out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(s * u));
+  out[i] = silu_mul_bits<false>(gate[j], up[j]);
 }
 
 // y[t, c] = bf16( sum_j w[t, j] * pair_out[t * k + j, c]  (+ shared[t, c]) ), fp32 in slot order

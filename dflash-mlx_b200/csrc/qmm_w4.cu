@@ -214,6 +214,7 @@ __device__ __forceinline__ uint16_t to_out16(float v) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(v));
 }
 
+
 // Reorders the 8 bf16 of a 16-byte x chunk from k = 0..7 to the order the
 // dequantised A operand uses: 0, 4, 1, 5, 2, 6, 3, 7.
 __device__ __forceinline__ uint4 permute_x_chunk(uint4 v) {
@@ -344,12 +345,16 @@ __device__ __forceinline__ void reduce_partials(const Params& p, int c_first, in
   }
 }
 
-template <int MT, bool GROUPED, bool F16 = false, bool PW = false>
+template <int MT, bool GROUPED, bool F16 = false, bool PW = false, bool SILU = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     qmm_w4g64_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
                      const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ Params p) {
   static_assert(!(PW && GROUPED), "pair-packed weights: dense layers only");
+  // SILU: the weights are a gate|up pair interleaved in blocks of 32 rows
+  // (16 gate rows, then the 16 up rows of the same outputs); the epilogue
+  // writes h = silu(gate) * up, [M, N / 2], instead of the N projections.
+  static_assert(!(SILU && GROUPED), "fused SiLU epilogue: dense layers only");
   using C = Cfg<MT, PW>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -799,15 +804,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int n = (t - pi * tpp) * BN + r;
         const int rows = GROUPED ? p.g_m[pi] : p.M;
         const int* outrow = GROUPED ? p.g_out + pi * 16 : nullptr;
-        const bool full_tile = (kb0 == 0) && (kb1 == ku);
-        if (full_tile) {
-          if (n < p.N) {
+        // Final values of this thread's output channel n -> y.  With SILU,
+        // lanes 0-15 of each warp hold gate channels and lanes 16-31 the up
+        // channels of the same h columns (N % 32 == 0, so validity is
+        // warp-uniform); both are rounded to the activation dtype first, as
+        // the separate projections would be.
+        auto store_final = [&](const float (&v)[MT]) {
+          if (n >= p.N) return;
+          if constexpr (SILU) {
+            const int ldh = p.N >> 1;
+            const int hcol = (n >> 5) * 16 + (lane & 15);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              const uint32_t mine = to_out16<F16>(v[m]);
+              const uint32_t up = __shfl_down_sync(0xffffffffu, mine, 16);
+              if (lane < 16 && m < rows)
+                p.y[(size_t)m * ldh + hcol] = silu_mul_bits<F16>(uint16_t(mine), uint16_t(up));
+            }
+          } else {
 #pragma unroll
             for (int m = 0; m < MT; ++m)
               if (m < rows)
-                p.y[(size_t)(GROUPED ? outrow[m] : m) * p.N + n] =
-                    to_out16<F16>(acc[m]);
+                p.y[(size_t)(GROUPED ? outrow[m] : m) * p.N + n] = to_out16<F16>(v[m]);
           }
+        };
+        const bool full_tile = (kb0 == 0) && (kb1 == ku);
+        if (full_tile) {
+          store_final(acc);
           continue;
         }
         // Partial tile, split over CTAs c_lo..c_hi.  The tile is the last one
@@ -829,13 +852,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         named_bar_sync(BAR_ID_RED, 128 + 32 * 4 * NDG);
         if (*abort_word) break;
         const float* red = reinterpret_cast<const float*>(smem);
-        if (n < p.N) {
 #pragma unroll
-          for (int m = 0; m < MT; ++m)
-            if (m < rows)
-              p.y[(size_t)(GROUPED ? outrow[m] : m) * p.N + n] =
-                  to_out16<F16>(acc[m] + red[m * BN + r]);
-        }
+        for (int m = 0; m < MT; ++m) acc[m] += red[m * BN + r];
+        store_final(acc);
       }
     }
   }
@@ -935,20 +954,21 @@ inline int make_weight_maps(const uint32_t* w_q, const uint16_t* scales, const u
   return DFL_OK;
 }
 
-template <int MT, bool GROUPED, bool F16 = false, bool PW = false>
+template <int MT, bool GROUPED, bool F16 = false, bool PW = false, bool SILU = false>
 int launch_kernel(const CUtensorMap& tm_w, const CUtensorMap& tm_s, const CUtensorMap& tm_b,
                   const CUtensorMap& tm_x,
                   const Params& p, int dev, cudaStream_t stream) {
   using C = Cfg<MT, PW>;
   static std::atomic<uint64_t> smem_done{0};
-  int st = host::ensure_smem(qmm_w4g64_kernel<MT, GROUPED, F16, PW>, C::SMEM_BYTES, dev, smem_done);
+  int st = host::ensure_smem(qmm_w4g64_kernel<MT, GROUPED, F16, PW, SILU>, C::SMEM_BYTES, dev,
+                             smem_done);
   if (st != DFL_OK) return st;
-  return host::launch_pdl(qmm_w4g64_kernel<MT, GROUPED, F16, PW>, p.grid,
+  return host::launch_pdl(qmm_w4g64_kernel<MT, GROUPED, F16, PW, SILU>, p.grid,
                           NUM_THREADS, C::SMEM_BYTES, stream,
                           tm_w, tm_s, tm_b, tm_x, p);
 }
 
-template <int MT, bool F16 = false, bool PW = false>
+template <int MT, bool F16 = false, bool PW = false, bool SILU = false>
 int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const uint16_t* biases,
            uint16_t* y, void* ws, int M, int K, int N, int num_sms, int dev,
            cudaStream_t stream) {
@@ -978,7 +998,7 @@ int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const
                           x, uint64_t(K), uint64_t(M),
                           uint64_t(K) * 2, GS, MT, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != DFL_OK) return st;
-  return launch_kernel<MT, false, F16, PW>(tm_w, tm_s, tm_b, tm_x, p, dev, stream);
+  return launch_kernel<MT, false, F16, PW, SILU>(tm_w, tm_s, tm_b, tm_x, p, dev, stream);
 }
 
 }  // namespace qmm
@@ -1000,12 +1020,13 @@ extern "C" size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* statu
 
 namespace dfl {
 namespace qmm {
-template <bool F16, bool PW = false>
+template <bool F16, bool PW = false, bool SILU = false>
 int verify_entry(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
                  const uint16_t* biases, uint16_t* y, void* workspace, size_t workspace_bytes,
                  int M, int K, int N, void* stream) {
   if (M < 1 || M > 32 || K < 64 || K % 64 != 0 || N < 1 || N > kMaxTiles * BN)
     return DFL_ERR_BAD_SHAPE;
+  if (SILU && N % 32 != 0) return DFL_ERR_BAD_SHAPE;
   if (!x || !w_q || !scales || !biases || !y) return DFL_ERR_NULL_POINTER;
   if (!host::aligned(x, 16) || !host::aligned(w_q, 16) || !host::aligned(scales, 2) ||
       !host::aligned(biases, 2) || !host::aligned(y, 2))
@@ -1018,8 +1039,8 @@ int verify_entry(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
   if (!host::aligned(workspace, 16)) return DFL_ERR_MISALIGNED;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (choose_mt(M) == 16)
-    return launch<16, F16, PW>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
-  return launch<32, F16, PW>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
+    return launch<16, F16, PW, SILU>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
+  return launch<32, F16, PW, SILU>(x, w_q, scales, biases, y, workspace, M, K, N, sms, dev, s);
 }
 
 // Pair-packed nibble order: word p of a row holds columns 8p..8p+7 with
@@ -1075,6 +1096,24 @@ extern "C" int dfl_verify_qmm_w4g64_pairs(const uint16_t* x, const uint32_t* w_q
                                           int M, int K, int N, void* stream) {
   return dfl::qmm::verify_entry<false, true>(x, w_q, scales, biases, y, workspace,
                                              workspace_bytes, M, K, N, stream);
+}
+
+extern "C" int dfl_verify_qmm_w4g64_pairs_silu(const uint16_t* x, const uint32_t* w_q,
+                                               const uint16_t* scales, const uint16_t* biases,
+                                               uint16_t* h, void* workspace,
+                                               size_t workspace_bytes, int M, int K, int N,
+                                               void* stream) {
+  return dfl::qmm::verify_entry<false, true, true>(x, w_q, scales, biases, h, workspace,
+                                                   workspace_bytes, M, K, N, stream);
+}
+
+extern "C" int dfl_verify_qmm_w4g64_pairs_silu_f16(const uint16_t* x, const uint32_t* w_q,
+                                                   const uint16_t* scales,
+                                                   const uint16_t* biases, uint16_t* h,
+                                                   void* workspace, size_t workspace_bytes,
+                                                   int M, int K, int N, void* stream) {
+  return dfl::qmm::verify_entry<true, true, true>(x, w_q, scales, biases, h, workspace,
+                                                  workspace_bytes, M, K, N, stream);
 }
 
 extern "C" int dfl_verify_qmm_w4g64_pairs_f16(const uint16_t* x, const uint32_t* w_q,

@@ -121,6 +121,64 @@ def qmm_w4g64(x2: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases:
     return out
 
 
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """Row-interleave two ``[I, *]`` tensors in blocks of 16 rows:
+    ``[gate 0..15, up 0..15, gate 16..31, up 16..31, ...]`` -> ``[2I, *]``.
+
+    The layout :func:`gate_up_silu` takes for the packed weights, scales and
+    biases of an MLP's gate/up pair (a load-time layout, like concatenating
+    projections that share an input)."""
+    if gate.shape != up.shape or gate.shape[0] % 16 != 0:
+        raise ValueError("gate and up must have the same shape with rows % 16 == 0")
+    i = gate.shape[0]
+    return torch.stack((gate.reshape(i // 16, 16, *gate.shape[1:]),
+                        up.reshape(i // 16, 16, *up.shape[1:])), dim=1).reshape(2 * i, *gate.shape[1:])
+
+
+_SILU_ENTRY = {torch.bfloat16: "dfl_verify_qmm_w4g64_pairs_silu",
+               torch.float16: "dfl_verify_qmm_w4g64_pairs_silu_f16"}
+
+
+def gate_up_silu(x2: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """``silu(x2 @ Wg.T) * (x2 @ Wu.T)`` in one launch -> ``[M, I]``.
+
+    ``w_q`` / ``scales`` / ``biases`` are the gate and up projections
+    interleaved by :func:`interleave_gate_up`, weights pair-packed
+    (:func:`repack_pairs`).  Each projection is rounded to the activation
+    dtype before the SiLU, so the result equals :func:`silu_mul` of the two
+    projections computed separately by the same kernel."""
+    for t, name in ((x2, "x"), (w_q, "w"), (scales, "scales"), (biases, "biases")):
+        require_cuda(t, name)
+    entry = _SILU_ENTRY.get(x2.dtype)
+    if entry is None:
+        raise NotImplementedError(f"activations must be bfloat16 or float16, got {x2.dtype}")
+    if scales.dtype != x2.dtype or biases.dtype != x2.dtype:
+        raise NotImplementedError("scales/biases must match the activations' dtype")
+    w_q = as_u32_bits(w_q)
+    x2, scales, biases = x2.contiguous(), scales.contiguous(), biases.contiguous()
+    m, k = x2.shape
+    n = w_q.shape[0]
+    if w_q.shape[1] * 8 != k or n % 32 != 0:
+        raise ValueError(f"weight shape {tuple(w_q.shape)} does not fit K={k} (rows % 32 == 0)")
+    if scales.shape != (n, k // 64) or biases.shape != (n, k // 64):
+        raise ValueError("scales/biases must be [N, K/64]")
+    if out is None:
+        out = torch.empty((m, n // 2), dtype=x2.dtype, device=x2.device)
+    if m == 0:
+        return out
+    fn = getattr(_lib.load(), entry)
+    with torch.cuda.device(x2.device):
+        sp = stream_ptr(x2.device)
+        for r0 in range(0, m, MAX_ROWS_PER_CALL):
+            r1 = min(m, r0 + MAX_ROWS_PER_CALL)
+            ws = workspace(x2.device, workspace_bytes(r1 - r0, k, n))
+            st = fn(x2[r0:r1].data_ptr(), w_q.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                    out[r0:r1].data_ptr(), ws.data_ptr(), ws.numel(), r1 - r0, k, n, sp)
+            _lib.check(entry, st)
+    return out
+
+
 def verify_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                   *, transpose: bool = True, group_size: int = 64, bits: int = 4) -> torch.Tensor:
     """``x @ dequant(w).T`` for MLX affine int4 g64 weights (reference ``verify_qmm.py:905``)."""

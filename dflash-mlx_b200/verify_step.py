@@ -34,7 +34,7 @@ import torch
 from . import lm_head as _lm
 from .kernels import gated_delta_kernel_with_tape, tape_replay_
 from .moe import QuantWeight, silu_mul
-from .verify_qmm import qmm_w4g64, repack_pairs
+from .verify_qmm import gate_up_silu, qmm_w4g64, repack_pairs
 
 
 @dataclass
@@ -66,12 +66,14 @@ class StackShape:
         return [("qkv", self.q_out + 2 * self.kv_out, h), ("o", h, self.q_out),
                 ("gate_up", 2 * self.inter, h), ("down", h, self.inter)]
 
-    def qmm_bytes_per_request(self) -> int:
+    def qmm_bytes_per_request(self, silu_fused: bool = False) -> int:
         """Algorithmic bytes of one request's projection stack: packed weights +
-        bf16 scales and biases + bf16 activations in and out, per launch."""
+        bf16 scales and biases + bf16 activations in and out, per launch (the
+        fused gate|up launch writes silu(gate) * up: half its rows)."""
         total = 0
-        for _, n, k in self.launches():
-            total += n * k // 2 + 2 * 2 * n * (k // 64) + 2 * self.block * (k + n)
+        for name, n, k in self.launches():
+            n_out = n // 2 if (silu_fused and name == "gate_up") else n
+            total += n * k // 2 + 2 * 2 * n * (k // 64) + 2 * self.block * (k + n_out)
         return total * self.layers
 
     def qmm_flops_per_request(self) -> int:
@@ -91,11 +93,17 @@ class VerifyStep:
 
     def __init__(self, device: torch.device, *, requests: int = 1, shape: Optional[StackShape] = None,
                  rank: int = 0, world: int = 1, group=None, seed: int = 0,
-                 weight_layout: str = "mlx"):
+                 weight_layout: str = "mlx", fuse_silu: bool = False):
         self.dev = torch.device(device)
         if weight_layout not in ("mlx", "pairs"):
             raise ValueError(f"unknown weight layout {weight_layout!r}")
         self.weight_layout = weight_layout
+        if fuse_silu and weight_layout != "pairs":
+            raise ValueError("the fused SiLU epilogue takes pair-packed weights")
+        # fuse_silu: the gate|up weights are read as the gate and up rows
+        # interleaved in blocks of 16 (interleave_gate_up) and one launch
+        # writes silu(gate) * up
+        self.fuse_silu = bool(fuse_silu)
         self.shape = shape or StackShape()
         self.requests = int(requests)
         self.rank, self.world, self.group = rank, world, group
@@ -158,8 +166,11 @@ class VerifyStep:
             for lw in self.layers:
                 self.last_qkv = qmm_w4g64(x, lw["qkv"].q, lw["qkv"].s, lw["qkv"].b, layout=lay)
                 qmm_w4g64(a, lw["o"].q, lw["o"].s, lw["o"].b, layout=lay)
-                gu = qmm_w4g64(x, lw["gate_up"].q, lw["gate_up"].s, lw["gate_up"].b, layout=lay)
-                h = silu_mul(gu[:, :sh.inter], gu[:, sh.inter:])
+                if self.fuse_silu:
+                    h = gate_up_silu(x, lw["gate_up"].q, lw["gate_up"].s, lw["gate_up"].b)
+                else:
+                    gu = qmm_w4g64(x, lw["gate_up"].q, lw["gate_up"].s, lw["gate_up"].b, layout=lay)
+                    h = silu_mul(gu[:, :sh.inter], gu[:, sh.inter:])
                 self.last_down = qmm_w4g64(h, lw["down"].q, lw["down"].s, lw["down"].b, layout=lay)
 
     def _keys(self, hidden_all):

@@ -101,6 +101,25 @@ int dfl_verify_qmm_w4g64_pairs_f16(const uint16_t* x, const uint32_t* w_q,
                                    void* workspace, size_t workspace_bytes, int M, int K, int N,
                                    void* stream);
 
+/* Gate/up projection pair with SiLU*up fused into the epilogue, on
+ * pair-packed weights: w_q / scales / biases hold the gate and up rows
+ * interleaved in blocks of 32 (rows 32b..32b+15 = gate rows 16b..16b+15,
+ * rows 32b+16..32b+31 = up rows 16b..16b+15), N = 2 * intermediate,
+ * N % 32 == 0.  h [M, N/2] = silu(gate) * up with gate and up each rounded
+ * to the activation dtype first and the SiLU in fp32, exactly as
+ * dfl_silu_mul_bf16 on the two projections.  Same workspace rules.
+ * Replaces the MLP's gate_proj/up_proj pair and nn.silu(gate) * up of the
+ * verify forward (mlx-lm's MLP, reached from the target model's layers at
+ * dflash_mlx/engine/target_qwen_gdn.py:863-865). */
+int dfl_verify_qmm_w4g64_pairs_silu(const uint16_t* x, const uint32_t* w_q,
+                                    const uint16_t* scales, const uint16_t* biases, uint16_t* h,
+                                    void* workspace, size_t workspace_bytes, int M, int K, int N,
+                                    void* stream);
+int dfl_verify_qmm_w4g64_pairs_silu_f16(const uint16_t* x, const uint32_t* w_q,
+                                        const uint16_t* scales, const uint16_t* biases,
+                                        uint16_t* h, void* workspace, size_t workspace_bytes,
+                                        int M, int K, int N, void* stream);
+
 /* Workspace bytes dfl_verify_qmm_w4g64 needs for this shape on the current
  * device; 0 with *status != DFL_OK on error. */
 size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status);
