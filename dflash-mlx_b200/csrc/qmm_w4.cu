@@ -821,11 +821,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               if (lane < 16 && m < rows)
                 p.y[(size_t)m * ldh + hcol] = silu_mul_bits<F16>(uint16_t(mine), uint16_t(up));
             }
-          } else {
+          } else if constexpr (GROUPED) {
 #pragma unroll
             for (int m = 0; m < MT; ++m)
-              if (m < rows)
-                p.y[(size_t)(GROUPED ? outrow[m] : m) * p.N + n] = to_out16<F16>(v[m]);
+              if (m < rows) p.y[(size_t)outrow[m] * p.N + n] = to_out16<F16>(v[m]);
+          } else {
+            uint16_t* yp = p.y + n;  // walking pointer: no per-row 64-bit index math
+#pragma unroll
+            for (int m = 0; m < MT; ++m, yp += p.N)
+              if (m < rows) *yp = to_out16<F16>(v[m]);
           }
         };
         const bool full_tile = (kb0 == 0) && (kb1 == ku);
