@@ -13,7 +13,7 @@ Every op runs hand-written sm_100a CUDA from ``libdflash_b200.so`` through
 its C ABI (``include/dflash_b200.h``); there is no CPU fallback.
 """
 
-from . import kernels, lm_head, moe
+from . import checkpoint, kernels, lm_head, moe
 from .lm_head import lm_head_argmax_keys, lm_head_verify, match_acceptance_length, verify_accept
 from .kernels import gated_delta_kernel_with_tape, tape_replay_kernel, tape_replay_
 from .recurrent_rollback_cache import (
@@ -34,6 +34,7 @@ from .verify_linear import (
 )
 
 __all__ = [
+    "checkpoint",
     "lm_head_argmax_keys",
     "lm_head_verify",
     "match_acceptance_length",
