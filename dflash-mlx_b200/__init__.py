@@ -15,7 +15,9 @@ its C ABI (``include/dflash_b200.h``); there is no CPU fallback.
 
 from . import checkpoint, kernels, lm_head, moe
 from .lm_head import lm_head_argmax_keys, lm_head_verify, match_acceptance_length, verify_accept
-from .kernels import gated_delta_kernel_with_tape, tape_replay_kernel, tape_replay_
+from .kernels import (gated_delta_kernel_with_tape, gated_delta_tree_kernel,
+                      gated_delta_tree_tape_kernel, tape_replay_, tape_replay_kernel,
+                      tree_depthwise_conv1d)
 from .recurrent_rollback_cache import (
     RecurrentRollbackCache,
     arm_rollback,
@@ -34,6 +36,9 @@ from .verify_linear import (
 )
 
 __all__ = [
+    "gated_delta_tree_kernel",
+    "gated_delta_tree_tape_kernel",
+    "tree_depthwise_conv1d",
     "checkpoint",
     "lm_head_argmax_keys",
     "lm_head_verify",

@@ -33,6 +33,10 @@ SIGNATURES = {
     "dfl_status_string": (ctypes.c_char_p, [_c_int]),
     "dfl_version": (ctypes.c_char_p, []),
     "dfl_get_device_error": (_c_int, [ctypes.POINTER(_c_int)]),
+    "dfl_gdn_tree_forward": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _vp, _vp,
+                                      _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),
+    "dfl_tree_depthwise_conv1d": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
+                                           _c_int, _c_int, _vp]),
     "dfl_verify_qmm_w4g64": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_size, _c_int, _c_int,
                                       _c_int, _vp]),
     "dfl_verify_qmm_w4g64_f16": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_size, _c_int, _c_int,

@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "dflash-b200 kernels target sm_100a only"
 #endif
@@ -27,6 +29,7 @@ enum DeviceError : int {
   kDevOk = 0,
   kDevWaitTimeout = 1,
   kDevBadGeometry = 2,
+  kDevBadInput = 3,  // an index argument outside its documented range
 };
 
 // Upper bound on any single mbarrier wait.  A healthy wait finishes in

@@ -8,6 +8,7 @@
 #include "qmm_noalloc.cu"
 #include "gdn_replay.cu"
 #include "gdn_forward.cu"
+#include "gdn_tree.cu"
 #include "lmhead.cu"
 #include "moe.cu"
 

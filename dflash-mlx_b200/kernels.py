@@ -147,3 +147,94 @@ def gated_delta_kernel_with_tape(q: torch.Tensor, k: torch.Tensor, v: torch.Tens
             tape.data_ptr(), b, t_steps, hv, hk, dv, dk, stream_ptr(state.device))
     _lib.check("dfl_gdn_forward_tape", st)
     return y, out, tape
+
+
+# ------------------------------------------------------------------ DDTree
+def _tree_inputs(q, k, v, g, beta, state, parent_ids):
+    for t, name in ((q, "q"), (k, "k"), (v, "v"), (g, "g"), (beta, "beta"), (state, "state")):
+        require_cuda(t, name)
+    if q.dtype not in (torch.bfloat16, torch.float32) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise NotImplementedError("q, k, v must all be bfloat16 or all float32")
+    if state.dtype != torch.float32:
+        raise NotImplementedError(f"state must be float32, got {state.dtype}")
+    b, t_steps, hk, dk = k.shape
+    hv, dv = v.shape[2:]
+    if q.shape != k.shape:
+        raise ValueError("q and k must have the same shape")
+    if hv % hk != 0:
+        raise ValueError(f"Cannot align K heads {hk} to V heads {hv}")
+    if g.shape not in ((b, t_steps, hv), (b, t_steps, hv, dk)):
+        raise ValueError(f"Unsupported gating shape {tuple(g.shape)}")
+    if beta.shape != (b, t_steps, hv) or state.shape != (b, hv, dv, dk):
+        raise ValueError("beta must be [B, T, Hv] and state [B, Hv, Dv, Dk]")
+    parent_ids = torch.as_tensor(parent_ids).to(device=state.device, dtype=torch.int32).reshape(-1)
+    if parent_ids.numel() != t_steps:
+        raise ValueError("parent_ids must have one entry per tree node")
+    # g and beta enter the kernel as fp32 (bf16 values widen exactly)
+    g = g.to(torch.float32)
+    beta = beta.to(torch.float32)
+    q, k, v, g, beta, state, parent_ids = (x.contiguous() for x in (q, k, v, g, beta, state, parent_ids))
+    return q, k, v, g, beta, state, parent_ids, (b, t_steps, hv, hk, dv, dk)
+
+
+def _tree_launch(q, k, v, g, beta, state, parent_ids, dims, want_tape):
+    b, t_steps, hv, hk, dv, dk = dims
+    y = torch.empty((b, t_steps, hv, dv), dtype=q.dtype, device=state.device)
+    nodes = torch.empty((b, t_steps, hv, dv, dk), dtype=torch.float32, device=state.device)
+    tape = torch.empty((b, t_steps, hv, dv), dtype=torch.float32, device=state.device) if want_tape else None
+    with torch.cuda.device(state.device):
+        st = _lib.load().dfl_gdn_tree_forward(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), 1 if g.dim() == 4 else 0,
+            beta.data_ptr(), state.data_ptr(), parent_ids.data_ptr(), y.data_ptr(), nodes.data_ptr(),
+            tape.data_ptr() if tape is not None else None, b, t_steps, hv, hk, dv, dk,
+            1 if q.dtype == torch.float32 else 0, stream_ptr(state.device))
+    _lib.check("dfl_gdn_tree_forward", st)
+    return y, nodes, tape
+
+
+def gated_delta_tree_kernel(q, k, v, g, beta, state, parent_ids):
+    """GDN over a token tree (reference ``kernels.py:501``): ``(y, tree_states)``,
+    node t starting from node ``parent_ids[t]`` (or ``state`` when < 0)."""
+    q, k, v, g, beta, state, parent_ids, dims = _tree_inputs(q, k, v, g, beta, state, parent_ids)
+    y, nodes, _ = _tree_launch(q, k, v, g, beta, state, parent_ids, dims, want_tape=False)
+    return y, nodes
+
+
+def gated_delta_tree_tape_kernel(q, k, v, g, beta, state, parent_ids):
+    """The tree recurrence recording the innovation tape (reference
+    ``kernels.py:545``): ``(y, tape)``; replaying a root-to-node path's tape rows
+    with ``tape_replay_kernel`` reproduces that node's state."""
+    q, k, v, g, beta, state, parent_ids, dims = _tree_inputs(q, k, v, g, beta, state, parent_ids)
+    y, _, tape = _tree_launch(q, k, v, g, beta, state, parent_ids, dims, want_tape=True)
+    return y, tape
+
+
+def tree_depthwise_conv1d(qkv, prefix, weight, bias, path_indices):
+    """Depthwise conv1d along tree paths + SiLU (reference ``kernels.py:647``).
+
+    ``qkv [B, T, C]``, ``prefix [B, K-1, C]`` (same dtype, bf16 or fp32),
+    ``weight [C, K, 1]`` (or ``[C, K]``), ``bias [C]`` or None,
+    ``path_indices [T, K]`` into ``concat(prefix, qkv)``."""
+    for t, name in ((qkv, "qkv"), (weight, "weight")):
+        require_cuda(t, name)
+    if qkv.dtype not in (torch.bfloat16, torch.float32):
+        raise NotImplementedError(f"qkv must be bfloat16 or float32, got {qkv.dtype}")
+    b, t_steps, c = qkv.shape
+    w = weight[..., 0] if weight.dim() == 3 else weight
+    if w.shape[0] != c:
+        raise ValueError(f"weight must be [C, K(, 1)] with C = {c}")
+    kk = int(w.shape[1])
+    if prefix.shape != (b, kk - 1, c) or prefix.dtype != qkv.dtype:
+        raise ValueError(f"prefix must be [B, K-1, C] = {(b, kk - 1, c)} in qkv's dtype")
+    path = torch.as_tensor(path_indices).to(device=qkv.device, dtype=torch.int32).reshape(t_steps, kk)
+    w = w.to(torch.float32).contiguous()
+    bias = bias.to(device=qkv.device, dtype=torch.float32).contiguous() if bias is not None else None
+    qkv, prefix, path = qkv.contiguous(), prefix.contiguous(), path.contiguous()
+    out = torch.empty_like(qkv)
+    with torch.cuda.device(qkv.device):
+        st = _lib.load().dfl_tree_depthwise_conv1d(
+            qkv.data_ptr(), prefix.data_ptr(), w.data_ptr(), bias.data_ptr() if bias is not None else None,
+            path.data_ptr(), out.data_ptr(), b, t_steps, c, kk, 1 if qkv.dtype == torch.float32 else 0,
+            stream_ptr(qkv.device))
+    _lib.check("dfl_tree_depthwise_conv1d", st)
+    return out

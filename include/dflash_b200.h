@@ -13,6 +13,9 @@
  *                             (stock mx.quantized_matmul(transpose=True) for other M)
  *   dfl_gdn_tape_replay    <- tape_replay_kernel       dflash_mlx/kernels.py:822-868
  *   dfl_gdn_forward_tape   <- gated_delta_kernel_with_tape dflash_mlx/kernels.py:169-219
+ *   dfl_gdn_tree_forward   <- gated_delta_tree_kernel / gated_delta_tree_tape_kernel
+ *                                                      dflash_mlx/kernels.py:501-586
+ *   dfl_tree_depthwise_conv1d <- tree_depthwise_conv1d dflash_mlx/kernels.py:647-688
  *   dfl_lmhead_argmax + dfl_lmhead_accept
  *                          <- logits_from_hidden       dflash_mlx/engine/target_qwen_gdn.py:774-778
  *                             greedy_tokens_with_mask  dflash_mlx/engine/sampling.py:47-55
@@ -184,6 +187,40 @@ int dfl_gdn_forward_tape(const uint16_t* q, const uint16_t* k, const uint16_t* v
                          int g_vectorized, const float* beta, const uint8_t* mask,
                          const float* state_in, float* state_out, uint16_t* y, float* tape,
                          int B, int T, int Hv, int Hk, int Dv, int Dk, void* stream);
+
+/* ------------------------------------------------------------------------
+ * DDTree verify: the GDN recurrence over a token tree.
+ *
+ * Node t starts from the state of node parent_ids[t] (parents before
+ * children; -1 = state_in) and applies one gated delta step (the update of
+ * dfl_gdn_forward_tape).  Writes y [B, T, Hv, Dv] (input dtype), every node's
+ * state to node_states [B, T, Hv, Dv, Dk] (fp32) and, when tape != NULL,
+ * delta to tape [B, T, Hv, Dv] (fp32).  q, k [B, T, Hk, Dk] and v are bf16
+ * (inputs_f32 = 0) or fp32 (inputs_f32 = 1); g fp32 [B, T, Hv] or
+ * [B, T, Hv, Dk] (g_vectorized); beta fp32 [B, T, Hv]; parent_ids int32 [T]
+ * on the device.  A parent id outside [-1, t) is recorded in the device error
+ * word and that node starts from state_in.
+ * Constraints: Dk in {32, 64, 128, 256}, Dv % 4 == 0, Hv % Hk == 0, T <= 64.
+ * Replaces gated_delta_tree_kernel (node_states = its tree_states) and
+ * gated_delta_tree_tape_kernel (node_states as scratch)
+ * (dflash_mlx/kernels.py:501-586; Metal bodies :222-420). */
+int dfl_gdn_tree_forward(const void* q, const void* k, const void* v, const float* g,
+                         int g_vectorized, const float* beta, const float* state_in,
+                         const int32_t* parent_ids, void* y, float* node_states, float* tape,
+                         int B, int T, int Hv, int Hk, int Dv, int Dk, int inputs_f32,
+                         void* stream);
+
+/* Depthwise causal conv1d along tree paths, then SiLU:
+ *   out[b, t, c] = silu(sum_w x(path_indices[t, w]) * weight[c, w] (+ bias[c]))
+ * where slot s < K-1 reads prefix[b, s, c] and slot s >= K-1 reads
+ * qkv[b, s - (K-1), c]; fp32 accumulation in w order.  qkv / prefix / out are
+ * bf16 (inputs_f32 = 0) or fp32; weight fp32 [C, K]; bias fp32 [C] or NULL;
+ * path_indices int32 [T, K].  A slot outside [0, K-1+T) is recorded in the
+ * device error word and reads 0.  Replaces tree_depthwise_conv1d
+ * (dflash_mlx/kernels.py:647-688; Metal body :588-629). */
+int dfl_tree_depthwise_conv1d(const void* qkv, const void* prefix, const float* weight,
+                              const float* bias, const int32_t* path_indices, void* out, int B,
+                              int T, int C, int K, int inputs_f32, void* stream);
 
 /* ------------------------------------------------------------------------
  * lm_head verify epilogue.

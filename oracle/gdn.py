@@ -157,3 +157,27 @@ def tape_replay_accepted(tape, k, g, state, accepted_steps):
     t_steps = np.asarray(tape).shape[1]
     mask = np.arange(t_steps)[None, :] < a[:, None]
     return tape_replay(tape, k, g, state, mask)
+
+
+def tree_depthwise_conv1d(qkv, prefix, weight, bias, path_indices):
+    """``_tree_depthwise_conv1d_ops`` restated (``kernels.py:631-644``).
+
+    ``qkv [B, T, C]``, ``prefix [B, K-1, C]``, ``weight [C, K, 1]`` or
+    ``[C, K]``, ``bias [C]`` or None, ``path_indices [T, K]`` into
+    ``concat(prefix, qkv, axis=1)``; fp32 accumulation in window order, then
+    silu(x) = x / (1 + exp(-x)).
+    """
+    qkv = np.asarray(qkv, np.float32)
+    prefix = np.asarray(prefix, np.float32)
+    w = np.asarray(weight, np.float32)
+    if w.ndim == 3:
+        w = w[..., 0]
+    pool = np.concatenate([prefix, qkv], axis=1)
+    path = np.asarray(path_indices, np.int64)
+    b, t_steps, c = qkv.shape
+    acc = np.zeros((b, t_steps, c), np.float32)
+    for j in range(w.shape[1]):
+        acc = (acc + pool[:, path[:, j], :] * w[None, None, :, j]).astype(np.float32)
+    if bias is not None:
+        acc = (acc + np.asarray(bias, np.float32)[None, None, :]).astype(np.float32)
+    return (acc / (np.float32(1.0) + np.exp(-acc))).astype(np.float32)
