@@ -776,6 +776,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int ix = 0; ix < XD && ix < n_units; ++ix) issue_x(ix);
         __syncwarp();
       }
+      if constexpr (PW) {
+        // Right after the previous launch completes every CTA asks for x at
+        // once; asking for one unit first and the rest once it has landed
+        // keeps that burst small, so the first MMAs start sooner.
+        stage_x(0);
+        staged = 1;
+        if (n_units > 1 && et == 0) wait(&xtma[0], 0);
+        __syncwarp();
+      }
       for (; staged < n_units && staged < C::XS; ++staged) stage_x(staged);
       const int t_first = u0 / ku;
       const int t_last = (u1 - 1) / ku;
