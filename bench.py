@@ -328,6 +328,87 @@ def run_ours(args):
     return 0
 
 
+def run_moe(args):
+    """BASELINE config 2 on one GPU: the MoE verify layer (hidden 2048, 256
+    experts, top-8, expert intermediate 512, one shared expert) at 16 tokens.
+    Reports the HBM GB/s of the layer (bytes of the experts the routing
+    activates + the shared expert + activations) from CUDA events around a
+    graph of ``--moe-layers`` layers with distinct weights (1.9 GB, larger than
+    L2).  Not the default workload: the driver's bench line is the verify
+    step."""
+    import torch
+
+    import __graft_entry__
+
+    __graft_entry__.load_package()
+    from dflash_mlx_b200 import moe as M
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"workload": "moe", "unavailable": "the MoE measurement runs on one GPU"}))
+        return 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hid, inter, e, topk, tok = 2048, 512, 256, 8, 16
+    gen = torch.Generator(device=dev).manual_seed(7)
+
+    def qweight(shape_n, shape_k, lead=()):
+        q = torch.randint(-2**31, 2**31 - 1, (*lead, shape_n, shape_k // 8), dtype=torch.int64,
+                          generator=gen, device=dev).to(torch.int32)
+        sc = torch.rand((*lead, shape_n, shape_k // 64), generator=gen, device=dev) * 0.016 + 0.004
+        bi = -8 * sc + torch.randn(sc.shape, generator=gen, device=dev) * 0.1 * sc
+        return M.QuantWeight(q, sc.to(torch.bfloat16), bi.to(torch.bfloat16))
+
+    layers = []
+    for _ in range(args.moe_layers):
+        experts = {"gate": qweight(inter, hid, (e,)), "up": qweight(inter, hid, (e,)),
+                   "down": qweight(hid, inter, (e,))}
+        shared = {"gate": qweight(inter, hid), "up": qweight(inter, hid), "down": qweight(hid, inter)}
+        logits = torch.randn((tok, e), generator=gen, device=dev)
+        layers.append((experts, shared, logits))
+    x = torch.randn((tok, hid), generator=gen, device=dev).to(torch.bfloat16)
+    active = []
+    for _, _, logits in layers:
+        _, _, ids = M.route(logits, topk)
+        active.append(int(torch.unique(ids).numel()))
+    per_expert = 3 * (inter * hid // 2 + 4 * inter * hid // 64)
+    act_bytes = 2 * tok * hid * 2 + 2 * tok * topk * (inter * 2 + hid) + 2 * tok * (3 * inter + hid)
+    bytes_total = sum(a * per_expert + per_expert + act_bytes for a in active)
+    stream = torch.cuda.Stream(dev)
+
+    def body():
+        for experts, shared, logits in layers:
+            M.moe_layer(x, logits, experts, shared, top_k=topk)
+
+    with torch.cuda.stream(stream):
+        body()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            body()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / args.steps
+    peak, kind = _peaks()
+    gbs = bytes_total / t / 1e9
+    print(json.dumps({
+        "workload": "moe", "metric": "MoE verify layer (BASELINE config 2) HBM GB/s", "value": gbs,
+        "unit": "GB/s", "us_per_layer": t / len(layers) * 1e6, "layers": len(layers),
+        "active_experts_per_layer": active, "bytes_per_layer": bytes_total / len(layers),
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                     "peak_source": kind},
+        "steps": args.steps, "warmup": args.warmup, "dtype": "bf16", "data": "synthetic"}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -344,11 +425,16 @@ def main():
     ap.add_argument("--no-fuse-silu", action="store_true",
                     help="run SiLU*up as its own launch after the gate|up projection")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["verify", "moe"], default="verify",
+                    help="verify: the benchmark's verify step (default); moe: BASELINE config 2")
+    ap.add_argument("--moe-layers", type=int, default=4)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "moe":
+        return run_moe(args)
     return run_ours(args)
 
 

@@ -651,6 +651,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         constexpr int NT = 32 * 4 * NDG;
         constexpr int EPT = MT * BN / NT;  // partial-sum elements per dequant thread
         float sum[EPT];
+        // The partial slots are shared with the previous launch on the stream
+        // (same workspace), which may still be reducing its own: read them
+        // only once it has completed.
+        griddep_wait();
         reduce_partials<MT>(p, cta + 1, c_hi, threadIdx.x - WARP_DQ0 * 32, abort_word, sum);
         named_bar_sync(BAR_ID_DQ, NT);  // every dequant warp is done with the stage ring
         float* red = reinterpret_cast<float*>(smem);
