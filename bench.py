@@ -359,11 +359,22 @@ def run_moe(args):
         bi = -8 * sc + torch.randn(sc.shape, generator=gen, device=dev) * 0.1 * sc
         return M.QuantWeight(q, sc.to(torch.bfloat16), bi.to(torch.bfloat16))
 
+    from dflash_mlx_b200.verify_qmm import interleave_gate_up
+
     layers = []
     for _ in range(args.moe_layers):
         experts = {"gate": qweight(inter, hid, (e,)), "up": qweight(inter, hid, (e,)),
                    "down": qweight(hid, inter, (e,))}
         shared = {"gate": qweight(inter, hid), "up": qweight(inter, hid), "down": qweight(hid, inter)}
+        if not args.no_fuse_silu:
+            # load-time layout: gate/up interleaved, SiLU*up fused into their launch
+            experts = {"gate_up": M.fuse_expert_gate_up(experts["gate"], experts["up"]),
+                       "down": experts["down"]}
+            g, u = shared["gate"], shared["up"]
+            shared = {"gate_up": M.QuantWeight(interleave_gate_up(g.q, u.q).contiguous(),
+                                               interleave_gate_up(g.s, u.s).contiguous(),
+                                               interleave_gate_up(g.b, u.b).contiguous()),
+                      "down": shared["down"]}
         logits = torch.randn((tok, e), generator=gen, device=dev)
         layers.append((experts, shared, logits))
     x = torch.randn((tok, hid), generator=gen, device=dev).to(torch.bfloat16)
@@ -405,6 +416,7 @@ def run_moe(args):
         "active_experts_per_layer": active, "bytes_per_layer": bytes_total / len(layers),
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                      "peak_source": kind},
+        "silu_fused": not args.no_fuse_silu, "gpu_launches_per_layer": 6 if not args.no_fuse_silu else 10,
         "steps": args.steps, "warmup": args.warmup, "dtype": "bf16", "data": "synthetic"}))
     return 0
 

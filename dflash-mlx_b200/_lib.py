@@ -66,6 +66,10 @@ SIGNATURES = {
     "dfl_moe_route_table_ints": (_c_size, [_c_int]),
     "dfl_moe_qmm_w4g64": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
                                    _c_int, _vp, _c_size, _vp]),
+    "dfl_moe_qmm_w4g64_silu": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
+                                        _c_int, _c_int, _vp, _c_size, _vp]),
+    "dfl_verify_qmm_w4g64_silu": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_size, _c_int, _c_int,
+                                           _c_int, _vp]),
     "dfl_moe_qmm_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
     "dfl_silu_mul_bf16": (_c_int, [_vp, _vp, _vp, _c_int, _vp]),
     "dfl_silu_mul_rows_bf16": (_c_int, [_vp, _vp, _c_int, _vp, _c_int, _c_int, _vp]),

@@ -67,27 +67,31 @@ __global__ void route_kernel(const float* logits, int T, int E, int k, int32_t* 
     }
   }
   __syncthreads();
+  // Active experts in increasing id order (serial over E in shared memory).
   if (tid == 0) {
     int P = 0;
-    for (int e = 0; e < E; ++e) {
-      if (cnt[e] > 0) {
-        start[e] = P;
-        table[1 + P] = e;
-        table[1 + E + P] = 0;
-        ++P;
-      } else {
-        start[e] = -1;
-      }
-    }
+    for (int e = 0; e < E; ++e) start[e] = cnt[e] > 0 ? P++ : -1;
     table[0] = P;
-    // rows in token order (t ascending, then slot), deterministic
-    for (int pr = 0; pr < T * k; ++pr) {
-      const int e = ids[pr];
-      const int pi = start[e];
-      const int m = table[1 + E + pi]++;
-      table[1 + 2 * E + pi * 16 + m] = pr / k;          // token row
-      table[1 + 2 * E + 16 * E + pi * 16 + m] = pr;     // pair row
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) {
+    const int pi = start[e];
+    if (pi >= 0) {
+      table[1 + pi] = e;
+      table[1 + E + pi] = cnt[e];
     }
+  }
+  // Rows of each problem in token order (t ascending, then slot): pair pr
+  // is row m of its expert's problem, m = number of earlier pairs routed to
+  // the same expert.  Computed per pair in parallel (deterministic).
+  const int pairs = T * k;
+  for (int pr = tid; pr < pairs; pr += blockDim.x) {
+    const int e = ids[pr];
+    int m = 0;
+    for (int q = 0; q < pr; ++q) m += (ids[q] == e);
+    const int pi = start[e];
+    table[1 + 2 * E + pi * 16 + m] = pr / k;          // token row
+    table[1 + 2 * E + 16 * E + pi * 16 + m] = pr;     // pair row
   }
 }
 

@@ -351,10 +351,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                      const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ Params p) {
   static_assert(!(PW && GROUPED), "pair-packed weights: dense layers only");
-  // SILU: the weights are a gate|up pair interleaved in blocks of 32 rows
-  // (16 gate rows, then the 16 up rows of the same outputs); the epilogue
-  // writes h = silu(gate) * up, [M, N / 2], instead of the N projections.
-  static_assert(!(SILU && GROUPED), "fused SiLU epilogue: dense layers only");
+  // SILU: the weights (of every expert, when grouped) are a gate|up pair
+  // interleaved in blocks of 32 rows (16 gate rows, then the 16 up rows of
+  // the same outputs); the epilogue writes h = silu(gate) * up, [rows, N / 2],
+  // instead of the N projections.
   using C = Cfg<MT, PW>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -832,7 +832,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               const uint32_t mine = to_out16<F16>(v[m]);
               const uint32_t up = __shfl_down_sync(0xffffffffu, mine, 16);
               if (lane < 16 && m < rows)
-                p.y[(size_t)m * ldh + hcol] = silu_mul_bits<F16>(uint16_t(mine), uint16_t(up));
+                p.y[(size_t)(GROUPED ? outrow[m] : m) * ldh + hcol] =
+                    silu_mul_bits<F16>(uint16_t(mine), uint16_t(up));
             }
           } else if constexpr (GROUPED) {
 #pragma unroll
@@ -1115,6 +1116,14 @@ extern "C" int dfl_verify_qmm_w4g64_pairs(const uint16_t* x, const uint32_t* w_q
                                              workspace_bytes, M, K, N, stream);
 }
 
+extern "C" int dfl_verify_qmm_w4g64_silu(const uint16_t* x, const uint32_t* w_q,
+                                         const uint16_t* scales, const uint16_t* biases,
+                                         uint16_t* h, void* workspace, size_t workspace_bytes,
+                                         int M, int K, int N, void* stream) {
+  return dfl::qmm::verify_entry<false, false, true>(x, w_q, scales, biases, h, workspace,
+                                                    workspace_bytes, M, K, N, stream);
+}
+
 extern "C" int dfl_verify_qmm_w4g64_pairs_silu(const uint16_t* x, const uint32_t* w_q,
                                                const uint16_t* scales, const uint16_t* biases,
                                                uint16_t* h, void* workspace,
@@ -1192,24 +1201,27 @@ extern "C" size_t dfl_moe_qmm_workspace_bytes(int max_problems, int K, int N, in
   return dfl::qmm::grouped_workspace_bytes(max_problems, K, N, sms);
 }
 
-extern "C" int dfl_moe_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
-                                 const uint16_t* biases, uint16_t* y, const int32_t* route,
-                                 int gather_by_pair, int max_problems, int E, int K, int N,
-                                 void* workspace, size_t workspace_bytes, void* stream) {
-  using namespace dfl;
+namespace dfl {
+namespace qmm {
+template <bool SILU>
+int moe_entry(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
+              const uint16_t* biases, uint16_t* y, const int32_t* route, int gather_by_pair,
+              int max_problems, int E, int K, int N, void* workspace, size_t workspace_bytes,
+              void* stream) {
   if (max_problems < 1 || max_problems > E || E < 1 || K < 64 || K % 64 != 0 || N < 1 ||
-      (long long)max_problems * ((N + 127) / 128) > qmm::kMaxTiles)
+      (long long)max_problems * ((N + 127) / 128) > kMaxTiles)
     return DFL_ERR_BAD_SHAPE;
+  if (SILU && N % 32 != 0) return DFL_ERR_BAD_SHAPE;
   if (!x || !w_q || !scales || !biases || !y || !route) return DFL_ERR_NULL_POINTER;
   if (!host::aligned(x, 16) || !host::aligned(w_q, 16) || !host::aligned(route, 4))
     return DFL_ERR_MISALIGNED;
   int dev, sms;
   int st = host::current_device(&dev, &sms);
   if (st != DFL_OK) return st;
-  if (!workspace || workspace_bytes < qmm::grouped_workspace_bytes(max_problems, K, N, sms))
+  if (!workspace || workspace_bytes < grouped_workspace_bytes(max_problems, K, N, sms))
     return DFL_ERR_WORKSPACE;
   if (!host::aligned(workspace, 16)) return DFL_ERR_MISALIGNED;
-  qmm::Params p;
+  Params p;
   std::memset(&p, 0, sizeof(p));
   p.x = x;
   p.scales = scales;
@@ -1218,10 +1230,10 @@ extern "C" int dfl_moe_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const u
   p.M = 16;
   p.K = K;
   p.N = N;
-  qmm::grouped_geometry(max_problems, K, N, sms, &p.tpp, &p.k_units, &p.grid);
+  grouped_geometry(max_problems, K, N, sms, &p.tpp, &p.k_units, &p.grid);
   p.n_tiles = max_problems * p.tpp;
-  p.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + qmm::kCounterBytes);
-  p.sb_tma = (K % qmm::UNIT_K == 0) && host::aligned(scales, 16) && host::aligned(biases, 16);
+  p.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kCounterBytes);
+  p.sb_tma = (K % UNIT_K == 0) && host::aligned(scales, 16) && host::aligned(biases, 16);
   // route table layout (int32): [0] problem count P, then E expert ids,
   // E row counts, E x 16 token rows, E x 16 pair rows (see dfl_moe_route)
   p.g_count = route;
@@ -1231,8 +1243,27 @@ extern "C" int dfl_moe_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const u
   p.g_out = route + 1 + 2 * E + 16 * E;
   CUtensorMap tm_w, tm_s, tm_b, tm_x;
   std::memset(&tm_x, 0, sizeof(tm_x));  // grouped mode gathers x rows with plain loads
-  st = qmm::make_weight_maps(w_q, scales, biases, E, K, N, p.sb_tma != 0, &tm_w, &tm_s, &tm_b);
+  st = make_weight_maps(w_q, scales, biases, E, K, N, p.sb_tma != 0, &tm_w, &tm_s, &tm_b);
   if (st != DFL_OK) return st;
-  return qmm::launch_kernel<16, true>(tm_w, tm_s, tm_b, tm_x, p, dev,
-                                      reinterpret_cast<cudaStream_t>(stream));
+  return launch_kernel<16, true, false, false, SILU>(tm_w, tm_s, tm_b, tm_x, p, dev,
+                                                    reinterpret_cast<cudaStream_t>(stream));
+}
+}  // namespace qmm
+}  // namespace dfl
+
+extern "C" int dfl_moe_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
+                                 const uint16_t* biases, uint16_t* y, const int32_t* route,
+                                 int gather_by_pair, int max_problems, int E, int K, int N,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  return dfl::qmm::moe_entry<false>(x, w_q, scales, biases, y, route, gather_by_pair,
+                                    max_problems, E, K, N, workspace, workspace_bytes, stream);
+}
+
+extern "C" int dfl_moe_qmm_w4g64_silu(const uint16_t* x, const uint32_t* w_q,
+                                      const uint16_t* scales, const uint16_t* biases, uint16_t* h,
+                                      const int32_t* route, int gather_by_pair, int max_problems,
+                                      int E, int K, int N, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  return dfl::qmm::moe_entry<true>(x, w_q, scales, biases, h, route, gather_by_pair,
+                                   max_problems, E, K, N, workspace, workspace_bytes, stream);
 }

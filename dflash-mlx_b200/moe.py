@@ -72,22 +72,38 @@ def route(router_logits: torch.Tensor, top_k: int = 8):
 
 def gather_qmm(x: torch.Tensor, weight: QuantWeight, table: torch.Tensor, *, rows_out: int,
                gather_by_pair: bool, max_problems: Optional[int] = None,
-               out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Grouped int4 qmm over the route table's active experts -> bf16 ``[rows_out, N]``."""
+               out: Optional[torch.Tensor] = None, silu: bool = False) -> torch.Tensor:
+    """Grouped int4 qmm over the route table's active experts -> bf16 ``[rows_out, N]``.
+
+    ``silu=True``: each expert's weights are its gate/up pair interleaved
+    (:func:`fuse_expert_gate_up`) and the result is ``silu(gate) * up``,
+    ``[rows_out, N/2]``."""
     e = int(weight.q.shape[0])
     k, n = weight.k, weight.n
     x = x.contiguous()
+    n_out = n // 2 if silu else n
     if out is None:
-        out = torch.empty((rows_out, n), dtype=torch.bfloat16, device=x.device)
+        out = torch.empty((rows_out, n_out), dtype=torch.bfloat16, device=x.device)
     mp = e if max_problems is None else int(max_problems)
+    entry = "dfl_moe_qmm_w4g64_silu" if silu else "dfl_moe_qmm_w4g64"
     with torch.cuda.device(x.device):
         ws = workspace(x.device, _moe_ws_bytes(mp, k, n))
-        st = _lib.load().dfl_moe_qmm_w4g64(
+        st = getattr(_lib.load(), entry)(
             x.data_ptr(), weight.q.data_ptr(), weight.s.data_ptr(), weight.b.data_ptr(),
             out.data_ptr(), table.data_ptr(), 1 if gather_by_pair else 0, mp, e, k, n,
             ws.data_ptr(), ws.numel(), stream_ptr(x.device))
-    _lib.check("dfl_moe_qmm_w4g64", st)
+    _lib.check(entry, st)
     return out
+
+
+def fuse_expert_gate_up(gate: QuantWeight, up: QuantWeight) -> QuantWeight:
+    """Stacked expert gate and up weights ``[E, I, *]`` interleaved per expert in
+    16-row blocks -> ``[E, 2I, *]`` (the layout of ``gather_qmm(..., silu=True)``)."""
+    from .verify_qmm import interleave_gate_up
+
+    return QuantWeight(interleave_gate_up(gate.q, up.q, dim=-2).contiguous(),
+                       interleave_gate_up(gate.s, up.s, dim=-2).contiguous(),
+                       interleave_gate_up(gate.b, up.b, dim=-2).contiguous())
 
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
@@ -126,6 +142,15 @@ def combine(pair_out: torch.Tensor, weights: torch.Tensor, shared: Optional[torc
     return y
 
 
+def dense_mlp_fused(x: torch.Tensor, gate_up: QuantWeight, down: QuantWeight) -> torch.Tensor:
+    """The shared-expert MLP on an interleaved gate/up weight (MLX packing):
+    one fused gate/up + SiLU launch, then down."""
+    from .verify_qmm import gate_up_silu
+
+    h = gate_up_silu(x.contiguous(), gate_up.q, gate_up.s, gate_up.b, layout="mlx")
+    return qmm_w4g64(h, down.q, down.s, down.b)
+
+
 def dense_mlp(x: torch.Tensor, gate: QuantWeight, up: QuantWeight, down: QuantWeight) -> torch.Tensor:
     g = qmm_w4g64(x, gate.q, gate.s, gate.b)
     u = qmm_w4g64(x, up.q, up.s, up.b)
@@ -136,19 +161,29 @@ def moe_layer(x: torch.Tensor, router_logits: torch.Tensor, experts: dict, share
               top_k: int = 8) -> torch.Tensor:
     """One MoE verify layer: ``x`` bf16 ``[T, H]`` -> bf16 ``[T, H]``.
 
-    ``experts``: QuantWeight stacks ``gate`` / ``up`` ``[E, I, H/8]`` and
-    ``down`` ``[E, H, I/8]``; ``shared``: unstacked QuantWeights (or None).
+    ``experts``: QuantWeight stacks ``gate`` / ``up`` ``[E, I, H/8]`` (or one
+    interleaved ``gate_up`` stack ``[E, 2I, H/8]``, :func:`fuse_expert_gate_up`)
+    and ``down`` ``[E, H, I/8]``; ``shared``: unstacked QuantWeights ``gate`` /
+    ``up`` (or an interleaved ``gate_up``) and ``down``, or None.
     """
     require_cuda(x, "x")
     t = x.shape[0]
     table, w, _ = route(router_logits, top_k)
-    e = int(experts["gate"].q.shape[0])
+    fused = "gate_up" in experts
+    e = int((experts["gate_up"] if fused else experts["gate"]).q.shape[0])
     mp = min(e, t * top_k)
-    g = gather_qmm(x, experts["gate"], table, rows_out=t * top_k, gather_by_pair=False, max_problems=mp)
-    u = gather_qmm(x, experts["up"], table, rows_out=t * top_k, gather_by_pair=False, max_problems=mp)
-    h = silu_mul(g, u)
+    if fused:
+        h = gather_qmm(x, experts["gate_up"], table, rows_out=t * top_k, gather_by_pair=False,
+                       max_problems=mp, silu=True)
+    else:
+        g = gather_qmm(x, experts["gate"], table, rows_out=t * top_k, gather_by_pair=False, max_problems=mp)
+        u = gather_qmm(x, experts["up"], table, rows_out=t * top_k, gather_by_pair=False, max_problems=mp)
+        h = silu_mul(g, u)
     d = gather_qmm(h, experts["down"], table, rows_out=t * top_k, gather_by_pair=True, max_problems=mp)
     so = None
     if shared is not None:
-        so = dense_mlp(x, shared["gate"], shared["up"], shared["down"])
+        if "gate_up" in shared:
+            so = dense_mlp_fused(x, shared["gate_up"], shared["down"])
+        else:
+            so = dense_mlp(x, shared["gate"], shared["up"], shared["down"])
     return combine(d, w, so)

@@ -121,38 +121,43 @@ def qmm_w4g64(x2: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases:
     return out
 
 
-def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
-    """Row-interleave two ``[I, *]`` tensors in blocks of 16 rows:
-    ``[gate 0..15, up 0..15, gate 16..31, up 16..31, ...]`` -> ``[2I, *]``.
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, dim: int = 0) -> torch.Tensor:
+    """Row-interleave two tensors along ``dim`` (size I) in blocks of 16 rows:
+    ``[gate 0..15, up 0..15, gate 16..31, up 16..31, ...]`` -> size 2I.
 
-    The layout :func:`gate_up_silu` takes for the packed weights, scales and
+    The layout :func:`gate_up_silu` (and the grouped MoE variant, with
+    ``dim=1`` over an expert stack) takes for the packed weights, scales and
     biases of an MLP's gate/up pair (a load-time layout, like concatenating
     projections that share an input)."""
-    if gate.shape != up.shape or gate.shape[0] % 16 != 0:
+    dim = dim % gate.dim()
+    if gate.shape != up.shape or gate.shape[dim] % 16 != 0:
         raise ValueError("gate and up must have the same shape with rows % 16 == 0")
-    i = gate.shape[0]
-    return torch.stack((gate.reshape(i // 16, 16, *gate.shape[1:]),
-                        up.reshape(i // 16, 16, *up.shape[1:])), dim=1).reshape(2 * i, *gate.shape[1:])
+    i = gate.shape[dim]
+    lead, tail = gate.shape[:dim], gate.shape[dim + 1:]
+    return torch.stack((gate.reshape(*lead, i // 16, 16, *tail), up.reshape(*lead, i // 16, 16, *tail)),
+                       dim=dim + 1).reshape(*lead, 2 * i, *tail)
 
 
-_SILU_ENTRY = {torch.bfloat16: "dfl_verify_qmm_w4g64_pairs_silu",
-               torch.float16: "dfl_verify_qmm_w4g64_pairs_silu_f16"}
+_SILU_ENTRY = {("pairs", torch.bfloat16): "dfl_verify_qmm_w4g64_pairs_silu",
+               ("pairs", torch.float16): "dfl_verify_qmm_w4g64_pairs_silu_f16",
+               ("mlx", torch.bfloat16): "dfl_verify_qmm_w4g64_silu"}
 
 
 def gate_up_silu(x2: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
+                 out: torch.Tensor | None = None, *, layout: str = "pairs") -> torch.Tensor:
     """``silu(x2 @ Wg.T) * (x2 @ Wu.T)`` in one launch -> ``[M, I]``.
 
     ``w_q`` / ``scales`` / ``biases`` are the gate and up projections
-    interleaved by :func:`interleave_gate_up`, weights pair-packed
-    (:func:`repack_pairs`).  Each projection is rounded to the activation
-    dtype before the SiLU, so the result equals :func:`silu_mul` of the two
-    projections computed separately by the same kernel."""
+    interleaved by :func:`interleave_gate_up`; ``layout`` is ``"pairs"``
+    (weights passed through :func:`repack_pairs`) or ``"mlx"`` (bf16 only).
+    Each projection is rounded to the activation dtype before the SiLU, so the
+    result equals :func:`silu_mul` of the two projections computed separately
+    by the same kernel."""
     for t, name in ((x2, "x"), (w_q, "w"), (scales, "scales"), (biases, "biases")):
         require_cuda(t, name)
-    entry = _SILU_ENTRY.get(x2.dtype)
+    entry = _SILU_ENTRY.get((layout, x2.dtype))
     if entry is None:
-        raise NotImplementedError(f"activations must be bfloat16 or float16, got {x2.dtype}")
+        raise NotImplementedError(f"no fused SiLU kernel for layout {layout!r} and {x2.dtype}")
     if scales.dtype != x2.dtype or biases.dtype != x2.dtype:
         raise NotImplementedError("scales/biases must match the activations' dtype")
     w_q = as_u32_bits(w_q)

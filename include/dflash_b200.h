@@ -104,8 +104,9 @@ int dfl_verify_qmm_w4g64_pairs_f16(const uint16_t* x, const uint32_t* w_q,
                                    void* workspace, size_t workspace_bytes, int M, int K, int N,
                                    void* stream);
 
-/* Gate/up projection pair with SiLU*up fused into the epilogue, on
- * pair-packed weights: w_q / scales / biases hold the gate and up rows
+/* Gate/up projection pair with SiLU*up fused into the epilogue, on MLX-packed
+ * (dfl_verify_qmm_w4g64_silu) or pair-packed (_pairs_silu, _pairs_silu_f16)
+ * weights: w_q / scales / biases hold the gate and up rows
  * interleaved in blocks of 32 (rows 32b..32b+15 = gate rows 16b..16b+15,
  * rows 32b+16..32b+31 = up rows 16b..16b+15), N = 2 * intermediate,
  * N % 32 == 0.  h [M, N/2] = silu(gate) * up with gate and up each rounded
@@ -114,6 +115,9 @@ int dfl_verify_qmm_w4g64_pairs_f16(const uint16_t* x, const uint32_t* w_q,
  * Replaces the MLP's gate_proj/up_proj pair and nn.silu(gate) * up of the
  * verify forward (mlx-lm's MLP, reached from the target model's layers at
  * dflash_mlx/engine/target_qwen_gdn.py:863-865). */
+int dfl_verify_qmm_w4g64_silu(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
+                              const uint16_t* biases, uint16_t* h, void* workspace,
+                              size_t workspace_bytes, int M, int K, int N, void* stream);
 int dfl_verify_qmm_w4g64_pairs_silu(const uint16_t* x, const uint32_t* w_q,
                                     const uint16_t* scales, const uint16_t* biases, uint16_t* h,
                                     void* workspace, size_t workspace_bytes, int M, int K, int N,
@@ -301,6 +305,13 @@ int dfl_moe_qmm_w4g64(const uint16_t* x, const uint32_t* w_q, const uint16_t* sc
                       int gather_by_pair, int max_problems, int E, int K, int N, void* workspace,
                       size_t workspace_bytes, void* stream);
 size_t dfl_moe_qmm_workspace_bytes(int max_problems, int K, int N, int* status);
+/* The grouped qmm over each expert's gate/up pair interleaved in blocks of
+ * 32 rows (as dfl_verify_qmm_w4g64_pairs_silu; N = 2 * intermediate,
+ * N % 32 == 0) with SiLU*up fused into the epilogue: h [rows_out, N/2]. */
+int dfl_moe_qmm_w4g64_silu(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
+                           const uint16_t* biases, uint16_t* h, const int32_t* route,
+                           int gather_by_pair, int max_problems, int E, int K, int N,
+                           void* workspace, size_t workspace_bytes, void* stream);
 int dfl_silu_mul_bf16(const uint16_t* gate, const uint16_t* up, uint16_t* out, int n,
                       void* stream);
 

@@ -164,3 +164,35 @@ def test_fused_projection_equals_separate_launches(pkg, dev):
         e = ys.float().cpu().numpy()
         assert np.all(np.abs(a - e) <= 1e-2 + 2e-2 * np.abs(e))
         col += n
+
+
+def _fused(pkg, experts, sh):
+    from dflash_mlx_b200.verify_qmm import interleave_gate_up
+
+    fe = {"gate_up": pkg.moe.fuse_expert_gate_up(experts["gate"], experts["up"]), "down": experts["down"]}
+    fsh = None
+    if sh is not None:
+        W = pkg.moe.QuantWeight
+        fsh = {"gate_up": W(interleave_gate_up(sh["gate"].q, sh["up"].q).contiguous(),
+                            interleave_gate_up(sh["gate"].s, sh["up"].s).contiguous(),
+                            interleave_gate_up(sh["gate"].b, sh["up"].b).contiguous()),
+               "down": sh["down"]}
+    return fe, fsh
+
+
+@pytest.mark.parametrize("case", ["small", "config2"])
+def test_fused_gate_up_silu_experts(pkg, dev, case):
+    """Experts' gate/up interleaved and SiLU*up fused into the grouped launch
+    (and the shared expert's into a dense launch): same layer output as the
+    oracle, within the same tolerance."""
+    if case == "small":
+        x, logits, experts, sh = _layer(pkg, dev, 1, 16, 16, 512, 256, 4)
+        k = 4
+    else:
+        x, logits, experts, sh = _layer(pkg, dev, 3, 16, 256, 2048, 512, 8)
+        k = 8
+    fe, fsh = _fused(pkg, experts, sh)
+    y = pkg.moe.moe_layer(x, logits, fe, fsh, top_k=k)
+    _assert_close(bf16_to_np_bits(y), _oracle(x, logits, experts, sh, k))
+    from dflash_mlx_b200 import _lib
+    assert _lib.device_error() == 0
