@@ -421,6 +421,81 @@ def run_moe(args):
     return 0
 
 
+def run_gdn(args):
+    """GDN kernels off the bench step, on one GPU, at BASELINE config 4's head
+    sizes (48 value heads, Dk = Dv = 128, 16 tokens): the verify forward that
+    records the tape (``--workload gdn-forward``, 48 layers in one launch as
+    the batch) and the DDTree forward over a 16-node tree
+    (``--workload ddtree``, per-node states written).  Reports HBM GB/s of the
+    algorithmic bytes (fp32 states in and out, bf16 q/k/v, fp32 g/beta/tape)
+    from CUDA events around a CUDA graph of the launch."""
+    import numpy as np
+    import torch
+
+    import __graft_entry__
+
+    pkg = __graft_entry__.load_package()
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"workload": args.workload, "unavailable": "runs on one GPU"}))
+        return 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(11)
+    hv, hk, dk, dv, t = 48, 16, 128, 128, 16
+    b = 48 if args.workload == "gdn-forward" else 4
+
+    def unit(shape):
+        a = torch.randn(shape, generator=gen, device=dev)
+        return (a / a.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+
+    q, k = unit((b, t, hk, dk)), unit((b, t, hk, dk))
+    v = torch.randn((b, t, hv, dv), generator=gen, device=dev).to(torch.bfloat16)
+    g = torch.exp(-torch.nn.functional.softplus(torch.randn((b, t, hv), generator=gen, device=dev)))
+    beta = torch.sigmoid(torch.randn((b, t, hv), generator=gen, device=dev))
+    state = torch.randn((b, hv, dv, dk), generator=gen, device=dev) * 0.05
+    parents = torch.tensor([-1] + [int(x) for x in np.random.default_rng(1).integers(-1, np.arange(1, t))],
+                           dtype=torch.int32, device=dev)
+    state_bytes = b * hv * dv * dk * 4
+    io_bytes = 2 * b * t * hk * dk * 2 + b * t * hv * dv * 2 + 2 * b * t * hv * 4
+    if args.workload == "gdn-forward":
+        fn = lambda: pkg.gated_delta_kernel_with_tape(q, k, v, g, beta, state)
+        alg = 2 * state_bytes + io_bytes + b * t * hv * dv * (2 + 4)       # state in/out, y, tape
+        what = "gated_delta_kernel_with_tape, 48 layers x 1 request (layer folded into the batch)"
+    else:
+        fn = lambda: pkg.gated_delta_tree_kernel(q, k, v, g, beta, state, parents)
+        # snapshot read, every node state written and (for non-roots) its parent's read back
+        n_reads = int((parents >= 0).sum())
+        alg = state_bytes * (1 + t + n_reads) // 1 + io_bytes + b * t * hv * dv * 2
+        what = f"gated_delta_tree_kernel, {b} requests x 16-node tree ({n_reads} non-root nodes)"
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / args.steps
+    peak, kind = _peaks()
+    gbs = alg / sec / 1e9
+    print(json.dumps({"workload": args.workload, "metric": f"{what}: HBM GB/s", "value": gbs, "unit": "GB/s",
+                      "us_per_launch": sec * 1e6, "bytes_per_launch": alg,
+                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                                   "frac": gbs / peak, "peak_source": kind},
+                      "steps": args.steps, "warmup": args.warmup, "data": "synthetic (config 4 distributions)"}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -437,8 +512,9 @@ def main():
     ap.add_argument("--no-fuse-silu", action="store_true",
                     help="run SiLU*up as its own launch after the gate|up projection")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["verify", "moe"], default="verify",
-                    help="verify: the benchmark's verify step (default); moe: BASELINE config 2")
+    ap.add_argument("--workload", choices=["verify", "moe", "gdn-forward", "ddtree"], default="verify",
+                    help="verify: the benchmark's verify step (default); moe: BASELINE config 2; "
+                         "gdn-forward / ddtree: the GDN tape producer and the tree kernel alone")
     ap.add_argument("--moe-layers", type=int, default=4)
     args = ap.parse_args()
     if args.warmup < 3:
@@ -447,6 +523,8 @@ def main():
         return run_reference(args)
     if args.workload == "moe":
         return run_moe(args)
+    if args.workload in ("gdn-forward", "ddtree"):
+        return run_gdn(args)
     return run_ours(args)
 
 
