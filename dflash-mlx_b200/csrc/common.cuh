@@ -176,6 +176,49 @@ __device__ __forceinline__ uint16_t silu_mul_bits(uint16_t gb, uint16_t ub) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(s * u));
 }
 
+// Warp sums of four values per lane (rows 0..3 of a warp, each spread over
+// all 32 lanes) with 6 shuffles instead of 4 x 5: after the first two levels
+// every lane carries one row; the result is the full sum of row
+// ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1), held by the 8 lanes of that row.
+__device__ __forceinline__ int row_of_lane4(int lane) { return ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1); }
+
+__device__ __forceinline__ float warp_reduce_rows4(const float (&v)[4], int lane) {
+  const bool hi16 = (lane & 16) != 0;
+  float a = hi16 ? v[2] : v[0];
+  float b = hi16 ? v[3] : v[1];
+  a += __shfl_xor_sync(0xffffffffu, hi16 ? v[0] : v[2], 16);
+  b += __shfl_xor_sync(0xffffffffu, hi16 ? v[1] : v[3], 16);
+  const bool hi8 = (lane & 8) != 0;
+  float k = hi8 ? b : a;
+  k += __shfl_xor_sync(0xffffffffu, hi8 ? a : b, 8);
+  k += __shfl_xor_sync(0xffffffffu, k, 4);
+  k += __shfl_xor_sync(0xffffffffu, k, 2);
+  k += __shfl_xor_sync(0xffffffffu, k, 1);
+  return k;
+}
+
+// n consecutive floats of shared memory into registers, 16 bytes at a time
+// when n % 4 == 0 (the address must then be 16-byte aligned).
+template <int N>
+__device__ __forceinline__ void lds_vec(const float* src, float (&r)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(src + i);
+      r[i] = v.x; r[i + 1] = v.y; r[i + 2] = v.z; r[i + 3] = v.w;
+    }
+  } else if constexpr (N % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 2) {
+      const float2 v = *reinterpret_cast<const float2*>(src + i);
+      r[i] = v.x; r[i + 1] = v.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) r[i] = src[i];
+  }
+}
+
 // Relaxed (gpu scope, L2-coherent) 32-bit global load / store.  Each aligned
 // 32-bit access is single-copy atomic, so a word that carries its own
 // validity bit can be polled without a separate flag.

@@ -132,14 +132,24 @@ __global__ void __launch_bounds__(THREADS) gdn_forward_tape_kernel(const FwdPara
     load_row<NPL>(p.state_in + head_off + (size_t)(row0 + warp * ROWS_PER_WARP + j) * DK + c0, s[j]);
   __syncthreads();
 
+  static_assert(ROWS_PER_WARP == 4, "warp_reduce_rows4 reduces four rows");
+  const int my_row = row_of_lane4(lane);  // the row whose sums this lane ends up with
+  const bool writer = (lane & 7) == 0;    // lanes 0, 8, 16, 24 write rows 0..3
   for (int t = 0; t < T; ++t) {
-    const float* kt = k_s + t * DK + c0;
-    const float* qt = q_s + t * DK + c0;
+    float kt[NPL], qt[NPL], gv[NPL];
+    lds_vec<NPL>(k_s + t * DK + c0, kt);
+    lds_vec<NPL>(q_s + t * DK + c0, qt);
+    if (p.g_vec) {
+      lds_vec<NPL>(g_s + t * DK + c0, gv);
+    } else {
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) gv[i] = g_s[t];
+    }
     const size_t out_off = (((size_t)b * T + t) * p.Hv + hv) * p.Dv + row0 + warp * ROWS_PER_WARP;
     if (!m_s[t]) {
-      if (lane < ROWS_PER_WARP) {
-        p.tape[out_off + lane] = 0.f;
-        p.y[out_off + lane] = __float2bfloat16_rn(0.f);
+      if (writer) {
+        p.tape[out_off + my_row] = 0.f;
+        p.y[out_off + my_row] = __float2bfloat16_rn(0.f);
       }
       continue;
     }
@@ -149,40 +159,31 @@ __global__ void __launch_bounds__(THREADS) gdn_forward_tape_kernel(const FwdPara
       float acc = 0.f;
 #pragma unroll
       for (int i = 0; i < NPL; ++i) {
-        const float gd = p.g_vec ? g_s[t * DK + c0 + i] : g_s[t];
-        s[j][i] = __fmul_rn(s[j][i], gd);
+        s[j][i] = __fmul_rn(s[j][i], gv[i]);
         acc = __fmaf_rn(s[j][i], kt[i], acc);
       }
       kv[j] = acc;
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-      for (int j = 0; j < ROWS_PER_WARP; ++j) kv[j] += __shfl_xor_sync(0xffffffffu, kv[j], off);
-    float delta[ROWS_PER_WARP], out[ROWS_PER_WARP];
+    // the row's delta is formed by the lanes holding its sum, then broadcast
+    const float kv_row = warp_reduce_rows4(kv, lane);
+    const float d_row =
+        __fmul_rn(__fsub_rn(v_s[t * ROWS + warp * ROWS_PER_WARP + my_row], kv_row), b_s[t]);
+    float out[ROWS_PER_WARP];
 #pragma unroll
     for (int j = 0; j < ROWS_PER_WARP; ++j) {
-      delta[j] = __fmul_rn(__fsub_rn(v_s[t * ROWS + warp * ROWS_PER_WARP + j], kv[j]), b_s[t]);
+      const float dj = __shfl_sync(0xffffffffu, d_row, 8 * (j & 1) + 16 * (j >> 1));
       float acc = 0.f;
 #pragma unroll
       for (int i = 0; i < NPL; ++i) {
-        s[j][i] = __fadd_rn(s[j][i], __fmul_rn(kt[i], delta[j]));
+        s[j][i] = __fadd_rn(s[j][i], __fmul_rn(kt[i], dj));
         acc = __fmaf_rn(s[j][i], qt[i], acc);
       }
       out[j] = acc;
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-      for (int j = 0; j < ROWS_PER_WARP; ++j) out[j] += __shfl_xor_sync(0xffffffffu, out[j], off);
-    if (lane < ROWS_PER_WARP) {
-      // lane j writes row j (values are uniform across the warp after the butterfly)
-      float dj = delta[0], oj = out[0];
-#pragma unroll
-      for (int j = 1; j < ROWS_PER_WARP; ++j)
-        if (lane == j) { dj = delta[j]; oj = out[j]; }
-      p.tape[out_off + lane] = dj;
-      p.y[out_off + lane] = __float2bfloat16_rn(oj);
+    const float out_row = warp_reduce_rows4(out, lane);
+    if (writer) {
+      p.tape[out_off + my_row] = d_row;
+      p.y[out_off + my_row] = __float2bfloat16_rn(out_row);
     }
   }
 

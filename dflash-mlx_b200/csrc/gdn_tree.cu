@@ -155,50 +155,50 @@ __global__ void __launch_bounds__(THREADS) gdn_tree_kernel(const TreeParams p) {
 #pragma unroll
     for (int j = 0; j < ROWS_PER_WARP; ++j)
       load_slice<NPL>(par < 0 ? p.state_in + (head_rows + rw + j) * DK + c0 : node_row(par, rw + j), s[j]);
-    const float* kt = k_s + t * DK + c0;
-    const float* qt = q_s + t * DK + c0;
+    float kt[NPL], qt[NPL], gv[NPL];
+    lds_vec<NPL>(k_s + t * DK + c0, kt);
+    lds_vec<NPL>(q_s + t * DK + c0, qt);
+    if (p.g_vec) {
+      lds_vec<NPL>(g_s + t * DK + c0, gv);
+    } else {
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) gv[i] = g_s[t];
+    }
     float kv[ROWS_PER_WARP];
 #pragma unroll
     for (int j = 0; j < ROWS_PER_WARP; ++j) {
       float acc = 0.f;
 #pragma unroll
       for (int i = 0; i < NPL; ++i) {
-        const float gd = p.g_vec ? g_s[t * DK + c0 + i] : g_s[t];
-        s[j][i] = __fmul_rn(s[j][i], gd);
+        s[j][i] = __fmul_rn(s[j][i], gv[i]);
         acc = __fmaf_rn(s[j][i], kt[i], acc);
       }
       kv[j] = acc;
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-      for (int j = 0; j < ROWS_PER_WARP; ++j) kv[j] += __shfl_xor_sync(0xffffffffu, kv[j], off);
-    float delta[ROWS_PER_WARP], out[ROWS_PER_WARP];
+    // the lanes holding a row's sum form its delta; then it is broadcast
+    const int my_row = row_of_lane4(lane);
+    const float kv_row = warp_reduce_rows4(kv, lane);
+    const float d_row =
+        __fmul_rn(__fsub_rn(v_s[t * ROWS + warp * ROWS_PER_WARP + my_row], kv_row), b_s[t]);
+    float out[ROWS_PER_WARP];
 #pragma unroll
     for (int j = 0; j < ROWS_PER_WARP; ++j) {
-      delta[j] = __fmul_rn(__fsub_rn(v_s[t * ROWS + warp * ROWS_PER_WARP + j], kv[j]), b_s[t]);
+      const float dj = __shfl_sync(0xffffffffu, d_row, 8 * (j & 1) + 16 * (j >> 1));
       float acc = 0.f;
 #pragma unroll
       for (int i = 0; i < NPL; ++i) {
-        s[j][i] = __fadd_rn(s[j][i], __fmul_rn(kt[i], delta[j]));
+        s[j][i] = __fadd_rn(s[j][i], __fmul_rn(kt[i], dj));
         acc = __fmaf_rn(s[j][i], qt[i], acc);
       }
       out[j] = acc;
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-      for (int j = 0; j < ROWS_PER_WARP; ++j) out[j] += __shfl_xor_sync(0xffffffffu, out[j], off);
+    const float out_row = warp_reduce_rows4(out, lane);
 #pragma unroll
     for (int j = 0; j < ROWS_PER_WARP; ++j) store_slice<NPL>(node_row(t, rw + j), s[j]);
-    if (lane < ROWS_PER_WARP) {
-      float dj = delta[0], oj = out[0];
-#pragma unroll
-      for (int j = 1; j < ROWS_PER_WARP; ++j)
-        if (lane == j) { dj = delta[j]; oj = out[j]; }
-      const size_t o = (((size_t)b * T + t) * p.Hv + hv) * p.Dv + rw + lane;
-      y[o] = from_f<InT>(oj);
-      if (p.tape) p.tape[o] = dj;
+    if ((lane & 7) == 0) {
+      const size_t o = (((size_t)b * T + t) * p.Hv + hv) * p.Dv + rw + my_row;
+      y[o] = from_f<InT>(out_row);
+      if (p.tape) p.tape[o] = d_row;
     }
   }
 }
