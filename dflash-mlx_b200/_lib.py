@@ -50,6 +50,7 @@ SIGNATURES = {
                                                  _c_int, _c_int, _vp]),
     "dfl_verify_qmm_w4g64_pairs_silu_f16": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_size,
                                                      _c_int, _c_int, _c_int, _vp]),
+    "dfl_qmm_stream_k_ranges": (_c_int, [_c_int, _c_int, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "dfl_verify_qmm_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
     "dfl_verify_qmm_w4g64_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
                                               _vp]),

@@ -124,6 +124,7 @@ struct Params {
   const int* g_rows;       // [P][16]
   const int* g_out;        // [P][16]
   int tpp;                 // 128-row tiles per problem (all tiles when dense)
+  int table_ready;         // grouped: the route table predates the previous launch
   // Dense: first unit of every CTA's stream-K range, ubeg[grid] = total
   // (computed on the host, see split_ranges).  Grouped launches know their
   // unit count only on the device and split evenly.
@@ -384,9 +385,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int tpp = p.tpp;
   // Launched with programmatic serialization: the route table of grouped
   // mode may be written by the kernel just before, so grouped CTAs wait for
-  // it first.  Dense CTAs only wait in the warps that read x and write y or
-  // the workspace; weight loads and dequant start at once.
-  if (GROUPED) griddep_wait();
+  // it first unless the caller states that it was complete before the
+  // previous launch started.  Otherwise (and in dense mode) only the warps
+  // that read x or the workspace and write y wait; weight loads and dequant
+  // start at once.
+  if (GROUPED && !p.table_ready) griddep_wait();
   const int total = GROUPED ? (*p.g_count) * tpp * ku : p.total_units;
   const int u0 = unit_begin(p, GROUPED, cta, total);
   const int u1 = unit_begin(p, GROUPED, cta + 1, total);
@@ -1022,6 +1025,15 @@ int launch(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales, const
 }  // namespace qmm
 }  // namespace dfl
 
+extern "C" int dfl_qmm_stream_k_ranges(int total, int grid, int* ubeg, int* skew_used) {
+  if (total < 1 || grid < 1 || grid > total || grid > dfl::qmm::kMaxGrid) return DFL_ERR_BAD_SHAPE;
+  if (!ubeg) return DFL_ERR_NULL_POINTER;
+  const int skew = dfl::qmm::clamp_skew(dfl::qmm::kSplitSkew, total, grid);
+  dfl::qmm::split_ranges(total, grid, skew, ubeg);
+  if (skew_used) *skew_used = skew;
+  return DFL_OK;
+}
+
 extern "C" size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status) {
   int dummy;
   int* st = status ? status : &dummy;
@@ -1239,7 +1251,8 @@ int moe_entry(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
   p.g_count = route;
   p.g_expert = route + 1;
   p.g_m = route + 1 + E;
-  p.g_rows = gather_by_pair ? route + 1 + 2 * E + 16 * E : route + 1 + 2 * E;
+  p.g_rows = (gather_by_pair & 1) ? route + 1 + 2 * E + 16 * E : route + 1 + 2 * E;
+  p.table_ready = (gather_by_pair & 2) ? 1 : 0;
   p.g_out = route + 1 + 2 * E + 16 * E;
   CUtensorMap tm_w, tm_s, tm_b, tm_x;
   std::memset(&tm_x, 0, sizeof(tm_x));  // grouped mode gathers x rows with plain loads

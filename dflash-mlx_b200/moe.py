@@ -72,12 +72,14 @@ def route(router_logits: torch.Tensor, top_k: int = 8):
 
 def gather_qmm(x: torch.Tensor, weight: QuantWeight, table: torch.Tensor, *, rows_out: int,
                gather_by_pair: bool, max_problems: Optional[int] = None,
-               out: Optional[torch.Tensor] = None, silu: bool = False) -> torch.Tensor:
+               out: Optional[torch.Tensor] = None, silu: bool = False,
+               table_ready: bool = False) -> torch.Tensor:
     """Grouped int4 qmm over the route table's active experts -> bf16 ``[rows_out, N]``.
 
     ``silu=True``: each expert's weights are its gate/up pair interleaved
     (:func:`fuse_expert_gate_up`) and the result is ``silu(gate) * up``,
-    ``[rows_out, N/2]``."""
+    ``[rows_out, N/2]``.  ``table_ready``: the route table was complete before
+    the previous launch on the stream started, so weights may stream early."""
     e = int(weight.q.shape[0])
     k, n = weight.k, weight.n
     x = x.contiguous()
@@ -90,7 +92,8 @@ def gather_qmm(x: torch.Tensor, weight: QuantWeight, table: torch.Tensor, *, row
         ws = workspace(x.device, _moe_ws_bytes(mp, k, n))
         st = getattr(_lib.load(), entry)(
             x.data_ptr(), weight.q.data_ptr(), weight.s.data_ptr(), weight.b.data_ptr(),
-            out.data_ptr(), table.data_ptr(), 1 if gather_by_pair else 0, mp, e, k, n,
+            out.data_ptr(), table.data_ptr(), (1 if gather_by_pair else 0) | (2 if table_ready else 0),
+            mp, e, k, n,
             ws.data_ptr(), ws.numel(), stream_ptr(x.device))
     _lib.check(entry, st)
     return out
@@ -169,21 +172,28 @@ def moe_layer(x: torch.Tensor, router_logits: torch.Tensor, experts: dict, share
     require_cuda(x, "x")
     t = x.shape[0]
     table, w, _ = route(router_logits, top_k)
-    fused = "gate_up" in experts
-    e = int((experts["gate_up"] if fused else experts["gate"]).q.shape[0])
-    mp = min(e, t * top_k)
-    if fused:
-        h = gather_qmm(x, experts["gate_up"], table, rows_out=t * top_k, gather_by_pair=False,
-                       max_problems=mp, silu=True)
-    else:
-        g = gather_qmm(x, experts["gate"], table, rows_out=t * top_k, gather_by_pair=False, max_problems=mp)
-        u = gather_qmm(x, experts["up"], table, rows_out=t * top_k, gather_by_pair=False, max_problems=mp)
-        h = silu_mul(g, u)
-    d = gather_qmm(h, experts["down"], table, rows_out=t * top_k, gather_by_pair=True, max_problems=mp)
+    # The shared expert does not depend on the routing: run it first, so the
+    # grouped launches after it find the route table already complete and can
+    # stream their weights while the launch before them finishes.
     so = None
     if shared is not None:
         if "gate_up" in shared:
             so = dense_mlp_fused(x, shared["gate_up"], shared["down"])
         else:
             so = dense_mlp(x, shared["gate"], shared["up"], shared["down"])
+    ready = shared is not None
+    fused = "gate_up" in experts
+    e = int((experts["gate_up"] if fused else experts["gate"]).q.shape[0])
+    mp = min(e, t * top_k)
+    if fused:
+        h = gather_qmm(x, experts["gate_up"], table, rows_out=t * top_k, gather_by_pair=False,
+                       max_problems=mp, silu=True, table_ready=ready)
+    else:
+        g = gather_qmm(x, experts["gate"], table, rows_out=t * top_k, gather_by_pair=False,
+                       max_problems=mp, table_ready=ready)
+        u = gather_qmm(x, experts["up"], table, rows_out=t * top_k, gather_by_pair=False, max_problems=mp,
+                       table_ready=True)
+        h = silu_mul(g, u)
+    d = gather_qmm(h, experts["down"], table, rows_out=t * top_k, gather_by_pair=True, max_problems=mp,
+                   table_ready=True)
     return combine(d, w, so)

@@ -127,6 +127,14 @@ int dfl_verify_qmm_w4g64_pairs_silu_f16(const uint16_t* x, const uint32_t* w_q,
                                         uint16_t* h, void* workspace, size_t workspace_bytes,
                                         int M, int K, int N, void* stream);
 
+/* The dense qmm's stream-K split of `total` (tile, K unit) pairs over `grid`
+ * CTAs, as the launches use it: CTA c takes units [ubeg[c], ubeg[c + 1]),
+ * ubeg has grid + 1 entries, the first half of the CTAs weigh 1 and the
+ * weight falls linearly to 1 - skew / 256 at the last CTA (*skew_used, the
+ * built-in skew clamped so every range keeps at least one unit).  Host-only
+ * (no device access); exposed for tests of the split. */
+int dfl_qmm_stream_k_ranges(int total, int grid, int* ubeg, int* skew_used);
+
 /* Workspace bytes dfl_verify_qmm_w4g64 needs for this shape on the current
  * device; 0 with *status != DFL_OK on error. */
 size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status);
@@ -287,7 +295,11 @@ int dfl_match_acceptance(const int32_t* drafted, const int32_t* posterior, int B
  * (gather_by_pair = 0; x is [T, K]) or its pair rows (gather_by_pair = 1; x is
  * [T * top_k, K]); y is [T * top_k, N].  Each active expert's weights are read
  * once.  max_problems bounds P (grid size); workspace as for the dense qmm
- * with dfl_moe_qmm_workspace_bytes.
+ * with dfl_moe_qmm_workspace_bytes.  gather_by_pair bit 1 (value 2) states
+ * that the route table was complete before the previous launch on the stream
+ * started (e.g. two launches back, with plain stream order before that):
+ * the kernel then streams weights before the previous launch finishes, like
+ * the dense qmm.
  *
  * dfl_silu_mul_bf16: out = bf16(silu(gate) * up), fp32 math.
  * dfl_moe_combine: y[t] = bf16(sum_j weights[t, j] * pair_out[t * top_k + j]

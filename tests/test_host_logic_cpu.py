@@ -213,3 +213,39 @@ def test_install_swaps_eligible_modules_once(pkg):
     only_down = nn.Module()
     only_down.mlp = Block()
     assert pkg.install_verify_linears(only_down, predicate=lambda path, m: path.endswith("down_proj")) == 1
+
+
+# ------------------------------------------------------------ stream-K split
+@pytest.mark.parametrize("total", [1, 2, 3, 147, 148, 149, 296, 480, 640, 1360, 2720, 3392, 99999])
+def test_stream_k_ranges_cover_every_unit_once(pkg, total):
+    """The split the qmm launches use (host code of the library, no device):
+    ranges are contiguous, non-empty, cover [0, total) exactly once, and the
+    later CTAs (which start last under programmatic launch) never get more
+    units than the first half."""
+    import ctypes
+
+    from dflash_mlx_b200 import _lib
+
+    grid = min(total, 148)
+    ubeg = (ctypes.c_int * (grid + 1))()
+    skew = ctypes.c_int(-1)
+    assert _lib.load().dfl_qmm_stream_k_ranges(total, grid, ubeg, ctypes.byref(skew)) == 0
+    u = np.array(list(ubeg))
+    n = np.diff(u)
+    assert u[0] == 0 and u[-1] == total
+    assert (n >= 1).all()
+    assert 0 <= skew.value <= 255
+    if skew.value > 0:
+        h = grid // 2
+        assert n[h:].max() <= n[:h].max()
+        assert n[-1] <= n[0]
+
+
+def test_stream_k_ranges_reject_bad_input(pkg):
+    import ctypes
+
+    from dflash_mlx_b200 import _lib
+
+    ubeg = (ctypes.c_int * 8)()
+    assert _lib.load().dfl_qmm_stream_k_ranges(3, 5, ubeg, None) == 2   # grid > total
+    assert _lib.load().dfl_qmm_stream_k_ranges(0, 1, ubeg, None) == 2
