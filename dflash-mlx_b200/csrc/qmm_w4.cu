@@ -10,37 +10,33 @@
 //
 // Mapping onto Blackwell (M is tiny, so the MMA is "swapped"):
 //   * a CTA tile is 128 output channels (the UMMA M dimension) x MT tokens
-//     (the UMMA N dimension, MT = 16 or 32);
-//   * the pipeline unit is 512 of K (8 quant groups).  TMA streams only the
-//     packed nibbles (2 boxes of [128 rows x 128 B], 128-byte swizzle) into a
-//     4-stage ring: TMA cost scales with the number of box rows, so nothing
-//     with short rows goes through it.  The producer warp's 32 lanes copy the
-//     unit's 8 scales and 8 biases per row with 16-byte cp.async into the
-//     same stage, completing on the stage's mbarrier;
-//   * dequant warps (groups of four, one warp per TMEM lane quadrant, one
-//     thread per output channel) unpack nibbles in registers: one shift + one
-//     LOP3 per bf16 pair gives 128 + n exactly, then one bf16x2 subtract and
-//     one bf16x2 FMA give n * s + b with a single rounding.  The pairs come
-//     out in the within-8 K order 0,4,1,5,2,6,3,7; the tile goes straight
-//     into TMEM with tcgen05.st (one lane per output channel, 32 columns per
-//     quant group, 8 slots = one unit);
-//   * the four epilogue warps also stage x: one unit ahead they load the x
-//     slice from global memory (L2), apply the same within-8 K permutation in
-//     registers and store it into a shared-memory ring in the UMMA
-//     128-byte-swizzled K-major layout;
+//     (the UMMA N dimension, MT = 16 or 32); one CTA per SM, 25 warps;
+//   * the pipeline unit is 512 of K (8 quant groups).  The producer warp
+//     streams the packed nibbles by TMA (2 boxes of [128 rows x 128 B],
+//     128-byte swizzle) into a 4-stage ring and the scales / biases in
+//     4-unit chunks into a 2-slot ring, without waiting for the previous
+//     launch (programmatic dependent launch);
+//   * 16 dequant warps (4 groups x 4 TMEM lane quadrants, thread = output
+//     channel) unpack nibbles in registers: 3 shifts + 4 LOP3 per word give
+//     128 + n exactly, then per pair one exact bf16x2 FMA (v - 128) and one
+//     bf16x2 FMA n * s + b with a single rounding.  MLX-packed words come out
+//     in the within-8 K order 0,4,1,5,2,6,3,7, pair-packed words (PW) in
+//     natural order; tiles go to 12 rotating TMEM A slots with tcgen05.st;
+//   * x: with PW weights one x-warp thread loads it by TMA straight into a
+//     4-slot ring; with MLX packing the x warps stage it and permute each
+//     16-byte chunk to the within-8 order; grouped (MoE) mode gathers rows;
 //   * four MMA warps each own an accumulator and two of the eight sub-blocks
-//     of a unit.  A thread keeps one tcgen05.mma in flight for ~50-65 cycles
-//     whatever N is, and any dependent scalar work between two MMAs adds to
-//     that, so the issue loops do nothing but wait and issue MMAs with
-//     precomputed descriptors; four issuers keep up with HBM at N = 16;
-//   * the epilogue warps drain and sum the four accumulators (fixed order);
-//     accumulators are double-buffered so the epilogue overlaps the next tile.
+//     of a unit and only wait and issue (one MMA per ~64+ cycles per thread
+//     at N = 16, so four issuers are needed);
+//   * the x warps run the epilogue (TMEM -> registers -> y; with SILU the
+//     gate/up pairs of a warp's lanes are combined by one shuffle).
 // Work is split "stream-K" style: the (tile, K unit) space is cut into one
-// contiguous range per CTA (grid = min(#SMs, #units)), so every SM streams
-// the same number of bytes whatever N and K are.  Tiles shared by several
-// CTAs are reduced through an fp32 workspace; the last CTA to arrive (one
-// atomic counter per tile, no spin-waits) sums the partials in CTA order,
-// so results are bit-reproducible, writes bf16 and resets the counter.
+// contiguous range per CTA (grid = min(#SMs, #units)), ranges computed on the
+// host and skewed towards the CTAs that start first.  A tile shared by CTAs
+// c_lo..c_hi is the last of c_lo's range: the others store tagged fp32
+// partials (low mantissa bit set), c_lo's dequant warps poll, sum them in
+// CTA order and clear them, and its epilogue adds its own accumulator, so
+// results are bit-reproducible.
 #include "common.cuh"
 #include "host_common.cuh"
 
@@ -896,11 +892,11 @@ namespace qmm {
 
 inline int choose_mt(int M) { return M <= 16 ? 16 : 32; }
 
-// Zero-invariant counter area at the start of every workspace (one int per
-// 128-row tile): N <= kMaxTiles * 128.
+// Reserved area at the start of every workspace; it also bounds the tile
+// count of one launch: N <= kMaxTiles * 128.
 constexpr size_t kCounterBytes = host::kWorkspaceCounterBytes;
 constexpr int kMaxTiles = int(kCounterBytes / sizeof(int));
-// Stream-K split skew of the dense launches (see split_weight).
+// Stream-K split skew of the dense launches (see split_ranges).
 constexpr int kSplitSkew = 64;
 
 // Largest skew <= want (in steps of 8) that still leaves the last CTA a
