@@ -273,8 +273,8 @@ def run_ours(args):
 
     # roofline of the dominant kernel (the int4 verify qmm)
     peak, peak_kind = _peaks()
-    launches = len(sh.launches()) * sh.layers * b
-    bytes_per_step = sh.qmm_bytes_per_request(silu_fused=step.fuse_silu) * b
+    launches = len(sh.launches()) * sh.layers * (((b + 1) // 2) if step.pack_requests else b)
+    bytes_per_step = sh.qmm_bytes_per_step(b, step.pack_requests, silu_fused=step.fuse_silu)
     achieved = bytes_per_step / (t_qmm / args.steps) / 1e9
     traffic, _ = _traffic_per_launch()
 
@@ -296,6 +296,7 @@ def run_ours(args):
                             "ranks) + config4 (48-layer GDN tape-replay rollback)",
                 "requests_per_gpu": b, "tokens_per_request": sh.block,
                 "weight_layout": args.weight_layout,
+                "requests_share_launches": step.pack_requests,
                 "mlp_silu_fused": step.fuse_silu,
                 "parallelism": f"request-DP x{world}, lm_head vocab split x{world}",
                 "l2": "inputs larger than L2 (12.3 GB of packed weights per step)",
@@ -312,7 +313,7 @@ def run_ours(args):
             # ours per step: 4 qmm per layer and request (+ 1 SiLU*up launch unless it
             # is fused into the gate|up epilogue), lm_head argmax, accept, one tape
             # replay over all GDN layers
-            "gpu_launches": args.steps * (launches + (0 if step.fuse_silu else sh.layers * b)
+            "gpu_launches": args.steps * (launches + (0 if step.fuse_silu else launches // 4)
                                           + 2 + 1),
             "e2e": {"value": world * b / t_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},

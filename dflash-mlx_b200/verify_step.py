@@ -8,7 +8,9 @@ for ``requests`` independent requests of 16 verify tokens on this GPU:
    request (q, k, v, o, gate, up, down; ``verify_linear.py`` ->
    ``verify_qmm.py``), with SiLU * up feeding down.  Projections that read
    the same input are stored concatenated (q|k|v, gate|up) and run as one
-   launch each, 4 launches per layer;
+   launch each, 4 launches per layer; with several requests on the GPU two
+   requests' rows share each launch (32 rows), so weights are read once per
+   pair of requests;
 2. the lm_head argmax + greedy acceptance epilogue (``spec_epoch.py:2067-2072``)
    on a vocabulary shard, keys all-gathered across ranks when the vocabulary
    is split;
@@ -66,6 +68,18 @@ class StackShape:
         return [("qkv", self.q_out + 2 * self.kv_out, h), ("o", h, self.q_out),
                 ("gate_up", 2 * self.inter, h), ("down", h, self.inter)]
 
+    def qmm_bytes_per_step(self, requests: int, packed: bool, silu_fused: bool = False) -> int:
+        """Algorithmic bytes of the projection stack for ``requests`` requests on
+        one GPU: weights (+ scales, biases) once per launch, i.e. once per pair
+        of requests when their rows share launches (32 rows per launch), and
+        each request's activations."""
+        launches = (requests + 1) // 2 if packed else requests
+        total = 0
+        for name, n, k in self.launches():
+            n_out = n // 2 if (silu_fused and name == "gate_up") else n
+            total += launches * (n * k // 2 + 2 * 2 * n * (k // 64)) + requests * 2 * self.block * (k + n_out)
+        return total * self.layers
+
     def qmm_bytes_per_request(self, silu_fused: bool = False) -> int:
         """Algorithmic bytes of one request's projection stack: packed weights +
         bf16 scales and biases + bf16 activations in and out, per launch (the
@@ -93,7 +107,7 @@ class VerifyStep:
 
     def __init__(self, device: torch.device, *, requests: int = 1, shape: Optional[StackShape] = None,
                  rank: int = 0, world: int = 1, group=None, seed: int = 0,
-                 weight_layout: str = "mlx", fuse_silu: bool = False):
+                 weight_layout: str = "mlx", fuse_silu: bool = False, pack_requests: bool = True):
         self.dev = torch.device(device)
         if weight_layout not in ("mlx", "pairs"):
             raise ValueError(f"unknown weight layout {weight_layout!r}")
@@ -104,6 +118,7 @@ class VerifyStep:
         # interleaved in blocks of 16 (interleave_gate_up) and one launch
         # writes silu(gate) * up
         self.fuse_silu = bool(fuse_silu)
+        self.pack_requests = bool(pack_requests)
         self.shape = shape or StackShape()
         self.requests = int(requests)
         self.rank, self.world, self.group = rank, world, group
@@ -159,9 +174,13 @@ class VerifyStep:
     # -------------------------------------------------------------- parts
     def _qmm_stack(self):
         sh = self.shape
-        for r in range(self.requests):
-            x = self.x[r * sh.block:(r + 1) * sh.block]
-            a = self.attn_out[r * sh.block:(r + 1) * sh.block]
+        # With several requests on this GPU their rows go through each launch
+        # together: the qmm takes up to 32 rows per launch (two requests'
+        # 16-token blocks), so each weight is read once per pair of requests.
+        groups = [(0, self.requests)] if self.pack_requests else [(r, r + 1) for r in range(self.requests)]
+        for r0, r1 in groups:
+            x = self.x[r0 * sh.block:r1 * sh.block]
+            a = self.attn_out[r0 * sh.block:r1 * sh.block]
             lay = self.weight_layout
             for lw in self.layers:
                 self.last_qkv = qmm_w4g64(x, lw["qkv"].q, lw["qkv"].s, lw["qkv"].b, layout=lay)
