@@ -15,6 +15,9 @@
 //     slots it consumes, so the array is zero again for the next call and
 //     calls in stream order are safe; calls that may overlap in time
 //     (different streams or host threads) race on the array.
+//   * A call that timed out (device error word set) can leave partial sums
+//     behind; nothing zero-fills the array a second time, so later results
+//     in that process are not to be trusted.
 // Nothing here calls cudaMalloc / cudaFree or any allocating routine.
 
 namespace dfl {

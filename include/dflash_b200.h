@@ -150,7 +150,10 @@ size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status);
  *     before any stream capture there);
  *   - the first call on a device zero-fills the array on `stream`; every
  *     call leaves it zero again, so calls in stream order are safe; calls
- *     that can overlap in time race.
+ *     that can overlap in time race;
+ *   - a call that timed out (dfl_get_device_error non-zero) can leave partial
+ *     sums behind, and nothing clears the array again: results of later
+ *     calls in that process are not to be trusted.
  * Allocates nothing. */
 int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
                                  const uint16_t* biases, uint16_t* y, int M, int K, int N,
