@@ -249,3 +249,40 @@ def test_stream_k_ranges_reject_bad_input(pkg):
     ubeg = (ctypes.c_int * 8)()
     assert _lib.load().dfl_qmm_stream_k_ranges(3, 5, ubeg, None) == 2   # grid > total
     assert _lib.load().dfl_qmm_stream_k_ranges(0, 1, ubeg, None) == 2
+
+
+# ------------------------------------------------------------ byte accounting
+def test_stack_bytes_per_layer_match_launch_shapes(pkg):
+    """The roofline's algorithmic bytes: per launch, packed nibbles N K / 2,
+    bf16 scales and biases 2 x 2 N K / 64, bf16 rows in and out 2 x 16 x
+    (K + N_out), with N_out = N / 2 for the fused gate|up + SiLU launch.  For
+    the benchmark's decoder layer (q|k|v 8192 x 5120, o 5120 x 6144, gate|up
+    34816 x 5120, down 5120 x 17408) that is 193,921,024 bytes."""
+    from dflash_mlx_b200.verify_step import StackShape
+
+    def launch_bytes(n, k, n_out):
+        return n * k // 2 + 4 * n * (k // 64) + 2 * 16 * (k + n_out)
+
+    expect = (launch_bytes(8192, 5120, 8192) + launch_bytes(5120, 6144, 5120)
+              + launch_bytes(34816, 5120, 17408) + launch_bytes(5120, 17408, 5120))
+    assert expect == 193_921_024
+    one = StackShape(layers=1)
+    assert one.qmm_bytes_per_request(silu_fused=True) == expect
+    assert one.qmm_bytes_per_step(1, packed=True, silu_fused=True) == expect
+    assert StackShape().qmm_bytes_per_step(1, packed=True, silu_fused=True) == 64 * expect
+
+
+@pytest.mark.parametrize("requests", [1, 2, 3, 8])
+def test_stack_bytes_count_weights_once_per_shared_launch(pkg, requests):
+    """Two requests' rows share each launch when packed, so weights are read
+    ceil(requests / 2) times; activations are per request either way."""
+    from dflash_mlx_b200.verify_step import StackShape
+
+    sh = StackShape(layers=2)
+    per_req = sh.qmm_bytes_per_request(silu_fused=True)
+    acts = sum(2 * sh.block * (k + (n // 2 if name == "gate_up" else n))
+               for name, n, k in sh.launches()) * sh.layers
+    weights = per_req - acts
+    assert sh.qmm_bytes_per_step(requests, packed=False, silu_fused=True) == requests * per_req
+    assert (sh.qmm_bytes_per_step(requests, packed=True, silu_fused=True)
+            == (requests + 1) // 2 * weights + requests * acts)
