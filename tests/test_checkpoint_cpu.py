@@ -147,6 +147,48 @@ def test_rejects_non_safetensors(pkg, tmp_path):
         pkg.checkpoint.Checkpoint(tmp_path)
 
 
+def test_single_file_quantization_config_and_bias(pkg, tmp_path):
+    """One safetensors file without an index, the quantization under
+    ``quantization_config``, a projection with an additive ``.bias``, and a
+    projection stored without ``.biases`` (not affine int4: refused)."""
+    rng = np.random.default_rng(11)
+    w, s, b = _linear(rng, 64, 128)
+    bias = obf16.from_f32(rng.standard_normal(64).astype(np.float32))
+    w2, s2, _ = _linear(rng, 64, 128)
+    _write_safetensors(tmp_path / "model.safetensors", {
+        "proj.weight": ("U32", w), "proj.scales": ("BF16", s), "proj.biases": ("BF16", b),
+        "proj.bias": ("BF16", bias)})
+    (tmp_path / "config.json").write_text(json.dumps({"quantization_config": {"group_size": 64, "bits": 4}}))
+    mods = pkg.checkpoint.load_quantized_linears(tmp_path, "cpu")
+    assert sorted(mods) == ["proj"]
+    m = mods["proj"]
+    assert (m.in_features, m.out_features) == (128, 64)
+    assert np.array_equal(_bits16(m.bias), bias)
+    with pytest.raises(NotImplementedError):
+        pkg.checkpoint.fuse_rows([m])
+
+    other = tmp_path / "no_biases"
+    other.mkdir()
+    _write_safetensors(other / "model.safetensors", {"p.weight": ("U32", w2), "p.scales": ("BF16", s2)})
+    (other / "config.json").write_text(json.dumps({"quantization": {"group_size": 64, "bits": 4,
+                                                                    "mode": "mxfp4"}}))
+    with pytest.raises(NotImplementedError):
+        pkg.checkpoint.load_quantized_linears(other, "cpu")
+
+
+def test_rejects_tensor_size_mismatch(pkg, tmp_path):
+    """A header whose data offsets disagree with the shape is refused."""
+    rng = np.random.default_rng(12)
+    w, s, b = _linear(rng, 64, 128)
+    _write_safetensors(tmp_path / "model.safetensors", {"p.weight": ("U32", w), "p.scales": ("BF16", s),
+                                                        "p.biases": ("BF16", b)})
+    ck = pkg.checkpoint.Checkpoint(tmp_path)
+    ref = ck.tensors["p.weight"]
+    bad = pkg.checkpoint.TensorRef(ref.file, ref.dtype, (64, 8), ref.begin, ref.end)
+    with pytest.raises(ValueError):
+        bad.numpy()
+
+
 @pytest.mark.gpu
 def test_loaded_layers_run_on_the_gpu(pkg, ckpt):
     """Loaded to the GPU: a verify linear of the checkpoint matches the oracle
