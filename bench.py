@@ -102,6 +102,13 @@ def cpu_step_sample(scale_layers: bool = True):
     return total, sample, {"qmm_s": t_qmm, "lm_head_s": t_lm, "gdn_s": t_gdn}
 
 
+def workload_name(layers: int = 64) -> str:
+    """The verify-step workload both arms time (config.workload)."""
+    return (f"verify step = config1 ({layers}-layer int4 g64 qmm stack, hidden 5120, "
+            "M=16 per request) + config3 (lm_head 248320x5120 bf16, vocab split over "
+            "ranks) + config4 (48-layer GDN tape-replay rollback)")
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -122,8 +129,9 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded, BASELINE distributions)",
-        "config": {"workload": "verify step: config1 stack + config3 lm_head + config4 rollback",
-                   "requests_per_gpu": 1, "tokens_per_request": 16},
+        "config": {"workload": workload_name(), "requests_per_gpu": args.requests_per_gpu,
+                   "tokens_per_request": 16,
+                   "parallelism": "host cores of rank 0 (request-steps/s do not depend on the GPU count)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -291,9 +299,7 @@ def run_ours(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random weights with BASELINE distributions; no checkpoints offline)",
             "config": {
-                "workload": f"verify step = config1 ({sh.layers}-layer int4 g64 qmm stack, hidden 5120, "
-                            "M=16 per request) + config3 (lm_head 248320x5120 bf16, vocab split over "
-                            "ranks) + config4 (48-layer GDN tape-replay rollback)",
+                "workload": workload_name(sh.layers),
                 "requests_per_gpu": b, "tokens_per_request": sh.block,
                 "weight_layout": args.weight_layout,
                 "requests_share_launches": step.pack_requests,
