@@ -88,3 +88,46 @@ def test_python_surface_refuses_cpu_tensors(pkg):
         pkg.verify_matmul(x, w, s, s)
     with pytest.raises(NotImplementedError):
         pkg.verify_matmul(x, w, s, s, bits=8)
+
+
+def _declarations():
+    """(return type, name, [parameter types]) of every declaration in include/*.h."""
+    out = []
+    for h in sorted((ROOT / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for ret, name, params in re.findall(
+                r"([A-Za-z_][A-Za-z0-9_ \*]*?)\b(dfl_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+            ps = [] if params.strip() in ("", "void") else [p.strip() for p in params.split(",")]
+            types = [p.rsplit(" ", 1)[0] if not p.endswith("*") else p for p in ps]
+            out.append((ret.strip(), name, types))
+    return out
+
+
+def _ctypes_kind(t):
+    if t in (ctypes.c_void_p, ctypes.c_char_p) or isinstance(t, type(ctypes.POINTER(ctypes.c_int))):
+        return "pointer"
+    # c_size_t and c_uint64 are the same ctypes class on LP64 Linux
+    return {ctypes.c_int: "int", ctypes.c_size_t: "u64", ctypes.c_uint64: "u64",
+            ctypes.c_float: "float"}.get(t, repr(t))
+
+
+def _c_kind(t):
+    t = t.replace("const ", "").strip()
+    if t.endswith("*"):
+        return "pointer"
+    return {"int": "int", "int32_t": "int", "size_t": "u64", "uint64_t": "u64",
+            "float": "float"}.get(t, t)
+
+
+def test_binding_signatures_match_the_header(pkg):
+    """Every ctypes signature has the header's arity and, position by position,
+    the same kind of argument (pointer / 32-bit int / 64-bit size), so no call passes a
+    64-bit pointer where the library reads a 32-bit int or the reverse."""
+    from dflash_mlx_b200 import _lib
+
+    decls = _declarations()
+    assert sorted(n for _, n, _ in decls) == _declared_functions()
+    for ret, name, params in decls:
+        restype, argtypes = _lib.SIGNATURES[name]
+        assert [_ctypes_kind(a) for a in argtypes] == [_c_kind(p) for p in params], name
+        assert _ctypes_kind(restype) == _c_kind(ret), name
