@@ -124,7 +124,15 @@ def check(fn: str, status: int) -> None:
 
 
 def device_error() -> int:
-    """Read and clear the kernels' device error word (synchronises the device)."""
+    """Read and clear the kernels' device error word (synchronises the device).
+
+    A non-zero word also zeroes the package's cached workspaces again: a
+    kernel that timed out may have left split-K partial sums in them.
+    """
     v = _c_int(0)
     check("dfl_get_device_error", load().dfl_get_device_error(ctypes.byref(v)))
+    if v.value != 0:
+        from ._runtime import reset_workspaces
+
+        reset_workspaces()
     return int(v.value)

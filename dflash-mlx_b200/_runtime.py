@@ -42,6 +42,23 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
         return buf
 
 
+def reset_workspaces() -> int:
+    """Zero every cached workspace again; returns how many were cleared.
+
+    Kernels leave their workspace zero when they finish normally.  A kernel
+    that gave up on a bounded wait (the device error word is set) can leave
+    partial sums behind, so after a reported device error every buffer is
+    cleared before the next call uses it.
+    """
+    with _ws_lock:
+        bufs = list(_workspaces.values())
+        for buf in bufs:
+            buf.zero_()
+        for dev in {buf.device for buf in bufs if buf.is_cuda}:
+            torch.cuda.synchronize(dev)
+    return len(bufs)
+
+
 def require_cuda(t: torch.Tensor, name: str) -> None:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")

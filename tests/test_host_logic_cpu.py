@@ -286,3 +286,26 @@ def test_stack_bytes_count_weights_once_per_shared_launch(pkg, requests):
     assert sh.qmm_bytes_per_step(requests, packed=False, silu_fused=True) == requests * per_req
     assert (sh.qmm_bytes_per_step(requests, packed=True, silu_fused=True)
             == (requests + 1) // 2 * weights + requests * acts)
+
+
+def test_device_error_clears_cached_workspaces(pkg, monkeypatch):
+    """A reported device error zeroes the cached workspaces (a timed-out
+    kernel may have left partial sums); no error leaves them alone.  The
+    library call is faked: no device is involved."""
+    from dflash_mlx_b200 import _lib, _runtime
+
+    word = {"v": 0}
+
+    class FakeLib:
+        def dfl_get_device_error(self, ptr):
+            ptr._obj.value = word["v"]
+            return 0
+
+    monkeypatch.setattr(_lib, "load", lambda path=None: FakeLib())
+    bufs = {(0, 1): torch.full((64,), 7, dtype=torch.uint8), (0, 2): torch.full((32,), 9, dtype=torch.uint8)}
+    monkeypatch.setattr(_runtime, "_workspaces", bufs)
+    assert _lib.device_error() == 0
+    assert all(int(b.sum()) > 0 for b in bufs.values())
+    word["v"] = 3
+    assert _lib.device_error() == 3
+    assert all(int(b.sum()) == 0 for b in bufs.values())
