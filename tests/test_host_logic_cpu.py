@@ -309,3 +309,32 @@ def test_device_error_clears_cached_workspaces(pkg, monkeypatch):
     word["v"] = 3
     assert _lib.device_error() == 3
     assert all(int(b.sum()) == 0 for b in bufs.values())
+
+
+# ------------------------------------------------------------ load-time layouts
+def test_interleave_gate_up_row_order(pkg):
+    """Rows [g0..g15, u0..u15, g16..g31, u16..u31, ...] along the chosen dim;
+    the expert-stack form interleaves each expert on its own."""
+    from dflash_mlx_b200.verify_qmm import interleave_gate_up
+
+    gate = torch.arange(48 * 3, dtype=torch.int32).reshape(48, 3)
+    up = -1 - gate
+    out = interleave_gate_up(gate, up)
+    assert out.shape == (96, 3)
+    for blk in range(3):
+        assert torch.equal(out[32 * blk:32 * blk + 16], gate[16 * blk:16 * blk + 16])
+        assert torch.equal(out[32 * blk + 16:32 * blk + 32], up[16 * blk:16 * blk + 16])
+    eg = torch.arange(2 * 32 * 4, dtype=torch.int32).reshape(2, 32, 4)
+    eu = eg + 1000
+    stacked = interleave_gate_up(eg, eu, dim=-2)
+    for e in range(2):
+        assert torch.equal(stacked[e], interleave_gate_up(eg[e], eu[e]))
+    qe = pkg.moe.QuantWeight(eg, eg[..., :1].to(torch.bfloat16), eg[..., 1:2].to(torch.bfloat16))
+    qu = pkg.moe.QuantWeight(eu, eu[..., :1].to(torch.bfloat16), eu[..., 1:2].to(torch.bfloat16))
+    fused = pkg.moe.fuse_expert_gate_up(qe, qu)
+    assert torch.equal(fused.q, stacked)
+    assert torch.equal(fused.s, interleave_gate_up(qe.s, qu.s, dim=-2))
+    with pytest.raises(ValueError):
+        interleave_gate_up(gate[:40], up[:40])
+    with pytest.raises(ValueError):
+        interleave_gate_up(gate, up[:32])
