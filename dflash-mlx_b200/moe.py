@@ -47,6 +47,24 @@ class QuantWeight:
         return int(self.q.shape[-1]) * 8
 
 
+def _check_stack(w: QuantWeight, name: str) -> None:
+    """An expert stack: contiguous CUDA ``q`` int32/uint32 ``[E, N, K/8]`` and
+    bf16 ``s``/``b`` ``[E, N, K/64]`` (the grouped kernel's tensor maps assume
+    exactly this layout)."""
+    for part, t in (("q", w.q), ("s", w.s), ("b", w.b)):
+        require_cuda(t, f"{name}.{part}")
+        if not t.is_contiguous():
+            raise ValueError(f"{name}.{part} must be contiguous")
+    if w.q.dim() != 3 or w.q.dtype not in (torch.int32, torch.uint32):
+        raise ValueError(f"{name}.q must be int32/uint32 [E, N, K/8], got {w.q.dtype} {tuple(w.q.shape)}")
+    e, n, k8 = w.q.shape
+    if k8 % 8 != 0:
+        raise ValueError(f"{name}: K = {8 * k8} is not a multiple of the group size 64")
+    for part, t in (("s", w.s), ("b", w.b)):
+        if t.dtype != torch.bfloat16 or tuple(t.shape) != (e, n, k8 // 8):
+            raise ValueError(f"{name}.{part} must be bf16 {(e, n, k8 // 8)}, got {t.dtype} {tuple(t.shape)}")
+
+
 def _moe_ws_bytes(max_problems: int, k: int, n: int) -> int:
     st = ctypes.c_int(0)
     nb = _lib.load().dfl_moe_qmm_workspace_bytes(int(max_problems), int(k), int(n), ctypes.byref(st))
@@ -80,12 +98,23 @@ def gather_qmm(x: torch.Tensor, weight: QuantWeight, table: torch.Tensor, *, row
     (:func:`fuse_expert_gate_up`) and the result is ``silu(gate) * up``,
     ``[rows_out, N/2]``.  ``table_ready``: the route table was complete before
     the previous launch on the stream started, so weights may stream early."""
+    require_cuda(x, "x")
+    require_cuda(table, "table")
+    _check_stack(weight, "weight")
     e = int(weight.q.shape[0])
     k, n = weight.k, weight.n
+    if x.dim() != 2 or x.dtype != torch.bfloat16 or x.shape[1] != k:
+        raise ValueError(f"x must be bf16 [rows, {k}], got {x.dtype} {tuple(x.shape)}")
+    if gather_by_pair and x.shape[0] < rows_out:
+        raise ValueError(f"gather_by_pair reads one x row per output row: {x.shape[0]} < {rows_out}")
+    if table.dtype != torch.int32 or table.numel() < int(_lib.load().dfl_moe_route_table_ints(e)):
+        raise ValueError("table must be the int32 route table of route() for this expert count")
     x = x.contiguous()
     n_out = n // 2 if silu else n
     if out is None:
         out = torch.empty((rows_out, n_out), dtype=torch.bfloat16, device=x.device)
+    elif out.dtype != torch.bfloat16 or tuple(out.shape) != (rows_out, n_out) or not out.is_contiguous():
+        raise ValueError(f"out must be contiguous bf16 {(rows_out, n_out)}")
     mp = e if max_problems is None else int(max_problems)
     entry = "dfl_moe_qmm_w4g64_silu" if silu else "dfl_moe_qmm_w4g64"
     with torch.cuda.device(x.device):
@@ -113,6 +142,10 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """``bf16(silu(gate) * up)`` (fp32 math).  2-D ``gate``/``up`` may be
     row-strided views with the same row stride (e.g. the two halves of a
     fused gate|up projection output); the result is contiguous."""
+    require_cuda(gate, "gate")
+    require_cuda(up, "up")
+    if gate.dtype != torch.bfloat16 or up.dtype != torch.bfloat16:
+        raise ValueError(f"silu_mul takes bf16 gate and up, got {gate.dtype} and {up.dtype}")
     if gate.shape != up.shape:
         raise ValueError(f"gate {tuple(gate.shape)} and up {tuple(up.shape)} differ")
     if (gate.dim() == 2 and gate.stride() == up.stride() and gate.stride(1) == 1
@@ -134,8 +167,19 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
 
 
 def combine(pair_out: torch.Tensor, weights: torch.Tensor, shared: Optional[torch.Tensor]) -> torch.Tensor:
+    """``y[t] = sum_j weights[t, j] * pair_out[t * k + j] (+ shared[t])``, bf16 ``[T, H]``."""
+    require_cuda(pair_out, "pair_out")
+    require_cuda(weights, "weights")
+    if weights.dim() != 2 or weights.dtype != torch.float32:
+        raise ValueError(f"weights must be fp32 [T, k], got {weights.dtype} {tuple(weights.shape)}")
     t, k = weights.shape
     h = pair_out.shape[-1]
+    if pair_out.dtype != torch.bfloat16 or tuple(pair_out.shape) != (t * k, h) or not pair_out.is_contiguous():
+        raise ValueError(f"pair_out must be contiguous bf16 {(t * k, h)}, got {tuple(pair_out.shape)}")
+    if shared is not None:
+        require_cuda(shared, "shared")
+        if shared.dtype != torch.bfloat16 or tuple(shared.shape) != (t, h):
+            raise ValueError(f"shared must be bf16 {(t, h)}, got {shared.dtype} {tuple(shared.shape)}")
     y = torch.empty((t, h), dtype=torch.bfloat16, device=pair_out.device)
     with torch.cuda.device(y.device):
         st = _lib.load().dfl_moe_combine(pair_out.data_ptr(), weights.contiguous().data_ptr(),

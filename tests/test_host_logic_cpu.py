@@ -338,3 +338,50 @@ def test_interleave_gate_up_row_order(pkg):
         interleave_gate_up(gate[:40], up[:40])
     with pytest.raises(ValueError):
         interleave_gate_up(gate, up[:32])
+
+
+def test_moe_helpers_refuse_bad_arguments_before_any_launch(pkg, monkeypatch):
+    """gather_qmm / silu_mul / combine check dtypes, shapes and layouts on the
+    host.  The CUDA-residency check is lifted so CPU tensors reach the other
+    checks; every case here is refused before the library is asked to launch."""
+    from dflash_mlx_b200 import moe
+
+    monkeypatch.setattr(moe, "require_cuda", lambda t, name: None)
+    bf, i32 = torch.bfloat16, torch.int32
+    e, n, k = 4, 64, 128
+
+    def stack(n_=n, k_=k, sdt=bf):
+        return moe.QuantWeight(torch.zeros((e, n_, k_ // 8), dtype=i32), torch.zeros((e, n_, k_ // 64), dtype=sdt),
+                               torch.zeros((e, n_, k_ // 64), dtype=sdt))
+
+    table = torch.zeros(int(moe._lib.load().dfl_moe_route_table_ints(e)), dtype=i32)
+    x = torch.zeros((16, k), dtype=bf)
+    cases = {
+        "x width": lambda: moe.gather_qmm(torch.zeros((16, 64), dtype=bf), stack(), table, rows_out=32,
+                                          gather_by_pair=False),
+        "x dtype": lambda: moe.gather_qmm(x.float(), stack(), table, rows_out=32, gather_by_pair=False),
+        "scales dtype": lambda: moe.gather_qmm(x, stack(sdt=torch.float16), table, rows_out=32,
+                                               gather_by_pair=False),
+        "scales shape": lambda: moe.gather_qmm(
+            x, moe.QuantWeight(stack().q, torch.zeros((e, n, 1), dtype=bf), torch.zeros((e, n, 1), dtype=bf)),
+            table, rows_out=32, gather_by_pair=False),
+        "non-contiguous q": lambda: moe.gather_qmm(
+            x, moe.QuantWeight(torch.zeros((e, k // 8, n), dtype=i32).transpose(1, 2), stack().s, stack().b),
+            table, rows_out=32, gather_by_pair=False),
+        "short table": lambda: moe.gather_qmm(x, stack(), table[:8], rows_out=32, gather_by_pair=False),
+        "pair rows": lambda: moe.gather_qmm(x, stack(), table, rows_out=32, gather_by_pair=True),
+        "out shape": lambda: moe.gather_qmm(x, stack(), table, rows_out=32, gather_by_pair=False,
+                                            out=torch.zeros((32, n + 1), dtype=bf)),
+        "silu dtype": lambda: moe.silu_mul(torch.zeros(16, 8, dtype=torch.float16),
+                                           torch.zeros(16, 8, dtype=torch.float16)),
+        "silu shapes": lambda: moe.silu_mul(torch.zeros(16, 8, dtype=bf), torch.zeros(16, 9, dtype=bf)),
+        "combine weights dtype": lambda: moe.combine(torch.zeros((32, 8), dtype=bf), torch.zeros((16, 2), dtype=bf),
+                                                     None),
+        "combine rows": lambda: moe.combine(torch.zeros((31, 8), dtype=bf), torch.zeros((16, 2)), None),
+        "combine shared": lambda: moe.combine(torch.zeros((32, 8), dtype=bf), torch.zeros((16, 2)),
+                                              torch.zeros((16, 9), dtype=bf)),
+    }
+    for name, call in cases.items():
+        with pytest.raises(ValueError):
+            call()
+            pytest.fail(name)
