@@ -385,3 +385,57 @@ def test_moe_helpers_refuse_bad_arguments_before_any_launch(pkg, monkeypatch):
         with pytest.raises(ValueError):
             call()
             pytest.fail(name)
+
+
+@pytest.mark.parametrize("fused,shared", [(False, False), (False, True), (True, True)])
+def test_moe_layer_valid_arguments_pass_host_checks(pkg, monkeypatch, fused, shared):
+    """The argument checks accept every call a BASELINE config-2 layer makes
+    (fused and unfused gate/up, with and without the shared expert).  The
+    library is replaced by a recorder: no kernel runs, only the launches that
+    would be issued are listed."""
+    from dflash_mlx_b200 import moe, verify_qmm
+
+    real = moe._lib.load()
+    calls = []
+
+    class Recorder:
+        def __getattr__(self, name):
+            if name.endswith(("_workspace_bytes", "_table_ints")):
+                return getattr(real, name)
+
+            def launch(*args):
+                calls.append(name)
+                return 0
+            return launch
+
+    for mod in (moe, verify_qmm):
+        monkeypatch.setattr(mod, "require_cuda", lambda t, name: None)
+        monkeypatch.setattr(mod, "stream_ptr", lambda dev: 0)
+    monkeypatch.setattr(moe._lib, "load", lambda path=None: Recorder())
+    monkeypatch.setattr(moe, "workspace", lambda dev, n: torch.zeros(max(n, 1), dtype=torch.uint8))
+    monkeypatch.setattr(verify_qmm, "workspace", lambda dev, n: torch.zeros(max(n, 1), dtype=torch.uint8))
+    monkeypatch.setattr(verify_qmm, "workspace_bytes", lambda m, k, n: 1 << 16)
+    monkeypatch.setattr(moe, "_moe_ws_bytes", lambda mp, k, n: 1 << 16)
+    monkeypatch.setattr(torch.cuda, "device", lambda d: __import__("contextlib").nullcontext())
+
+    t, e, hid, inter, top_k = 16, 256, 2048, 512, 8
+
+    def qw(n, k, lead=()):
+        return moe.QuantWeight(torch.zeros((*lead, n, k // 8), dtype=torch.int32),
+                               torch.zeros((*lead, n, k // 64), dtype=torch.bfloat16),
+                               torch.zeros((*lead, n, k // 64), dtype=torch.bfloat16))
+
+    experts = {"gate": qw(inter, hid, (e,)), "up": qw(inter, hid, (e,)), "down": qw(hid, inter, (e,))}
+    sh = {"gate": qw(inter, hid), "up": qw(inter, hid), "down": qw(hid, inter)} if shared else None
+    if fused:
+        il = verify_qmm.interleave_gate_up
+        experts = {"gate_up": moe.fuse_expert_gate_up(experts["gate"], experts["up"]), "down": experts["down"]}
+        g, u = sh["gate"], sh["up"]
+        sh = {"gate_up": moe.QuantWeight(il(g.q, u.q).contiguous(), il(g.s, u.s).contiguous(),
+                                         il(g.b, u.b).contiguous()), "down": sh["down"]}
+    x = torch.zeros((t, hid), dtype=torch.bfloat16)
+    y = moe.moe_layer(x, torch.zeros((t, e)), experts, sh, top_k=top_k)
+    assert tuple(y.shape) == (t, hid)
+    grouped = [c for c in calls if c.startswith("dfl_moe_qmm")]
+    assert calls[0] == "dfl_moe_route" and calls[-1] == "dfl_moe_combine"
+    assert grouped == (["dfl_moe_qmm_w4g64_silu", "dfl_moe_qmm_w4g64"] if fused else ["dfl_moe_qmm_w4g64"] * 3)
