@@ -77,6 +77,9 @@ def verify_accept(keys: torch.Tensor, verify_ids: Optional[torch.Tensor], *, blo
     Returns (posterior int32 [B, T], acceptance int32 [B], next_token int32 [B],
     max_logit fp32 [B, T]).  ``verify_ids`` int32 [B, T] or None.
     """
+    require_cuda(keys, "keys")
+    if keys.dtype != torch.int64:
+        raise ValueError(f"keys must be the int64 keys of lm_head_argmax_keys, got {keys.dtype}")
     keys = keys.reshape(-1, keys.shape[-1]) if keys.dim() > 1 else keys.reshape(1, -1)
     g, r = keys.shape
     if r % block != 0:
