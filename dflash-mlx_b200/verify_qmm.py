@@ -51,6 +51,17 @@ _ENTRY = {("mlx", torch.bfloat16): "dfl_verify_qmm_w4g64",
           ("pairs", torch.float16): "dfl_verify_qmm_w4g64_pairs_f16"}
 
 
+def _check_out(out: torch.Tensor, shape: tuple, dtypes, device: torch.device) -> None:
+    """A caller-provided output must be exactly what the kernel writes:
+    contiguous, of this shape and dtype, on the inputs' device."""
+    require_cuda(out, "out")
+    dtypes = dtypes if isinstance(dtypes, tuple) else (dtypes,)
+    if (out.dtype not in dtypes or tuple(out.shape) != tuple(shape) or not out.is_contiguous()
+            or out.device != device):
+        raise ValueError(f"out must be a contiguous {dtypes[0]} tensor of shape {tuple(shape)} on {device}, "
+                         f"got {out.dtype} {tuple(out.shape)} on {out.device}")
+
+
 def repack_pairs(w_q: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """MLX-packed int4 weights -> the pair-packed order (``out`` may be ``w_q``).
 
@@ -62,11 +73,12 @@ def repack_pairs(w_q: torch.Tensor, out: torch.Tensor | None = None) -> torch.Te
     """
     require_cuda(w_q, "w")
     src = as_u32_bits(w_q)
-    if not src.is_contiguous():
-        raise ValueError("weights must be contiguous")
-    dst = torch.empty_like(src) if out is None else as_u32_bits(out)
-    if dst.shape != src.shape or not dst.is_contiguous():
-        raise ValueError("out must be a contiguous tensor of the weights' shape")
+    if out is None:
+        dst = torch.empty_like(src)
+    else:
+        # written in place: never through a contiguous copy of ``out``
+        _check_out(out, tuple(src.shape), (torch.int32, torch.uint32), src.device)
+        dst = out
     with torch.cuda.device(src.device):
         st = _lib.load().dfl_repack_w4_pairs(src.data_ptr(), dst.data_ptr(), src.numel(),
                                              stream_ptr(src.device))
@@ -104,6 +116,8 @@ def qmm_w4g64(x2: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, biases:
         raise ValueError("scales/biases must be [N, K/64]")
     if out is None:
         out = torch.empty((m, n), dtype=x2.dtype, device=x2.device)
+    else:
+        _check_out(out, (m, n), x2.dtype, x2.device)
     if m == 0 or n == 0:
         return out
     fn = getattr(_lib.load(), entry)
@@ -170,6 +184,8 @@ def gate_up_silu(x2: torch.Tensor, w_q: torch.Tensor, scales: torch.Tensor, bias
         raise ValueError("scales/biases must be [N, K/64]")
     if out is None:
         out = torch.empty((m, n // 2), dtype=x2.dtype, device=x2.device)
+    else:
+        _check_out(out, (m, n // 2), x2.dtype, x2.device)
     if m == 0:
         return out
     fn = getattr(_lib.load(), entry)

@@ -439,3 +439,26 @@ def test_moe_layer_valid_arguments_pass_host_checks(pkg, monkeypatch, fused, sha
     grouped = [c for c in calls if c.startswith("dfl_moe_qmm")]
     assert calls[0] == "dfl_moe_route" and calls[-1] == "dfl_moe_combine"
     assert grouped == (["dfl_moe_qmm_w4g64_silu", "dfl_moe_qmm_w4g64"] if fused else ["dfl_moe_qmm_w4g64"] * 3)
+
+
+def test_qmm_wrappers_refuse_mismatched_outputs(pkg, monkeypatch):
+    """A caller-provided ``out`` must be exactly what the kernel writes
+    (contiguous, shape, dtype); ``repack_pairs(w, out=w)`` never writes into a
+    contiguous copy.  Refused on the host, before any launch."""
+    from dflash_mlx_b200 import verify_qmm
+
+    monkeypatch.setattr(verify_qmm, "require_cuda", lambda t, name: None)
+    bf = torch.bfloat16
+    x = torch.zeros((16, 128), dtype=bf)
+    w = torch.zeros((64, 16), dtype=torch.int32)
+    s = torch.zeros((64, 2), dtype=bf)
+    for bad in (torch.zeros((16, 63), dtype=bf), torch.zeros((16, 64), dtype=torch.float16),
+                torch.zeros((64, 16), dtype=bf).t()):
+        with pytest.raises(ValueError):
+            verify_qmm.qmm_w4g64(x, w, s, s, out=bad)
+    with pytest.raises(ValueError):
+        verify_qmm.gate_up_silu(x, w, s, s, out=torch.zeros((16, 64), dtype=bf))
+    with pytest.raises(ValueError):
+        verify_qmm.repack_pairs(w, out=torch.zeros((16, 64), dtype=torch.int32).t())
+    with pytest.raises(ValueError):
+        verify_qmm.repack_pairs(w, out=torch.zeros((64, 16), dtype=torch.int64))
