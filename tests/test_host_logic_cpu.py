@@ -462,3 +462,62 @@ def test_qmm_wrappers_refuse_mismatched_outputs(pkg, monkeypatch):
         verify_qmm.repack_pairs(w, out=torch.zeros((16, 64), dtype=torch.int32).t())
     with pytest.raises(ValueError):
         verify_qmm.repack_pairs(w, out=torch.zeros((64, 16), dtype=torch.int64))
+
+
+def _split_k_protocol(ubeg, ku):
+    """Host model of the dense qmm's split-K hand-off (one CTA per range
+    ``[ubeg[c], ubeg[c + 1])`` of (tile, K unit) pairs, ``ku`` units per
+    tile): which CTA writes a partial slot for which tile, and which CTA
+    reduces which slots.  Mirrors the kernel's rules: a tile's owner is the
+    CTA holding its first unit; a shared tile is the last of its owner's
+    range; the owner sums the slots of CTAs owner+1 .. (CTA of the tile's
+    last unit)."""
+    grid = len(ubeg) - 1
+
+    def cta_of(u):
+        return int(np.searchsorted(ubeg, u, side="right") - 1)
+
+    writes, reads, finals = {}, {}, {}
+    for c in range(grid):
+        u0, u1 = ubeg[c], ubeg[c + 1]
+        for t in range(u0 // ku, (u1 - 1) // ku + 1):
+            kb0 = max(u0, t * ku) - t * ku
+            kb1 = min(u1, (t + 1) * ku) - t * ku
+            if kb0 == 0 and kb1 == ku:
+                finals.setdefault(t, []).append(c)
+            elif cta_of(t * ku) != c:
+                writes.setdefault(c, []).append(t)
+            else:
+                assert t == (u1 - 1) // ku, "a shared tile is the last of its owner's range"
+                reads[c] = (t, list(range(c + 1, cta_of(t * ku + ku - 1) + 1)))
+                finals.setdefault(t, []).append(c)
+    return writes, reads, finals
+
+
+@pytest.mark.parametrize("n_tiles,ku", [(1, 1), (1, 12), (3, 34), (40, 12), (64, 10), (80, 10),
+                                        (148, 1), (149, 1), (272, 10), (40, 34), (8, 2), (640, 4)])
+def test_split_k_slots_written_once_and_reduced_once(pkg, n_tiles, ku):
+    """On the library's own ranges (dfl_qmm_stream_k_ranges) for the
+    benchmark's launch shapes and edge cases: every tile gets exactly one
+    final store; each CTA writes at most one partial slot; every written slot
+    is read by exactly one reducer, for the tile it was written for, and
+    every slot a reducer reads was written."""
+    import ctypes
+
+    from dflash_mlx_b200 import _lib
+
+    total = n_tiles * ku
+    grid = min(total, 148)
+    ubeg = (ctypes.c_int * (grid + 1))()
+    assert _lib.load().dfl_qmm_stream_k_ranges(total, grid, ubeg, None) == 0
+    writes, reads, finals = _split_k_protocol(np.array(list(ubeg)), ku)
+    assert sorted(finals) == list(range(n_tiles))
+    assert all(len(v) == 1 for v in finals.values())
+    assert all(len(v) == 1 for v in writes.values())
+    read_by = {}
+    for owner, (t, srcs) in reads.items():
+        for c in srcs:
+            assert c not in read_by, "a slot is reduced twice"
+            read_by[c] = owner
+            assert writes.get(c) == [t], f"CTA {c} holds no partial of tile {t}"
+    assert set(read_by) == set(writes)
