@@ -521,3 +521,30 @@ def test_split_k_slots_written_once_and_reduced_once(pkg, n_tiles, ku):
             read_by[c] = owner
             assert writes.get(c) == [t], f"CTA {c} holds no partial of tile {t}"
     assert set(read_by) == set(writes)
+
+
+@pytest.mark.parametrize("problems,tpp,ku", [(0, 8, 4), (1, 8, 4), (3, 8, 4), (37, 8, 4), (102, 8, 4),
+                                             (1, 16, 1), (5, 16, 1), (102, 16, 1), (128, 4, 1),
+                                             (7, 1, 34), (200, 2, 3)])
+def test_grouped_split_k_even_ranges(problems, tpp, ku):
+    """Grouped (MoE) launches know their unit count only on the device and
+    cut it evenly over a grid sized for the largest count (CTA c starts at
+    floor(c * total / grid)), so CTAs may get empty ranges.  The closed-form
+    owner of a unit the kernel uses, ceil((u + 1) grid / total) - 1, is the
+    last CTA whose range starts at or before u (hence a non-empty one), and
+    the hand-off invariants hold with empty ranges."""
+    grid = 148
+    total = problems * tpp * ku
+    ubeg = np.array([c * total // grid for c in range(grid + 1)])
+    for u in range(total):
+        closed = ((u + 1) * grid + total - 1) // total - 1
+        assert closed == int(np.searchsorted(ubeg, u, side="right") - 1)
+        assert ubeg[closed] <= u < ubeg[closed + 1]
+    writes, reads, finals = _split_k_protocol(ubeg, ku)
+    assert sorted(finals) == list(range(problems * tpp))
+    assert all(len(v) == 1 for v in finals.values())
+    assert all(len(v) == 1 for v in writes.values())
+    read = [c for _, srcs in reads.values() for c in srcs]
+    assert sorted(read) == sorted(writes)
+    for owner, (t, srcs) in reads.items():
+        assert all(writes[c] == [t] for c in srcs)
