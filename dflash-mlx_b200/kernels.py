@@ -61,6 +61,11 @@ def _check(tape, k, g, state, steps=None, mask=None):
             raise ValueError("vector g must be [B, T, Hv, Dk]")
     else:
         raise ValueError(f"Unsupported gating shape {tuple(g.shape)}")
+    # the kernel reads steps[b] for every sequence and mask[b, t] for every step
+    if steps is not None and steps.numel() != b:
+        raise ValueError(f"steps must hold one count per sequence ({b}), got {steps.numel()}")
+    if mask is not None and mask.numel() != b * t_steps:
+        raise ValueError(f"mask must be [B, T] = {(b, t_steps)}, got {tuple(mask.shape)}")
     return b, t_steps, hv, hk, dv, dk
 
 

@@ -101,6 +101,8 @@ class RecurrentRollbackCache:
                 steps = torch.full((snap_state.shape[0],), int(n_accepted) + 1, dtype=torch.int32)
             else:
                 steps = torch.as_tensor(n_accepted, dtype=torch.int32).reshape(-1) + 1
+                if steps.numel() == 1:   # one count for every sequence of the batch
+                    steps = steps.expand(snap_state.shape[0])
             # reuse the live state buffer: restore the snapshot into it, replay in place
             target = state_now if state_now is not None and state_now.shape == snap_state.shape \
                 else torch.empty_like(snap_state)

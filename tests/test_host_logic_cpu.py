@@ -548,3 +548,22 @@ def test_grouped_split_k_even_ranges(problems, tpp, ku):
     assert sorted(read) == sorted(writes)
     for owner, (t, srcs) in reads.items():
         assert all(writes[c] == [t] for c in srcs)
+
+
+def test_replay_refuses_step_counts_and_masks_of_the_wrong_size(pkg, monkeypatch):
+    """The replay kernel reads one step count per sequence and one mask byte
+    per (sequence, step): other sizes are refused on the host."""
+    from dflash_mlx_b200 import kernels
+
+    monkeypatch.setattr(kernels, "require_cuda", lambda t, name: None)
+    b, t, h, d = 3, 4, 2, 32
+    tape = torch.zeros((b, t, h, d))
+    k = torch.zeros((b, t, h, d), dtype=torch.bfloat16)
+    g = torch.ones((b, t, h))
+    state = torch.zeros((b, h, d, d))
+    with pytest.raises(ValueError):
+        kernels.tape_replay_(state, tape, k, g, torch.ones(1, dtype=torch.int32))
+    with pytest.raises(ValueError):
+        kernels.tape_replay_(state, tape, k, g, torch.ones(b + 1, dtype=torch.int32))
+    with pytest.raises(ValueError):
+        kernels.tape_replay_kernel(tape, k, g, state, torch.ones((b, t - 1), dtype=torch.bool))
