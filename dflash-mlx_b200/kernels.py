@@ -220,7 +220,7 @@ def tree_depthwise_conv1d(qkv, prefix, weight, bias, path_indices):
     ``qkv [B, T, C]``, ``prefix [B, K-1, C]`` (same dtype, bf16 or fp32),
     ``weight [C, K, 1]`` (or ``[C, K]``), ``bias [C]`` or None,
     ``path_indices [T, K]`` into ``concat(prefix, qkv)``."""
-    for t, name in ((qkv, "qkv"), (weight, "weight")):
+    for t, name in ((qkv, "qkv"), (prefix, "prefix"), (weight, "weight")):
         require_cuda(t, name)
     if qkv.dtype not in (torch.bfloat16, torch.float32):
         raise NotImplementedError(f"qkv must be bfloat16 or float32, got {qkv.dtype}")
@@ -231,6 +231,8 @@ def tree_depthwise_conv1d(qkv, prefix, weight, bias, path_indices):
     kk = int(w.shape[1])
     if prefix.shape != (b, kk - 1, c) or prefix.dtype != qkv.dtype:
         raise ValueError(f"prefix must be [B, K-1, C] = {(b, kk - 1, c)} in qkv's dtype")
+    if bias is not None and bias.numel() != c:
+        raise ValueError(f"bias must hold one value per channel ({c}), got {bias.numel()}")
     path = torch.as_tensor(path_indices).to(device=qkv.device, dtype=torch.int32).reshape(t_steps, kk)
     w = w.to(torch.float32).contiguous()
     bias = bias.to(device=qkv.device, dtype=torch.float32).contiguous() if bias is not None else None

@@ -567,3 +567,19 @@ def test_replay_refuses_step_counts_and_masks_of_the_wrong_size(pkg, monkeypatch
         kernels.tape_replay_(state, tape, k, g, torch.ones(b + 1, dtype=torch.int32))
     with pytest.raises(ValueError):
         kernels.tape_replay_kernel(tape, k, g, state, torch.ones((b, t - 1), dtype=torch.bool))
+
+
+def test_tree_conv_refuses_mismatched_bias_and_prefix(pkg, monkeypatch):
+    from dflash_mlx_b200 import kernels
+
+    seen = []
+    monkeypatch.setattr(kernels, "require_cuda", lambda t, name: seen.append(name))
+    qkv = torch.zeros((1, 4, 8))
+    prefix = torch.zeros((1, 3, 8))
+    w = torch.ones((8, 4, 1))
+    path = torch.zeros((4, 4), dtype=torch.int32)
+    with pytest.raises(ValueError):
+        kernels.tree_depthwise_conv1d(qkv, prefix, w, torch.zeros(7), path)
+    assert "prefix" in seen  # the prefix is read by the kernel: it must be on the device too
+    with pytest.raises(ValueError):
+        kernels.tree_depthwise_conv1d(qkv, torch.zeros((1, 2, 8)), w, None, path)
