@@ -54,8 +54,14 @@ def lm_head_argmax_keys(hidden: torch.Tensor, weight: torch.Tensor, *, v_begin: 
     if w.shape[1] != d:
         raise ValueError(f"weight {tuple(w.shape)} does not match hidden dim {d}")
     r, v = h2.shape[0], w.shape[0]
+    if v_begin < 0:
+        raise ValueError(f"v_begin must be >= 0, got {v_begin}")
     if out is None:
         out = torch.empty(r, dtype=torch.int64, device=h2.device)
+    else:
+        require_cuda(out, "out")
+        if out.dtype != torch.int64 or out.numel() != r or not out.is_contiguous() or out.device != h2.device:
+            raise ValueError(f"out must be a contiguous int64 tensor of {r} keys on {h2.device}")
     sup_ptr = None
     if suppress_token_mask is not None:
         sup = suppress_token_mask.to(device=h2.device, dtype=torch.uint8).contiguous()

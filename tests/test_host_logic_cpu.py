@@ -583,3 +583,19 @@ def test_tree_conv_refuses_mismatched_bias_and_prefix(pkg, monkeypatch):
     assert "prefix" in seen  # the prefix is read by the kernel: it must be on the device too
     with pytest.raises(ValueError):
         kernels.tree_depthwise_conv1d(qkv, torch.zeros((1, 2, 8)), w, None, path)
+
+
+def test_lm_head_keys_refuse_bad_outputs_and_offsets(pkg, monkeypatch):
+    from dflash_mlx_b200 import lm_head
+
+    monkeypatch.setattr(lm_head, "require_cuda", lambda t, name: None)
+    h = torch.zeros((16, 64), dtype=torch.bfloat16)
+    w = torch.zeros((100, 64), dtype=torch.bfloat16)
+    for bad in (torch.zeros(15, dtype=torch.int64), torch.zeros(16, dtype=torch.int32),
+                torch.zeros((16, 2), dtype=torch.int64)[:, 0]):
+        with pytest.raises(ValueError):
+            lm_head.lm_head_argmax_keys(h, w, out=bad)
+    with pytest.raises(ValueError):
+        lm_head.lm_head_argmax_keys(h, w, v_begin=-1)
+    with pytest.raises(ValueError):
+        lm_head.lm_head_argmax_keys(h, w, v_begin=10, suppress_token_mask=torch.zeros(100, dtype=torch.bool))
