@@ -169,23 +169,31 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.fh.close()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.path.read_text().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 6:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[2:]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
+        out = parse_clock_samples(self.path.read_text())
         self.path.unlink(missing_ok=True)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons)}
+        return out
+
+
+def parse_clock_samples(text: str) -> dict:
+    """Median SM clock, max SM clock and the throttle reasons seen in the
+    sampler's CSV lines (sm, max sm, hw_slowdown, hw_thermal_slowdown,
+    sw_thermal_slowdown, sw_power_cap; reasons read "Active" / "Not Active")."""
+    sm, mx, reasons = [], None, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in text.splitlines():
+        parts = [p.strip() for p in line.split(",")]
+        if len(parts) < 6:
+            continue
+        try:
+            sm.append(float(parts[0]))
+            mx = float(parts[1])
+        except ValueError:
+            continue
+        for n, v in zip(names, parts[2:]):
+            if v.lower().startswith("active"):
+                reasons.add(n)
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+            "reasons": sorted(reasons)}
 
 
 def run_ours(args):

@@ -44,3 +44,17 @@ def test_reference_arm_other_ranks_exit_without_work():
     r = _run({"RANK": "1", "WORLD_SIZE": "2"})
     assert r.returncode == 0, r.stderr[-2000:]
     assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_clock_samples_summary():
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    text = ("1965, 1965, Not Active, Not Active, Not Active, Not Active\n"
+            "1905, 1965, Not Active, Not Active, Not Active, Active\n"
+            "[N/A], 1965, Not Active, Not Active, Not Active, Not Active\n"
+            "1950, 1965, Not Active, Not Active, Not Active, Not Active\n"
+            "garbage\n")
+    d = bench.parse_clock_samples(text)
+    assert d == {"sm_mhz": 1950.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"]}
+    assert bench.parse_clock_samples("") == {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
