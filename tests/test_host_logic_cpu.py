@@ -387,12 +387,14 @@ def test_moe_helpers_refuse_bad_arguments_before_any_launch(pkg, monkeypatch):
             pytest.fail(name)
 
 
-@pytest.mark.parametrize("fused,shared", [(False, False), (False, True), (True, True)])
-def test_moe_layer_valid_arguments_pass_host_checks(pkg, monkeypatch, fused, shared):
-    """The argument checks accept every call a BASELINE config-2 layer makes
-    (fused and unfused gate/up, with and without the shared expert).  The
-    library is replaced by a recorder: no kernel runs, only the launches that
-    would be issued are listed."""
+@pytest.mark.parametrize("fused,shared", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("e,hid,inter,top_k", [(256, 2048, 512, 8), (16, 512, 256, 4), (8, 512, 128, 2)])
+def test_moe_layer_valid_arguments_pass_host_checks(pkg, monkeypatch, fused, shared, e, hid, inter, top_k):
+    """The argument checks accept every call a MoE layer makes (BASELINE
+    config 2 and the GPU suite's smaller layers; fused and unfused gate/up,
+    with and without the shared expert).  The library is replaced by a
+    recorder: no kernel runs, only the launches that would be issued are
+    listed."""
     from dflash_mlx_b200 import moe, verify_qmm
 
     real = moe._lib.load()
@@ -418,7 +420,7 @@ def test_moe_layer_valid_arguments_pass_host_checks(pkg, monkeypatch, fused, sha
     monkeypatch.setattr(moe, "_moe_ws_bytes", lambda mp, k, n: 1 << 16)
     monkeypatch.setattr(torch.cuda, "device", lambda d: __import__("contextlib").nullcontext())
 
-    t, e, hid, inter, top_k = 16, 256, 2048, 512, 8
+    t = 16
 
     def qw(n, k, lead=()):
         return moe.QuantWeight(torch.zeros((*lead, n, k // 8), dtype=torch.int32),
@@ -430,9 +432,10 @@ def test_moe_layer_valid_arguments_pass_host_checks(pkg, monkeypatch, fused, sha
     if fused:
         il = verify_qmm.interleave_gate_up
         experts = {"gate_up": moe.fuse_expert_gate_up(experts["gate"], experts["up"]), "down": experts["down"]}
-        g, u = sh["gate"], sh["up"]
-        sh = {"gate_up": moe.QuantWeight(il(g.q, u.q).contiguous(), il(g.s, u.s).contiguous(),
-                                         il(g.b, u.b).contiguous()), "down": sh["down"]}
+        if sh is not None:
+            g, u = sh["gate"], sh["up"]
+            sh = {"gate_up": moe.QuantWeight(il(g.q, u.q).contiguous(), il(g.s, u.s).contiguous(),
+                                             il(g.b, u.b).contiguous()), "down": sh["down"]}
     x = torch.zeros((t, hid), dtype=torch.bfloat16)
     y = moe.moe_layer(x, torch.zeros((t, e)), experts, sh, top_k=top_k)
     assert tuple(y.shape) == (t, hid)
