@@ -602,3 +602,56 @@ def test_lm_head_keys_refuse_bad_outputs_and_offsets(pkg, monkeypatch):
         lm_head.lm_head_argmax_keys(h, w, v_begin=-1)
     with pytest.raises(ValueError):
         lm_head.lm_head_argmax_keys(h, w, v_begin=10, suppress_token_mask=torch.zeros(100, dtype=torch.bool))
+
+
+@pytest.mark.parametrize("layout,fuse_silu,pack", [("mlx", False, True), ("pairs", False, True),
+                                                   ("pairs", True, True), ("pairs", True, False)])
+def test_verify_step_host_path(pkg, monkeypatch, layout, fuse_silu, pack):
+    """The benchmark step's host side on CPU, library replaced by a recorder:
+    set-up (pair repack, tape recording), the qmm stack, lm_head keys and the
+    accept + rollback part all pass the wrappers' argument checks and issue
+    the expected launches (two requests' rows share each qmm launch when
+    packed: 3 requests -> 2 launches per projection)."""
+    import contextlib
+
+    from dflash_mlx_b200 import _lib, kernels, lm_head, verify_qmm, verify_step
+
+    calls = []
+
+    class Recorder:
+        def __getattr__(self, name):
+            def launch(*args):
+                calls.append(name)
+                return 0
+            return launch
+
+    monkeypatch.setattr(_lib, "load", lambda path=None: Recorder())
+    for mod in (verify_qmm, lm_head, kernels, pkg.moe):
+        for attr, fake in (("require_cuda", lambda t, name: None), ("stream_ptr", lambda dev: 0),
+                           ("workspace", lambda dev, n: torch.zeros(16, dtype=torch.uint8))):
+            if hasattr(mod, attr):
+                monkeypatch.setattr(mod, attr, fake)
+    monkeypatch.setattr(verify_qmm, "workspace_bytes", lambda m, k, n: 16)
+    monkeypatch.setattr(lm_head, "workspace_bytes", lambda r, d, v: 16)
+    monkeypatch.setattr(torch.cuda, "Stream", lambda dev=None: None)
+    monkeypatch.setattr(torch.cuda, "device", lambda dev: contextlib.nullcontext())
+
+    shape = verify_step.StackShape(hidden=256, layers=2, q_out=256, kv_out=128, inter=512, vocab=1000,
+                                   gdn_layers=2, gdn_heads=2, gdn_dk=32, gdn_dv=32)
+    step = verify_step.VerifyStep("cpu", requests=3, shape=shape, weight_layout=layout,
+                                  fuse_silu=fuse_silu, pack_requests=pack)
+    setup = list(calls)
+    assert setup.count("dfl_gdn_forward_tape") == shape.gdn_layers
+    assert setup.count("dfl_repack_w4_pairs") == (4 * shape.layers if layout == "pairs" else 0)
+    calls.clear()
+    step._qmm_stack()
+    per_proj = 2 if pack else 3
+    qmm = [c for c in calls if c.startswith("dfl_verify_qmm")]
+    assert len(qmm) == per_proj * 4 * shape.layers
+    groups = 1 if pack else 3   # the unfused SiLU*up runs once per group of rows
+    assert calls.count("dfl_silu_mul_rows_bf16") == (0 if fuse_silu else groups * shape.layers)
+    calls.clear()
+    step._keys(step.x)
+    keys_all = torch.zeros((1, 3 * shape.block), dtype=torch.int64)
+    step._accept_and_rollback(keys_all, step.verify_ids)
+    assert calls == ["dfl_lmhead_argmax", "dfl_lmhead_accept", "dfl_gdn_tape_replay"]
