@@ -163,3 +163,97 @@ def test_key_packing_orders_like_argmax():
             else:
                 want = a
             assert int(bi) == int(ids[want]), (a, b)
+
+
+def _step_rank_main(rank: int, world: int, port: int, q):
+    """One rank of the benchmark step's multi-rank host path on gloo: the
+    library is a recorder (no kernel runs), the three CUDA graphs are the
+    step's parts called directly, the all-gathers between them are real."""
+    import contextlib
+    import types
+
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        pkg = __graft_entry__.load_package()
+        from dflash_mlx_b200 import _lib, kernels, lm_head, verify_qmm, verify_step
+
+        calls = []
+
+        class Recorder:
+            def __getattr__(self, name):
+                def launch(*args):
+                    calls.append(name)
+                    return 0
+                return launch
+
+        _lib.load = lambda path=None: Recorder()
+        for mod in (verify_qmm, lm_head, kernels, pkg.moe):
+            mod.require_cuda = lambda t, name: None
+            mod.stream_ptr = lambda dev: 0
+            if hasattr(mod, "workspace"):
+                mod.workspace = lambda dev, n: torch.zeros(16, dtype=torch.uint8)
+        verify_qmm.workspace_bytes = lambda m, k, n: 16
+        lm_head.workspace_bytes = lambda r, d, v: 16
+        torch.cuda.Stream = lambda dev=None: None
+        torch.cuda.device = lambda dev: contextlib.nullcontext()
+        torch.cuda.stream = lambda s: contextlib.nullcontext()
+
+        shape = verify_step.StackShape(hidden=256, layers=1, q_out=256, kv_out=128, inter=512, vocab=1000,
+                                       gdn_layers=2, gdn_heads=2, gdn_dk=32, gdn_dv=32)
+        step = verify_step.VerifyStep("cpu", requests=2, shape=shape, rank=rank, world=world, group=None,
+                                      weight_layout="pairs", fuse_silu=True)
+        rows = step.requests * shape.block
+        step.x_all = torch.empty((world * rows, shape.hidden), dtype=torch.bfloat16)
+        step.ids_all = torch.empty((world * step.requests, shape.block), dtype=torch.int32)
+        step.keys_all = torch.empty((world, world * rows), dtype=torch.int64)
+        step.x.fill_(rank + 1)
+        step.verify_ids.fill_(10 * (rank + 1))
+        parts = (step._qmm_stack, lambda: step._keys(step.x_all),
+                 lambda: step._accept_and_rollback(step.keys_all, step.ids_all))
+        step.graphs = [types.SimpleNamespace(replay=f) for f in parts]
+        calls.clear()
+        step.run_step()
+        q.put((rank, list(calls), step.x_all[:, 0].float().tolist(), step.ids_all[:, 0].tolist(),
+               tuple(step.keys_all.shape)))
+        dist.destroy_process_group()
+    except BaseException as e:  # report, never hang the parent
+        q.put((rank, repr(e), None, None, None))
+
+
+def test_verify_step_multirank_host_path():
+    """Two gloo ranks run the step's N > 1 branch: every rank issues the same
+    launches in the same order, the hidden rows and verify ids of both ranks
+    arrive in rank order, and the key exchange has one row of keys per rank."""
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_step_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(world):
+            rank, calls, x0, ids0, kshape = q.get(timeout=180)
+            out[rank] = (calls, x0, ids0, kshape)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    for rank in range(world):
+        calls, x0, ids0, kshape = out[rank]
+        assert not isinstance(calls, str), calls
+        assert calls == out[0][0]
+        assert calls[-3:] == ["dfl_lmhead_argmax", "dfl_lmhead_accept", "dfl_gdn_tape_replay"]
+        assert x0 == [1.0] * 32 + [2.0] * 32
+        assert ids0 == [10, 10, 20, 20]
+        assert kshape == (world, world * 32)
