@@ -136,7 +136,9 @@ int dfl_verify_qmm_w4g64_pairs_silu_f16(const uint16_t* x, const uint32_t* w_q,
 int dfl_qmm_stream_k_ranges(int total, int grid, int* ubeg, int* skew_used);
 
 /* Workspace bytes dfl_verify_qmm_w4g64 needs for this shape on the current
- * device; 0 with *status != DFL_OK on error. */
+ * device; 0 with *status != DFL_OK on error.  No counterpart in the
+ * reference (MLX allocates the split-K buffer of verify_qmm.py:993-1001
+ * itself). */
 size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status);
 
 /* dfl_verify_qmm_w4g64 without a workspace argument, for callers that cannot
