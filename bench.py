@@ -43,6 +43,13 @@ def _peaks():
         return 6650.0, "fallback"
 
 
+def _peak_tflops():
+    try:
+        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
 def _traffic_per_launch():
     """DRAM bytes per qmm launch (mean over the four launch kinds of a layer)
     from the committed ncu summary, if present."""
@@ -57,49 +64,76 @@ def _traffic_per_launch():
 
 
 # ------------------------------------------------------------------ CPU arm
-def cpu_step_sample(scale_layers: bool = True):
-    """Time the reference algorithm (oracle restatement) on a bounded sample of
-    one step and scale it to the full step.  Returns (seconds per step, sample text)."""
+_CPU_SAMPLE = {}
+CPU_ROW_FRACTION = 8   # the CPU sample computes 1/8 of each launch's output rows
+
+
+def _cpu_sample_inputs():
+    """Seeded inputs of the CPU sample, made once per process (input
+    generation is not part of the timed sample): 1/8 of the output rows of
+    each of the four qmm launch shapes of a decoder layer (q|k|v 8192x5120,
+    o 5120x6144, gate|up 34816x5120, down 5120x17408; full K), a 1/64 slice
+    of the lm_head vocabulary and one GDN layer's tape."""
+    import numpy as np
+
+    from oracle import bf16 as obf16
+    from oracle import qmm as oqmm
+
+    if _CPU_SAMPLE:
+        return _CPU_SAMPLE
+    rng = np.random.default_rng(0)
+    layer = []
+    for n, k in ((8192, 5120), (5120, 6144), (34816, 5120), (5120, 17408)):
+        # 1/CPU_ROW_FRACTION of each launch's output rows, full K
+        layer.append((oqmm.synth_x(rng, 16, k), *oqmm.synth_weights(rng, n // CPU_ROW_FRACTION, k)))
+    _CPU_SAMPLE["layer"] = layer
+    _CPU_SAMPLE["h"] = oqmm.synth_x(rng, 16, 5120)
+    _CPU_SAMPLE["lm_w"] = obf16.from_f32((rng.standard_normal((248320 // 64, 5120)) * 0.02)
+                                         .astype(np.float32))
+    _CPU_SAMPLE["gdn"] = ((rng.standard_normal((1, 48, 128, 128)) * 0.05).astype(np.float32),
+                          rng.standard_normal((1, 16, 48, 128)).astype(np.float32),
+                          rng.standard_normal((1, 16, 48, 128)).astype(np.float32),
+                          rng.random((1, 16, 48)).astype(np.float32))
+    _CPU_SAMPLE["rng"] = rng
+    return _CPU_SAMPLE
+
+
+def cpu_step_sample():
+    """Time the reference algorithm (oracle restatement, all host threads via
+    BLAS) on a bounded sample of one verify step and extrapolate it to the
+    full step: 1/8 of the output rows of one decoder layer's four qmm
+    launches (x8 x64 layers), the lm_head on 1/64 of the vocabulary (x64) and
+    one GDN layer's replay (x48).
+    Returns (extrapolated seconds per step, sample text, parts, seconds the
+    sample itself took)."""
     import numpy as np
 
     from oracle import gdn as ogdn
     from oracle import lmhead as olm
     from oracle import qmm as oqmm
 
-    rng = np.random.default_rng(0)
-    x = oqmm.synth_x(rng, 16, 5120)
-    t_qmm = 0.0
-    # sample: the q projection of one layer (31.5 M weights) -> scale by the
-    # stack's weight count
-    w_q, s, b = oqmm.synth_weights(rng, 6144, 5120)
+    d = _cpu_sample_inputs()
     t0 = time.perf_counter()
-    oqmm.qmm(x, w_q, s, b, accum=np.float32)
-    t_q = time.perf_counter() - t0
-    stack_weights = 64 * (6144 * 5120 + 2 * 1024 * 5120 + 5120 * 6144 + 2 * 17408 * 5120 + 5120 * 17408)
-    t_qmm = t_q * stack_weights / (6144 * 5120)
-    # lm_head: 16 rows against a 1/64 vocabulary slice, scaled by 64
-    h = oqmm.synth_x(rng, 16, 5120)
-    from oracle import bf16 as obf16
-    w = obf16.from_f32((rng.standard_normal((248320 // 64, 5120)) * 0.02).astype(np.float32))
+    for x, w_q, sc, bi in d["layer"]:
+        oqmm.qmm(x, w_q, sc, bi, accum=np.float32)
+    t_layer = time.perf_counter() - t0
     t0 = time.perf_counter()
-    lg = olm.logits_bf16(h, w)
+    lg = olm.logits_bf16(d["h"], d["lm_w"])
     post = olm.greedy_tokens(lg).reshape(1, 16)
-    ids = olm.synth_verify_ids(rng, post, 248320)
+    ids = olm.synth_verify_ids(d["rng"], post, 248320)
     olm.verify_accept(lg.reshape(1, 16, -1), ids)
-    t_lm = (time.perf_counter() - t0) * 64
-    # GDN: one layer of 48 heads, 16 recorded steps, scaled by 48 layers
-    st = (rng.standard_normal((1, 48, 128, 128)) * 0.05).astype(np.float32)
-    kk = rng.standard_normal((1, 16, 48, 128)).astype(np.float32)
-    tape = rng.standard_normal((1, 16, 48, 128)).astype(np.float32)
-    g = rng.random((1, 16, 48)).astype(np.float32)
+    t_lm = time.perf_counter() - t0
+    st, kk, tape, g = d["gdn"]
     t0 = time.perf_counter()
-    ogdn.tape_replay_accepted(tape, kk, g, st, np.array([9]))
-    t_gdn = (time.perf_counter() - t0) * 48
-    total = t_qmm + t_lm + t_gdn
-    sample = ("q projection 6144x5120 of one layer (scaled x%.1f to the 64-layer stack), lm_head "
-              "16 rows x 3880 vocab (x64), GDN replay 1 layer 48 heads (x48); numpy, %d host threads"
-              % (stack_weights / (6144 * 5120), os.cpu_count()))
-    return total, sample, {"qmm_s": t_qmm, "lm_head_s": t_lm, "gdn_s": t_gdn}
+    ogdn.tape_replay_accepted(tape, kk, g, st.copy(), np.array([9]))
+    t_gdn = time.perf_counter() - t0
+    parts = {"qmm_s": t_layer * 64 * CPU_ROW_FRACTION, "lm_head_s": t_lm * 64, "gdn_s": t_gdn * 48}
+    total = sum(parts.values())
+    sample = ("1/%d of the output rows of each of one decoder layer's four qmm launches (q|k|v, o, "
+              "gate|up, down; x%d rows x64 layers), lm_head 16 rows x 3880 vocab (x64), GDN replay "
+              "1 layer 48 heads (x48); numpy, %d host threads"
+              % (CPU_ROW_FRACTION, CPU_ROW_FRACTION, os.cpu_count()))
+    return total, sample, parts, t_layer + t_lm + t_gdn
 
 
 def workload_name(layers: int = 64) -> str:
@@ -113,15 +147,14 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    import numpy as np  # noqa: F401
-
     for _ in range(args.warmup):
         cpu_step_sample()
-    times = []
+    times, sampled = [], []
     sample = ""
     for _ in range(args.steps):
-        t, sample, _ = cpu_step_sample()
+        t, sample, _, t_sample = cpu_step_sample()
         times.append(t)
+        sampled.append(t_sample)
     t_step = sum(times) / len(times)
     value = 1.0 / t_step
     line = {
@@ -131,7 +164,9 @@ def run_reference(args):
         "data": "synthetic (seeded, BASELINE distributions)",
         "config": {"workload": workload_name(), "requests_per_gpu": args.requests_per_gpu,
                    "tokens_per_request": 16,
-                   "parallelism": "host cores of rank 0 (request-steps/s do not depend on the GPU count)"},
+                   "parallelism": "host cores of rank 0 (request-steps/s do not depend on the GPU count)",
+                   "cpu_baseline_method": "extrapolated from sampled layers",
+                   "sampled_s_per_step": sum(sampled) / len(sampled)},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -147,22 +182,43 @@ class ClockSampler:
         self.proc = None
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"dfl_clocks_{os.getpid()}.csv"
 
-    def start(self):
+    QUERY = ("--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def start(self, first_sample_timeout: float = 10.0):
+        """Start sampling every 200 ms; returns once the first sample is in
+        (nvidia-smi can take seconds to start when every rank starts one)."""
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index),
-                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
-                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap",
+                ["nvidia-smi", "-i", str(self.index), self.QUERY,
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t_end = time.time() + first_sample_timeout
+        while time.time() < t_end and self.proc.poll() is None:
+            if self.path.stat().st_size > 0:
+                break
+            time.sleep(0.05)
+
+    def _one_shot(self) -> str:
+        try:
+            return subprocess.run(["nvidia-smi", "-i", str(self.index), self.QUERY,
+                                   "--format=csv,noheader,nounits"], capture_output=True,
+                                  text=True, timeout=30).stdout
+        except Exception:
+            return ""
 
     def stop(self):
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+            out = parse_clock_samples(self._one_shot())
+            out["sampling"] = "one query after the timed region (sampler did not start)"
+            return out
+        # one more period so that a short timed region is followed by a sample
+        time.sleep(0.25)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -171,6 +227,9 @@ class ClockSampler:
         self.fh.close()
         out = parse_clock_samples(self.path.read_text())
         self.path.unlink(missing_ok=True)
+        if out["sm_mhz"] is None:
+            out = parse_clock_samples(self._one_shot())
+            out["sampling"] = "one query after the timed region (no sample during it)"
         return out
 
 
@@ -230,6 +289,14 @@ def run_ours(args):
     step.verify_ids.copy_(torch.randint(0, sh.vocab, step.verify_ids.shape, generator=gen, device=dev,
                                         dtype=torch.int64).to(torch.int32))
     step.capture()
+    # Config 3's verify ids: the target's true posterior for these hidden rows
+    # comes from one step at set-up (same lm_head, same vocabulary split);
+    # each draft then equals the previous position's posterior with
+    # probability 0.88, else a uniform token, so acceptance lengths (and the
+    # rollback's replayed step counts) follow that distribution.
+    step.run_step()
+    torch.cuda.synchronize(dev)
+    step.verify_ids.copy_(synth_verify_ids(step.posterior.clone(), sh.vocab, 0.88, gen))
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -246,7 +313,6 @@ def run_ours(args):
     e1 = torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local)
     clocks.start()
-    time.sleep(0.3)
     barrier()
     e0.record(step.stream)
     for i in range(args.steps):
@@ -287,6 +353,7 @@ def run_ours(args):
     h2d = x_host.numel() * 2 + ids_host.numel() * 4
     d2h = int(out.numel()) * 4
 
+    mean_acc = float(step.acceptance.float().mean())
     # roofline of the dominant kernel (the int4 verify qmm)
     peak, peak_kind = _peaks()
     launches = len(sh.launches()) * sh.layers * (((b + 1) // 2) if step.pack_requests else b)
@@ -298,9 +365,9 @@ def run_ours(args):
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            t_cpu, sample, parts = cpu_step_sample()
+            t_cpu, sample, parts, _ = cpu_step_sample()
             cpu = {"value": 1.0 / t_cpu, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                   "sample": sample}
+                   "sample": sample, "method": "extrapolated from sampled layers"}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True,
@@ -316,6 +383,8 @@ def run_ours(args):
                 "l2": "inputs larger than L2 (12.3 GB of packed weights per step)",
                 "qmm_ms_per_step": t_qmm / args.steps * 1e3,
                 "qmm_gbs": achieved,
+                "verify_ids": "P(draft = previous position's posterior) = 0.88, posterior from set-up",
+                "mean_acceptance": mean_acc,
             },
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -335,6 +404,12 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if world == 1 and not args.no_extra_configs:
+            # the other configurations, measured in this process after the
+            # timed loop (each in its own CUDA graph, CUDA events)
+            del step
+            torch.cuda.empty_cache()
+            line["config"].update(measure_other_configs(dev, args))
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -343,27 +418,140 @@ def run_ours(args):
     return 0
 
 
-def run_moe(args):
-    """BASELINE config 2 on one GPU: the MoE verify layer (hidden 2048, 256
-    experts, top-8, expert intermediate 512, one shared expert) at 16 tokens.
-    Reports the HBM GB/s of the layer (bytes of the experts the routing
-    activates + the shared expert + activations) from CUDA events around a
-    graph of ``--moe-layers`` layers with distinct weights (1.9 GB, larger than
-    L2).  Not the default workload: the driver's bench line is the verify
-    step."""
+def synth_verify_ids(posterior, vocab: int, p_match: float, gen):
+    """verify_ids [B, T] for posterior [B, T]: position 0 uniform, position j
+    the posterior of position j - 1 with probability p_match, else uniform."""
+    import torch
+
+    b, t = posterior.shape
+    dev = posterior.device
+    ids = torch.randint(0, vocab, (b, t), generator=gen, device=dev, dtype=torch.int64).to(torch.int32)
+    hit = torch.rand((b, t), generator=gen, device=dev) < p_match
+    ids[:, 1:] = torch.where(hit[:, 1:], posterior[:, :-1].to(torch.int32), ids[:, 1:])
+    return ids
+
+
+def _graph_time(fn, dev, reps: int, warmup: int = 3) -> float:
+    """Seconds per call of ``fn`` captured once in a CUDA graph and replayed
+    ``reps`` times between CUDA events on the capturing stream."""
+    import torch
+
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        fn()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+        for _ in range(warmup):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    del graph
+    return e0.elapsed_time(e1) / 1e3 / reps
+
+
+def measure_other_configs(dev, args) -> dict:
+    """BASELINE configs 0, 2, 4 and config 3 at B = 16 / 128 on one GPU, each
+    with its roofline fraction (of the measured peaks):
+
+    * config0: 16 x 4096 x 4096 int4 verify qmm (MLX packing, the drop-in
+      entry), 64 calls over 64 distinct weight copies (621 MB > L2) per graph;
+    * moe: the config-2 MoE layer (4 layers with distinct weights per graph);
+    * rollback_config4: tape replay of 64 sequences x 48 layers (a ~ U{0..16}
+      per sequence, Hk = Hv = 48), in place, one launch;
+    * lmhead_b16 / lmhead_b128: argmax keys of 256 / 2048 hidden rows over the
+      full 248,320 x 5120 vocabulary (tensor-bound at B = 128)."""
+    import torch
+
+    import __graft_entry__
+
+    pkg = __graft_entry__.load_package()
+    from dflash_mlx_b200.verify_qmm import qmm_w4g64
+
+    peak, _ = _peaks()
+    tflops = _peak_tflops()
+    out = {}
+    gen = torch.Generator(device=dev).manual_seed(17)
+    # config 0
+    m, k, n, copies = 16, 4096, 4096, 64
+    ws = []
+    for _ in range(copies):
+        q = torch.randint(-2**31, 2**31 - 1, (n, k // 8), dtype=torch.int64, generator=gen,
+                          device=dev).to(torch.int32)
+        sc = torch.rand((n, k // 64), generator=gen, device=dev) * 0.016 + 0.004
+        bi = -8 * sc + torch.randn(sc.shape, generator=gen, device=dev) * 0.1 * sc
+        ws.append((q, sc.to(torch.bfloat16), bi.to(torch.bfloat16)))
+    x0 = torch.randn((m, k), generator=gen, device=dev).to(torch.bfloat16)
+    y0 = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+
+    def cfg0():
+        for q, sc, bi in ws:
+            qmm_w4g64(x0, q, sc, bi, out=y0)
+
+    t = _graph_time(cfg0, dev, reps=10) / copies
+    b0 = n * k // 2 + 4 * n * (k // 64) + 2 * m * (k + n)
+    out["config0_qmm_us"] = t * 1e6
+    out["config0_qmm_gbs"] = b0 / t / 1e9
+    out["config0_qmm_frac"] = b0 / t / 1e9 / peak
+    del ws
+    # config 2
+    moe = measure_moe(dev, layers=4, steps=10, warmup=3, fuse_silu=True)
+    out["moe_layer_us"] = moe["us_per_layer"]
+    out["moe_layer_gbs"] = moe["value"]
+    out["moe_layer_frac"] = moe["roofline"]["frac"]
+    # config 4 at 64 sequences x 48 layers
+    seqs, layers, hv, dk, dv, tt = 64, 48, 48, 128, 128, 16
+    lb = seqs * layers
+    state = torch.randn((lb, hv, dv, dk), generator=gen, device=dev) * 0.05
+    tape = torch.randn((lb, tt, hv, dv), generator=gen, device=dev)
+    kk = torch.randn((lb, tt, hv, dk), generator=gen, device=dev)
+    kk = (kk / kk.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    g = torch.exp(-torch.nn.functional.softplus(torch.randn((lb, tt, hv), generator=gen, device=dev)))
+    a = torch.randint(0, tt + 1, (seqs,), generator=gen, device=dev, dtype=torch.int32)
+    steps = a.repeat(layers)
+    t = _graph_time(lambda: pkg.tape_replay_(state, tape, kk, g, steps), dev, reps=5)
+    a_host = a.cpu().long()
+    per_step = hv * dv * 4 + hv * dk * 2 + hv * 4
+    b4 = layers * int(((a_host > 0).long() * 2 * hv * dv * dk * 4 + a_host * per_step).sum())
+    out["rollback_config4_us"] = t * 1e6
+    out["rollback_config4_gbs"] = b4 / t / 1e9
+    out["rollback_config4_frac"] = b4 / t / 1e9 / peak
+    del state, tape, kk, g
+    # config 3 at B = 16 and 128 on the full vocabulary (one GPU)
+    v, d = 248320, 5120
+    w = (torch.randn((v, d), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    for bsz in (16, 128):
+        h = torch.randn((bsz * 16, d), generator=gen, device=dev).to(torch.bfloat16)
+        keys = torch.empty(bsz * 16, dtype=torch.int64, device=dev)
+        t = _graph_time(lambda: pkg.lm_head_argmax_keys(h, w, out=keys), dev, reps=5)
+        fl = 2.0 * bsz * 16 * v * d
+        by = v * d * 2 + bsz * 16 * d * 2
+        out[f"lmhead_b{bsz}_ms"] = t * 1e3
+        out[f"lmhead_b{bsz}_hbm_frac"] = by / t / 1e9 / peak
+        out[f"lmhead_b{bsz}_tensor_frac"] = fl / t / 1e12 / tflops
+    out["other_configs_note"] = ("measured after the timed loop, one CUDA graph each; fractions of "
+                                 "the measured HBM copy bandwidth / cuBLAS bf16 burst throughput")
+    return out
+
+
+def measure_moe(dev, layers: int, steps: int, warmup: int, fuse_silu: bool) -> dict:
+    """BASELINE config 2 (hidden 2048, 256 experts, top-8, intermediate 512,
+    one shared expert, 16 tokens): ``layers`` layers with distinct weights in
+    one CUDA graph; HBM GB/s of the bytes of the experts the routing
+    activates + the shared expert + activations."""
     import torch
 
     import __graft_entry__
 
     __graft_entry__.load_package()
     from dflash_mlx_b200 import moe as M
+    from dflash_mlx_b200.verify_qmm import interleave_gate_up
 
-    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-        if int(os.environ.get("RANK", "0")) == 0:
-            print(json.dumps({"workload": "moe", "unavailable": "the MoE measurement runs on one GPU"}))
-        return 0
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
     hid, inter, e, topk, tok = 2048, 512, 256, 8, 16
     gen = torch.Generator(device=dev).manual_seed(7)
 
@@ -374,14 +562,12 @@ def run_moe(args):
         bi = -8 * sc + torch.randn(sc.shape, generator=gen, device=dev) * 0.1 * sc
         return M.QuantWeight(q, sc.to(torch.bfloat16), bi.to(torch.bfloat16))
 
-    from dflash_mlx_b200.verify_qmm import interleave_gate_up
-
-    layers = []
-    for _ in range(args.moe_layers):
+    lay = []
+    for _ in range(layers):
         experts = {"gate": qweight(inter, hid, (e,)), "up": qweight(inter, hid, (e,)),
                    "down": qweight(hid, inter, (e,))}
         shared = {"gate": qweight(inter, hid), "up": qweight(inter, hid), "down": qweight(hid, inter)}
-        if not args.no_fuse_silu:
+        if fuse_silu:
             # load-time layout: gate/up interleaved, SiLU*up fused into their launch
             experts = {"gate_up": M.fuse_expert_gate_up(experts["gate"], experts["up"]),
                        "down": experts["down"]}
@@ -391,48 +577,47 @@ def run_moe(args):
                                                interleave_gate_up(g.b, u.b).contiguous()),
                       "down": shared["down"]}
         logits = torch.randn((tok, e), generator=gen, device=dev)
-        layers.append((experts, shared, logits))
+        lay.append((experts, shared, logits))
     x = torch.randn((tok, hid), generator=gen, device=dev).to(torch.bfloat16)
     active = []
-    for _, _, logits in layers:
+    for _, _, logits in lay:
         _, _, ids = M.route(logits, topk)
         active.append(int(torch.unique(ids).numel()))
     per_expert = 3 * (inter * hid // 2 + 4 * inter * hid // 64)
     act_bytes = 2 * tok * hid * 2 + 2 * tok * topk * (inter * 2 + hid) + 2 * tok * (3 * inter + hid)
     bytes_total = sum(a * per_expert + per_expert + act_bytes for a in active)
-    stream = torch.cuda.Stream(dev)
 
     def body():
-        for experts, shared, logits in layers:
+        for experts, shared, logits in lay:
             M.moe_layer(x, logits, experts, shared, top_k=topk)
 
-    with torch.cuda.stream(stream):
-        body()
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            body()
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record()
-        for _ in range(args.steps):
-            graph.replay()
-        e1.record()
-    torch.cuda.synchronize()
-    t = e0.elapsed_time(e1) / 1e3 / args.steps
+    t = _graph_time(body, dev, reps=steps, warmup=warmup)
     peak, kind = _peaks()
     gbs = bytes_total / t / 1e9
-    print(json.dumps({
+    return {
         "workload": "moe", "metric": "MoE verify layer (BASELINE config 2) HBM GB/s", "value": gbs,
-        "unit": "GB/s", "us_per_layer": t / len(layers) * 1e6, "layers": len(layers),
-        "active_experts_per_layer": active, "bytes_per_layer": bytes_total / len(layers),
+        "unit": "GB/s", "us_per_layer": t / layers * 1e6, "layers": layers,
+        "active_experts_per_layer": active, "bytes_per_layer": bytes_total / layers,
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                      "peak_source": kind},
-        "silu_fused": not args.no_fuse_silu, "gpu_launches_per_layer": 6 if not args.no_fuse_silu else 10,
-        "steps": args.steps, "warmup": args.warmup, "dtype": "bf16", "data": "synthetic"}))
+        "silu_fused": fuse_silu, "gpu_launches_per_layer": 6 if fuse_silu else 10,
+        "steps": steps, "warmup": warmup, "dtype": "bf16", "data": "synthetic"}
+
+
+def run_moe(args):
+    """BASELINE config 2 on one GPU (see measure_moe).  Not the default
+    workload: the driver's bench line is the verify step, which also carries
+    this measurement in its config."""
+    import torch
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"workload": "moe", "unavailable": "the MoE measurement runs on one GPU"}))
+        return 0
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    print(json.dumps(measure_moe(dev, args.moe_layers, args.steps, args.warmup,
+                                 fuse_silu=not args.no_fuse_silu)))
     return 0
 
 
@@ -527,6 +712,9 @@ def main():
     ap.add_argument("--no-fuse-silu", action="store_true",
                     help="run SiLU*up as its own launch after the gate|up projection")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra-configs", action="store_true",
+                    help="skip the config 0 / 2 / 4 and lm_head B=16/128 measurements that the "
+                         "one-GPU line carries in its config")
     ap.add_argument("--workload", choices=["verify", "moe", "gdn-forward", "ddtree"], default="verify",
                     help="verify: the benchmark's verify step (default); moe: BASELINE config 2; "
                          "gdn-forward / ddtree: the GDN tape producer and the tree kernel alone")

@@ -35,6 +35,13 @@ extern "C" int dfl_get_device_error(int* device_error) {
   if (cudaMemcpyFromSymbol(&v, dfl::g_device_error, sizeof(int)) != cudaSuccess) return DFL_ERR_CUDA;
   const int zero = 0;
   if (cudaMemcpyToSymbol(dfl::g_device_error, &zero, sizeof(int)) != cudaSuccess) return DFL_ERR_CUDA;
+  if (v != 0) {
+    // a timed-out qmm may have left partial sums in the no-allocation scratch
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return DFL_ERR_CUDA;
+    const int st = dfl::qmm_noalloc::reset_after_device_error(dev);
+    if (st != DFL_OK) return st;
+  }
   *device_error = v;
   return DFL_OK;
 }

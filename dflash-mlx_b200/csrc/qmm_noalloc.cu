@@ -16,8 +16,9 @@
 //     calls in stream order are safe; calls that may overlap in time
 //     (different streams or host threads) race on the array.
 //   * A call that timed out (device error word set) can leave partial sums
-//     behind; nothing zero-fills the array a second time, so later results
-//     in that process are not to be trusted.
+//     behind.  dfl_get_device_error, which synchronises the device, zero-fills
+//     the array again on that device whenever it finds the word set, so
+//     calls after that check are correct again.
 // Nothing here calls cudaMalloc / cudaFree or any allocating routine.
 
 namespace dfl {
@@ -26,6 +27,13 @@ namespace qmm_noalloc {
 constexpr size_t kScratchBytes = size_t(8) << 20;
 
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
+
+// The largest need of any accepted shape (M <= 32: tiles of 32 rows, at most
+// kMaxGrid CTAs) fits, so DFL_ERR_SCRATCH_LIMIT is only a guard against a
+// future change of the tile or grid constants.
+static_assert(qmm::kCounterBytes + size_t(qmm::kMaxGrid) * 32 * qmm::BN * sizeof(float) <=
+                  kScratchBytes,
+              "the fixed scratch array must hold the split-K slots of every accepted shape");
 
 struct DeviceScratch {
   std::atomic<void*> ptr{nullptr};
@@ -58,6 +66,20 @@ inline int scratch_for_device(int dev, cudaStream_t stream, void** out) {
     }
   }
   *out = p;
+  return DFL_OK;
+}
+
+// After a device error on `dev` (the current device, already synchronised):
+// zero the array again if this device has resolved it, since a timed-out
+// kernel may have left tagged partial sums in it.  Allocates nothing.
+inline int reset_after_device_error(int dev) {
+  if (dev < 0 || dev >= host::kMaxDevices) return DFL_OK;
+  void* p = scratch_slot(dev).ptr.load(std::memory_order_acquire);
+  if (!p) return DFL_OK;
+  if (cudaMemset(p, 0, kScratchBytes) != cudaSuccess) {
+    cudaGetLastError();
+    return DFL_ERR_CUDA;
+  }
   return DFL_OK;
 }
 

@@ -7,7 +7,8 @@ Mirrors ``dflash_mlx/verify_linear.py``:
   ``group_size``, ``bits``, ``mode``) as a torch module, so models built for
   the MLX layout can be held on a B200;
 * ``is_verify_eligible``       -- ``verify_linear.py:54-87`` (same env knobs
-  ``DFLASH_VERIFY_MAX_N`` / ``DFLASH_VERIFY_INCLUDE`` and path tags);
+  ``DFLASH_VERIFY_MAX_N`` / ``DFLASH_VERIFY_INCLUDE``, read by ``settings.py``,
+  and path tags);
 * ``VerifyQuantizedLinear``    -- ``verify_linear.py:89-116``; every row count
   goes through the sm_100a qmm (the reference special-cases M=16 and M=4 and
   sends the rest to stock ``mx.quantized_matmul``);
@@ -26,10 +27,8 @@ from typing import Callable, Optional
 import torch
 from torch import nn
 
-from .internal_debug import verify_include, verify_max_n, verify_qmm_enabled
+from . import settings as _settings
 from .verify_qmm import verify_matmul
-
-_VERIFY_MAX_N_DEFAULT = 100_000
 
 _PROJ_TAGS = {
     "mlp.gate_proj": "mlp_gate",
@@ -99,25 +98,21 @@ def is_verify_eligible(ql, path: str = "") -> bool:
     k = int(ql.weight.shape[1]) * (32 // ql.bits)
     if k % 64 != 0:
         return False
-    if n >= verify_max_n(_VERIFY_MAX_N_DEFAULT):
+    cfg = _settings.read()
+    if n >= cfg.max_n:
         return False
-    include = verify_include()
-    if include not in ("", "all"):
-        tag = _path_tag(path)
-        allowed = {s.strip() for s in include.split(",") if s.strip()}
-        if "mlp" in allowed:
-            allowed.update({"mlp_gate", "mlp_up", "mlp_down"})
-        if "attn" in allowed:
-            allowed.update({"attn_q", "attn_k", "attn_v", "attn_o"})
-        if "gdn" in allowed:
-            allowed.update({"gdn_qkv", "gdn_z", "gdn_o"})
-        if tag not in allowed:
-            return False
-    return True
+    return cfg.allows(_path_tag(path))
 
 
 class VerifyQuantizedLinear(QuantizedLinear):
-    """Verify-path wrapper; shares the wrapped module's tensors (no copy)."""
+    """Verify-path wrapper; shares the wrapped module's tensors (no copy).
+
+    ``enable_qmm`` (default: ``DFLASH_VERIFY_QMM == "1"``) is accepted and
+    stored as ``enable_qmm`` for callers that inspect it.  In the reference it
+    chooses between its Metal verify kernels and stock MLX; here every call
+    runs the sm_100a kernel whatever its value, because there is no second
+    implementation to choose (no CPU or library fallback).
+    """
 
     @classmethod
     def from_quantized(cls, ql: QuantizedLinear, *,
@@ -125,12 +120,9 @@ class VerifyQuantizedLinear(QuantizedLinear):
         obj = cls(ql.weight.contiguous(), ql.scales.contiguous(), ql.biases.contiguous(),
                   getattr(ql, "bias", None), group_size=ql.group_size, bits=ql.bits,
                   mode=getattr(ql, "mode", "affine"))
-        obj.enable_qmm = verify_qmm_enabled() if enable_qmm is None else bool(enable_qmm)
+        obj.enable_qmm = _settings.read().qmm if enable_qmm is None else bool(enable_qmm)
         obj.requires_grad_(False)
         return obj
-
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return super().forward(x)
 
 
 def prewarm_verify_kernels(model: nn.Module, *, input_dtype=torch.bfloat16) -> int:

@@ -24,7 +24,7 @@ import torch
 
 from . import _lib
 from ._runtime import as_u32_bits, require_cuda, stream_ptr, workspace
-from .internal_debug import verify_qmm_enabled
+from . import settings as _settings
 
 MAX_ROWS_PER_CALL = 32
 
@@ -32,10 +32,10 @@ MAX_ROWS_PER_CALL = 32
 def is_enabled() -> bool:
     """``DFLASH_VERIFY_QMM == "1"`` (reference ``verify_qmm.py:15-16``).
 
-    Kept for interface parity; the B200 kernel is the only implementation,
-    so the flag does not change which code runs.
+    Reports the switch for callers that read it; the sm_100a kernel is the
+    only implementation, so it does not change which code runs.
     """
-    return verify_qmm_enabled()
+    return _settings.read().qmm
 
 
 def workspace_bytes(m: int, k: int, n: int) -> int:

@@ -19,7 +19,8 @@ for ``requests`` independent requests of 16 verify tokens on this GPU:
    ``accepted + 1`` steps), so no value is read back to the host; all layers'
    states share one arena and roll back in one launch.
 
-Weights are random with BASELINE's distributions (no checkpoints offline).
+Weights are random: nibbles uniform, scales ~ U(0.004, 0.02), biases
+-8 * scale + N(0, 0.1 * scale) (no checkpoints offline).
 The per-request qmm stack runs the same x through every layer (no attention
 or residual stream: those are outside the hot path).  Each device-side part
 is captured once in a CUDA graph and replayed; NCCL collectives (vocabulary
@@ -139,7 +140,7 @@ class VerifyStep:
         self.lm_w = (torch.randn((v_len, sh.hidden), generator=wgen, device=self.dev) * 0.02).to(torch.bfloat16)
         # GDN rollback snapshot states [layer, B, Hv, Dv, Dk] fp32 ~ N(0, 0.05)
         # and the tapes of one verify block, recorded by the verify forward
-        # (gated_delta_kernel_with_tape) from BASELINE config 4's inputs:
+        # (gated_delta_kernel_with_tape) from synthetic inputs:
         # q, k, v bf16 ~ N(0, 1) (q, k L2-normalised), beta = sigmoid(N),
         # g = exp(-softplus(N)).
         b, t, hv, dk, dv = self.requests, sh.block, sh.gdn_heads, sh.gdn_dk, sh.gdn_dv

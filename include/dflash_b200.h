@@ -52,7 +52,10 @@ const char* dfl_version(void);
 
 /* Reads and clears the device error word written by kernels on the current
  * device (bounded-wait time-outs, bad geometry).  Synchronises the device.
- * Returns DFL_OK and stores the word (0 = no error) in *device_error. */
+ * Returns DFL_OK and stores the word (0 = no error) in *device_error.  When
+ * the word was set it also zero-fills the library's own no-allocation
+ * scratch on that device (dfl_verify_qmm_w4g64_noalloc); caller workspaces
+ * are the caller's to zero-fill. */
 int dfl_get_device_error(int* device_error);
 
 /* ------------------------------------------------------------------------
@@ -153,9 +156,9 @@ size_t dfl_verify_qmm_workspace_bytes(int M, int K, int N, int* status);
  *   - the first call on a device zero-fills the array on `stream`; every
  *     call leaves it zero again, so calls in stream order are safe; calls
  *     that can overlap in time race;
- *   - a call that timed out (dfl_get_device_error non-zero) can leave partial
- *     sums behind, and nothing clears the array again: results of later
- *     calls in that process are not to be trusted.
+ *   - a call that timed out can leave partial sums behind; the next
+ *     dfl_get_device_error on that device that finds the error word set
+ *     zero-fills the array again, so check it before trusting later calls.
  * Allocates nothing. */
 int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q, const uint16_t* scales,
                                  const uint16_t* biases, uint16_t* y, int M, int K, int N,

@@ -114,7 +114,7 @@ def top2_margin(logits: np.ndarray, suppress_mask=None) -> np.ndarray:
 
 def synth_verify_ids(rng: np.random.Generator, posterior: np.ndarray, vocab: int,
                      p_match: float = 0.88) -> np.ndarray:
-    """Verify ids with P(d_j == posterior_{j-1}) = p_match.
+    """Verify ids with P(d_j == posterior_{j-1}) = p_match (0.88 by default).
 
     ``verify_ids[:, 0]`` (the staged token) is uniform; each later position
     copies the target argmax of the previous position with probability

@@ -149,7 +149,7 @@ def affine_quantize(w: np.ndarray, group_size: int = GROUP_SIZE, dtype: str = "b
 
 def synth_weights(rng: np.random.Generator, n: int, k: int, group_size: int = GROUP_SIZE,
                   dtype: str = "bf16"):
-    """BASELINE config-0 weight distribution.
+    """Synthetic weight distribution of the benchmark's dense qmm.
 
     q ~ U{0..15}; scales bf16 ~ U(0.004, 0.02) per (row, group);
     biases = -8*scale + N(0, 0.1*scale).  Returns (w_q, scales, biases).

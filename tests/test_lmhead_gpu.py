@@ -9,7 +9,9 @@ against the oracle scan applied to the kernel's own posterior and, where all
 margins are clear, against the oracle's.  Also: the reference's golden
 acceptance table on device, suppressed ids, vocabulary shards combined by
 key max (the multi-GPU reduction), ragged row counts and BASELINE config 3
-(V = 248320, D = 5120) at B = 1.
+(V = 248320, D = 5120) at B = 1 and 16 on the full vocabulary and at B = 16
+and 128 (256 / 2048 hidden rows) on one 8-way vocabulary shard, each with
+P = 0.88 verify ids scored against the oracle's posterior.
 """
 
 from __future__ import annotations
@@ -133,16 +135,64 @@ def test_match_acceptance_golden_table_on_device(pkg, dev, drafted, posterior, e
     assert int(pkg.match_acceptance_length(d, p).item()) == expected
 
 
-def test_config3_full_vocab_b1(pkg, dev):
-    r, d, v = 16, 5120, 248320
-    rng = np.random.default_rng(3)
-    h = obf16.from_f32(rng.standard_normal((r, d)).astype(np.float32))
-    wt = (torch.randn(v, d, generator=torch.Generator().manual_seed(3)) * 0.02).to(torch.bfloat16)
+@pytest.fixture(scope="module")
+def config3_weight():
+    """BASELINE config 3's lm_head, bf16 [248320, 5120] ~ N(0, 0.02), on the host."""
+    v, d = 248320, 5120
+    return (torch.randn(v, d, generator=torch.Generator().manual_seed(3)) * 0.02).to(torch.bfloat16)
+
+
+def _check_config3(pkg, dev, h, wt, v_begin=0, seed=0):
+    """Keys of one vocabulary shard against the oracle, then acceptance of
+    P = 0.88 verify ids drawn against the oracle's posterior."""
     w = wt.view(torch.int16).numpy().view(np.uint16)
     logits = olm.logits_bf16(h, w)
     ref = np.argmax(logits, axis=-1)
-    got = _decode(pkg.lm_head_argmax_keys(to_dev_bf16(h, dev), wt.to(dev)))
+    keys = pkg.lm_head_argmax_keys(to_dev_bf16(h, dev), wt.to(dev), v_begin=v_begin)
+    got = _decode(keys) - v_begin
     clear = _clear(logits, ref)
+    assert clear.mean() > 0.5
     assert np.array_equal(got[clear], ref[clear])
+    r = h.shape[0]
+    best = logits[np.arange(r), ref]
+    tol = 2 * np.maximum(np.abs(best), 1e-3) * 2.0 ** -7
+    assert np.all(logits[np.arange(r), got] >= best - tol)
+    # greedy acceptance of the blocks (global ids: the shard starts at v_begin)
+    b = r // 16
+    rng = np.random.default_rng(seed)
+    post_ref = ref.reshape(b, 16) + v_begin
+    ids = olm.synth_verify_ids(rng, post_ref, v_begin + w.shape[0], p_match=0.88)
+    post, acc, nxt, _ = pkg.verify_accept(keys, torch.from_numpy(ids).to(dev))
+    post, acc, nxt = post.cpu().numpy(), acc.cpu().numpy(), nxt.cpu().numpy()
+    for i in range(b):
+        a = olm.match_acceptance_length(ids[i, 1:], post[i, :-1])
+        assert acc[i] == a and nxt[i] == post[i, a]
+    rows = clear.reshape(b, 16).all(axis=1)
+    for i in np.flatnonzero(rows):
+        assert acc[i] == olm.match_acceptance_length(ids[i, 1:], post_ref[i, :-1])
     from dflash_mlx_b200 import _lib
     assert _lib.device_error() == 0
+
+
+def test_config3_full_vocab_b1(pkg, dev, config3_weight):
+    rng = np.random.default_rng(3)
+    h = obf16.from_f32(rng.standard_normal((16, 5120)).astype(np.float32))
+    _check_config3(pkg, dev, h, config3_weight, seed=1)
+
+
+def test_config3_full_vocab_b16(pkg, dev, config3_weight):
+    # B = 16 verify blocks: 256 hidden rows in one launch (128-row groups)
+    rng = np.random.default_rng(4)
+    h = obf16.from_f32(rng.standard_normal((256, 5120)).astype(np.float32))
+    _check_config3(pkg, dev, h, config3_weight, seed=2)
+
+
+@pytest.mark.parametrize("r", [256, 2048])
+def test_config3_vocab_shard_large_batches(pkg, dev, config3_weight, r):
+    # B = 16 and B = 128 (R = 256 / 2048 rows, 256-row groups at B = 128) on the
+    # 31,040-row vocabulary shard one of 8 GPUs holds (rank 3: ids 93,120..)
+    v_begin, v_len = 3 * 31040, 31040
+    rng = np.random.default_rng(5 + r)
+    h = obf16.from_f32(rng.standard_normal((r, 5120)).astype(np.float32))
+    _check_config3(pkg, dev, h, config3_weight[v_begin:v_begin + v_len].contiguous(),
+                   v_begin=v_begin, seed=r)
