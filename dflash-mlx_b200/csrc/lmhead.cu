@@ -57,7 +57,7 @@ struct Cfg {
 struct Params {
   const uint8_t* suppress;   // [V_total] or null, indexed by global id
   unsigned long long* out_keys;  // [R]
-  unsigned long long* cta_keys;  // workspace [grid][R]
+  unsigned long long* row_max;   // workspace [R]: running key maximum per row, zero between calls
   int* counter;
   int R, D, V, v_begin;
   int n_vtiles, n_rg, units, grid;
@@ -225,11 +225,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   }
 
-  // publish this CTA's keys; the last CTA reduces all of them
+  // fold this CTA's row keys into the workspace's running maxima; the last
+  // CTA copies them out and zeroes them again, so the workspace is all zero
+  // when the kernel ends (the convention every workspace user relies on:
+  // one buffer serves any sequence of calls on a stream)
   tc_fence_before();
   __syncthreads();
-  for (int i = threadIdx.x; i < p.R; i += NUM_THREADS)
-    p.cta_keys[(size_t)blockIdx.x * p.R + i] = keys[i];
+  for (int i = threadIdx.x; i < p.R; i += NUM_THREADS) {
+    const unsigned long long k = keys[i];
+    if (k != 0ull) atomicMax(&p.row_max[i], k);
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) *flag = (atomicAdd(p.counter, 1) == p.grid - 1) ? 1 : 0;
@@ -237,12 +242,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (*flag) {
     __threadfence();
     for (int i = threadIdx.x; i < p.R; i += NUM_THREADS) {
-      unsigned long long best = 0ull;
-      for (int c = 0; c < p.grid; ++c) {
-        const unsigned long long k = __ldcg(&p.cta_keys[(size_t)c * p.R + i]);
-        best = k > best ? k : best;
-      }
-      p.out_keys[i] = best;
+      p.out_keys[i] = __ldcg(&p.row_max[i]);
+      __stcg(&p.row_max[i], 0ull);
     }
     if (threadIdx.x == 0) *p.counter = 0;
   }
@@ -317,7 +318,8 @@ inline void geometry(int R, int V, int num_sms, int* n_vtiles, int* n_rg, int* u
 inline size_t workspace_bytes_for(int R, int V, int num_sms) {
   int nv, nrg, units, grid;
   geometry(R, V, num_sms, &nv, &nrg, &units, &grid);
-  return kCounterBytes + size_t(grid) * R * sizeof(unsigned long long);
+  (void)nv; (void)nrg; (void)units; (void)grid;
+  return kCounterBytes + size_t(R) * sizeof(unsigned long long);
 }
 
 template <int RT>
@@ -332,7 +334,7 @@ int launch(const uint16_t* h, const uint16_t* w, int R, int D, int V, int v_begi
   p.suppress = suppress;
   p.out_keys = out_keys;
   p.counter = reinterpret_cast<int*>(ws);
-  p.cta_keys = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes);
+  p.row_max = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes);
   p.R = R;
   p.D = D;
   p.V = V;

@@ -255,9 +255,10 @@ int dfl_tree_depthwise_conv1d(const void* qkv, const void* prefix, const float* 
  * is the largest logit with ties to the lowest id (argmax's first index),
  * so keys of several shards combine with max.  Logits are never written.
  * Constraints: 1 <= R <= 4096, D % 8 == 0, h and w 16-byte aligned.
- * workspace: dfl_lmhead_workspace_bytes(R, D, V) bytes; the same convention
- * as every workspace here: the first 64 KB are counters that must be zero
- * before the first call and are left zero, scratch data follows.
+ * workspace: dfl_lmhead_workspace_bytes(R, D, V) bytes (64 KB of counters +
+ * 8 bytes per row); the same convention as every workspace here: zero
+ * before the first call, and every call leaves all of it zero again, so one
+ * buffer serves any sequence of calls (qmm, MoE qmm, lm_head) in stream order.
  * Replaces logits_from_hidden (dflash_mlx/engine/target_qwen_gdn.py:774-778)
  * + greedy_tokens_with_mask (dflash_mlx/engine/sampling.py:47-55).
  * ---------------------------------------------------------------------- */
