@@ -13,7 +13,7 @@ Every op runs hand-written sm_100a CUDA from ``libdflash_b200.so`` through
 its C ABI (``include/dflash_b200.h``); there is no CPU fallback.
 """
 
-from . import checkpoint, kernels, lm_head, moe
+from . import checkpoint, kernels, lm_head, moe, qmm_plan
 from .lm_head import lm_head_argmax_keys, lm_head_verify, match_acceptance_length, verify_accept
 from .kernels import (gated_delta_kernel_with_tape, gated_delta_tree_kernel,
                       gated_delta_tree_tape_kernel, tape_replay_, tape_replay_kernel,
@@ -27,6 +27,7 @@ from .recurrent_rollback_cache import (
 )
 from .verify_qmm import (is_enabled, verify_matmul, qmm_w4g64, repack_pairs, interleave_gate_up,
                          gate_up_silu)
+from .qmm_plan import PlanPhase, ProjectionPlan, TiledWeight, qmm_tiled, tile_weight
 from .verify_linear import (
     QuantizedLinear,
     VerifyQuantizedLinear,
@@ -54,6 +55,12 @@ __all__ = [
     "repack_pairs",
     "interleave_gate_up",
     "gate_up_silu",
+    "qmm_plan",
+    "PlanPhase",
+    "ProjectionPlan",
+    "TiledWeight",
+    "qmm_tiled",
+    "tile_weight",
     "QuantizedLinear",
     "VerifyQuantizedLinear",
     "install_verify_linears",

@@ -75,6 +75,12 @@ SIGNATURES = {
     "dfl_silu_mul_bf16": (_c_int, [_vp, _vp, _vp, _c_int, _vp]),
     "dfl_silu_mul_rows_bf16": (_c_int, [_vp, _vp, _c_int, _vp, _c_int, _c_int, _vp]),
     "dfl_moe_combine": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
+    "dfl_w4_tiled_bytes": (_c_size, [_c_int, _c_int]),
+    "dfl_repack_w4_tiled": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
+    "dfl_qmm_plan_bytes": (_c_size, [_c_int]),
+    "dfl_qmm_plan_encode": (_c_int, [_vp, _c_int, _vp, _c_size]),
+    "dfl_qmm_plan_workspace_bytes": (_c_size, [_vp, ctypes.POINTER(_c_int)]),
+    "dfl_qmm_plan_run": (_c_int, [_vp, _vp, _vp, _c_size, _vp]),
 }
 
 _lock = threading.Lock()

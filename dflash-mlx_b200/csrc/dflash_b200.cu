@@ -6,6 +6,7 @@
 
 #include "qmm_w4.cu"
 #include "qmm_noalloc.cu"
+#include "qmm_plan.cu"
 #include "gdn_replay.cu"
 #include "gdn_forward.cu"
 #include "gdn_tree.cu"

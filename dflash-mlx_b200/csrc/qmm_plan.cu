@@ -1,0 +1,938 @@
+// Projection plans: one persistent launch runs a whole sequence of int4 g64
+// verify projections (a decoder layer's q|k|v, o, gate|up + SiLU, down, or a
+// whole layer stack) at M <= 32 tokens.
+//
+// Same arithmetic as the per-call qmm (qmm_w4.cu, which replaces the
+// reference's M=16 verify kernels, dflash_mlx/verify_qmm.py:196-765, and
+// stock mx.quantized_matmul(transpose=True)): w = float(nib) * s + b rounded
+// to bf16 (verify_qmm.py:249), fp32 accumulation, bf16 out.  What changes is
+// how the work reaches the SMs:
+//
+//   * Tiled weights (load-time layout, dfl_repack_w4_tiled): every pipeline
+//     unit (128 output rows x 512 of K) is one contiguous 36 KB block -- the
+//     packed nibbles in the order the dequant threads read them (each warp's
+//     16-byte loads are 512 contiguous bytes) followed by the unit's scales
+//     and biases (8 bytes per thread).  One bulk copy per unit, streamed with
+//     an L2 evict-first hint (weights are read once per step).
+//   * Subnormal dequantiser.  A bf16 bit pattern whose exponent field is 0
+//     or 1 is worth exactly (bits) * 2^-133, so a nibble masked into bits
+//     0-3 of a half word is n * 2^-133 and one in bits 4-7 is n * 2^-129.
+//     With the scale stored as s * 2^133 (exact: a power-of-two scaling) one
+//     bf16x2 FMA per pair gives n * s + b with a single rounding, the same
+//     bits as the reference's dequantisation.  Per 8 weights: 1 shift, 4
+//     AND, 4 FMA (the general path needs 3 shifts, 4 LOP3 and 8 FMA).  It
+//     needs |s| < 2^-5 for every group; tensors with larger scales use the
+//     general "magic 128" path, chosen per projection.
+//   * One launch, many projections.  Every CTA walks every projection
+//     ("phase") in order and takes an even contiguous share of its
+//     (tile, K unit) space (split-K across CTAs as in qmm_w4.cu).  The
+//     producer streams the next phase's weights and the dequant warps
+//     convert them while the current phase drains, so HBM never waits for a
+//     launch boundary.  A phase whose input x is written by an earlier phase
+//     names it (dep); its x is loaded only once every CTA has signalled that
+//     phase complete (a release counter per phase), so the dataflow of a
+//     real forward pass is kept.
+//
+// Warp roles (one CTA per SM, 25 warps): 0 producer, 1-4 MMA issuers (one
+// accumulator each, two of the unit's eight 64-K sub-blocks), 5-20 dequant
+// (4 groups x 4 TMEM lane quadrants, thread = output row), 21-24 x loads +
+// epilogue + split-K reduction + phase signals.
+//
+// Split-K: a tile shared by CTAs c_lo..c_hi is the last of c_lo's range in
+// that phase and the first of the others'.  Contributors store fp32
+// partials with the lowest mantissa bit set as a validity tag into their
+// own slot (one per CTA and phase parity); c_lo's epilogue polls, sums them
+// in CTA order, clears them and releases the slot (consumption counter), so
+// results are bit-reproducible and a slot is never overwritten before it
+// was read.  Every wait is bounded; a time-out sets the device error word
+// and a plan-wide abort word, and every CTA winds down.
+#include "common.cuh"
+#include "host_common.cuh"
+
+namespace dfl {
+namespace plan {
+
+constexpr int BN = 128;
+constexpr int UNIT_K = 512;
+constexpr int GS = 64;
+constexpr int NSUB = UNIT_K / GS;                      // 8 sub-blocks (quant groups) per unit
+constexpr int A_COLS = 32;                             // TMEM columns per A slot
+constexpr int NUM_MMA_WARPS = 4;
+constexpr int NDG = 4;                                 // dequant warp groups
+constexpr int WARP_TMA = 0;
+constexpr int WARP_MMA0 = 1;
+constexpr int WARP_DQ0 = WARP_MMA0 + NUM_MMA_WARPS;    // 5
+constexpr int WARP_EPI0 = WARP_DQ0 + 4 * NDG;          // 21
+constexpr int NUM_WARPS = WARP_EPI0 + 4;               // 25
+constexpr int NUM_THREADS = NUM_WARPS * 32;            // 800
+constexpr int TMEM_COLS = 512;
+constexpr int BAR_ID_EPI = 1;
+constexpr int PACK_BYTES = BN * UNIT_K / 2;            // 32768: nibbles of a unit
+constexpr int SB_BYTES = NDG * BN * 8;                 // 4096: scales + biases of a unit
+constexpr int BLK_BYTES = PACK_BYTES + SB_BYTES;       // 36864
+constexpr int NSTAGE = 4;
+constexpr int kMaxGrid = 160;
+constexpr int kMaxPhases = 7936;
+constexpr uint32_t kPlanMagic = 0x504C4644u;           // "DFLP"
+constexpr int kPlanVersion = 1;
+constexpr int kHeaderBytes = 256;
+constexpr int kPhaseSilu = 1;                          // DFL_PHASE_SILU
+constexpr int kPhaseSubnormal = 2;                     // DFL_PHASE_SUBNORMAL
+// workspace: 64 KB of counter words, then the split-K partial slots
+constexpr size_t kCounterBytes = host::kWorkspaceCounterBytes;
+constexpr int kWordExit = kMaxPhases;                  // CTAs that finished the launch
+constexpr int kWordAbort = kMaxPhases + 1;             // plan-wide abort
+constexpr int kWordCons = kMaxPhases + 4;              // [kMaxGrid][2] slot consumption counts
+static_assert((kWordCons + 2 * kMaxGrid) * 4 <= int(kCounterBytes), "counter region");
+static_assert(BLK_BYTES % 1024 == 0, "stage alignment");
+
+template <int MT>
+struct Cfg {
+  static constexpr int XBLK_BYTES = MT * 128;          // one [MT rows x 64 K] bf16 block, SW128
+  static constexpr int XSLOT_BYTES = NSUB * XBLK_BYTES;
+  static constexpr int XS = (MT <= 16) ? 4 : 2;        // x ring depth (units)
+  static constexpr int OFF_XRING = NSTAGE * BLK_BYTES;
+  static constexpr int OFF_BARS = OFF_XRING + XS * XSLOT_BYTES;
+  static constexpr int SMEM_BYTES = OFF_BARS + 512 + 1024;
+  static constexpr int NASLOT = (MT <= 16) ? 12 : 8;   // TMEM A slots (1.5 / 1 unit)
+  static constexpr int ACC_COL0 = NASLOT * A_COLS;
+  static constexpr int ACC_COLS = NUM_MMA_WARPS * MT;  // one accumulator buffer
+  static_assert(ACC_COL0 + 2 * ACC_COLS <= TMEM_COLS, "TMEM budget");
+  static_assert(XBLK_BYTES % 1024 == 0, "x blocks keep the 1024-byte swizzle alignment");
+  static_assert(NASLOT % NDG == 0 && NASLOT % NUM_MMA_WARPS == 0 && NASLOT >= NSUB, "A slots");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+// One projection of a plan as the kernel reads it (device memory, 64-byte
+// aligned so the x tensor map may be used by TMA in place).
+struct alignas(64) Phase {
+  CUtensorMap tm_x;      // x [M, K] bf16, box [64 K x MT rows], 128-byte swizzle
+  const uint8_t* w;      // tiled blob: n_tiles * ku blocks of BLK_BYTES, tile-major
+  uint16_t* y;           // [M, N] (SiLU: [M, N/2]), row stride ldy
+  int M, K, N, ldy;
+  int n_tiles, ku, total;
+  int flags, dep;
+};
+static_assert(sizeof(Phase) == 192, "phase record size");
+
+struct Header {
+  uint32_t magic;
+  int version, n_phases, mt, grid, flags_or;
+  int pad[58];
+};
+static_assert(sizeof(Header) == kHeaderBytes, "plan header size");
+
+struct RunParams {
+  const Phase* phases;
+  int n_phases;
+  int* words;           // workspace counter words
+  float* partials;      // workspace [grid][2][MT][BN]
+};
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Untiled bulk copy global -> shared with an L2 cache-policy hint.
+__device__ __forceinline__ void bulk_load_hint(uint32_t dst_smem, const void* src, uint32_t bytes,
+                                               uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(dst_smem),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint2 ld_shared_v2(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
+// 8 pair-packed nibbles (bits 4i..4i+3 = column 2i, bits 16+4i.. = column
+// 2i+1) -> 4 bf16x2 words (columns 0-1, 2-3, 4-5, 6-7), subnormal method:
+// s_lo = s * 2^133 (fields in bits 0-3 of a half), s_hi = s * 2^129 (bits 4-7).
+__device__ __forceinline__ void dequant8_subn(uint32_t q, uint32_t s_lo, uint32_t s_hi, uint32_t b,
+                                              uint32_t* out) {
+  asm("{\n\t.reg .b32 t, e0, e1, e2, e3;\n\t"
+      "shr.b32 t, %4, 8;\n\t"
+      "and.b32 e0, %4, 0x000F000F;\n\t"
+      "and.b32 e1, %4, 0x00F000F0;\n\t"
+      "and.b32 e2, t, 0x000F000F;\n\t"
+      "and.b32 e3, t, 0x00F000F0;\n\t"
+      "fma.rn.bf16x2 %0, e0, %5, %7;\n\t"
+      "fma.rn.bf16x2 %1, e1, %6, %7;\n\t"
+      "fma.rn.bf16x2 %2, e2, %5, %7;\n\t"
+      "fma.rn.bf16x2 %3, e3, %6, %7;\n\t}"
+      : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
+      : "r"(q), "r"(s_lo), "r"(s_hi), "r"(b));
+}
+
+// Same output, general method for any scale: mask | exponent bits of 128.0
+// give 128 + n exactly, an exact FMA removes the 128, then n * s + b.
+__device__ __forceinline__ void dequant8_magic(uint32_t q, uint32_t s, uint32_t b, uint32_t* out) {
+  asm("{\n\t.reg .b32 h1, h2, h3, t0, t1, t2, t3;\n\t"
+      "shr.b32 h1, %4, 4;\n\t"
+      "shr.b32 h2, %4, 8;\n\t"
+      "shr.b32 h3, %4, 12;\n\t"
+      "lop3.b32 t0, %4, 0x000F000F, 0x43004300, 0xEA;\n\t"
+      "lop3.b32 t1, h1, 0x000F000F, 0x43004300, 0xEA;\n\t"
+      "lop3.b32 t2, h2, 0x000F000F, 0x43004300, 0xEA;\n\t"
+      "lop3.b32 t3, h3, 0x000F000F, 0x43004300, 0xEA;\n\t"
+      "fma.rn.bf16x2 t0, t0, %7, %8;\n\t"
+      "fma.rn.bf16x2 t1, t1, %7, %8;\n\t"
+      "fma.rn.bf16x2 t2, t2, %7, %8;\n\t"
+      "fma.rn.bf16x2 t3, t3, %7, %8;\n\t"
+      "fma.rn.bf16x2 %0, t0, %5, %6;\n\t"
+      "fma.rn.bf16x2 %1, t1, %5, %6;\n\t"
+      "fma.rn.bf16x2 %2, t2, %5, %6;\n\t"
+      "fma.rn.bf16x2 %3, t3, %5, %6;\n\t}"
+      : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
+      : "r"(q), "r"(s), "r"(b), "r"(0x3F803F80u), "r"(0xC300C300u));
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(0x80008000u));
+  return d;
+}
+
+// CTA c's share of a phase of `total` units on a grid of G CTAs:
+// [floor(c * total / G), floor((c + 1) * total / G)).
+__device__ __forceinline__ int unit_begin(int c, int total, int grid) {
+  return int((long long)c * total / grid);
+}
+
+// The CTA whose (non-empty) range holds unit u.
+__device__ __forceinline__ int owner_of(int u, int total, int grid) {
+  return int(((long long)(u + 1) * grid + total - 1) / total) - 1;
+}
+
+// Spin until *addr >= target (acquire, gpu scope).  Gives up at once when
+// the CTA or plan-wide abort word is set, or after kWaitLimitNs (then sets
+// the device error word and both abort words).  Returns false on give-up.
+__device__ __forceinline__ bool wait_counter(const int* addr, int target, volatile int* cta_abort,
+                                             volatile int* plan_abort) {
+  if (ld_acquire(addr) >= target) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+    __nanosleep(32);
+    if (ld_acquire(addr) >= target) return true;
+    if (*cta_abort) return false;
+    if (*plan_abort) {
+      *cta_abort = 1;
+      return false;
+    }
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicExch(&g_device_error, kDevWaitTimeout);
+      *plan_abort = 1;
+      *cta_abort = 1;
+      return false;
+    }
+  }
+}
+
+template <int MT>
+__global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_constant__ RunParams rp) {
+  using C = Cfg<MT>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BARS);
+  uint64_t* full = bars;                       // [NSTAGE] unit block landed
+  uint64_t* empty = full + NSTAGE;             // [NSTAGE] block read by the dequant warps
+  uint64_t* afull = empty + NSTAGE;            // [NASLOT] TMEM A slot written
+  uint64_t* aempty = afull + C::NASLOT;        // [NASLOT] TMEM A slot read by the MMAs
+  uint64_t* xfull = aempty + C::NASLOT;        // [XS] x slot landed (TMA)
+  uint64_t* xfree = xfull + C::XS;             // [XS] x slot read by all MMA warps
+  uint64_t* accfull = xfree + C::XS;           // [2]
+  uint64_t* accempty = accfull + 2;            // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
+  volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
+  volatile int* plan_abort = reinterpret_cast<volatile int*>(rp.words + kWordAbort);
+  auto wait = [abort_word](uint64_t* bar, uint32_t parity) {
+    return mbar_wait_abortable(bar, parity, abort_word);
+  };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cta = blockIdx.x;
+  const int G = gridDim.x;
+  const int P = rp.n_phases;
+  const Phase* phases = rp.phases;
+
+  if (threadIdx.x == 0) {
+    *abort_word = 0;
+    for (int i = 0; i < NSTAGE; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4 * NDG);
+    }
+    for (int i = 0; i < C::NASLOT; ++i) {
+      mbar_init(&afull[i], 4);
+      mbar_init(&aempty[i], 1);
+    }
+    for (int i = 0; i < C::XS; ++i) {
+      mbar_init(&xfull[i], 1);
+      mbar_init(&xfree[i], NUM_MMA_WARPS);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accfull[i], NUM_MMA_WARPS);
+      mbar_init(&accempty[i], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == WARP_TMA) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == WARP_TMA) {
+    // ------------------------------------------------------------ producer
+    // One bulk copy per unit into the NSTAGE ring; waits only for the
+    // dequant warps to release a stage, never for another CTA.
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      int it = 0;
+      bool ok = true;
+      for (int p = 0; ok && p < P; ++p) {
+        const int total = phases[p].total;
+        const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
+        const uint8_t* src = phases[p].w + size_t(u0) * BLK_BYTES;
+        for (int u = u0; u < u1; ++u, ++it, src += BLK_BYTES) {
+          const int s = it % NSTAGE;
+          if (!wait(&empty[s], ((it / NSTAGE) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], BLK_BYTES);
+          bulk_load_hint(smem_u32(smem + s * BLK_BYTES), src, BLK_BYTES, &full[s], pol);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp < WARP_DQ0) {
+    // ------------------------------------------------------------ MMA issuers
+    // Warp j issues the MMAs of sub-blocks j and j + 4 of every unit into
+    // accumulator j; one accumulator segment per (phase, tile) part.
+    const int j = warp - WARP_MMA0;
+    constexpr uint32_t idesc = make_idesc_16(BN, MT, false);
+    const uint64_t ring_desc = make_sw128_desc(smem_u32(smem + C::OFF_XRING));
+    constexpr uint64_t kSlotDesc = uint64_t(C::XSLOT_BYTES >> 4);
+    constexpr uint64_t kBlkDesc = uint64_t(C::XBLK_BYTES >> 4);
+    int it = 0, acc_it = 0;
+    uint32_t buf = 0;
+    for (int p = 0; p < P; ++p) {
+      const int total = phases[p].total, ku = phases[p].ku;
+      const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
+      int kb = u0 % ku;
+      for (int u = u0; u < u1; ++u, ++it, kb = (kb + 1 == ku) ? 0 : kb + 1) {
+        const bool seg_start = (u == u0) || (kb == 0);
+        const bool seg_end = (u == u1 - 1) || (kb == ku - 1);
+        const int xs = it % C::XS;
+        if (seg_start) {
+          buf = acc_it & 1;
+          wait(&accempty[buf], ((acc_it >> 1) & 1) ^ 1);
+        }
+        wait(&xfull[xs], (it / C::XS) & 1);
+        const uint32_t d_tmem = tmem_base + C::ACC_COL0 + buf * C::ACC_COLS + j * MT;
+        const uint64_t slot_desc = ring_desc + kSlotDesc * xs;
+        uint32_t acc0 = seg_start ? 0u : 1u;
+#pragma unroll
+        for (int i = 0; i < NSUB / NUM_MMA_WARPS; ++i) {
+          const int sb = j + i * NUM_MMA_WARPS;
+          const int g = it * NSUB + sb;
+          const int slot = g % C::NASLOT;
+          wait(&afull[slot], (g / C::NASLOT) & 1);
+          tc_fence_after();
+          if (!*abort_word) {
+            const uint32_t a_tmem = tmem_base + slot * A_COLS;
+            const uint64_t bdesc = slot_desc + kBlkDesc * sb;
+            mma_bf16_ts_warp(d_tmem, a_tmem, bdesc, idesc, acc0);
+            mma_bf16_ts_warp(d_tmem, a_tmem + 8, bdesc + 2, idesc, 1u);
+            mma_bf16_ts_warp(d_tmem, a_tmem + 16, bdesc + 4, idesc, 1u);
+            mma_bf16_ts_warp(d_tmem, a_tmem + 24, bdesc + 6, idesc, 1u);
+          }
+          acc0 = 1u;
+          tc_commit_warp(&aempty[slot]);
+        }
+        tc_commit_warp(&xfree[xs]);
+        if (seg_end) {
+          tc_commit_warp(&accfull[buf]);
+          ++acc_it;
+        }
+      }
+    }
+  } else if (warp < WARP_EPI0) {
+    // ------------------------------------------------------------ dequant
+    const int dw = warp - WARP_DQ0;
+    const int grp = dw >> 2;               // sub-blocks grp and grp + 4 of every unit
+    const int quad = warp & 3;             // TMEM lane quadrant
+    const int r = quad * 32 + lane;        // output row within the tile
+    const uint32_t lane_base = tmem_base + (uint32_t(quad * 32) << 16);
+    int it = 0;
+    for (int p = 0; p < P; ++p) {
+      const int total = phases[p].total;
+      const bool subn = (phases[p].flags & kPhaseSubnormal) != 0;
+      const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
+      for (int u = u0; u < u1; ++u, ++it) {
+        const int s = it % NSTAGE;
+        wait(&full[s], (it / NSTAGE) & 1);
+        const uint32_t st = smem_u32(smem + s * BLK_BYTES);
+        // this thread's packed words (2 sub-blocks x 8 words) and its
+        // scales / biases, then the stage goes back to the producer
+        const uint2 sbw = ld_shared_v2(st + PACK_BYTES + uint32_t(grp * BN + r) * 8u);
+        uint4 qv[2][2];
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            qv[jj][h] = ld_shared_v4(st + uint32_t(((grp + 4 * jj) * 2 + h) * BN + r) * 16u);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        int slots[2];
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int g = it * NSUB + grp + 4 * jj;
+          const int slot = g % C::NASLOT;
+          slots[jj] = slot;
+          wait(&aempty[slot], ((g / C::NASLOT) & 1) ^ 1);
+          tc_fence_after();
+          const uint32_t s2 = __byte_perm(sbw.x, 0, jj ? 0x3232u : 0x1010u);
+          const uint32_t b2 = __byte_perm(sbw.y, 0, jj ? 0x3232u : 0x1010u);
+          uint32_t w[32];
+          if (subn) {
+            const uint32_t s_hi = bf16x2_mul(s2, 0x3D803D80u);  // * 2^-4
+            dequant8_subn(qv[jj][0].x, s2, s_hi, b2, &w[0]);
+            dequant8_subn(qv[jj][0].y, s2, s_hi, b2, &w[4]);
+            dequant8_subn(qv[jj][0].z, s2, s_hi, b2, &w[8]);
+            dequant8_subn(qv[jj][0].w, s2, s_hi, b2, &w[12]);
+            dequant8_subn(qv[jj][1].x, s2, s_hi, b2, &w[16]);
+            dequant8_subn(qv[jj][1].y, s2, s_hi, b2, &w[20]);
+            dequant8_subn(qv[jj][1].z, s2, s_hi, b2, &w[24]);
+            dequant8_subn(qv[jj][1].w, s2, s_hi, b2, &w[28]);
+          } else {
+            dequant8_magic(qv[jj][0].x, s2, b2, &w[0]);
+            dequant8_magic(qv[jj][0].y, s2, b2, &w[4]);
+            dequant8_magic(qv[jj][0].z, s2, b2, &w[8]);
+            dequant8_magic(qv[jj][0].w, s2, b2, &w[12]);
+            dequant8_magic(qv[jj][1].x, s2, b2, &w[16]);
+            dequant8_magic(qv[jj][1].y, s2, b2, &w[20]);
+            dequant8_magic(qv[jj][1].z, s2, b2, &w[24]);
+            dequant8_magic(qv[jj][1].w, s2, b2, &w[28]);
+          }
+          tmem_st_32x32b_x32(lane_base + slot * A_COLS, w);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&afull[slots[0]]);
+          mbar_arrive(&afull[slots[1]]);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------ x loads + epilogue + phase signals
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int et = threadIdx.x - WARP_EPI0 * 32;   // 0..127
+    const uint32_t lane_base = tmem_base + (uint32_t(quad * 32) << 16);
+    constexpr int XD = C::XS - 1;
+    int* const cons = rp.words + kWordCons;
+
+    // x staging cursor (thread et == 0 only): next unit to load, by phase.
+    int sp = 0, su = 0, su1 = 0, s_seq = 0;
+    bool s_dep_ok = true;
+    auto s_enter = [&](int p) {
+      const int total = phases[p].total;
+      su = unit_begin(cta, total, G);
+      su1 = unit_begin(cta + 1, total, G);
+      s_dep_ok = phases[p].dep < 0;
+      if (su < su1) {
+        // the x tensor map was written by a host copy into global memory:
+        // order that write before the tensor-map reads of the TMA unit
+        asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(
+                         reinterpret_cast<uint64_t>(&phases[p].tm_x))
+                     : "memory");
+      }
+    };
+    auto s_skip_empty = [&]() {
+      while (sp < P && su == su1) {
+        ++sp;
+        if (sp < P) s_enter(sp);
+      }
+    };
+    if (et == 0 && P > 0) {
+      s_enter(0);
+      s_skip_empty();
+    }
+    // Load x for the unit at the cursor.  A phase whose x depends on phase d
+    // is loaded only after every CTA signalled d complete, and only once this
+    // CTA's own epilogues of d are done (d < epi_phase); otherwise defer.
+    auto try_stage = [&](int epi_phase) -> bool {
+      const Phase& ph = phases[sp];
+      if (!s_dep_ok) {
+        const int d = ph.dep;
+        if (d >= epi_phase) return false;
+        if (!wait_counter(rp.words + d, G, abort_word, plan_abort)) return false;
+        fence_proxy_async_global();   // the x rows were written by other CTAs' stores
+        s_dep_ok = true;
+      }
+      const int xs = s_seq % C::XS;
+      if (s_seq >= C::XS) wait(&xfree[xs], ((s_seq / C::XS) - 1) & 1);
+      if (!*abort_word) {
+        const int k0 = (su % ph.ku) * UNIT_K;
+        uint8_t* dst = smem + C::OFF_XRING + xs * C::XSLOT_BYTES;
+        mbar_arrive_expect_tx(&xfull[xs], C::XSLOT_BYTES);
+#pragma unroll
+        for (int b = 0; b < NSUB; ++b)
+          tma_load_2d(dst + b * C::XBLK_BYTES, &ph.tm_x, &xfull[xs], k0 + b * GS, 0);
+      }
+      ++s_seq;
+      ++su;
+      s_skip_empty();
+      return true;
+    };
+
+    int seq = 0;           // sequence number of this CTA's first unit of phase p
+    int acc_it = 0;
+    int wpar[2] = {0, 0};  // partials this CTA has stored per slot parity
+    bool ok = true;
+    for (int p = 0; ok && p < P; ++p) {
+      const Phase& ph = phases[p];
+      const int total = ph.total, ku = ph.ku, M = ph.M, N = ph.N, ldy = ph.ldy;
+      const bool silu = (ph.flags & kPhaseSilu) != 0;
+      uint16_t* const y = ph.y;
+      const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
+      const int par = p & 1;
+      if (u0 < u1) {
+        const int t_first = u0 / ku, t_last = (u1 - 1) / ku;
+        for (int t = t_first; t <= t_last; ++t) {
+          const int kb0 = (t == t_first) ? (u0 - t * ku) : 0;
+          const int kb1 = (t == t_last) ? (u1 - t * ku) : ku;
+          const int last_seq = seq + (t * ku + kb1 - 1 - u0);
+          // x through this segment's last unit (its MMAs need it) and XD beyond
+          if (et == 0) {
+            while (sp < P && s_seq <= last_seq + XD)
+              if (!try_stage(p)) break;
+          }
+          __syncwarp();
+          const uint32_t buf = acc_it & 1;
+          const bool got = wait(&accfull[buf], (acc_it >> 1) & 1);
+          if (!named_bar_and(BAR_ID_EPI, 128, got && !*abort_word)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          float acc[MT];
+          {
+            uint32_t rr[16];
+#pragma unroll
+            for (int c = 0; c < MT; c += 16) {
+#pragma unroll
+              for (int a = 0; a < NUM_MMA_WARPS; ++a) {
+                tmem_ld_32x32b_x16(lane_base + C::ACC_COL0 + buf * C::ACC_COLS + a * MT + c, rr);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                  acc[c + i] = (a == 0) ? __uint_as_float(rr[i]) : acc[c + i] + __uint_as_float(rr[i]);
+              }
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&accempty[buf]);
+          ++acc_it;
+
+          const int n = t * BN + r;
+          auto store_final = [&](const float (&v)[MT]) {
+            if (n >= N) return;
+            if (silu) {
+              // rows interleaved in blocks of 32 (16 gate, then the 16 up rows
+              // of the same outputs): lanes 0-15 gate, 16-31 up
+              const int hcol = (n >> 5) * 16 + (lane & 15);
+#pragma unroll
+              for (int m = 0; m < MT; ++m) {
+                const uint32_t mine = __bfloat16_as_ushort(__float2bfloat16_rn(v[m]));
+                const uint32_t up = __shfl_down_sync(0xffffffffu, mine, 16);
+                if (lane < 16 && m < M)
+                  y[(size_t)m * ldy + hcol] = silu_mul_bits<false>(uint16_t(mine), uint16_t(up));
+              }
+            } else {
+              uint16_t* yp = y + n;
+#pragma unroll
+              for (int m = 0; m < MT; ++m, yp += ldy)
+                if (m < M) *yp = __bfloat16_as_ushort(__float2bfloat16_rn(v[m]));
+            }
+          };
+          if (kb0 == 0 && kb1 == ku) {
+            store_final(acc);
+            continue;
+          }
+          const int c_lo = owner_of(t * ku, total, G);
+          if (cta != c_lo) {
+            // contributor: wait until this slot's previous partial was consumed
+            bool gok = true;
+            if (et == 0) gok = wait_counter(cons + 2 * cta + par, wpar[par], abort_word, plan_abort);
+            if (!named_bar_and(BAR_ID_EPI, 128, gok && !*abort_word)) {
+              ok = false;
+              break;
+            }
+            uint32_t* mine = reinterpret_cast<uint32_t*>(rp.partials) + size_t(2 * cta + par) * MT * BN;
+#pragma unroll
+            for (int m = 0; m < MT; ++m) st_relaxed_u32(mine + m * BN + r, __float_as_uint(acc[m]) | 1u);
+            ++wpar[par];
+            continue;
+          }
+          // c_lo: add the contributors' partials to this CTA's accumulator in
+          // CTA order (8 rows at a time), clearing and releasing each slot
+          const int c_hi = owner_of(t * ku + ku - 1, total, G);
+          for (int c = c_lo + 1; ok && c <= c_hi; ++c) {
+            if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
+            uint32_t* slot = reinterpret_cast<uint32_t*>(rp.partials) + size_t(2 * c + par) * MT * BN;
+            bool pok = true;
+#pragma unroll
+            for (int m0 = 0; m0 < MT; m0 += 8) {
+              uint32_t v[8];
+#pragma unroll
+              for (int m = 0; m < 8; ++m) v[m] = ld_relaxed_u32(slot + (m0 + m) * BN + r);
+              const unsigned long long t0 = globaltimer_ns();
+              while (pok) {
+                bool all = true;
+#pragma unroll
+                for (int m = 0; m < 8; ++m)
+                  if (!(v[m] & 1u)) {
+                    all = false;
+                    v[m] = ld_relaxed_u32(slot + (m0 + m) * BN + r);
+                  }
+                if (all) break;
+                if (*abort_word) {
+                  pok = false;
+                } else if (*plan_abort) {
+                  *abort_word = 1;
+                  pok = false;
+                } else if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                  atomicExch(&g_device_error, kDevWaitTimeout);
+                  *plan_abort = 1;
+                  *abort_word = 1;
+                  pok = false;
+                }
+              }
+              if (pok) {
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                  acc[m0 + m] += __uint_as_float(v[m]);
+                  st_relaxed_u32(slot + (m0 + m) * BN + r, 0u);
+                }
+              }
+            }
+            if (!named_bar_and(BAR_ID_EPI, 128, pok && !*abort_word)) {
+              ok = false;
+              break;
+            }
+            if (et == 0) {
+              __threadfence();
+              red_release_add(cons + 2 * c + par, 1);
+            }
+          }
+          if (!ok) break;
+          store_final(acc);
+        }
+      }
+      if (!ok) break;
+      // every final value of phase p this CTA owes is stored: signal it
+      if (!named_bar_and(BAR_ID_EPI, 128, !*abort_word)) {
+        ok = false;
+        break;
+      }
+      if (et == 0) {
+        __threadfence();
+        red_release_add(rp.words + p, 1);
+      }
+      seq += u1 - u0;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == WARP_TMA) tmem_dealloc(tmem_base, TMEM_COLS);
+  // The last CTA to leave zeroes the phase counters and slot counts for the
+  // next launch (every other CTA is past its last use of them).
+  if (threadIdx.x == 0) {
+    __threadfence();
+    *last_flag = (atomicAdd(rp.words + kWordExit, 1) == G - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (*last_flag) {
+    __threadfence();
+    for (int i = threadIdx.x; i < P; i += NUM_THREADS) rp.words[i] = 0;
+    for (int i = threadIdx.x; i < 2 * kMaxGrid; i += NUM_THREADS) rp.words[kWordCons + i] = 0;
+    if (threadIdx.x == 0) {
+      rp.words[kWordAbort] = 0;
+      rp.words[kWordExit] = 0;
+    }
+  }
+}
+
+// MLX-packed int4 [N, K/8] + bf16 scales / biases [N, K/64] -> tiled blob.
+// Work item i of a block: i < 2048 is the 16-byte nibble chunk (ch, r) at
+// offset (ch * 128 + r) * 16 -- words w = 0..3 hold columns
+// sb * 64 + h * 32 + 8w .. +8 of the unit (sb = ch / 2, h = ch % 2) in the
+// pair-packed nibble order; i >= 2048 are two 8-byte scale/bias records
+// (g, r) at PACK_BYTES + (g * 128 + r) * 8 = {s_g, s_g+4, b_g, b_g+4}.
+__device__ __forceinline__ uint32_t pair_pack(uint32_t q) {
+  uint32_t o = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    o |= ((q >> (8 * j)) & 0xFu) << (4 * j);
+    o |= ((q >> (8 * j + 4)) & 0xFu) << (4 * (j + 4));
+  }
+  return o;
+}
+
+__device__ __forceinline__ uint16_t tiled_scale(uint16_t sv, bool subn) {
+  if (!subn) return sv;
+  float f = __bfloat162float(__ushort_as_bfloat16(sv));
+  if (!(fabsf(f) < 0.03125f)) {   // also catches NaN / inf
+    atomicExch(&g_device_error, kDevBadInput);
+    return 0;
+  }
+  f = (f * 0x1p66f) * 0x1p67f;    // exact: a power-of-two scaling inside the range
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__global__ void repack_tiled_kernel(const uint32_t* __restrict__ wq, const uint16_t* __restrict__ sc,
+                                    const uint16_t* __restrict__ bi, int N, int K, int ku,
+                                    int subn, uint8_t* __restrict__ dst, long long n_items) {
+  constexpr int PER_BLOCK = PACK_BYTES / 16 + SB_BYTES / 16;  // 2304
+  const int kw = K / 8, kg = K / GS;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_items;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long blk = i / PER_BLOCK;
+    const int e = int(i - blk * PER_BLOCK);
+    const int t = int(blk / ku), kb = int(blk - (long long)t * ku);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (e < PACK_BYTES / 16) {
+      const int ch = e / BN, r = e - ch * BN;
+      const int n = t * BN + r;
+      const int kcol0 = kb * UNIT_K + (ch >> 1) * GS + (ch & 1) * 32;
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int kc = kcol0 + 8 * q;
+        w[q] = (n < N && kc < K) ? pair_pack(wq[(size_t)n * kw + kc / 8]) : 0u;
+      }
+      v = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      uint32_t rec[4];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int idx = 2 * (e - PACK_BYTES / 16) + half;   // record (g, r), 0..511
+        const int g = idx / BN, r = idx - g * BN;
+        const int n = t * BN + r;
+        const int g0 = kb * NSUB + g, g1 = g0 + 4;
+        uint16_t s0 = 0, s1 = 0, b0 = 0, b1 = 0;
+        if (n < N) {
+          if (g0 < kg) {
+            s0 = tiled_scale(sc[(size_t)n * kg + g0], subn != 0);
+            b0 = bi[(size_t)n * kg + g0];
+          }
+          if (g1 < kg) {
+            s1 = tiled_scale(sc[(size_t)n * kg + g1], subn != 0);
+            b1 = bi[(size_t)n * kg + g1];
+          }
+        }
+        rec[2 * half] = uint32_t(s0) | (uint32_t(s1) << 16);
+        rec[2 * half + 1] = uint32_t(b0) | (uint32_t(b1) << 16);
+      }
+      v = make_uint4(rec[0], rec[1], rec[2], rec[3]);
+    }
+    *reinterpret_cast<uint4*>(dst + blk * BLK_BYTES + size_t(e) * 16) = v;
+  }
+}
+
+// ------------------------------------------------------------------ host
+inline size_t tiled_bytes(int N, int K) {
+  return size_t((N + BN - 1) / BN) * size_t((K + UNIT_K - 1) / UNIT_K) * BLK_BYTES;
+}
+
+inline size_t plan_bytes(int n) { return kHeaderBytes + size_t(n) * sizeof(Phase); }
+
+inline size_t workspace_bytes(int mt, int grid) {
+  return kCounterBytes + size_t(grid) * 2 * mt * BN * sizeof(float);
+}
+
+template <int MT>
+int launch(const Header& h, const void* plan_dev, void* ws, int dev, cudaStream_t stream) {
+  using C = Cfg<MT>;
+  static std::atomic<uint64_t> smem_done{0};
+  int st = host::ensure_smem(qmm_plan_kernel<MT>, C::SMEM_BYTES, dev, smem_done);
+  if (st != DFL_OK) return st;
+  RunParams rp;
+  rp.phases = reinterpret_cast<const Phase*>(static_cast<const uint8_t*>(plan_dev) + kHeaderBytes);
+  rp.n_phases = h.n_phases;
+  rp.words = static_cast<int*>(ws);
+  rp.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
+  // CTAs wait on one another (phase counters, split-K partials): launched
+  // cooperatively so that all of them are resident at once.
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(h.grid);
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, qmm_plan_kernel<MT>, rp) != cudaSuccess) {
+    cudaGetLastError();
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}
+
+inline int check_header(const void* plan_host, Header* out) {
+  if (!plan_host) return DFL_ERR_NULL_POINTER;
+  std::memcpy(out, plan_host, sizeof(Header));
+  if (out->magic != kPlanMagic || out->version != kPlanVersion || out->n_phases < 1 ||
+      out->n_phases > kMaxPhases || (out->mt != 16 && out->mt != 32) || out->grid < 1 ||
+      out->grid > kMaxGrid)
+    return DFL_ERR_BAD_SHAPE;
+  return DFL_OK;
+}
+
+}  // namespace plan
+}  // namespace dfl
+
+extern "C" size_t dfl_w4_tiled_bytes(int N, int K) {
+  if (N < 1 || K < 64 || K % 64 != 0) return 0;
+  return dfl::plan::tiled_bytes(N, K);
+}
+
+extern "C" int dfl_repack_w4_tiled(const uint32_t* w_q, const uint16_t* scales,
+                                   const uint16_t* biases, int N, int K, int subnormal, void* dst,
+                                   size_t dst_bytes, void* stream) {
+  using namespace dfl;
+  if (N < 1 || K < 64 || K % 64 != 0 || N > (1 << 24)) return DFL_ERR_BAD_SHAPE;
+  if (!w_q || !scales || !biases || !dst) return DFL_ERR_NULL_POINTER;
+  if (!host::aligned(w_q, 4) || !host::aligned(scales, 2) || !host::aligned(biases, 2) ||
+      !host::aligned(dst, 16))
+    return DFL_ERR_MISALIGNED;
+  if (dst_bytes < plan::tiled_bytes(N, K)) return DFL_ERR_WORKSPACE;
+  int dev, sms;
+  int st = host::current_device(&dev, &sms);
+  if (st != DFL_OK) return st;
+  const int ku = (K + plan::UNIT_K - 1) / plan::UNIT_K;
+  const long long n_items =
+      (long long)((N + plan::BN - 1) / plan::BN) * ku * (plan::PACK_BYTES / 16 + plan::SB_BYTES / 16);
+  const long long want = (n_items + 255) / 256;
+  const int blocks = int(want < (long long)sms * 16 ? want : (long long)sms * 16);
+  plan::repack_tiled_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      w_q, scales, biases, N, K, ku, subnormal ? 1 : 0, static_cast<uint8_t*>(dst), n_items);
+  return host::launch_status();
+}
+
+extern "C" size_t dfl_qmm_plan_bytes(int n_phases) {
+  if (n_phases < 1 || n_phases > dfl::plan::kMaxPhases) return 0;
+  return dfl::plan::plan_bytes(n_phases);
+}
+
+extern "C" int dfl_qmm_plan_encode(const dfl_qmm_phase* phases, int n_phases, void* plan_host,
+                                   size_t plan_bytes) {
+  using namespace dfl;
+  using namespace dfl::plan;
+  if (n_phases < 1 || n_phases > kMaxPhases) return DFL_ERR_BAD_SHAPE;
+  if (!phases || !plan_host) return DFL_ERR_NULL_POINTER;
+  if (plan_bytes < plan::plan_bytes(n_phases)) return DFL_ERR_WORKSPACE;
+  int dev, sms;
+  int st = host::current_device(&dev, &sms);
+  if (st != DFL_OK) return st;
+  int max_m = 0, flags_or = 0;
+  for (int p = 0; p < n_phases; ++p) {
+    const dfl_qmm_phase& q = phases[p];
+    if (q.M < 1 || q.M > 32 || q.K < 64 || q.K % 64 != 0 || q.N < 1 || q.N > (1 << 24))
+      return DFL_ERR_BAD_SHAPE;
+    if ((q.flags & ~(kPhaseSilu | kPhaseSubnormal)) != 0) return DFL_ERR_BAD_SHAPE;
+    const bool silu = (q.flags & kPhaseSilu) != 0;
+    if (silu && q.N % 32 != 0) return DFL_ERR_BAD_SHAPE;
+    if (q.ldx < q.K || q.ldy < (silu ? q.N / 2 : q.N)) return DFL_ERR_BAD_SHAPE;
+    if (q.dep < -1 || q.dep >= p) return DFL_ERR_BAD_SHAPE;
+    if (!q.x || !q.y || !q.w_tiled) return DFL_ERR_NULL_POINTER;
+    if (!host::aligned(q.x, 16) || q.ldx % 8 != 0 || !host::aligned(q.y, 2) ||
+        !host::aligned(q.w_tiled, 16))
+      return DFL_ERR_MISALIGNED;
+    const long long tiles = (q.N + BN - 1) / BN, ku = (q.K + UNIT_K - 1) / UNIT_K;
+    if (tiles * ku > (1LL << 31) / (kMaxGrid + 1)) return DFL_ERR_BAD_SHAPE;
+    max_m = q.M > max_m ? q.M : max_m;
+    flags_or |= q.flags;
+  }
+  const int mt = max_m <= 16 ? 16 : 32;
+  uint8_t* out = static_cast<uint8_t*>(plan_host);
+  Header h;
+  std::memset(&h, 0, sizeof(h));
+  h.magic = kPlanMagic;
+  h.version = kPlanVersion;
+  h.n_phases = n_phases;
+  h.mt = mt;
+  h.grid = sms < kMaxGrid ? sms : kMaxGrid;
+  h.flags_or = flags_or;
+  std::memcpy(out, &h, sizeof(h));
+  for (int p = 0; p < n_phases; ++p) {
+    const dfl_qmm_phase& q = phases[p];
+    Phase ph;
+    std::memset(&ph, 0, sizeof(ph));
+    st = host::make_tmap_2d(&ph.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q.x, uint64_t(q.K),
+                            uint64_t(q.M), uint64_t(q.ldx) * 2, GS, mt, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != DFL_OK) return st;
+    ph.w = static_cast<const uint8_t*>(q.w_tiled);
+    ph.y = static_cast<uint16_t*>(q.y);
+    ph.M = q.M;
+    ph.K = q.K;
+    ph.N = q.N;
+    ph.ldy = q.ldy;
+    ph.n_tiles = (q.N + BN - 1) / BN;
+    ph.ku = (q.K + UNIT_K - 1) / UNIT_K;
+    ph.total = ph.n_tiles * ph.ku;
+    ph.flags = q.flags;
+    ph.dep = q.dep;
+    std::memcpy(out + kHeaderBytes + size_t(p) * sizeof(Phase), &ph, sizeof(Phase));
+  }
+  return DFL_OK;
+}
+
+extern "C" size_t dfl_qmm_plan_workspace_bytes(const void* plan_host, int* status) {
+  int dummy;
+  int* st = status ? status : &dummy;
+  dfl::plan::Header h;
+  *st = dfl::plan::check_header(plan_host, &h);
+  if (*st != DFL_OK) return 0;
+  return dfl::plan::workspace_bytes(h.mt, h.grid);
+}
+
+extern "C" int dfl_qmm_plan_run(const void* plan_host, const void* plan_dev, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  using namespace dfl;
+  plan::Header h;
+  int st = plan::check_header(plan_host, &h);
+  if (st != DFL_OK) return st;
+  if (!plan_dev || !workspace) return DFL_ERR_NULL_POINTER;
+  if (!host::aligned(plan_dev, 64) || !host::aligned(workspace, 16)) return DFL_ERR_MISALIGNED;
+  if (workspace_bytes < plan::workspace_bytes(h.mt, h.grid)) return DFL_ERR_WORKSPACE;
+  int dev, sms;
+  st = host::current_device(&dev, &sms);
+  if (st != DFL_OK) return st;
+  if (h.grid > sms) return DFL_ERR_UNSUPPORTED;   // encoded for a larger device
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (h.mt == 16) return plan::launch<16>(h, plan_dev, workspace, dev, s);
+  return plan::launch<32>(h, plan_dev, workspace, dev, s);
+}

@@ -1,0 +1,185 @@
+"""Projection plans: many int4 g64 verify projections in one persistent launch.
+
+The reference runs one Metal kernel per quantized linear of the verify
+forward (``dflash_mlx/verify_linear.py:266-286`` -> ``verify_qmm.py``).  On
+B200 the projections of a decoder layer (or a whole layer stack) go through
+one launch of ``dfl_qmm_plan_run``: the weights of the next projection
+stream from HBM while the current one drains, and a projection that reads
+an earlier one's output waits for it on the device (``dep``).
+
+* :func:`tile_weight` -- load-time repack of MLX-packed weights into the
+  tiled layout the plan kernel streams (36 KB contiguous blocks).  Scales
+  below 2^-5 (the common case) select the kernel's subnormal dequantiser;
+  both dequantisers give the reference's ``nib * s + b`` rounded to bf16.
+* :class:`ProjectionPlan` -- phases (x, tiled weight, y, SiLU, dep) encoded
+  once, run many times (CUDA-graph capturable: the run allocates nothing).
+* :func:`qmm_tiled` -- one projection through a one-phase plan.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._runtime import as_u32_bits, require_cuda, stream_ptr
+
+PHASE_SILU = 1
+PHASE_SUBNORMAL = 2
+SUBNORMAL_SCALE_LIMIT = 2.0 ** -5
+
+
+class _Phase(ctypes.Structure):
+    _fields_ = [("x", ctypes.c_void_p), ("y", ctypes.c_void_p), ("w_tiled", ctypes.c_void_p),
+                ("M", ctypes.c_int), ("K", ctypes.c_int), ("N", ctypes.c_int),
+                ("ldx", ctypes.c_int), ("ldy", ctypes.c_int), ("flags", ctypes.c_int),
+                ("dep", ctypes.c_int)]
+
+
+@dataclass
+class TiledWeight:
+    """A weight [N, K] in the plan kernel's tiled layout (``blob`` uint8)."""
+    blob: torch.Tensor
+    n: int
+    k: int
+    subnormal: bool
+
+
+def scales_fit_subnormal(scales: torch.Tensor) -> bool:
+    """True when every scale is finite with magnitude below 2^-5 (the
+    subnormal dequantiser's range).  Reads one value back to the host."""
+    s = scales.float()
+    return bool(torch.isfinite(s).all().item()) and float(s.abs().max().item()) < SUBNORMAL_SCALE_LIMIT
+
+
+def tiled_bytes(n: int, k: int) -> int:
+    return int(_lib.load().dfl_w4_tiled_bytes(int(n), int(k)))
+
+
+def tile_weight(w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *,
+                subnormal: Optional[bool] = None) -> TiledWeight:
+    """MLX-packed ``w_q`` uint32 [N, K/8] + bf16 ``scales`` / ``biases``
+    [N, K/64] -> :class:`TiledWeight`.  ``subnormal=None`` checks the scales."""
+    for t, name in ((w_q, "w"), (scales, "scales"), (biases, "biases")):
+        require_cuda(t, name)
+    if scales.dtype != torch.bfloat16 or biases.dtype != torch.bfloat16:
+        raise NotImplementedError("the tiled layout takes bfloat16 scales and biases")
+    w_q = as_u32_bits(w_q)
+    n, k = int(w_q.shape[0]), int(w_q.shape[1]) * 8
+    if k % 64 != 0:
+        raise ValueError(f"K={k} must be a multiple of 64")
+    scales, biases = scales.contiguous(), biases.contiguous()
+    if tuple(scales.shape) != (n, k // 64) or tuple(biases.shape) != (n, k // 64):
+        raise ValueError("scales/biases must be [N, K/64]")
+    if subnormal is None:
+        subnormal = scales_fit_subnormal(scales)
+    nbytes = tiled_bytes(n, k)
+    blob = torch.empty(nbytes, dtype=torch.uint8, device=w_q.device)
+    with torch.cuda.device(w_q.device):
+        st = _lib.load().dfl_repack_w4_tiled(w_q.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                                             n, k, 1 if subnormal else 0, blob.data_ptr(), nbytes,
+                                             stream_ptr(w_q.device))
+    _lib.check("dfl_repack_w4_tiled", st)
+    return TiledWeight(blob, n, k, bool(subnormal))
+
+
+@dataclass
+class PlanPhase:
+    """One projection of a plan: ``y = x @ W.T`` (or ``silu(gate) * up`` with
+    ``silu`` over gate/up rows interleaved by ``interleave_gate_up``); ``dep``
+    = index of an earlier phase whose outputs ``x`` reads (-1: none)."""
+    x: torch.Tensor
+    weight: TiledWeight
+    y: torch.Tensor
+    silu: bool = False
+    dep: int = -1
+
+
+def _check_rows(t: torch.Tensor, name: str, cols: int) -> int:
+    if t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a bfloat16 [rows, cols] tensor with unit column stride")
+    if t.shape[1] != cols:
+        raise ValueError(f"{name} has {t.shape[1]} columns, expected {cols}")
+    return int(t.stride(0))
+
+
+class ProjectionPlan:
+    """A sequence of projections encoded once and launched as one kernel.
+
+    The tensors' addresses are baked into the plan: keep them (the plan holds
+    references) and write new inputs into them in place between runs."""
+
+    def __init__(self, phases: Sequence[PlanPhase]):
+        if not phases:
+            raise ValueError("a plan needs at least one phase")
+        lib = _lib.load()
+        dev = phases[0].x.device
+        arr = (_Phase * len(phases))()
+        for i, ph in enumerate(phases):
+            for t, name in ((ph.x, "x"), (ph.y, "y"), (ph.weight.blob, "weight")):
+                require_cuda(t, name)
+                if t.device != dev:
+                    raise ValueError("every tensor of a plan must be on one device")
+            w = ph.weight
+            m = int(ph.x.shape[0])
+            if not 1 <= m <= 32:
+                raise ValueError(f"phase {i}: {m} rows (a plan takes 1..32 rows per phase)")
+            ldx = _check_rows(ph.x, f"phase {i} x", w.k)
+            n_out = w.n // 2 if ph.silu else w.n
+            ldy = _check_rows(ph.y, f"phase {i} y", n_out)
+            if int(ph.y.shape[0]) != m:
+                raise ValueError(f"phase {i}: y has {ph.y.shape[0]} rows, x has {m}")
+            if ph.silu and w.n % 32 != 0:
+                raise ValueError(f"phase {i}: SiLU needs N % 32 == 0 (interleaved gate/up rows)")
+            if not -1 <= ph.dep < i:
+                raise ValueError(f"phase {i}: dep {ph.dep} must name an earlier phase or be -1")
+            flags = (PHASE_SILU if ph.silu else 0) | (PHASE_SUBNORMAL if w.subnormal else 0)
+            arr[i] = _Phase(ph.x.data_ptr(), ph.y.data_ptr(), w.blob.data_ptr(), m, w.k, w.n,
+                            ldx, ldy, flags, int(ph.dep))
+        nbytes = int(lib.dfl_qmm_plan_bytes(len(phases)))
+        if nbytes == 0:
+            raise ValueError(f"{len(phases)} phases is outside the plan limit")
+        self._host = (ctypes.c_uint8 * nbytes)()
+        with torch.cuda.device(dev):
+            st = lib.dfl_qmm_plan_encode(arr, len(phases), self._host, nbytes)
+            _lib.check("dfl_qmm_plan_encode", st)
+            status = ctypes.c_int(0)
+            ws_bytes = int(lib.dfl_qmm_plan_workspace_bytes(self._host, ctypes.byref(status)))
+            _lib.check("dfl_qmm_plan_workspace_bytes", status.value)
+            host_t = torch.frombuffer(bytearray(self._host), dtype=torch.uint8)
+            self.plan_dev = host_t.to(dev)
+            self.workspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+        self.device = dev
+        self.phases: List[PlanPhase] = list(phases)
+
+    def run(self) -> None:
+        """Launch the plan on the current stream of its device."""
+        with torch.cuda.device(self.device):
+            st = _lib.load().dfl_qmm_plan_run(self._host, self.plan_dev.data_ptr(),
+                                              self.workspace.data_ptr(), self.workspace.numel(),
+                                              stream_ptr(self.device))
+        _lib.check("dfl_qmm_plan_run", st)
+
+    def reset_workspace(self) -> None:
+        """Zero the workspace again (needed after a reported device error)."""
+        self.workspace.zero_()
+
+
+def qmm_tiled(x: torch.Tensor, weight: TiledWeight, out: Optional[torch.Tensor] = None, *,
+              silu: bool = False) -> torch.Tensor:
+    """``x [M, K] @ W.T`` (or the fused SiLU*up) through a one-phase plan, M <= 32."""
+    require_cuda(x, "x")
+    if x.dtype != torch.bfloat16:
+        raise NotImplementedError("the plan kernel takes bfloat16 activations")
+    x = x.contiguous()
+    m = int(x.shape[0])
+    n_out = weight.n // 2 if silu else weight.n
+    if out is None:
+        out = torch.empty((m, n_out), dtype=torch.bfloat16, device=x.device)
+    # the plan's device buffers are freed to torch's stream-ordered allocator
+    # after the launch is queued, so they are not reused before it ran
+    ProjectionPlan([PlanPhase(x, weight, out, silu=silu)]).run()
+    return out

@@ -165,6 +165,74 @@ int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q, const u
                                  void* stream);
 
 /* ------------------------------------------------------------------------
+ * Projection plans: one persistent launch for a sequence of int4 g64
+ * verify projections (a decoder layer, or a whole layer stack).
+ *
+ * Weights first go through a load-time repack into the tiled layout:
+ * dfl_w4_tiled_bytes(N, K) bytes (ceil(N/128) * ceil(K/512) blocks of
+ * 36864 bytes: one contiguous block per 128 rows x 512 columns, nibbles in
+ * the order the kernel's dequant threads read them, then that block's
+ * scales and biases).  dfl_repack_w4_tiled reads MLX-packed w_q [N, K/8]
+ * and bf16 scales / biases [N, K/64] (K % 64 == 0); rows and columns past
+ * N / K are stored as zero weights.  subnormal = 1 stores every scale as
+ * scale * 2^133 for the kernel's subnormal dequantiser and needs
+ * |scale| < 2^-5 (finite) for every group; a scale outside that range is
+ * stored as 0 and sets the device error word (kDevBadInput), so check the
+ * scales first and pass subnormal = 0 for such a tensor.  Both forms give
+ * the dequantised weights bit for bit (w = nib * scale + bias, rounded
+ * once to bf16, as dflash_mlx/verify_qmm.py:249).  Not a reference format
+ * (the reference keeps MLX order, verify_qmm.py:905); like concatenating
+ * projections, it is done once per weight.
+ *
+ * A plan is an array of phases run in order.  Phase p computes
+ * y = x @ dequant(W)^T for M <= 32 rows (bf16 x [M, K] with row stride ldx,
+ * ldx % 8 == 0, x 16-byte aligned; y [M, N] with row stride ldy) or, with
+ * DFL_PHASE_SILU, h [M, N/2] = silu(gate) * up over gate/up rows
+ * interleaved in blocks of 16 (N % 32 == 0, as dfl_verify_qmm_w4g64_silu).
+ * DFL_PHASE_SUBNORMAL must match the subnormal flag of the phase's repack.
+ * dep = q (an earlier phase) makes the phase read x only after every output
+ * of phase q is written (x may be phase q's y); dep = -1 reads x at once.
+ * Results equal dfl_verify_qmm_w4g64 on the same weights up to fp32
+ * summation order; each phase's split over the SMs depends only on its own
+ * shape, so a phase gives the same bits in any plan.
+ *
+ * dfl_qmm_plan_encode writes the plan for the current device into a host
+ * buffer of dfl_qmm_plan_bytes(n_phases) bytes; copy those bytes to a
+ * 64-byte-aligned device buffer (any stream-ordered copy) before the first
+ * run.  The x / y / weight pointers are baked in: re-encode when they
+ * change.  dfl_qmm_plan_run launches the plan (one cooperative launch of
+ * one CTA per SM) with a workspace of dfl_qmm_plan_workspace_bytes bytes,
+ * zero before the first run; every run leaves it zero.  After a run that
+ * reported a device error (dfl_get_device_error) zero it again.  One
+ * workspace must not be shared by runs that may overlap.  No counterpart in
+ * the reference (it launches one Metal kernel per projection through
+ * VerifyQuantizedLinear, dflash_mlx/verify_linear.py:266-286); it replaces
+ * that sequence of calls for a block of 16 or 32 verify rows.
+ * ---------------------------------------------------------------------- */
+#define DFL_PHASE_SILU 1
+#define DFL_PHASE_SUBNORMAL 2
+
+typedef struct dfl_qmm_phase {
+  const void* x;        /* bf16 [M, K], row stride ldx elements */
+  void* y;              /* bf16 [M, N] (SiLU: [M, N/2]), row stride ldy elements */
+  const void* w_tiled;  /* dfl_repack_w4_tiled output for this [N, K] weight */
+  int M, K, N;
+  int ldx, ldy;
+  int flags;            /* DFL_PHASE_SILU | DFL_PHASE_SUBNORMAL */
+  int dep;              /* -1, or an earlier phase whose outputs x reads */
+} dfl_qmm_phase;
+
+size_t dfl_w4_tiled_bytes(int N, int K);
+int dfl_repack_w4_tiled(const uint32_t* w_q, const uint16_t* scales, const uint16_t* biases,
+                        int N, int K, int subnormal, void* dst, size_t dst_bytes, void* stream);
+size_t dfl_qmm_plan_bytes(int n_phases);
+int dfl_qmm_plan_encode(const dfl_qmm_phase* phases, int n_phases, void* plan_host,
+                        size_t plan_bytes);
+size_t dfl_qmm_plan_workspace_bytes(const void* plan_host, int* status);
+int dfl_qmm_plan_run(const void* plan_host, const void* plan_dev, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * GatedDeltaNet tape-replay rollback.
  *
  * For every sequence b, value head hv and replayed step t:
