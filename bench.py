@@ -50,6 +50,18 @@ def _peak_tflops():
         return 1590.0
 
 
+def _profile_value(fname: str, key: str):
+    """An integer recorded as ``key value`` in a committed ncu summary."""
+    f = ROOT / "profiles" / fname
+    try:
+        for line in f.read_text().splitlines():
+            if line.startswith(key):
+                return int(line.split(":")[1].strip()), line
+    except Exception:
+        pass
+    return None, None
+
+
 def _traffic_per_launch():
     """DRAM bytes per qmm launch (mean over the four launch kinds of a layer)
     from the committed ncu summary, if present."""
@@ -281,7 +293,7 @@ def run_ours(args):
     shape = StackShape(layers=args.layers)
     step = VerifyStep(dev, requests=args.requests_per_gpu, shape=shape, rank=rank, world=world,
                       group=group, weight_layout=args.weight_layout,
-                      fuse_silu=args.weight_layout == "pairs" and not args.no_fuse_silu)
+                      fuse_silu=args.weight_layout != "mlx" and not args.no_fuse_silu)
     sh = step.shape
     b = args.requests_per_gpu
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -356,10 +368,18 @@ def run_ours(args):
     mean_acc = float(step.acceptance.float().mean())
     # roofline of the dominant kernel (the int4 verify qmm)
     peak, peak_kind = _peaks()
+    plan = step.plan is not None
     launches = len(sh.launches()) * sh.layers * (((b + 1) // 2) if step.pack_requests else b)
-    bytes_per_step = sh.qmm_bytes_per_step(b, step.pack_requests, silu_fused=step.fuse_silu)
+    bytes_per_step = sh.qmm_bytes_per_step(b, step.pack_requests or plan, silu_fused=step.fuse_silu)
     achieved = bytes_per_step / (t_qmm / args.steps) / 1e9
-    traffic, _ = _traffic_per_launch()
+    if plan:
+        # one launch runs the whole stack: DRAM bytes of a layer (ncu) x layers
+        per_layer, _ = _profile_value("qmm_plan_verify_stack.md", "dram_bytes_per_layer:")
+        traffic = None if per_layer is None else per_layer * sh.layers
+        qmm_launches = 1
+    else:
+        traffic, _ = _traffic_per_launch()
+        qmm_launches = launches + (0 if step.fuse_silu else launches // 4)
 
     line = None
     if rank == 0:
@@ -378,9 +398,13 @@ def run_ours(args):
                 "requests_per_gpu": b, "tokens_per_request": sh.block,
                 "weight_layout": args.weight_layout,
                 "requests_share_launches": step.pack_requests,
+                "qmm_launch": ("one plan launch per step; each projection waits on the device for "
+                               "the previous one (q|k|v -> o -> gate|up -> down -> next layer)"
+                               if plan else "one launch per projection (programmatic dependent "
+                               "launch)"),
                 "mlp_silu_fused": step.fuse_silu,
                 "parallelism": f"request-DP x{world}, lm_head vocab split x{world}",
-                "l2": "inputs larger than L2 (12.3 GB of packed weights per step)",
+                "l2": "inputs larger than L2 (12.4 GB of packed weights per step)",
                 "qmm_ms_per_step": t_qmm / args.steps * 1e3,
                 "qmm_gbs": achieved,
                 "verify_ids": "P(draft = previous position's posterior) = 0.88, posterior from set-up",
@@ -388,16 +412,18 @@ def run_ours(args):
             },
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "qmm_w4g64 (int4 verify qmm, M=16)",
+                         "kernel": ("qmm_plan_kernel (int4 verify qmm, M=16: the step's %d "
+                                    "projections in one persistent launch)" % (4 * sh.layers)
+                                    if plan else "qmm_w4g64 (int4 verify qmm, M=16)"),
                          "peak_source": peak_kind,
-                         "note": "achieved = algorithmic bytes of the qmm launches of a step (4 per "
-                                 "layer: q|k|v, o, gate|up, down) / their CUDA-event time inside "
-                                 "the timed region"},
-            # ours per step: 4 qmm per layer and request (+ 1 SiLU*up launch unless it
-            # is fused into the gate|up epilogue), lm_head argmax, accept, one tape
-            # replay over all GDN layers
-            "gpu_launches": args.steps * (launches + (0 if step.fuse_silu else launches // 4)
-                                          + 2 + 1),
+                         "note": "achieved = algorithmic bytes of the step's projections (4 per "
+                                 "layer: q|k|v, o, gate|up + SiLU, down; packed weights + bf16 "
+                                 "scales/biases + activations) / their CUDA-event time inside "
+                                 "the timed region; traffic = ncu DRAM bytes per launch"},
+            # ours per step: the qmm stack (one plan launch, or 4 launches per layer
+            # and request pair, + 1 SiLU*up launch unless fused), lm_head argmax,
+            # accept, one tape replay over all GDN layers
+            "gpu_launches": args.steps * (qmm_launches + 2 + 1),
             "e2e": {"value": world * b / t_e2e, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "clocks": clk,
@@ -706,9 +732,10 @@ def main():
     ap.add_argument("--layers", type=int, default=64,
                     help="decoder layers of the qmm stack (64 = the benchmark; fewer only for "
                          "profiling small cases)")
-    ap.add_argument("--weight-layout", choices=["mlx", "pairs"], default="pairs",
-                    help="int4 nibble order of the stack's weights: the reference's MLX packing, "
-                         "or repacked once at load into the kernel's pair-packed order")
+    ap.add_argument("--weight-layout", choices=["mlx", "pairs", "tiled"], default="tiled",
+                    help="int4 layout of the stack's weights: the reference's MLX packing or the "
+                         "pair-packed order (one qmm launch per projection), or the tiled layout "
+                         "(the whole stack as one projection plan: one persistent launch per step)")
     ap.add_argument("--no-fuse-silu", action="store_true",
                     help="run SiLU*up as its own launch after the gate|up projection")
     ap.add_argument("--no-cpu-baseline", action="store_true")

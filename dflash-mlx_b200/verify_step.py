@@ -37,6 +37,7 @@ import torch
 from . import lm_head as _lm
 from .kernels import gated_delta_kernel_with_tape, tape_replay_
 from .moe import QuantWeight, silu_mul
+from .qmm_plan import PlanPhase, ProjectionPlan, tile_weight
 from .verify_qmm import gate_up_silu, qmm_w4g64, repack_pairs
 
 
@@ -110,11 +111,13 @@ class VerifyStep:
                  rank: int = 0, world: int = 1, group=None, seed: int = 0,
                  weight_layout: str = "mlx", fuse_silu: bool = False, pack_requests: bool = True):
         self.dev = torch.device(device)
-        if weight_layout not in ("mlx", "pairs"):
+        if weight_layout not in ("mlx", "pairs", "tiled"):
             raise ValueError(f"unknown weight layout {weight_layout!r}")
         self.weight_layout = weight_layout
-        if fuse_silu and weight_layout != "pairs":
-            raise ValueError("the fused SiLU epilogue takes pair-packed weights")
+        if fuse_silu and weight_layout == "mlx":
+            raise ValueError("the fused SiLU epilogue takes pair-packed or tiled weights")
+        if weight_layout == "tiled" and not fuse_silu:
+            raise ValueError("the tiled (plan) stack runs gate|up with the fused SiLU epilogue")
         # fuse_silu: the gate|up weights are read as the gate and up rows
         # interleaved in blocks of 16 (interleave_gate_up) and one launch
         # writes silu(gate) * up
@@ -134,6 +137,15 @@ class VerifyStep:
             for lw in self.layers:
                 for qw in lw.values():
                     repack_pairs(qw.q, out=qw.q)
+        elif weight_layout == "tiled":
+            # load-time repack into the plan kernel's tiled layout; the MLX-packed
+            # copies are dropped once tiled
+            tiled = []
+            for lw in self.layers:
+                tiled.append({name: tile_weight(qw.q, qw.s, qw.b) for name, qw in lw.items()})
+                lw.clear()
+            self.tiled = tiled
+            self.layers = None
         # this rank's vocabulary shard of the bf16 lm_head, N(0, 0.02)
         self.v_begin, v_len = _lm.vocab_shard(sh.vocab, rank, world)
         wgen = torch.Generator(device=self.dev).manual_seed(seed + 1000 + rank)
@@ -171,9 +183,49 @@ class VerifyStep:
         self.stream = torch.cuda.Stream(self.dev)
         self.graphs = None
         self.ev = None
+        self.plan = self._build_plan() if weight_layout == "tiled" else None
+
+    def _build_plan(self) -> ProjectionPlan:
+        """The whole projection stack as one plan.  Requests go through the
+        plan in groups of two (32 rows per phase).  Each phase waits for the
+        previous phase of its group to complete, as it would in a forward
+        pass where attention and norms sit between the projections (q|k|v ->
+        o -> gate|up -> down -> next layer's q|k|v); down reads the
+        gate|up phase's SiLU output.  The qkv / o / gate|up inputs are the
+        synthetic x and attention rows (attention and norms are not on this
+        path)."""
+        sh = self.shape
+        rows = self.requests * sh.block
+        groups = [(g0, min(rows, g0 + 2 * sh.block)) for g0 in range(0, rows, 2 * sh.block)]
+        self.plan_out = []
+        for g0, g1 in groups:
+            m = g1 - g0
+            self.plan_out.append({
+                "qkv": torch.empty((m, sh.q_out + 2 * sh.kv_out), dtype=torch.bfloat16, device=self.dev),
+                "o": torch.empty((m, sh.hidden), dtype=torch.bfloat16, device=self.dev),
+                "h": torch.empty((m, sh.inter if self.fuse_silu else 2 * sh.inter),
+                                 dtype=torch.bfloat16, device=self.dev),
+                "down": torch.empty((m, sh.hidden), dtype=torch.bfloat16, device=self.dev)})
+        phases = []
+        group_last = [-1] * len(groups)
+        for lt in self.tiled:
+            for gi, ((g0, g1), out) in enumerate(zip(groups, self.plan_out)):
+                x, a = self.x[g0:g1], self.attn_out[g0:g1]
+                base = len(phases)
+                phases.append(PlanPhase(x, lt["qkv"], out["qkv"], dep=group_last[gi]))
+                phases.append(PlanPhase(a, lt["o"], out["o"], dep=base))
+                phases.append(PlanPhase(x, lt["gate_up"], out["h"], silu=self.fuse_silu, dep=base + 1))
+                phases.append(PlanPhase(out["h"], lt["down"], out["down"], dep=base + 2))
+                group_last[gi] = base + 3
+        self.last_qkv = self.plan_out[0]["qkv"]
+        self.last_down = self.plan_out[0]["down"]
+        return ProjectionPlan(phases)
 
     # -------------------------------------------------------------- parts
     def _qmm_stack(self):
+        if self.plan is not None:
+            self.plan.run()
+            return
         sh = self.shape
         # With several requests on this GPU their rows go through each launch
         # together: the qmm takes up to 32 rows per launch (two requests'

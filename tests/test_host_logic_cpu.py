@@ -655,3 +655,75 @@ def test_verify_step_host_path(pkg, monkeypatch, layout, fuse_silu, pack):
     keys_all = torch.zeros((1, 3 * shape.block), dtype=torch.int64)
     step._accept_and_rollback(keys_all, step.verify_ids)
     assert calls == ["dfl_lmhead_argmax", "dfl_lmhead_accept", "dfl_gdn_tape_replay"]
+
+
+def test_verify_step_plan_host_path(pkg, monkeypatch):
+    """Tiled layout on CPU, library replaced by a recorder: set-up repacks
+    every projection once into the tiled layout and encodes one plan whose
+    phases are the stack's projections per group of two requests, each
+    waiting for the previous phase of its group (q|k|v -> o -> gate|up + SiLU
+    -> down -> next layer's q|k|v); the qmm stack is one plan launch."""
+    import contextlib
+
+    from dflash_mlx_b200 import _lib, kernels, lm_head, qmm_plan, verify_step
+
+    calls, encoded = [], []
+
+    class Recorder:
+        def dfl_w4_tiled_bytes(self, n, k):
+            calls.append("dfl_w4_tiled_bytes")
+            return ((n + 127) // 128) * ((k + 511) // 512) * 36864
+
+        def dfl_qmm_plan_bytes(self, n):
+            return 256 + 192 * n
+
+        def dfl_qmm_plan_encode(self, arr, n, host, nbytes):
+            calls.append("dfl_qmm_plan_encode")
+            assert nbytes == 256 + 192 * n
+            encoded.extend((p.M, p.K, p.N, p.ldx, p.ldy, p.flags, p.dep) for p in arr[:n])
+            return 0
+
+        def dfl_qmm_plan_workspace_bytes(self, host, status):
+            return 64
+
+        def __getattr__(self, name):
+            def launch(*args):
+                calls.append(name)
+                return 0
+            return launch
+
+    monkeypatch.setattr(_lib, "load", lambda path=None: Recorder())
+    for mod in (qmm_plan, lm_head, kernels, pkg.moe, pkg.verify_qmm):
+        for attr, fake in (("require_cuda", lambda t, name: None), ("stream_ptr", lambda dev: 0),
+                           ("workspace", lambda dev, n: torch.zeros(16, dtype=torch.uint8))):
+            if hasattr(mod, attr):
+                monkeypatch.setattr(mod, attr, fake)
+    monkeypatch.setattr(lm_head, "workspace_bytes", lambda r, d, v: 16)
+    monkeypatch.setattr(torch.cuda, "Stream", lambda dev=None: None)
+    monkeypatch.setattr(torch.cuda, "device", lambda dev: contextlib.nullcontext())
+
+    shape = verify_step.StackShape(hidden=256, layers=2, q_out=256, kv_out=128, inter=512, vocab=1000,
+                                   gdn_layers=2, gdn_heads=2, gdn_dk=32, gdn_dv=32)
+    with pytest.raises(ValueError):
+        verify_step.VerifyStep("cpu", requests=1, shape=shape, weight_layout="tiled", fuse_silu=False)
+    calls.clear()
+    encoded.clear()
+    step = verify_step.VerifyStep("cpu", requests=3, shape=shape, weight_layout="tiled", fuse_silu=True)
+    assert calls.count("dfl_repack_w4_tiled") == 4 * shape.layers
+    assert calls.count("dfl_qmm_plan_encode") == 1
+    assert step.layers is None and len(step.tiled) == shape.layers
+    h, q_n, inter = shape.hidden, shape.q_out + 2 * shape.kv_out, shape.inter
+    want = []
+    last = {0: -1, 1: -1}
+    for _ in range(shape.layers):
+        for g, m in ((0, 32), (1, 16)):       # 3 requests: rows 0-31 and 32-47
+            base = len(want)
+            want += [(m, h, q_n, h, q_n, 2, last[g]),
+                     (m, shape.q_out, h, shape.q_out, h, 2, base),
+                     (m, h, 2 * inter, h, inter, 3, base + 1),
+                     (m, inter, h, inter, h, 2, base + 2)]
+            last[g] = base + 3
+    assert encoded == want
+    calls.clear()
+    step._qmm_stack()
+    assert calls == ["dfl_qmm_plan_run"]
