@@ -233,7 +233,11 @@ __device__ __forceinline__ void st_relaxed_u32(uint32_t* addr, uint32_t v) {
 }
 
 // Arrive at named barrier `id` of `count` threads without waiting for it.
+// Like every bar.* form here it is an aligned barrier (each warp must reach
+// it converged), so the calling warp is reconverged first: its lanes may
+// come from different iterations of their own bounded waits.
 __device__ __forceinline__ void named_bar_arrive(int id, int count) {
+  __syncwarp();
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
@@ -442,13 +446,16 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
       : "memory");
 }
 
-// Named barrier over a subset of warps.
+// Named barrier over a subset of whole warps (aligned: reconverge first).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
+  __syncwarp();
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Named barrier that also returns the AND of `pred` over all participants.
+// Named barrier that also returns the AND of `pred` over all participants
+// (whole warps; aligned: reconverge first).
 __device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t nthreads, bool pred) {
+  __syncwarp();
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"

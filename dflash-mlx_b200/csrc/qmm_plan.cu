@@ -39,13 +39,14 @@
 // epilogue + split-K reduction + phase signals.
 //
 // Split-K: a tile shared by CTAs c_lo..c_hi is the last of c_lo's range in
-// that phase and the first of the others'.  Contributors store fp32
-// partials with the lowest mantissa bit set as a validity tag into their
-// own slot (one per CTA and phase parity); c_lo's epilogue polls, sums them
-// in CTA order, clears them and releases the slot (consumption counter), so
-// results are bit-reproducible and a slot is never overwritten before it
-// was read.  Every wait is bounded; a time-out sets the device error word
-// and a plan-wide abort word, and every CTA winds down.
+// that phase and the first of the others'.  A contributor stores its fp32
+// partial in its own slot (one per CTA and phase parity) and publishes the
+// slot with a release store of the phase number; c_lo's epilogue acquires
+// that exact stamp, adds the partials to its accumulator in CTA order (so
+// results are bit-reproducible) and publishes that it has read them; a
+// contributor refills a slot only after its previous partial there was
+// read.  Every wait is bounded; a time-out sets the device error word and a
+// plan-wide abort word, and every CTA winds down.
 #include "common.cuh"
 #include "host_common.cuh"
 
@@ -62,9 +63,10 @@ constexpr int NDG = 4;                                 // dequant warp groups
 constexpr int WARP_TMA = 0;
 constexpr int WARP_MMA0 = 1;
 constexpr int WARP_DQ0 = WARP_MMA0 + NUM_MMA_WARPS;    // 5
-constexpr int WARP_EPI0 = WARP_DQ0 + 4 * NDG;          // 21
-constexpr int NUM_WARPS = WARP_EPI0 + 4;               // 25
-constexpr int NUM_THREADS = NUM_WARPS * 32;            // 800
+constexpr int WARP_EPI0 = WARP_DQ0 + 4 * NDG;          // 21: 4 epilogue warps
+constexpr int WARP_X = WARP_EPI0 + 4;                  // 25: x loads
+constexpr int NUM_WARPS = WARP_X + 1;                  // 26
+constexpr int NUM_THREADS = NUM_WARPS * 32;            // 832
 constexpr int TMEM_COLS = 512;
 constexpr int BAR_ID_EPI = 1;
 constexpr int PACK_BYTES = BN * UNIT_K / 2;            // 32768: nibbles of a unit
@@ -82,8 +84,14 @@ constexpr int kPhaseSubnormal = 2;                     // DFL_PHASE_SUBNORMAL
 constexpr size_t kCounterBytes = host::kWorkspaceCounterBytes;
 constexpr int kWordExit = kMaxPhases;                  // CTAs that finished the launch
 constexpr int kWordAbort = kMaxPhases + 1;             // plan-wide abort
-constexpr int kWordCons = kMaxPhases + 4;              // [kMaxGrid][2] slot consumption counts
-static_assert((kWordCons + 2 * kMaxGrid) * 4 <= int(kCounterBytes), "counter region");
+constexpr int kWordWhere = kMaxPhases + 2;             // first time-out: (role << 24) | phase
+constexpr int kWordWhereCta = kMaxPhases + 3;          // first time-out: CTA
+constexpr int kWordDiag = kMaxPhases + 4;              // [8] details of the first time-out
+// per CTA and phase parity: the phase (+1) whose partial the slot holds, and
+// the phase (+1) whose partial its consumer has read
+constexpr int kWordReady = kMaxPhases + 16;            // [kMaxGrid][2]
+constexpr int kWordConsumed = kWordReady + 2 * kMaxGrid;  // [kMaxGrid][2]
+static_assert((kWordConsumed + 2 * kMaxGrid) * 4 <= int(kCounterBytes), "counter region");
 static_assert(BLK_BYTES % 1024 == 0, "stage alignment");
 
 template <int MT>
@@ -94,10 +102,15 @@ struct Cfg {
   static constexpr int OFF_XRING = NSTAGE * BLK_BYTES;
   static constexpr int OFF_BARS = OFF_XRING + XS * XSLOT_BYTES;
   static constexpr int SMEM_BYTES = OFF_BARS + 512 + 1024;
-  static constexpr int NASLOT = (MT <= 16) ? 12 : 8;   // TMEM A slots (1.5 / 1 unit)
+  static constexpr int NASLOT = 8;                     // TMEM A slots (one unit)
   static constexpr int ACC_COL0 = NASLOT * A_COLS;
   static constexpr int ACC_COLS = NUM_MMA_WARPS * MT;  // one accumulator buffer
-  static_assert(ACC_COL0 + 2 * ACC_COLS <= TMEM_COLS, "TMEM budget");
+  // accumulator buffers: the MMAs may run this many tile segments ahead of
+  // the epilogue (segments are short: 2-10 units per CTA and phase)
+  static constexpr int NACCBUF = (MT <= 16) ? 4 : 2;
+  static_assert(ACC_COL0 + NACCBUF * ACC_COLS <= TMEM_COLS, "TMEM budget");
+  static constexpr int NUM_BARS = 2 * NSTAGE + 2 * NASLOT + 2 * XS + 2 * NACCBUF;
+  static_assert(NUM_BARS * 8 + 16 <= 512, "barrier area");
   static_assert(XBLK_BYTES % 1024 == 0, "x blocks keep the 1024-byte swizzle alignment");
   static_assert(NASLOT % NDG == 0 && NASLOT % NUM_MMA_WARPS == 0 && NASLOT >= NSUB, "A slots");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -199,6 +212,21 @@ __device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
   return d;
 }
 
+// A phase field read through the non-coherent path, issued where it is
+// written (volatile) so a role can fetch the next phase's fields one phase
+// ahead and never stall on them at a phase boundary.
+__device__ __forceinline__ int ld_field(const int* p) {
+  int v;
+  asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ const void* ld_field_ptr(const void* const* p) {
+  uint64_t v;
+  asm volatile("ld.global.nc.b64 %0, [%1];" : "=l"(v) : "l"(p));
+  return reinterpret_cast<const void*>(v);
+}
+
 // CTA c's share of a phase of `total` units on a grid of G CTAs:
 // [floor(c * total / G), floor((c + 1) * total / G)).
 __device__ __forceinline__ int unit_begin(int c, int total, int grid) {
@@ -210,11 +238,60 @@ __device__ __forceinline__ int owner_of(int u, int total, int grid) {
   return int(((long long)(u + 1) * grid + total - 1) / total) - 1;
 }
 
+// Where a wait gave up (recorded once per launch in the workspace, read by
+// tests and diagnostics; reset by the launch's last CTA): role code in the
+// high byte, phase below.
+enum WaitRole : int {
+  kWhereDep = 1, kWhereGuard = 2, kWherePartial = 3, kWhereProducer = 4, kWhereMma = 5,
+  kWhereDequant = 6, kWhereXFree = 7, kWhereAcc = 8,
+};
+
+__device__ __forceinline__ void record_timeout(int* words, int role, int phase, int d0 = 0,
+                                               int d1 = 0, int d2 = 0, int d3 = 0) {
+  atomicExch(&g_device_error, kDevWaitTimeout);
+  if (atomicCAS(words + kWordWhere, 0, (role << 24) | (phase & 0xFFFFFF)) == 0) {
+    atomicExch(words + kWordWhereCta, int(blockIdx.x));
+    atomicExch(words + kWordDiag + 0, d0);
+    atomicExch(words + kWordDiag + 1, d1);
+    atomicExch(words + kWordDiag + 2, d2);
+    atomicExch(words + kWordDiag + 3, d3);
+  }
+}
+
+// Bounded mbarrier wait of the plan kernel: gives up at once when this CTA
+// or the plan is aborting; on a time-out records where, and aborts both.
+__device__ __forceinline__ bool plan_wait(uint64_t* bar, uint32_t parity, volatile int* cta_abort,
+                                          volatile int* plan_abort, int* words, int role,
+                                          int phase) {
+  if (mbar_try_wait(bar, parity)) return true;
+  if (*cta_abort) return false;
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*cta_abort) return false;
+    if (*plan_abort) {
+      *cta_abort = 1;
+      return false;
+    }
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_timeout(words, role, phase);
+      *plan_abort = 1;
+      *cta_abort = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void st_release(int* addr, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
 // Spin until *addr >= target (acquire, gpu scope).  Gives up at once when
 // the CTA or plan-wide abort word is set, or after kWaitLimitNs (then sets
 // the device error word and both abort words).  Returns false on give-up.
 __device__ __forceinline__ bool wait_counter(const int* addr, int target, volatile int* cta_abort,
-                                             volatile int* plan_abort) {
+                                             volatile int* plan_abort, int* words, int role,
+                                             int phase) {
   if (ld_acquire(addr) >= target) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (;;) {
@@ -226,13 +303,17 @@ __device__ __forceinline__ bool wait_counter(const int* addr, int target, volati
       return false;
     }
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      atomicExch(&g_device_error, kDevWaitTimeout);
+      record_timeout(words, role, phase, target, ld_acquire(addr), int(addr - words));
       *plan_abort = 1;
       *cta_abort = 1;
       return false;
     }
   }
 }
+
+// Vote of the 128 epilogue threads (named_bar_and reconverges each warp
+// first: lanes may arrive from different iterations of their own waits).
+__device__ __forceinline__ bool epi_all(bool pred) { return named_bar_and(BAR_ID_EPI, 128, pred); }
 
 template <int MT>
 __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_constant__ RunParams rp) {
@@ -247,14 +328,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
   uint64_t* aempty = afull + C::NASLOT;        // [NASLOT] TMEM A slot read by the MMAs
   uint64_t* xfull = aempty + C::NASLOT;        // [XS] x slot landed (TMA)
   uint64_t* xfree = xfull + C::XS;             // [XS] x slot read by all MMA warps
-  uint64_t* accfull = xfree + C::XS;           // [2]
-  uint64_t* accempty = accfull + 2;            // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + 2);
+  uint64_t* accfull = xfree + C::XS;           // [NACCBUF]
+  uint64_t* accempty = accfull + C::NACCBUF;   // [NACCBUF]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + C::NACCBUF);
   volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
   volatile int* plan_abort = reinterpret_cast<volatile int*>(rp.words + kWordAbort);
-  auto wait = [abort_word](uint64_t* bar, uint32_t parity) {
-    return mbar_wait_abortable(bar, parity, abort_word);
+  int* const words = rp.words;
+  auto wait = [abort_word, plan_abort, words](uint64_t* bar, uint32_t parity, int role, int phase) {
+    return plan_wait(bar, parity, abort_word, plan_abort, words, role, phase);
   };
 
   const int warp = threadIdx.x >> 5;
@@ -278,7 +360,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
       mbar_init(&xfull[i], 1);
       mbar_init(&xfree[i], NUM_MMA_WARPS);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::NACCBUF; ++i) {
       mbar_init(&accfull[i], NUM_MMA_WARPS);
       mbar_init(&accempty[i], 4);
     }
@@ -300,17 +382,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       int it = 0;
-      bool ok = true;
-      for (int p = 0; ok && p < P; ++p) {
-        const int total = phases[p].total;
+      int n_total = ld_field(&phases[0].total);
+      const uint8_t* n_w = static_cast<const uint8_t*>(ld_field_ptr(reinterpret_cast<const void* const*>(&phases[0].w)));
+      for (int p = 0; p < P && !*abort_word; ++p) {
+        const int total = n_total;
+        const uint8_t* w = n_w;
+        if (p + 1 < P) {
+          n_total = ld_field(&phases[p + 1].total);
+          n_w = static_cast<const uint8_t*>(ld_field_ptr(reinterpret_cast<const void* const*>(&phases[p + 1].w)));
+        }
         const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
-        const uint8_t* src = phases[p].w + size_t(u0) * BLK_BYTES;
+        const uint8_t* src = w + size_t(u0) * BLK_BYTES;
         for (int u = u0; u < u1; ++u, ++it, src += BLK_BYTES) {
           const int s = it % NSTAGE;
-          if (!wait(&empty[s], ((it / NSTAGE) & 1) ^ 1)) {
-            ok = false;
-            break;
-          }
+          if (!wait(&empty[s], ((it / NSTAGE) & 1) ^ 1, kWhereProducer, p)) break;
           mbar_arrive_expect_tx(&full[s], BLK_BYTES);
           bulk_load_hint(smem_u32(smem + s * BLK_BYTES), src, BLK_BYTES, &full[s], pol);
         }
@@ -328,8 +413,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
     constexpr uint64_t kBlkDesc = uint64_t(C::XBLK_BYTES >> 4);
     int it = 0, acc_it = 0;
     uint32_t buf = 0;
+    int n_total = ld_field(&phases[0].total), n_ku = ld_field(&phases[0].ku);
     for (int p = 0; p < P; ++p) {
-      const int total = phases[p].total, ku = phases[p].ku;
+      const int total = n_total, ku = n_ku;
+      if (p + 1 < P) {
+        n_total = ld_field(&phases[p + 1].total);
+        n_ku = ld_field(&phases[p + 1].ku);
+      }
       const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
       int kb = u0 % ku;
       for (int u = u0; u < u1; ++u, ++it, kb = (kb + 1 == ku) ? 0 : kb + 1) {
@@ -337,10 +427,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
         const bool seg_end = (u == u1 - 1) || (kb == ku - 1);
         const int xs = it % C::XS;
         if (seg_start) {
-          buf = acc_it & 1;
-          wait(&accempty[buf], ((acc_it >> 1) & 1) ^ 1);
+          buf = acc_it % C::NACCBUF;
+          wait(&accempty[buf], ((acc_it / C::NACCBUF) & 1) ^ 1, kWhereMma, p);
         }
-        wait(&xfull[xs], (it / C::XS) & 1);
+        wait(&xfull[xs], (it / C::XS) & 1, kWhereMma, p);
         const uint32_t d_tmem = tmem_base + C::ACC_COL0 + buf * C::ACC_COLS + j * MT;
         const uint64_t slot_desc = ring_desc + kSlotDesc * xs;
         uint32_t acc0 = seg_start ? 0u : 1u;
@@ -349,7 +439,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
           const int sb = j + i * NUM_MMA_WARPS;
           const int g = it * NSUB + sb;
           const int slot = g % C::NASLOT;
-          wait(&afull[slot], (g / C::NASLOT) & 1);
+          wait(&afull[slot], (g / C::NASLOT) & 1, kWhereMma, p);
           tc_fence_after();
           if (!*abort_word) {
             const uint32_t a_tmem = tmem_base + slot * A_COLS;
@@ -377,13 +467,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
     const int r = quad * 32 + lane;        // output row within the tile
     const uint32_t lane_base = tmem_base + (uint32_t(quad * 32) << 16);
     int it = 0;
+    int n_total = ld_field(&phases[0].total), n_flags = ld_field(&phases[0].flags);
     for (int p = 0; p < P; ++p) {
-      const int total = phases[p].total;
-      const bool subn = (phases[p].flags & kPhaseSubnormal) != 0;
+      const int total = n_total;
+      const bool subn = (n_flags & kPhaseSubnormal) != 0;
+      if (p + 1 < P) {
+        n_total = ld_field(&phases[p + 1].total);
+        n_flags = ld_field(&phases[p + 1].flags);
+      }
       const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
       for (int u = u0; u < u1; ++u, ++it) {
         const int s = it % NSTAGE;
-        wait(&full[s], (it / NSTAGE) & 1);
+        wait(&full[s], (it / NSTAGE) & 1, kWhereDequant, p);
         const uint32_t st = smem_u32(smem + s * BLK_BYTES);
         // this thread's packed words (2 sub-blocks x 8 words) and its
         // scales / biases, then the stage goes back to the producer
@@ -402,7 +497,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
           const int g = it * NSUB + grp + 4 * jj;
           const int slot = g % C::NASLOT;
           slots[jj] = slot;
-          wait(&aempty[slot], ((g / C::NASLOT) & 1) ^ 1);
+          wait(&aempty[slot], ((g / C::NASLOT) & 1) ^ 1, kWhereDequant, p);
           tc_fence_after();
           const uint32_t s2 = __byte_perm(sbw.x, 0, jj ? 0x3232u : 0x1010u);
           const uint32_t b2 = __byte_perm(sbw.y, 0, jj ? 0x3232u : 0x1010u);
@@ -438,95 +533,85 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
         }
       }
     }
+  } else if (warp == WARP_X) {
+    // ------------------------------------------------------------ x loads
+    // x for every unit of this CTA, in order, into the XS-slot ring: waits
+    // only for the MMAs to free a slot and, for a phase with a dependency,
+    // for every CTA to have signalled that phase complete (this CTA's own
+    // epilogues of it need no x beyond what is already loaded, so the wait
+    // always ends).
+    if (lane == 0) {
+      int seq = 0;
+      bool ok = true;
+      for (int p = 0; ok && p < P; ++p) {
+        const Phase& ph = phases[p];
+        const int total = ld_field(&ph.total), ku = ld_field(&ph.ku), dep = ld_field(&ph.dep);
+        const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
+        if (u0 == u1) continue;
+        // the x tensor map was written into global memory by a host copy:
+        // order that write before the TMA unit's reads of the map
+        asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(
+                         reinterpret_cast<uint64_t>(&ph.tm_x))
+                     : "memory");
+        if (dep >= 0) {
+          if (!wait_counter(rp.words + dep, G, abort_word, plan_abort, words, kWhereDep, p)) break;
+          fence_proxy_async_global();   // x rows written by other CTAs' stores
+        }
+        for (int u = u0; u < u1; ++u, ++seq) {
+          const int xs = seq % C::XS;
+          if (seq >= C::XS && !wait(&xfree[xs], ((seq / C::XS) - 1) & 1, kWhereXFree, p)) {
+            ok = false;
+            break;
+          }
+          const int k0 = (u % ku) * UNIT_K;
+          uint8_t* dst = smem + C::OFF_XRING + xs * C::XSLOT_BYTES;
+          mbar_arrive_expect_tx(&xfull[xs], C::XSLOT_BYTES);
+#pragma unroll
+          for (int b = 0; b < NSUB; ++b)
+            tma_load_2d(dst + b * C::XBLK_BYTES, &ph.tm_x, &xfull[xs], k0 + b * GS, 0);
+        }
+      }
+    }
+    __syncwarp();
   } else {
-    // ------------------------------------ x loads + epilogue + phase signals
+    // ------------------------------------ epilogue + split-K + phase signals
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int et = threadIdx.x - WARP_EPI0 * 32;   // 0..127
     const uint32_t lane_base = tmem_base + (uint32_t(quad * 32) << 16);
-    constexpr int XD = C::XS - 1;
-    int* const cons = rp.words + kWordCons;
+    int* const ready = rp.words + kWordReady;
+    int* const consumed = rp.words + kWordConsumed;
 
-    // x staging cursor (thread et == 0 only): next unit to load, by phase.
-    int sp = 0, su = 0, su1 = 0, s_seq = 0;
-    bool s_dep_ok = true;
-    auto s_enter = [&](int p) {
-      const int total = phases[p].total;
-      su = unit_begin(cta, total, G);
-      su1 = unit_begin(cta + 1, total, G);
-      s_dep_ok = phases[p].dep < 0;
-      if (su < su1) {
-        // the x tensor map was written by a host copy into global memory:
-        // order that write before the tensor-map reads of the TMA unit
-        asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(
-                         reinterpret_cast<uint64_t>(&phases[p].tm_x))
-                     : "memory");
-      }
-    };
-    auto s_skip_empty = [&]() {
-      while (sp < P && su == su1) {
-        ++sp;
-        if (sp < P) s_enter(sp);
-      }
-    };
-    if (et == 0 && P > 0) {
-      s_enter(0);
-      s_skip_empty();
-    }
-    // Load x for the unit at the cursor.  A phase whose x depends on phase d
-    // is loaded only after every CTA signalled d complete, and only once this
-    // CTA's own epilogues of d are done (d < epi_phase); otherwise defer.
-    auto try_stage = [&](int epi_phase) -> bool {
-      const Phase& ph = phases[sp];
-      if (!s_dep_ok) {
-        const int d = ph.dep;
-        if (d >= epi_phase) return false;
-        if (!wait_counter(rp.words + d, G, abort_word, plan_abort)) return false;
-        fence_proxy_async_global();   // the x rows were written by other CTAs' stores
-        s_dep_ok = true;
-      }
-      const int xs = s_seq % C::XS;
-      if (s_seq >= C::XS) wait(&xfree[xs], ((s_seq / C::XS) - 1) & 1);
-      if (!*abort_word) {
-        const int k0 = (su % ph.ku) * UNIT_K;
-        uint8_t* dst = smem + C::OFF_XRING + xs * C::XSLOT_BYTES;
-        mbar_arrive_expect_tx(&xfull[xs], C::XSLOT_BYTES);
-#pragma unroll
-        for (int b = 0; b < NSUB; ++b)
-          tma_load_2d(dst + b * C::XBLK_BYTES, &ph.tm_x, &xfull[xs], k0 + b * GS, 0);
-      }
-      ++s_seq;
-      ++su;
-      s_skip_empty();
-      return true;
-    };
-
-    int seq = 0;           // sequence number of this CTA's first unit of phase p
     int acc_it = 0;
-    int wpar[2] = {0, 0};  // partials this CTA has stored per slot parity
+    int lastw[2] = {0, 0};  // phase + 1 of this CTA's last partial per slot parity
     bool ok = true;
+    int n_total = ld_field(&phases[0].total), n_ku = ld_field(&phases[0].ku);
     for (int p = 0; ok && p < P; ++p) {
       const Phase& ph = phases[p];
-      const int total = ph.total, ku = ph.ku, M = ph.M, N = ph.N, ldy = ph.ldy;
-      const bool silu = (ph.flags & kPhaseSilu) != 0;
-      uint16_t* const y = ph.y;
+      const int total = n_total, ku = n_ku;
+      if (p + 1 < P) {
+        n_total = ld_field(&phases[p + 1].total);
+        n_ku = ld_field(&phases[p + 1].ku);
+      }
       const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
       const int par = p & 1;
       if (u0 < u1) {
+        const int M = ph.M, N = ph.N, ldy = ph.ldy;
+        const bool silu = (ph.flags & kPhaseSilu) != 0;
+        uint16_t* const y = ph.y;
         const int t_first = u0 / ku, t_last = (u1 - 1) / ku;
         for (int t = t_first; t <= t_last; ++t) {
           const int kb0 = (t == t_first) ? (u0 - t * ku) : 0;
           const int kb1 = (t == t_last) ? (u1 - t * ku) : ku;
-          const int last_seq = seq + (t * ku + kb1 - 1 - u0);
-          // x through this segment's last unit (its MMAs need it) and XD beyond
-          if (et == 0) {
-            while (sp < P && s_seq <= last_seq + XD)
-              if (!try_stage(p)) break;
-          }
-          __syncwarp();
-          const uint32_t buf = acc_it & 1;
-          const bool got = wait(&accfull[buf], (acc_it >> 1) & 1);
-          if (!named_bar_and(BAR_ID_EPI, 128, got && !*abort_word)) {
+          const bool full_tile = (kb0 == 0 && kb1 == ku);
+          const int c_lo = full_tile ? cta : owner_of(t * ku, total, G);
+          // a contributor checks (before its accumulator is ready) that the
+          // consumer of its previous partial in this slot has read it
+          int cons_seen = 0x7fffffff;
+          if (cta != c_lo && et == 0 && lastw[par] > 0) cons_seen = ld_acquire(consumed + 2 * cta + par);
+          const uint32_t buf = acc_it % C::NACCBUF;
+          const bool got = wait(&accfull[buf], (acc_it / C::NACCBUF) & 1, kWhereAcc, p);
+          if (!epi_all(got && !*abort_word)) {
             ok = false;
             break;
           }
@@ -572,91 +657,68 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                 if (m < M) *yp = __bfloat16_as_ushort(__float2bfloat16_rn(v[m]));
             }
           };
-          if (kb0 == 0 && kb1 == ku) {
+          if (full_tile) {
             store_final(acc);
             continue;
           }
-          const int c_lo = owner_of(t * ku, total, G);
           if (cta != c_lo) {
-            // contributor: wait until this slot's previous partial was consumed
+            // contributor: its partial goes to its own slot once the slot's
+            // previous partial was read (almost always already true), then
+            // the slot is stamped with this phase
             bool gok = true;
-            if (et == 0) gok = wait_counter(cons + 2 * cta + par, wpar[par], abort_word, plan_abort);
-            if (!named_bar_and(BAR_ID_EPI, 128, gok && !*abort_word)) {
+            if (et == 0 && lastw[par] > 0 && cons_seen < lastw[par])
+              gok = wait_counter(consumed + 2 * cta + par, lastw[par], abort_word, plan_abort, words,
+                                 kWhereGuard, p);
+            if (!epi_all(gok && !*abort_word)) {
               ok = false;
               break;
             }
             uint32_t* mine = reinterpret_cast<uint32_t*>(rp.partials) + size_t(2 * cta + par) * MT * BN;
 #pragma unroll
-            for (int m = 0; m < MT; ++m) st_relaxed_u32(mine + m * BN + r, __float_as_uint(acc[m]) | 1u);
-            ++wpar[par];
-            continue;
-          }
-          // c_lo: add the contributors' partials to this CTA's accumulator in
-          // CTA order (8 rows at a time), clearing and releasing each slot
-          const int c_hi = owner_of(t * ku + ku - 1, total, G);
-          for (int c = c_lo + 1; ok && c <= c_hi; ++c) {
-            if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
-            uint32_t* slot = reinterpret_cast<uint32_t*>(rp.partials) + size_t(2 * c + par) * MT * BN;
-            bool pok = true;
-#pragma unroll
-            for (int m0 = 0; m0 < MT; m0 += 8) {
-              uint32_t v[8];
-#pragma unroll
-              for (int m = 0; m < 8; ++m) v[m] = ld_relaxed_u32(slot + (m0 + m) * BN + r);
-              const unsigned long long t0 = globaltimer_ns();
-              while (pok) {
-                bool all = true;
-#pragma unroll
-                for (int m = 0; m < 8; ++m)
-                  if (!(v[m] & 1u)) {
-                    all = false;
-                    v[m] = ld_relaxed_u32(slot + (m0 + m) * BN + r);
-                  }
-                if (all) break;
-                if (*abort_word) {
-                  pok = false;
-                } else if (*plan_abort) {
-                  *abort_word = 1;
-                  pok = false;
-                } else if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                  atomicExch(&g_device_error, kDevWaitTimeout);
-                  *plan_abort = 1;
-                  *abort_word = 1;
-                  pok = false;
-                }
-              }
-              if (pok) {
-#pragma unroll
-                for (int m = 0; m < 8; ++m) {
-                  acc[m0 + m] += __uint_as_float(v[m]);
-                  st_relaxed_u32(slot + (m0 + m) * BN + r, 0u);
-                }
-              }
-            }
-            if (!named_bar_and(BAR_ID_EPI, 128, pok && !*abort_word)) {
+            for (int m = 0; m < MT; ++m) st_relaxed_u32(mine + m * BN + r, __float_as_uint(acc[m]));
+            // the barrier orders every thread's partial stores before the
+            // stamp's release (cumulativity)
+            if (!epi_all(!*abort_word)) {
               ok = false;
               break;
             }
-            if (et == 0) {
-              __threadfence();
-              red_release_add(cons + 2 * c + par, 1);
+            if (et == 0) st_release(ready + 2 * cta + par, p + 1);
+            lastw[par] = p + 1;
+            continue;
+          }
+          // c_lo: add the contributors' partials to this CTA's accumulator in
+          // CTA order once each slot carries this phase's stamp, then mark
+          // the slot read
+          const int c_hi = owner_of(t * ku + ku - 1, total, G);
+          for (int c = c_lo + 1; ok && c <= c_hi; ++c) {
+            if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
+            const bool pok = wait_counter(ready + 2 * c + par, p + 1, abort_word, plan_abort, words,
+                                          kWherePartial, p);
+            if (pok) {
+              const uint32_t* slot =
+                  reinterpret_cast<const uint32_t*>(rp.partials) + size_t(2 * c + par) * MT * BN;
+#pragma unroll
+              for (int m = 0; m < MT; ++m) acc[m] += __uint_as_float(ld_relaxed_u32(slot + m * BN + r));
             }
+            // every thread has read the slot: its contributor may refill it
+            if (!epi_all(pok && !*abort_word)) {
+              ok = false;
+              break;
+            }
+            if (et == 0) st_release(consumed + 2 * c + par, p + 1);
           }
           if (!ok) break;
           store_final(acc);
         }
       }
       if (!ok) break;
-      // every final value of phase p this CTA owes is stored: signal it
-      if (!named_bar_and(BAR_ID_EPI, 128, !*abort_word)) {
+      // every final value of phase p this CTA owes is stored: signal it (the
+      // barrier orders all 128 threads' stores before the release)
+      if (!epi_all(!*abort_word)) {
         ok = false;
         break;
       }
-      if (et == 0) {
-        __threadfence();
-        red_release_add(rp.words + p, 1);
-      }
-      seq += u1 - u0;
+      if (et == 0) red_release_add(rp.words + p, 1);
     }
   }
 
@@ -674,11 +736,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
   if (*last_flag) {
     __threadfence();
     for (int i = threadIdx.x; i < P; i += NUM_THREADS) rp.words[i] = 0;
-    for (int i = threadIdx.x; i < 2 * kMaxGrid; i += NUM_THREADS) rp.words[kWordCons + i] = 0;
+    for (int i = threadIdx.x; i < 4 * kMaxGrid; i += NUM_THREADS) rp.words[kWordReady + i] = 0;
     if (threadIdx.x == 0) {
       rp.words[kWordAbort] = 0;
       rp.words[kWordExit] = 0;
     }
+    // kWordWhere / kWordWhereCta stay set after a time-out for the host to
+    // read (dfl_qmm_plan_last_timeout); the host clears them with the rest of
+    // the workspace after a device error
   }
 }
 

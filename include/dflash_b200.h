@@ -202,8 +202,10 @@ int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q, const u
  * run.  The x / y / weight pointers are baked in: re-encode when they
  * change.  dfl_qmm_plan_run launches the plan (one cooperative launch of
  * one CTA per SM) with a workspace of dfl_qmm_plan_workspace_bytes bytes,
- * zero before the first run; every run leaves it zero.  After a run that
- * reported a device error (dfl_get_device_error) zero it again.  One
+ * zero before the first run; every run leaves its first 64 KB (counters and
+ * phase stamps) zero again, and the split-K area after it may keep data
+ * that no later run reads before stamping it.  After a run that reported a
+ * device error (dfl_get_device_error) zero the workspace again.  One
  * workspace must not be shared by runs that may overlap.  No counterpart in
  * the reference (it launches one Metal kernel per projection through
  * VerifyQuantizedLinear, dflash_mlx/verify_linear.py:266-286); it replaces

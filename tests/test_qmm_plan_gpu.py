@@ -12,7 +12,7 @@
   plans bit for bit, and the oracle within tolerance;
 * a chain where each phase reads the previous phase's output;
 * repeated runs and CUDA-graph replays give identical bits and leave the
-  workspace zero.
+  workspace's counters zero.
 """
 
 from __future__ import annotations
@@ -28,6 +28,7 @@ pytestmark = pytest.mark.gpu
 
 ATOL = 1e-2
 RTOL = 2e-2
+COUNTER_BYTES = 64 * 1024   # a plan workspace's counter region (zero between runs)
 
 
 def _assert_close(y_bits, ref_bits, what=""):
@@ -186,7 +187,7 @@ def test_layer_plan_equals_separate_plans_and_oracle(pkg, dev):
     _assert_close(bf16_to_np_bits(got["o"]), oqmm.qmm(ab, *ws["o"], accum=np.float32), "o")
     _assert_close(bf16_to_np_bits(got["down"]),
                   oqmm.qmm(bf16_to_np_bits(got["h"]), *ws["down"], accum=np.float32), "down")
-    assert int(plan.workspace.count_nonzero()) == 0
+    assert int(plan.workspace[:COUNTER_BYTES].count_nonzero()) == 0
     from dflash_mlx_b200 import _lib
     assert _lib.device_error() == 0
 
@@ -218,7 +219,7 @@ def test_chain_reads_previous_outputs(pkg, dev):
         for i, (w_q, s, b) in enumerate(raw):
             _assert_close(bf16_to_np_bits(outs[i]), oqmm.qmm(xb, w_q, s, b, accum=np.float32), f"link {i}")
             xb = bf16_to_np_bits(outs[i])
-        assert int(plan.workspace.count_nonzero()) == 0
+        assert int(plan.workspace[:COUNTER_BYTES].count_nonzero()) == 0
 
 
 def test_plan_repeats_and_replays_in_a_cuda_graph(pkg, dev):
@@ -245,7 +246,7 @@ def test_plan_repeats_and_replays_in_a_cuda_graph(pkg, dev):
     torch.cuda.synchronize(dev)
     for k in bufs:
         assert torch.equal(bufs[k], first[k]), k
-    assert int(plan.workspace.count_nonzero()) == 0
+    assert int(plan.workspace[:COUNTER_BYTES].count_nonzero()) == 0
     del g
     from dflash_mlx_b200 import _lib
     assert _lib.device_error() == 0
