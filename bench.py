@@ -293,7 +293,8 @@ def run_ours(args):
     shape = StackShape(layers=args.layers)
     step = VerifyStep(dev, requests=args.requests_per_gpu, shape=shape, rank=rank, world=world,
                       group=group, weight_layout=args.weight_layout,
-                      fuse_silu=args.weight_layout != "mlx" and not args.no_fuse_silu)
+                      fuse_silu=args.weight_layout != "mlx" and not args.no_fuse_silu,
+                      qmm_deps=args.qmm_deps)
     sh = step.shape
     b = args.requests_per_gpu
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -366,6 +367,28 @@ def run_ours(args):
     d2h = int(out.numel()) * 4
 
     mean_acc = float(step.acceptance.float().mean())
+    # the stack with every projection chained to the one before it, timed
+    # outside the loop above (same weights, one plan launch per run)
+    t_chain = None
+    if step.plan is not None and args.qmm_deps != "chain" and not args.no_extra_configs:
+        headline_plan = step.plan
+        chained = step._build_plan("chain")
+        with torch.cuda.device(dev), torch.cuda.stream(step.stream):
+            for _ in range(3):
+                chained.run()
+            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0.record(step.stream)
+            for _ in range(args.steps):
+                chained.run()
+            c1.record(step.stream)
+        torch.cuda.synchronize(dev)
+        t_chain = c0.elapsed_time(c1) / args.steps
+        tc = torch.tensor([t_chain], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(tc, op=dist.ReduceOp.MAX)
+        t_chain = float(tc[0])
+        step.plan = headline_plan
+        del chained
     # roofline of the dominant kernel (the int4 verify qmm)
     peak, peak_kind = _peaks()
     plan = step.plan is not None
@@ -398,10 +421,16 @@ def run_ours(args):
                 "requests_per_gpu": b, "tokens_per_request": sh.block,
                 "weight_layout": args.weight_layout,
                 "requests_share_launches": step.pack_requests,
-                "qmm_launch": ("one plan launch per step; each projection waits on the device for "
-                               "the previous one (q|k|v -> o -> gate|up -> down -> next layer)"
-                               if plan else "one launch per projection (programmatic dependent "
-                               "launch)"),
+                "qmm_launch": (("one plan launch per step; each projection waits on the device "
+                                "for the projections whose outputs it reads (down for gate|up's "
+                                "SiLU output, the next layer's q|k|v for this layer's down); o "
+                                "and gate|up read stand-ins for the attention output and the "
+                                "normalised residual (ops outside this path)")
+                               if plan and args.qmm_deps == "dataflow" else
+                               "one plan launch per step; every projection waits for the one "
+                               "before it" if plan else
+                               "one launch per projection (programmatic dependent launch)"),
+                "qmm_ms_per_step_chained": t_chain,
                 "mlp_silu_fused": step.fuse_silu,
                 "parallelism": f"request-DP x{world}, lm_head vocab split x{world}",
                 "l2": "inputs larger than L2 (12.4 GB of packed weights per step)",
@@ -736,6 +765,10 @@ def main():
                     help="int4 layout of the stack's weights: the reference's MLX packing or the "
                          "pair-packed order (one qmm launch per projection), or the tiled layout "
                          "(the whole stack as one projection plan: one persistent launch per step)")
+    ap.add_argument("--qmm-deps", choices=["dataflow", "chain"], default="dataflow",
+                    help="tiled layout: dataflow = each projection waits only for the projections "
+                         "whose outputs it reads; chain = every projection also waits for the one "
+                         "before it")
     ap.add_argument("--no-fuse-silu", action="store_true",
                     help="run SiLU*up as its own launch after the gate|up projection")
     ap.add_argument("--no-cpu-baseline", action="store_true")

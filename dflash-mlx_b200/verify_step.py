@@ -109,7 +109,8 @@ class VerifyStep:
 
     def __init__(self, device: torch.device, *, requests: int = 1, shape: Optional[StackShape] = None,
                  rank: int = 0, world: int = 1, group=None, seed: int = 0,
-                 weight_layout: str = "mlx", fuse_silu: bool = False, pack_requests: bool = True):
+                 weight_layout: str = "mlx", fuse_silu: bool = False, pack_requests: bool = True,
+                 qmm_deps: str = "dataflow"):
         self.dev = torch.device(device)
         if weight_layout not in ("mlx", "pairs", "tiled"):
             raise ValueError(f"unknown weight layout {weight_layout!r}")
@@ -183,42 +184,56 @@ class VerifyStep:
         self.stream = torch.cuda.Stream(self.dev)
         self.graphs = None
         self.ev = None
-        self.plan = self._build_plan() if weight_layout == "tiled" else None
+        self.qmm_deps = qmm_deps
+        self.plan = self._build_plan(qmm_deps) if weight_layout == "tiled" else None
 
-    def _build_plan(self) -> ProjectionPlan:
-        """The whole projection stack as one plan.  Requests go through the
-        plan in groups of two (32 rows per phase).  Each phase waits for the
-        previous phase of its group to complete, as it would in a forward
-        pass where attention and norms sit between the projections (q|k|v ->
-        o -> gate|up -> down -> next layer's q|k|v); down reads the
-        gate|up phase's SiLU output.  The qkv / o / gate|up inputs are the
-        synthetic x and attention rows (attention and norms are not on this
-        path)."""
+    def _build_plan(self, deps: str = "dataflow") -> ProjectionPlan:
+        """The whole projection stack as one plan, requests in groups of two
+        (32 rows per phase).  Every layer writes its own output buffers.
+
+        ``deps="dataflow"``: a projection waits on the device for exactly the
+        projections whose outputs it reads -- down for gate|up's SiLU output,
+        and the next layer's q|k|v for this layer's down output (its input).
+        o and gate|up read fixed stand-ins for the attention output and the
+        normalised residual, which ops outside this path produce.
+        ``deps="chain"``: every projection also waits for the one before it
+        (q|k|v -> o -> gate|up -> down -> next q|k|v), as when attention and
+        norms run between them in the same launch order."""
+        if deps not in ("dataflow", "chain"):
+            raise ValueError(f"unknown dependency mode {deps!r}")
         sh = self.shape
         rows = self.requests * sh.block
         groups = [(g0, min(rows, g0 + 2 * sh.block)) for g0 in range(0, rows, 2 * sh.block)]
-        self.plan_out = []
-        for g0, g1 in groups:
-            m = g1 - g0
-            self.plan_out.append({
-                "qkv": torch.empty((m, sh.q_out + 2 * sh.kv_out), dtype=torch.bfloat16, device=self.dev),
-                "o": torch.empty((m, sh.hidden), dtype=torch.bfloat16, device=self.dev),
-                "h": torch.empty((m, sh.inter if self.fuse_silu else 2 * sh.inter),
-                                 dtype=torch.bfloat16, device=self.dev),
-                "down": torch.empty((m, sh.hidden), dtype=torch.bfloat16, device=self.dev)})
+
+        def buf(m, n):
+            return torch.empty((m, n), dtype=torch.bfloat16, device=self.dev)
+
+        outs = []
         phases = []
-        group_last = [-1] * len(groups)
+        last_down = [None] * len(groups)      # (phase index, tensor) of each group's last down
         for lt in self.tiled:
-            for gi, ((g0, g1), out) in enumerate(zip(groups, self.plan_out)):
-                x, a = self.x[g0:g1], self.attn_out[g0:g1]
+            layer_out = []
+            for gi, (g0, g1) in enumerate(groups):
+                m = g1 - g0
+                out = {"qkv": buf(m, sh.q_out + 2 * sh.kv_out), "o": buf(m, sh.hidden),
+                       "h": buf(m, sh.inter), "down": buf(m, sh.hidden)}
+                layer_out.append(out)
+                prev = last_down[gi]
+                x_in = self.x[g0:g1] if prev is None else prev[1]
+                a = self.attn_out[g0:g1]
                 base = len(phases)
-                phases.append(PlanPhase(x, lt["qkv"], out["qkv"], dep=group_last[gi]))
-                phases.append(PlanPhase(a, lt["o"], out["o"], dep=base))
-                phases.append(PlanPhase(x, lt["gate_up"], out["h"], silu=self.fuse_silu, dep=base + 1))
+                chain = deps == "chain"
+                dep_qkv = -1 if prev is None else prev[0]
+                phases.append(PlanPhase(x_in, lt["qkv"], out["qkv"], dep=dep_qkv))
+                phases.append(PlanPhase(a, lt["o"], out["o"], dep=base if chain else -1))
+                phases.append(PlanPhase(self.x[g0:g1], lt["gate_up"], out["h"], silu=True,
+                                        dep=base + 1 if chain else -1))
                 phases.append(PlanPhase(out["h"], lt["down"], out["down"], dep=base + 2))
-                group_last[gi] = base + 3
-        self.last_qkv = self.plan_out[0]["qkv"]
-        self.last_down = self.plan_out[0]["down"]
+                last_down[gi] = (base + 3, out["down"])
+            outs.append(layer_out)
+        self.plan_out = outs
+        self.last_qkv = outs[-1][0]["qkv"]
+        self.last_down = outs[-1][0]["down"]
         return ProjectionPlan(phases)
 
     # -------------------------------------------------------------- parts

@@ -718,12 +718,18 @@ def test_verify_step_plan_host_path(pkg, monkeypatch):
     for _ in range(shape.layers):
         for g, m in ((0, 32), (1, 16)):       # 3 requests: rows 0-31 and 32-47
             base = len(want)
+            # dataflow: q|k|v waits for the group's previous down (its input),
+            # down for gate|up's SiLU output; o and gate|up read stand-ins
             want += [(m, h, q_n, h, q_n, 2, last[g]),
-                     (m, shape.q_out, h, shape.q_out, h, 2, base),
-                     (m, h, 2 * inter, h, inter, 3, base + 1),
+                     (m, shape.q_out, h, shape.q_out, h, 2, -1),
+                     (m, h, 2 * inter, h, inter, 3, -1),
                      (m, inter, h, inter, h, 2, base + 2)]
             last[g] = base + 3
     assert encoded == want
+    # the chained form: every phase also waits for the one before it
+    encoded.clear()
+    step._build_plan("chain")
+    assert [e[-1] for e in encoded] == [w[-1] if i % 4 == 0 else i - 1 for i, w in enumerate(want)]
     calls.clear()
     step._qmm_stack()
     assert calls == ["dfl_qmm_plan_run"]
