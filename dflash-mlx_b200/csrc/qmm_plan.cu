@@ -73,7 +73,6 @@ constexpr int PACK_BYTES = BN * UNIT_K / 2;            // 32768: nibbles of a un
 constexpr int SB_BYTES = NDG * BN * 8;                 // 4096: scales + biases of a unit
 constexpr int BLK_BYTES = PACK_BYTES + SB_BYTES;       // 36864
 constexpr int NSTAGE = 4;
-constexpr int kPrefetchUnits = 12;
 constexpr int kMaxGrid = 160;
 constexpr int kMaxPhases = 7936;
 constexpr uint32_t kPlanMagic = 0x504C4644u;           // "DFLP"
@@ -131,15 +130,14 @@ static_assert(sizeof(Phase) == 192, "phase record size");
 
 struct Header {
   uint32_t magic;
-  int version, n_phases, mt, grid, flags_or, prefetch_units;
-  int pad[57];
+  int version, n_phases, mt, grid, flags_or;
+  int pad[58];
 };
 static_assert(sizeof(Header) == kHeaderBytes, "plan header size");
 
 struct RunParams {
   const Phase* phases;
   int n_phases;
-  int prefetch_units;   // weight blocks the producer prefetches into L2 ahead of the ring
   int* words;           // workspace counter words
   float* partials;      // workspace [grid][2][MT][BN]
 };
@@ -158,11 +156,6 @@ __device__ __forceinline__ void bulk_load_hint(uint32_t dst_smem, const void* sr
       " [%0], [%1], %2, [%3], %4;" ::"r"(dst_smem),
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
-}
-
-// Bulk prefetch of global memory into L2 (no shared-memory destination).
-__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ uint2 ld_shared_v2(uint32_t addr) {
@@ -385,30 +378,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
   if (warp == WARP_TMA) {
     // ------------------------------------------------------------ producer
     // One bulk copy per unit into the NSTAGE ring; waits only for the
-    // dequant warps to release a stage, never for another CTA.  A second
-    // cursor runs prefetch_units blocks ahead and prefetches them into L2,
-    // so HBM keeps streaming while the ring is full (a phase boundary whose
-    // dependency holds the MMAs back lasts longer than the ring covers).
+    // dequant warps to release a stage, never for another CTA.  (Prefetching
+    // blocks further ahead into L2 was measured to gain nothing.)
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
-      int pf_p = 0, pf_u = 0, pf_u1 = 0;
-      const uint8_t* pf_w = nullptr;
-      auto pf_enter = [&](int q) {
-        const int tq = ld_field(&phases[q].total);
-        pf_u = unit_begin(cta, tq, G);
-        pf_u1 = unit_begin(cta + 1, tq, G);
-        pf_w = static_cast<const uint8_t*>(ld_field_ptr(reinterpret_cast<const void* const*>(&phases[q].w)));
-      };
-      auto pf_next = [&]() {
-        while (pf_p < P && pf_u == pf_u1) {
-          if (++pf_p < P) pf_enter(pf_p);
-        }
-        if (pf_p >= P) return;
-        prefetch_l2(pf_w + size_t(pf_u) * BLK_BYTES, BLK_BYTES);
-        ++pf_u;
-      };
-      pf_enter(0);
-      for (int i = 0; i < rp.prefetch_units; ++i) pf_next();
       int it = 0;
       int n_total = ld_field(&phases[0].total);
       const uint8_t* n_w = static_cast<const uint8_t*>(ld_field_ptr(reinterpret_cast<const void* const*>(&phases[0].w)));
@@ -426,7 +399,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
           if (!wait(&empty[s], ((it / NSTAGE) & 1) ^ 1, kWhereProducer, p)) break;
           mbar_arrive_expect_tx(&full[s], BLK_BYTES);
           bulk_load_hint(smem_u32(smem + s * BLK_BYTES), src, BLK_BYTES, &full[s], pol);
-          if (rp.prefetch_units > 0) pf_next();
         }
       }
     }
@@ -882,7 +854,6 @@ int launch(const Header& h, const void* plan_dev, void* ws, int dev, cudaStream_
   RunParams rp;
   rp.phases = reinterpret_cast<const Phase*>(static_cast<const uint8_t*>(plan_dev) + kHeaderBytes);
   rp.n_phases = h.n_phases;
-  rp.prefetch_units = h.prefetch_units;
   rp.words = static_cast<int*>(ws);
   rp.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
   // CTAs wait on one another (phase counters, split-K partials): launched
@@ -990,13 +961,6 @@ extern "C" int dfl_qmm_plan_encode(const dfl_qmm_phase* phases, int n_phases, vo
   h.mt = mt;
   h.grid = sms < kMaxGrid ? sms : kMaxGrid;
   h.flags_or = flags_or;
-  // L2 prefetch distance in weight blocks per CTA (12 x 36 KB x 148 SMs =
-  // 64 MB, half the L2); DFL_QMM_PLAN_PREFETCH_UNITS overrides it (0..64)
-  h.prefetch_units = kPrefetchUnits;
-  if (const char* env = std::getenv("DFL_QMM_PLAN_PREFETCH_UNITS")) {
-    const int v = std::atoi(env);
-    if (v >= 0 && v <= 64) h.prefetch_units = v;
-  }
   std::memcpy(out, &h, sizeof(h));
   for (int p = 0; p < n_phases; ++p) {
     const dfl_qmm_phase& q = phases[p];
