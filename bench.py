@@ -282,13 +282,10 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     group = None
+    from dflash_mlx_b200.verify_step import StackShape, init_process_group
+
     if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-        group = dist.group.WORLD
-
-    from dflash_mlx_b200.verify_step import StackShape
+        group = init_process_group("nccl", timeout_s=120, device=dev)
 
     shape = StackShape(layers=args.layers)
     step = VerifyStep(dev, requests=args.requests_per_gpu, shape=shape, rank=rank, world=world,

@@ -81,6 +81,9 @@ SIGNATURES = {
     "dfl_qmm_plan_encode": (_c_int, [_vp, _c_int, _vp, _c_size]),
     "dfl_qmm_plan_workspace_bytes": (_c_size, [_vp, ctypes.POINTER(_c_int)]),
     "dfl_qmm_plan_run": (_c_int, [_vp, _vp, _vp, _c_size, _vp]),
+    "dfl_qmm_plan_set_test_fault": (_c_int, [_vp, _c_int, ctypes.c_uint64]),
+    "dfl_qmm_plan_last_timeout": (_c_int, [_vp, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int),
+                                           ctypes.POINTER(_c_int)]),
 }
 
 _lock = threading.Lock()

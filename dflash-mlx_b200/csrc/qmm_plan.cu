@@ -109,7 +109,7 @@ struct Cfg {
   // the epilogue (segments are short: 2-10 units per CTA and phase)
   static constexpr int NACCBUF = (MT <= 16) ? 4 : 2;
   static_assert(ACC_COL0 + NACCBUF * ACC_COLS <= TMEM_COLS, "TMEM budget");
-  static constexpr int NUM_BARS = 2 * NSTAGE + 2 * NASLOT + 2 * XS + 2 * NACCBUF;
+  static constexpr int NUM_BARS = 2 * NSTAGE + 2 * NASLOT + 2 * XS + 2 * NACCBUF + NUM_MMA_WARPS;
   static_assert(NUM_BARS * 8 + 16 <= 512, "barrier area");
   static_assert(XBLK_BYTES % 1024 == 0, "x blocks keep the 1024-byte swizzle alignment");
   static_assert(NASLOT % NDG == 0 && NASLOT % NUM_MMA_WARPS == 0 && NASLOT >= NSUB, "A slots");
@@ -131,13 +131,20 @@ static_assert(sizeof(Phase) == 192, "phase record size");
 struct Header {
   uint32_t magic;
   int version, n_phases, mt, grid, flags_or;
-  int pad[58];
+  // fault injection for tests (dfl_qmm_plan_set_test_fault): a CTA that
+  // withholds its split-K partials, and the bound on every wait
+  int test_skip_partial_cta;
+  int pad0;
+  unsigned long long wait_limit_ns;
+  int pad[54];
 };
 static_assert(sizeof(Header) == kHeaderBytes, "plan header size");
 
 struct RunParams {
   const Phase* phases;
   int n_phases;
+  int skip_partial_cta;        // -1 normally
+  unsigned long long wait_limit_ns;
   int* words;           // workspace counter words
   float* partials;      // workspace [grid][2][MT][BN]
 };
@@ -262,7 +269,7 @@ __device__ __forceinline__ void record_timeout(int* words, int role, int phase, 
 // or the plan is aborting; on a time-out records where, and aborts both.
 __device__ __forceinline__ bool plan_wait(uint64_t* bar, uint32_t parity, volatile int* cta_abort,
                                           volatile int* plan_abort, int* words, int role,
-                                          int phase) {
+                                          int phase, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   if (*cta_abort) return false;
   const unsigned long long t0 = globaltimer_ns();
@@ -273,7 +280,7 @@ __device__ __forceinline__ bool plan_wait(uint64_t* bar, uint32_t parity, volati
       *cta_abort = 1;
       return false;
     }
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       record_timeout(words, role, phase);
       *plan_abort = 1;
       *cta_abort = 1;
@@ -287,11 +294,11 @@ __device__ __forceinline__ void st_release(int* addr, int v) {
 }
 
 // Spin until *addr >= target (acquire, gpu scope).  Gives up at once when
-// the CTA or plan-wide abort word is set, or after kWaitLimitNs (then sets
+// the CTA or plan-wide abort word is set, or after limit_ns (then sets
 // the device error word and both abort words).  Returns false on give-up.
 __device__ __forceinline__ bool wait_counter(const int* addr, int target, volatile int* cta_abort,
                                              volatile int* plan_abort, int* words, int role,
-                                             int phase) {
+                                             int phase, unsigned long long limit_ns) {
   if (ld_acquire(addr) >= target) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (;;) {
@@ -302,7 +309,7 @@ __device__ __forceinline__ bool wait_counter(const int* addr, int target, volati
       *cta_abort = 1;
       return false;
     }
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       record_timeout(words, role, phase, target, ld_acquire(addr), int(addr - words));
       *plan_abort = 1;
       *cta_abort = 1;
@@ -330,13 +337,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
   uint64_t* xfree = xfull + C::XS;             // [XS] x slot read by all MMA warps
   uint64_t* accfull = xfree + C::XS;           // [NACCBUF]
   uint64_t* accempty = accfull + C::NACCBUF;   // [NACCBUF]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accempty + C::NACCBUF);
+  uint64_t* drained = accempty + C::NACCBUF;   // [NUM_MMA_WARPS] an MMA warp's last ops done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + NUM_MMA_WARPS);
   volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
   volatile int* plan_abort = reinterpret_cast<volatile int*>(rp.words + kWordAbort);
   int* const words = rp.words;
-  auto wait = [abort_word, plan_abort, words](uint64_t* bar, uint32_t parity, int role, int phase) {
-    return plan_wait(bar, parity, abort_word, plan_abort, words, role, phase);
+  const unsigned long long limit_ns = rp.wait_limit_ns;
+  auto wait = [abort_word, plan_abort, words, limit_ns](uint64_t* bar, uint32_t parity, int role,
+                                                        int phase) {
+    return plan_wait(bar, parity, abort_word, plan_abort, words, role, phase, limit_ns);
   };
 
   const int warp = threadIdx.x >> 5;
@@ -364,6 +374,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
       mbar_init(&accfull[i], NUM_MMA_WARPS);
       mbar_init(&accempty[i], 4);
     }
+    for (int i = 0; i < NUM_MMA_WARPS; ++i) mbar_init(&drained[i], 1);
     fence_barrier_init();
   }
   if (warp == WARP_TMA) {
@@ -460,6 +471,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
         }
       }
     }
+    // TMEM is freed only after this warp's MMAs completed.  On the normal
+    // path the epilogue already waited for them; after an abort some may
+    // still run, so wait (bounded, whatever the abort words say).
+    tc_commit_warp(&drained[j]);
+    mbar_wait(&drained[j], 0);
   } else if (warp < WARP_EPI0) {
     // ------------------------------------------------------------ dequant
     const int dw = warp - WARP_DQ0;
@@ -555,7 +571,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                          reinterpret_cast<uint64_t>(&ph.tm_x))
                      : "memory");
         if (dep >= 0) {
-          if (!wait_counter(rp.words + dep, G, abort_word, plan_abort, words, kWhereDep, p)) break;
+          if (!wait_counter(rp.words + dep, G, abort_word, plan_abort, words, kWhereDep, p, limit_ns)) break;
           fence_proxy_async_global();   // x rows written by other CTAs' stores
         }
         for (int u = u0; u < u1; ++u, ++seq) {
@@ -622,7 +638,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             for (int c = c_lo + 1; ok && c <= c_hi; ++c) {
               if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
               const bool pok = wait_counter(ready + 2 * c + par, p + 1, abort_word, plan_abort, words,
-                                            kWherePartial, p);
+                                            kWherePartial, p, limit_ns);
               if (pok) {
                 const uint32_t* slot =
                     reinterpret_cast<const uint32_t*>(rp.partials) + size_t(2 * c + par) * MT * BN;
@@ -697,7 +713,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             bool gok = true;
             if (et == 0 && lastw[par] > 0 && cons_seen < lastw[par])
               gok = wait_counter(consumed + 2 * cta + par, lastw[par], abort_word, plan_abort, words,
-                                 kWhereGuard, p);
+                                 kWhereGuard, p, limit_ns);
             if (!epi_all(gok && !*abort_word)) {
               ok = false;
               break;
@@ -711,7 +727,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
               ok = false;
               break;
             }
-            if (et == 0) st_release(ready + 2 * cta + par, p + 1);
+            // (a test can make one CTA withhold its partials: the consumer's
+            // bounded wait then runs out and the plan winds down)
+            if (et == 0 && cta != rp.skip_partial_cta) st_release(ready + 2 * cta + par, p + 1);
             lastw[par] = p + 1;
             continue;
           }
@@ -854,6 +872,8 @@ int launch(const Header& h, const void* plan_dev, void* ws, int dev, cudaStream_
   RunParams rp;
   rp.phases = reinterpret_cast<const Phase*>(static_cast<const uint8_t*>(plan_dev) + kHeaderBytes);
   rp.n_phases = h.n_phases;
+  rp.skip_partial_cta = h.test_skip_partial_cta;
+  rp.wait_limit_ns = h.wait_limit_ns;
   rp.words = static_cast<int*>(ws);
   rp.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
   // CTAs wait on one another (phase counters, split-K partials): launched
@@ -881,7 +901,7 @@ inline int check_header(const void* plan_host, Header* out) {
   std::memcpy(out, plan_host, sizeof(Header));
   if (out->magic != kPlanMagic || out->version != kPlanVersion || out->n_phases < 1 ||
       out->n_phases > kMaxPhases || (out->mt != 16 && out->mt != 32) || out->grid < 1 ||
-      out->grid > kMaxGrid)
+      out->grid > kMaxGrid || out->wait_limit_ns == 0 || out->wait_limit_ns > kWaitLimitNs)
     return DFL_ERR_BAD_SHAPE;
   return DFL_OK;
 }
@@ -961,6 +981,8 @@ extern "C" int dfl_qmm_plan_encode(const dfl_qmm_phase* phases, int n_phases, vo
   h.mt = mt;
   h.grid = sms < kMaxGrid ? sms : kMaxGrid;
   h.flags_or = flags_or;
+  h.test_skip_partial_cta = -1;
+  h.wait_limit_ns = kWaitLimitNs;
   std::memcpy(out, &h, sizeof(h));
   for (int p = 0; p < n_phases; ++p) {
     const dfl_qmm_phase& q = phases[p];
@@ -1010,4 +1032,28 @@ extern "C" int dfl_qmm_plan_run(const void* plan_host, const void* plan_dev, voi
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (h.mt == 16) return plan::launch<16>(h, plan_dev, workspace, dev, s);
   return plan::launch<32>(h, plan_dev, workspace, dev, s);
+}
+
+extern "C" int dfl_qmm_plan_set_test_fault(void* plan_host, int skip_partial_cta,
+                                           uint64_t wait_limit_ns) {
+  dfl::plan::Header h;
+  const int st = dfl::plan::check_header(plan_host, &h);
+  if (st != DFL_OK) return st;
+  if (skip_partial_cta < -1 || skip_partial_cta >= h.grid) return DFL_ERR_BAD_SHAPE;
+  if (wait_limit_ns < 1000000ull || wait_limit_ns > dfl::kWaitLimitNs) return DFL_ERR_BAD_SHAPE;
+  h.test_skip_partial_cta = skip_partial_cta;
+  h.wait_limit_ns = wait_limit_ns;
+  std::memcpy(plan_host, &h, sizeof(h));
+  return DFL_OK;
+}
+
+extern "C" int dfl_qmm_plan_last_timeout(const void* workspace_host_words, int* role, int* phase,
+                                         int* cta) {
+  if (!workspace_host_words || !role || !phase || !cta) return DFL_ERR_NULL_POINTER;
+  const int* w = static_cast<const int*>(workspace_host_words);
+  const int where = w[dfl::plan::kWordWhere];
+  *role = where >> 24;
+  *phase = where & 0xFFFFFF;
+  *cta = w[dfl::plan::kWordWhereCta];
+  return DFL_OK;
 }

@@ -167,6 +167,24 @@ class ProjectionPlan:
         """Zero the workspace again (needed after a reported device error)."""
         self.workspace.zero_()
 
+    def set_test_fault(self, skip_partial_cta: int = -1, wait_limit_ns: int = 1_000_000_000) -> None:
+        """Tests only: make CTA ``skip_partial_cta`` withhold its split-K
+        partials and bound every wait by ``wait_limit_ns`` (the run then ends
+        with a device error instead of results); -1 / 1 s restore normal runs."""
+        _lib.check("dfl_qmm_plan_set_test_fault",
+                   _lib.load().dfl_qmm_plan_set_test_fault(self._host, int(skip_partial_cta),
+                                                           int(wait_limit_ns)))
+
+    def last_timeout(self):
+        """(role, phase, cta) of the first wait that ran out in the last run,
+        role 0 when none did (reads the workspace back to the host)."""
+        words = self.workspace[:64 * 1024].cpu().numpy()
+        role, phase, cta = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+        _lib.check("dfl_qmm_plan_last_timeout",
+                   _lib.load().dfl_qmm_plan_last_timeout(words.ctypes.data, ctypes.byref(role),
+                                                         ctypes.byref(phase), ctypes.byref(cta)))
+        return role.value, phase.value, cta.value
+
 
 def qmm_tiled(x: torch.Tensor, weight: TiledWeight, out: Optional[torch.Tensor] = None, *,
               silu: bool = False) -> torch.Tensor:

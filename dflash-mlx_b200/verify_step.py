@@ -41,6 +41,29 @@ from .qmm_plan import PlanPhase, ProjectionPlan, tile_weight
 from .verify_qmm import gate_up_silu, qmm_w4g64, repack_pairs
 
 
+def init_process_group(backend: str, *, timeout_s: float = 120.0, device=None):
+    """``torch.distributed`` start-up for one rank of the step (rank, world
+    size and rendezvous from RANK / WORLD_SIZE / MASTER_ADDR / MASTER_PORT),
+    bounded by ``timeout_s``: a rendezvous that cannot complete, or a
+    collective whose peer is gone, ends with an exception after that long
+    instead of waiting for ever.  Returns the default group."""
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    kw = {"device_id": device} if device is not None else {}
+    try:
+        dist.init_process_group(backend, rank=rank, world_size=world,
+                                timeout=timedelta(seconds=timeout_s), **kw)
+    except Exception as e:  # noqa: BLE001 - re-raised with the rendezvous named
+        where = f"{os.environ.get('MASTER_ADDR', '?')}:{os.environ.get('MASTER_PORT', '?')}"
+        raise RuntimeError(f"rank {rank}/{world}: {backend} process group at {where} did not start "
+                           f"within {timeout_s:g} s: {e}") from e
+    return dist.group.WORLD
+
+
 @dataclass
 class StackShape:
     hidden: int = 5120

@@ -234,6 +234,23 @@ size_t dfl_qmm_plan_workspace_bytes(const void* plan_host, int* status);
 int dfl_qmm_plan_run(const void* plan_host, const void* plan_dev, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* Failure handling of plans.  Every wait inside a plan run is bounded
+ * (1 s by default); when one runs out the run sets the device error word
+ * (dfl_get_device_error), records where it gave up in the workspace and
+ * every CTA winds down and exits: the launch ends, nothing hangs, and the
+ * workspace must be zero-filled before the next run.
+ * dfl_qmm_plan_last_timeout reads that record from a host copy of the
+ * workspace's first 64 KB: role (1 dependency, 2 slot guard, 3 split-K
+ * partial, 4 producer, 5 MMA, 6 dequant, 7 x-slot, 8 accumulator; 0 = none),
+ * phase and CTA of the first wait that ran out.
+ * dfl_qmm_plan_set_test_fault edits an encoded host plan for tests of that
+ * path: skip_partial_cta (-1 = none) makes that CTA withhold its split-K
+ * partials, so the CTA that sums them waits until wait_limit_ns (1 ms .. 1 s)
+ * runs out.  Re-encode the plan (or set -1 and 1e9) to run normally again.
+ * No counterpart in the reference (its Metal kernels have no waits). */
+int dfl_qmm_plan_set_test_fault(void* plan_host, int skip_partial_cta, uint64_t wait_limit_ns);
+int dfl_qmm_plan_last_timeout(const void* workspace_host_words, int* role, int* phase, int* cta);
+
 /* ------------------------------------------------------------------------
  * GatedDeltaNet tape-replay rollback.
  *

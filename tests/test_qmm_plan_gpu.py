@@ -269,3 +269,49 @@ def test_plan_rejects_bad_phases(pkg, dev):
         pkg.ProjectionPlan([pkg.PlanPhase(x, tw, y[:, :128])])          # wrong output width
     with pytest.raises(ValueError):
         pkg.ProjectionPlan([pkg.PlanPhase(x, tw, y, silu=True)])        # SiLU output is N/2 wide
+
+
+def test_withheld_partial_times_out_and_the_plan_recovers(pkg, dev):
+    """Failure path of a plan, made on the host: CTA 1 is told to withhold its
+    split-K partials (its range lies inside tile 0 of a 640-unit phase, so CTA
+    0 must sum its partial) and every wait is bounded by 20 ms.  CTA 0's wait
+    runs out, the plan-wide abort word stops every CTA (the second phase's
+    CTAs were waiting for the first phase to complete), the launch ends in
+    well under a second with the device error word set and the time-out
+    recorded (split-K partial, phase 0, CTA 0).  After the workspace is
+    zeroed, the same plan gives the oracle's results."""
+    import time
+
+    import torch
+
+    from dflash_mlx_b200 import _lib
+
+    rng = np.random.default_rng(66)
+    w0 = oqmm.synth_weights(rng, 8192, 5120)
+    w1 = oqmm.synth_weights(rng, 1024, 8192)
+    tw0, tw1 = _tiled(pkg, dev, *w0), _tiled(pkg, dev, *w1)
+    x = oqmm.synth_x(rng, 16, 5120)
+    xd = to_dev_bf16(x, dev)
+    y0 = torch.empty((16, 8192), dtype=torch.bfloat16, device=dev)
+    y1 = torch.empty((16, 1024), dtype=torch.bfloat16, device=dev)
+    plan = pkg.ProjectionPlan([pkg.PlanPhase(xd, tw0, y0), pkg.PlanPhase(y0, tw1, y1, dep=0)])
+    torch.cuda.synchronize(dev)
+    assert _lib.device_error() == 0
+    plan.set_test_fault(skip_partial_cta=1, wait_limit_ns=20_000_000)
+    t0 = time.perf_counter()
+    plan.run()
+    torch.cuda.synchronize(dev)
+    assert time.perf_counter() - t0 < 5.0
+    assert plan.last_timeout() == (3, 0, 0)
+    assert _lib.device_error() == 1
+    # normal runs again
+    plan.set_test_fault(-1, 1_000_000_000)
+    plan.reset_workspace()
+    plan.run()
+    torch.cuda.synchronize(dev)
+    assert plan.last_timeout() == (0, 0, 0)
+    assert _lib.device_error() == 0
+    ref0 = oqmm.qmm(x, *w0, accum=np.float32)
+    _assert_close(bf16_to_np_bits(y0), ref0, "phase 0 after recovery")
+    _assert_close(bf16_to_np_bits(y1), oqmm.qmm(bf16_to_np_bits(y0), *w1, accum=np.float32),
+                  "phase 1 after recovery")
