@@ -30,9 +30,10 @@ constexpr int THREADS = 256;
 constexpr int MAX_CHUNKS = 16;  // float4 state chunks per thread (Dv * Dk <= 16384)
 constexpr int MAX_STEPS = 64;
 // Largest staging area: MAX_STEPS * (Dv + 2 * Dk) floats with Dv * Dk <= 16384.
-constexpr int kMaxSmem = MAX_STEPS * (512 + 2 * 32) * 4 > MAX_STEPS * (64 + 2 * 256) * 4
-                             ? MAX_STEPS * (512 + 2 * 32) * 4
-                             : MAX_STEPS * (64 + 2 * 256) * 4;
+// (+16 bytes: the g region is padded to whole float4s)
+constexpr int kMaxSmem = (MAX_STEPS * (512 + 2 * 32) * 4 > MAX_STEPS * (64 + 2 * 256) * 4
+                              ? MAX_STEPS * (512 + 2 * 32) * 4
+                              : MAX_STEPS * (64 + 2 * 256) * 4) + 16;
 
 struct ReplayParams {
   const float* tape;
@@ -44,15 +45,33 @@ struct ReplayParams {
   float* state_out;
   int B, T, Hv, Hk, Dv, Dk;
   int g_vec;
+  int vec;                // tape, k, g 16-byte aligned and Dv % 4 == 0: stage by cp.async
 };
 
+// Four consecutive k values from shared memory as floats (bf16 -> fp32 is exact).
 template <typename KT>
-__device__ __forceinline__ float load_k(const KT* p);
+__device__ __forceinline__ float4 load_k4(const KT* p);
 template <>
-__device__ __forceinline__ float load_k<float>(const float* p) { return *p; }
+__device__ __forceinline__ float4 load_k4<float>(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
 template <>
-__device__ __forceinline__ float load_k<__nv_bfloat16>(const __nv_bfloat16* p) {
-  return __bfloat162float(*p);
+__device__ __forceinline__ float4 load_k4<__nv_bfloat16>(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+}
+
+// Copy `rows` rows of `row_bytes` (a multiple of 16) from global rows
+// `stride_bytes` apart into consecutive shared memory, 16 bytes per
+// cp.async; every thread of the CTA takes a share.
+__device__ __forceinline__ void stage_rows(uint8_t* dst, const uint8_t* src, int rows,
+                                           int row_bytes, size_t stride_bytes, int tid) {
+  const int per_row = row_bytes / 16;
+  for (int i = tid; i < rows * per_row; i += THREADS) {
+    const int r = i / per_row, c = i - r * per_row;
+    cp_async_16(smem_u32(dst + (size_t)r * row_bytes + c * 16), src + r * stride_bytes + c * 16, 16);
+  }
 }
 
 template <typename KT, int DK>
@@ -85,28 +104,10 @@ __global__ void __launch_bounds__(THREADS)
     return;
   }
 
-  // Stage this head's replayed steps: k [a][DK], g [a] or [a][DK], delta [a][Dv]
-  // (k and vector g first: their rows start on 16-byte boundaries).
-  const int gw = p.g_vec ? DK : 1;
-  float* s_k = sh;
-  float* s_g = s_k + nsteps * DK;
-  float* s_delta = s_g + nsteps * gw;
-  for (int i = tid; i < nsteps * p.Dv; i += THREADS) {
-    const int t = i / p.Dv, dv = i - t * p.Dv;
-    s_delta[i] = p.tape[(((size_t)b * p.T + t) * p.Hv + hv) * p.Dv + dv];
-  }
-  const KT* kp = reinterpret_cast<const KT*>(p.k);
-  for (int i = tid; i < nsteps * DK; i += THREADS) {
-    const int t = i / DK, dk = i - t * DK;
-    s_k[i] = load_k<KT>(kp + (((size_t)b * p.T + t) * p.Hk + hk) * DK + dk);
-  }
-  for (int i = tid; i < nsteps * gw; i += THREADS) {
-    const int t = i / gw, j = i - t * gw;
-    s_g[i] = p.g[(((size_t)b * p.T + t) * p.Hv + hv) * gw + j];
-  }
-
-  // Thread tid owns float4 chunks f = j * THREADS + tid: row dv = 4f / DK,
-  // columns dk0..dk0+3 with dk0 = 4f % DK = (4 * tid) % DK (DK divides 1024).
+  // The head's state first (16-byte loads into registers), so that it and the
+  // staging copies below are all in flight together.  Thread tid owns float4
+  // chunks f = j * THREADS + tid: row dv = 4f / DK, columns dk0..dk0+3 with
+  // dk0 = 4f % DK = (4 * tid) % DK (DK divides 1024).
   float4 st[MAX_CHUNKS];
   const int nchunk = (n4 + THREADS - 1) / THREADS;
 #pragma unroll
@@ -114,12 +115,52 @@ __global__ void __launch_bounds__(THREADS)
     const int f = j * THREADS + tid;
     if (j < nchunk && f < n4) st[j] = __ldcs(src + f);
   }
+
+  // Stage this head's replayed steps in shared memory: k [a][DK] (as stored),
+  // g [a][DK] or [a], delta [a][Dv]; k and vector g first (16-byte rows).
+  // Every region starts on a 16-byte boundary: k rows are DK * sizeof(KT) >= 64
+  // bytes and the g region is padded to whole float4s.
+  const int gw = p.g_vec ? DK : 1;
+  KT* s_k = reinterpret_cast<KT*>(sh);
+  float* s_g = reinterpret_cast<float*>(s_k + nsteps * DK);
+  float* s_delta = s_g + ((nsteps * gw + 3) & ~3);
+  const KT* kp = reinterpret_cast<const KT*>(p.k);
+  // rows of step t: k row (b, t, hk), g row (b, t, hv), delta row (b, t, hv)
+  const size_t k_row0 = ((size_t)b * p.T * p.Hk + hk) * DK;
+  const size_t g_row0 = (size_t)b * p.T * p.Hv + hv;
+  if (p.vec) {
+    stage_rows(reinterpret_cast<uint8_t*>(s_k), reinterpret_cast<const uint8_t*>(kp + k_row0), nsteps,
+               DK * int(sizeof(KT)), (size_t)p.Hk * DK * sizeof(KT), tid);
+    if (p.g_vec)
+      stage_rows(reinterpret_cast<uint8_t*>(s_g), reinterpret_cast<const uint8_t*>(p.g + g_row0 * DK),
+                 nsteps, DK * 4, (size_t)p.Hv * DK * 4, tid);
+    stage_rows(reinterpret_cast<uint8_t*>(s_delta),
+               reinterpret_cast<const uint8_t*>(p.tape + g_row0 * p.Dv), nsteps, p.Dv * 4,
+               (size_t)p.Hv * p.Dv * 4, tid);
+  } else {
+    for (int i = tid; i < nsteps * DK; i += THREADS) {
+      const int t = i / DK, dk = i - t * DK;
+      s_k[i] = kp[k_row0 + (size_t)t * p.Hk * DK + dk];
+    }
+    if (p.g_vec)
+      for (int i = tid; i < nsteps * DK; i += THREADS) {
+        const int t = i / DK, dk = i - t * DK;
+        s_g[i] = p.g[(g_row0 + (size_t)t * p.Hv) * DK + dk];
+      }
+    for (int i = tid; i < nsteps * p.Dv; i += THREADS) {
+      const int t = i / p.Dv, dv = i - t * p.Dv;
+      s_delta[i] = p.tape[(g_row0 + (size_t)t * p.Hv) * p.Dv + dv];
+    }
+  }
+  if (!p.g_vec)
+    for (int t = tid; t < nsteps; t += THREADS) s_g[t] = p.g[g_row0 + (size_t)t * p.Hv];
+  cp_async_wait_all();
   __syncthreads();
 
   const int dk0 = (4 * tid) % DK;
   for (int t = 0; t < nsteps; ++t) {
     if (!((active >> t) & 1)) continue;
-    const float4 kv = *reinterpret_cast<const float4*>(s_k + t * DK + dk0);
+    const float4 kv = load_k4<KT>(s_k + t * DK + dk0);
     float4 gv;
     if (p.g_vec) {
       gv = *reinterpret_cast<const float4*>(s_g + t * DK + dk0);
@@ -153,7 +194,7 @@ __global__ void __launch_bounds__(THREADS)
 template <typename KT>
 int launch_replay(const ReplayParams& p, cudaStream_t stream) {
   const int gw = p.g_vec ? p.Dk : 1;
-  const size_t smem = size_t(p.T) * (p.Dv + p.Dk + gw) * sizeof(float);
+  const size_t smem = size_t(p.T) * (p.Dv + p.Dk + gw) * sizeof(float) + 16;
   const int grid = p.B * p.Hv;
   switch (p.Dk) {
 #define DFL_CASE(D)                                                                        \
@@ -212,6 +253,8 @@ extern "C" int dfl_gdn_tape_replay(const float* tape, const void* k, int k_is_bf
   p.Dv = Dv;
   p.Dk = Dk;
   p.g_vec = g_vectorized ? 1 : 0;
+  p.vec = (Dv % 4 == 0 && host::aligned(tape, 16) && host::aligned(k, 16) && host::aligned(g, 16))
+              ? 1 : 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return k_is_bf16 ? gdn::launch_replay<__nv_bfloat16>(p, s) : gdn::launch_replay<float>(p, s);
 }
