@@ -70,7 +70,11 @@ constexpr int NUM_THREADS = NUM_WARPS * 32;            // 832
 constexpr int TMEM_COLS = 512;
 constexpr int BAR_ID_EPI = 1;
 constexpr int PACK_BYTES = BN * UNIT_K / 2;            // 32768: nibbles of a unit
-constexpr int SB_BYTES = NDG * BN * 8;                 // 4096: scales + biases of a unit
+constexpr int SB_RECORDS = 4;                          // per row: {s_g, s_g+4, b_g, b_g+4}, g = 0..3
+constexpr int SB_BYTES = SB_RECORDS * BN * 8;          // 4096: scales + biases of a unit
+constexpr int SPG = NSUB / NDG;                        // sub-blocks per dequant group and unit
+constexpr int RPG = SB_RECORDS / NDG;                  // scale/bias records per dequant thread
+static_assert(NSUB % NDG == 0 && SB_RECORDS % NDG == 0, "dequant groups");
 constexpr int BLK_BYTES = PACK_BYTES + SB_BYTES;       // 36864
 constexpr int NSTAGE = 4;
 constexpr int kMaxGrid = 160;
@@ -479,7 +483,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
   } else if (warp < WARP_EPI0) {
     // ------------------------------------------------------------ dequant
     const int dw = warp - WARP_DQ0;
-    const int grp = dw >> 2;               // sub-blocks grp and grp + 4 of every unit
+    const int grp = dw >> 2;               // sub-blocks grp + NDG * jj of every unit
     const int quad = warp & 3;             // TMEM lane quadrant
     const int r = quad * 32 + lane;        // output row within the tile
     const uint32_t lane_base = tmem_base + (uint32_t(quad * 32) << 16);
@@ -497,27 +501,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
         const int s = it % NSTAGE;
         wait(&full[s], (it / NSTAGE) & 1, kWhereDequant, p);
         const uint32_t st = smem_u32(smem + s * BLK_BYTES);
-        // this thread's packed words (2 sub-blocks x 8 words) and its
-        // scales / biases, then the stage goes back to the producer
-        const uint2 sbw = ld_shared_v2(st + PACK_BYTES + uint32_t(grp * BN + r) * 8u);
-        uint4 qv[2][2];
+        // this thread's packed words (SPG sub-blocks x 8 words) and its
+        // scales / biases, then the stage goes back to the producer.  Group
+        // grp converts sub-blocks sb = grp + NDG * jj; sub-block sb's scale
+        // and bias are half sb / 4 of record sb % 4.
+        uint2 sbw[RPG];
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj)
+        for (int q = 0; q < RPG; ++q)
+          sbw[q] = ld_shared_v2(st + PACK_BYTES + uint32_t((grp + NDG * q) * BN + r) * 8u);
+        uint4 qv[SPG][2];
+#pragma unroll
+        for (int jj = 0; jj < SPG; ++jj)
 #pragma unroll
           for (int h = 0; h < 2; ++h)
-            qv[jj][h] = ld_shared_v4(st + uint32_t(((grp + 4 * jj) * 2 + h) * BN + r) * 16u);
+            qv[jj][h] = ld_shared_v4(st + uint32_t(((grp + NDG * jj) * 2 + h) * BN + r) * 16u);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-        int slots[2];
+        int slots[SPG];
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          const int g = it * NSUB + grp + 4 * jj;
+        for (int jj = 0; jj < SPG; ++jj) {
+          const int g = it * NSUB + grp + NDG * jj;
           const int slot = g % C::NASLOT;
           slots[jj] = slot;
           wait(&aempty[slot], ((g / C::NASLOT) & 1) ^ 1, kWhereDequant, p);
           tc_fence_after();
-          const uint32_t s2 = __byte_perm(sbw.x, 0, jj ? 0x3232u : 0x1010u);
-          const uint32_t b2 = __byte_perm(sbw.y, 0, jj ? 0x3232u : 0x1010u);
+          const uint2 rec = sbw[jj % RPG];
+          const uint32_t sel = (jj / RPG) ? 0x3232u : 0x1010u;
+          const uint32_t s2 = __byte_perm(rec.x, 0, sel);
+          const uint32_t b2 = __byte_perm(rec.y, 0, sel);
           uint32_t w[32];
           if (subn) {
             const uint32_t s_hi = bf16x2_mul(s2, 0x3D803D80u);  // * 2^-4
@@ -545,8 +556,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&afull[slots[0]]);
-          mbar_arrive(&afull[slots[1]]);
+#pragma unroll
+          for (int jj = 0; jj < SPG; ++jj) mbar_arrive(&afull[slots[jj]]);
         }
       }
     }
@@ -571,7 +582,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                          reinterpret_cast<uint64_t>(&ph.tm_x))
                      : "memory");
         if (dep >= 0) {
-          if (!wait_counter(rp.words + dep, G, abort_word, plan_abort, words, kWhereDep, p, limit_ns)) break;
+          // a dependency wait spans the whole earlier phase, so it runs twice
+          // the limit: a stall inside that phase is then reported by the wait
+          // that sees it first-hand (split-K partial, guard, pipeline) rather
+          // than by this downstream wait
+          if (!wait_counter(rp.words + dep, G, abort_word, plan_abort, words, kWhereDep, p, 2 * limit_ns)) break;
           fence_proxy_async_global();   // x rows written by other CTAs' stores
         }
         for (int u = u0; u < u1; ++u, ++seq) {

@@ -246,7 +246,9 @@ int dfl_qmm_plan_run(const void* plan_host, const void* plan_dev, void* workspac
  * dfl_qmm_plan_set_test_fault edits an encoded host plan for tests of that
  * path: skip_partial_cta (-1 = none) makes that CTA withhold its split-K
  * partials, so the CTA that sums them waits until wait_limit_ns (1 ms .. 1 s)
- * runs out.  Re-encode the plan (or set -1 and 1e9) to run normally again.
+ * runs out (a wait on an earlier phase's completion counter runs twice the
+ * limit, so the first-hand wait is the one recorded).  Re-encode the plan (or
+ * set -1 and 1e9) to run normally again.
  * No counterpart in the reference (its Metal kernels have no waits). */
 int dfl_qmm_plan_set_test_fault(void* plan_host, int skip_partial_cta, uint64_t wait_limit_ns);
 int dfl_qmm_plan_last_timeout(const void* workspace_host_words, int* role, int* phase, int* cta);
