@@ -389,9 +389,11 @@ def run_ours(args):
     # roofline of the dominant kernel (the int4 verify qmm)
     peak, peak_kind = _peaks()
     plan = step.plan is not None
-    launches = len(sh.launches()) * sh.layers * (((b + 1) // 2) if step.pack_requests else b)
-    bytes_per_step = sh.qmm_bytes_per_step(b, step.pack_requests or plan, silu_fused=step.fuse_silu)
+    per_launch = step.requests_per_launch
+    launches = len(sh.launches()) * sh.layers * (-(-b // per_launch))
+    bytes_per_step = sh.qmm_bytes_per_step(b, per_launch, silu_fused=step.fuse_silu)
     achieved = bytes_per_step / (t_qmm / args.steps) / 1e9
+    qmm_tflops = b * sh.qmm_flops_per_request() / (t_qmm / args.steps) / 1e12
     if plan:
         # one launch runs the whole stack: DRAM bytes of a layer (ncu) x layers
         per_layer, _ = _profile_value("qmm_plan_verify_stack.md", "dram_bytes_per_layer:")
@@ -417,7 +419,7 @@ def run_ours(args):
                 "workload": workload_name(sh.layers),
                 "requests_per_gpu": b, "tokens_per_request": sh.block,
                 "weight_layout": args.weight_layout,
-                "requests_share_launches": step.pack_requests,
+                "requests_per_weight_read": per_launch,
                 "qmm_launch": (("one plan launch per step; each projection waits on the device "
                                 "for the projections whose outputs it reads (down for gate|up's "
                                 "SiLU output, the next layer's q|k|v for this layer's down); o "
@@ -433,6 +435,8 @@ def run_ours(args):
                 "l2": "inputs larger than L2 (12.4 GB of packed weights per step)",
                 "qmm_ms_per_step": t_qmm / args.steps * 1e3,
                 "qmm_gbs": achieved,
+                "qmm_tflops": qmm_tflops,
+                "qmm_tensor_frac": qmm_tflops / _peak_tflops(),
                 "verify_ids": "P(draft = previous position's posterior) = 0.88, posterior from set-up",
                 "mean_acceptance": mean_acc,
             },

@@ -1,6 +1,7 @@
 // Projection plans: one persistent launch runs a whole sequence of int4 g64
 // verify projections (a decoder layer's q|k|v, o, gate|up + SiLU, down, or a
-// whole layer stack) at M <= 32 tokens.
+// whole layer stack) at up to 128 token rows per projection: one request's
+// 16 verify tokens, or the rows of up to 8 requests sharing one weight read.
 //
 // Same arithmetic as the per-call qmm (qmm_w4.cu, which replaces the
 // reference's M=16 verify kernels, dflash_mlx/verify_qmm.py:196-765, and
@@ -33,10 +34,16 @@
 //     phase complete (a release counter per phase), so the dataflow of a
 //     real forward pass is kept.
 //
-// Warp roles (one CTA per SM, 25 warps): 0 producer, 1-4 MMA issuers (one
-// accumulator each, two of the unit's eight 64-K sub-blocks), 5-20 dequant
-// (4 groups x 4 TMEM lane quadrants, thread = output row), 21-24 x loads +
-// epilogue + split-K reduction + phase signals.
+// Warp roles (one CTA per SM, 26 warps): 0 producer, 1-4 MMA issuers, 5-20
+// dequant (4 groups x 4 TMEM lane quadrants, thread = output row), 21-24
+// epilogue + split-K reduction + phase signals, 25 x loads.  The token tile
+// MT (16, 32, 64 or 128 rows, the UMMA N) is chosen per plan from its
+// largest phase.  The four MMA warps issue four independent accumulation
+// chains (a chain into one accumulator is latency bound): up to 32 rows as
+// four K-interleaved accumulators, at 64 / 128 rows as four token-column
+// slices of one accumulator.  Larger tiles stage x in half / quarter units
+// and keep fewer weight blocks in flight (the tensor pipe, not HBM, bounds
+// them).  A projection over more rows is several phases, one per token tile.
 //
 // Split-K: a tile shared by CTAs c_lo..c_hi is the last of c_lo's range in
 // that phase and the first of the others'.  A contributor stores its fp32
@@ -76,8 +83,8 @@ constexpr int SPG = NSUB / NDG;                        // sub-blocks per dequant
 constexpr int RPG = SB_RECORDS / NDG;                  // scale/bias records per dequant thread
 static_assert(NSUB % NDG == 0 && SB_RECORDS % NDG == 0, "dequant groups");
 constexpr int BLK_BYTES = PACK_BYTES + SB_BYTES;       // 36864
-constexpr int NSTAGE = 4;
 constexpr int kMaxGrid = 160;
+constexpr int kMaxRows = 128;                         // token rows per phase (one token tile)
 constexpr int kMaxPhases = 7936;
 constexpr uint32_t kPlanMagic = 0x504C4644u;           // "DFLP"
 constexpr int kPlanVersion = 1;
@@ -100,23 +107,54 @@ static_assert(BLK_BYTES % 1024 == 0, "stage alignment");
 
 template <int MT>
 struct Cfg {
+  static_assert(MT == 16 || MT == 32 || MT == 64 || MT == 128, "token tile");
+  // MMAs into one accumulator form a dependent chain whose latency, not the
+  // tensor pipe, sets the rate, so the four MMA warps issue four independent
+  // chains.  Up to 32 tokens each warp takes every fourth sub-block into an
+  // accumulator of its own (NACC = 4, summed by the epilogue); at 64 / 128
+  // tokens each warp takes one quarter of the token columns (NSLICE = 4,
+  // N = 16 / 32 per MMA) of a single accumulator, which keeps the
+  // accumulator at MT columns so two buffers fit TMEM beside the A slots.
+  static constexpr int NACC = (MT <= 32) ? 4 : 1;
+  static constexpr int NSLICE = NUM_MMA_WARPS / NACC;
+  static constexpr int SLICE_N = MT / NSLICE;
+  static constexpr int NSTAGE = (MT <= 64) ? 4 : 3;    // weight blocks in flight
   static constexpr int XBLK_BYTES = MT * 128;          // one [MT rows x 64 K] bf16 block, SW128
-  static constexpr int XSLOT_BYTES = NSUB * XBLK_BYTES;
-  static constexpr int XS = (MT <= 16) ? 4 : 2;        // x ring depth (units)
+  // x is staged in chunks of XCH sub-blocks (a whole unit up to 32 rows)
+  static constexpr int XCH = (MT <= 32) ? NSUB : (MT == 64 ? 4 : 2);
+  static constexpr int NCH = NSUB / XCH;               // x chunks per unit
+  static constexpr int XCHUNK_BYTES = XCH * XBLK_BYTES;
+  static constexpr int XS = (MT <= 16) ? 4 : (MT == 128 ? 3 : 2);   // x ring depth (chunks)
   static constexpr int OFF_XRING = NSTAGE * BLK_BYTES;
-  static constexpr int OFF_BARS = OFF_XRING + XS * XSLOT_BYTES;
+  static constexpr int OFF_BARS = OFF_XRING + XS * XCHUNK_BYTES;
   static constexpr int SMEM_BYTES = OFF_BARS + 512 + 1024;
   static constexpr int NASLOT = 8;                     // TMEM A slots (one unit)
   static constexpr int ACC_COL0 = NASLOT * A_COLS;
-  static constexpr int ACC_COLS = NUM_MMA_WARPS * MT;  // one accumulator buffer
+  static constexpr int ACC_COLS = NACC * MT;           // one accumulator buffer
   // accumulator buffers: the MMAs may run this many tile segments ahead of
   // the epilogue (segments are short: 2-10 units per CTA and phase)
   static constexpr int NACCBUF = (MT <= 16) ? 4 : 2;
+  // epilogue columns per pass (registers); with
+  // one pass the split-K partials are summed before the accumulator is
+  // ready, with several they are summed pass by pass
+  // x chunks are released by the A-slot release of their last sub-block when
+  // every MMA warp reads every sub-block (token slices): that commit already
+  // covers all MMAs that read the chunk, and a separate x-release barrier
+  // with its own commits costs far more hand-off time per chunk.  Safe when a
+  // unit has at least XS chunks: sub-block g + NASLOT (the next use of the
+  // A slot) is in a chunk the x loader has not loaded yet when it waits for
+  // g, so the slot's barrier is never two phases ahead of that wait.
+  static constexpr bool kXReleaseByA = (NSLICE == NUM_MMA_WARPS) && (NCH >= XS);
+  static constexpr int EC = 16;
+  static constexpr bool kEarlyPartials = (EC == MT);
   static_assert(ACC_COL0 + NACCBUF * ACC_COLS <= TMEM_COLS, "TMEM budget");
   static constexpr int NUM_BARS = 2 * NSTAGE + 2 * NASLOT + 2 * XS + 2 * NACCBUF + NUM_MMA_WARPS;
   static_assert(NUM_BARS * 8 + 16 <= 512, "barrier area");
   static_assert(XBLK_BYTES % 1024 == 0, "x blocks keep the 1024-byte swizzle alignment");
-  static_assert(NASLOT % NDG == 0 && NASLOT % NUM_MMA_WARPS == 0 && NASLOT >= NSUB, "A slots");
+  static_assert(NASLOT % NDG == 0 && NASLOT >= NSUB, "A slots");
+  static_assert(NACC * NSLICE == NUM_MMA_WARPS && XCH % NACC == 0 && NSUB % XCH == 0, "MMA issue split");
+  static_assert(SLICE_N % 16 == 0 && (SLICE_N * 128) % 1024 == 0, "token slices: UMMA N, SW128 row groups");
+  static_assert(MT % EC == 0 && EC % 16 == 0, "epilogue passes");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -334,8 +372,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BARS);
   uint64_t* full = bars;                       // [NSTAGE] unit block landed
-  uint64_t* empty = full + NSTAGE;             // [NSTAGE] block read by the dequant warps
-  uint64_t* afull = empty + NSTAGE;            // [NASLOT] TMEM A slot written
+  uint64_t* empty = full + C::NSTAGE;             // [NSTAGE] block read by the dequant warps
+  uint64_t* afull = empty + C::NSTAGE;            // [NASLOT] TMEM A slot written
   uint64_t* aempty = afull + C::NASLOT;        // [NASLOT] TMEM A slot read by the MMAs
   uint64_t* xfull = aempty + C::NASLOT;        // [XS] x slot landed (TMA)
   uint64_t* xfree = xfull + C::XS;             // [XS] x slot read by all MMA warps
@@ -362,13 +400,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
 
   if (threadIdx.x == 0) {
     *abort_word = 0;
-    for (int i = 0; i < NSTAGE; ++i) {
+    for (int i = 0; i < C::NSTAGE; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 4 * NDG);
     }
     for (int i = 0; i < C::NASLOT; ++i) {
       mbar_init(&afull[i], 4);
-      mbar_init(&aempty[i], 1);
+      mbar_init(&aempty[i], C::NSLICE);
     }
     for (int i = 0; i < C::XS; ++i) {
       mbar_init(&xfull[i], 1);
@@ -410,8 +448,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
         const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
         const uint8_t* src = w + size_t(u0) * BLK_BYTES;
         for (int u = u0; u < u1; ++u, ++it, src += BLK_BYTES) {
-          const int s = it % NSTAGE;
-          if (!wait(&empty[s], ((it / NSTAGE) & 1) ^ 1, kWhereProducer, p)) break;
+          const int s = it % C::NSTAGE;
+          if (!wait(&empty[s], ((it / C::NSTAGE) & 1) ^ 1, kWhereProducer, p)) break;
           mbar_arrive_expect_tx(&full[s], BLK_BYTES);
           bulk_load_hint(smem_u32(smem + s * BLK_BYTES), src, BLK_BYTES, &full[s], pol);
         }
@@ -420,58 +458,70 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
     __syncwarp();
   } else if (warp < WARP_DQ0) {
     // ------------------------------------------------------------ MMA issuers
-    // Warp j issues the MMAs of sub-blocks j and j + 4 of every unit into
-    // accumulator j; one accumulator segment per (phase, tile) part.
+    // Warp j = a * NSLICE + sl issues the MMAs of sub-blocks a, a + NACC, ...
+    // of every unit for token columns [sl * SLICE_N, (sl + 1) * SLICE_N) of
+    // accumulator a; one accumulator segment per (phase, tile) part.  x
+    // arrives in NCH chunks per unit; a chunk's slot is released once every
+    // MMA warp's MMAs that read it completed.
     const int j = warp - WARP_MMA0;
-    constexpr uint32_t idesc = make_idesc_16(BN, MT, false);
-    const uint64_t ring_desc = make_sw128_desc(smem_u32(smem + C::OFF_XRING));
-    constexpr uint64_t kSlotDesc = uint64_t(C::XSLOT_BYTES >> 4);
+    const int a_idx = j / C::NSLICE, sl = j % C::NSLICE;
+    constexpr uint32_t idesc = make_idesc_16(BN, C::SLICE_N, false);
+    const uint64_t ring_desc =
+        make_sw128_desc(smem_u32(smem + C::OFF_XRING + sl * C::SLICE_N * 128));
+    constexpr uint64_t kChunkDesc = uint64_t(C::XCHUNK_BYTES >> 4);
     constexpr uint64_t kBlkDesc = uint64_t(C::XBLK_BYTES >> 4);
-    int it = 0, acc_it = 0;
-    uint32_t buf = 0;
-    int n_total = ld_field(&phases[0].total), n_ku = ld_field(&phases[0].ku);
-    for (int p = 0; p < P; ++p) {
-      const int total = n_total, ku = n_ku;
-      if (p + 1 < P) {
-        n_total = ld_field(&phases[p + 1].total);
-        n_ku = ld_field(&phases[p + 1].ku);
-      }
-      const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
-      int kb = u0 % ku;
-      for (int u = u0; u < u1; ++u, ++it, kb = (kb + 1 == ku) ? 0 : kb + 1) {
-        const bool seg_start = (u == u0) || (kb == 0);
-        const bool seg_end = (u == u1 - 1) || (kb == ku - 1);
-        const int xs = it % C::XS;
-        if (seg_start) {
-          buf = acc_it % C::NACCBUF;
-          wait(&accempty[buf], ((acc_it / C::NACCBUF) & 1) ^ 1, kWhereMma, p);
+    {
+      int it = 0, acc_it = 0;
+      uint32_t buf = 0;
+      int n_total = ld_field(&phases[0].total), n_ku = ld_field(&phases[0].ku);
+      for (int p = 0; p < P; ++p) {
+        const int total = n_total, ku = n_ku;
+        if (p + 1 < P) {
+          n_total = ld_field(&phases[p + 1].total);
+          n_ku = ld_field(&phases[p + 1].ku);
         }
-        wait(&xfull[xs], (it / C::XS) & 1, kWhereMma, p);
-        const uint32_t d_tmem = tmem_base + C::ACC_COL0 + buf * C::ACC_COLS + j * MT;
-        const uint64_t slot_desc = ring_desc + kSlotDesc * xs;
-        uint32_t acc0 = seg_start ? 0u : 1u;
-#pragma unroll
-        for (int i = 0; i < NSUB / NUM_MMA_WARPS; ++i) {
-          const int sb = j + i * NUM_MMA_WARPS;
-          const int g = it * NSUB + sb;
-          const int slot = g % C::NASLOT;
-          wait(&afull[slot], (g / C::NASLOT) & 1, kWhereMma, p);
-          tc_fence_after();
-          if (!*abort_word) {
-            const uint32_t a_tmem = tmem_base + slot * A_COLS;
-            const uint64_t bdesc = slot_desc + kBlkDesc * sb;
-            mma_bf16_ts_warp(d_tmem, a_tmem, bdesc, idesc, acc0);
-            mma_bf16_ts_warp(d_tmem, a_tmem + 8, bdesc + 2, idesc, 1u);
-            mma_bf16_ts_warp(d_tmem, a_tmem + 16, bdesc + 4, idesc, 1u);
-            mma_bf16_ts_warp(d_tmem, a_tmem + 24, bdesc + 6, idesc, 1u);
+        const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
+        int kb = u0 % ku;
+        for (int u = u0; u < u1; ++u, ++it, kb = (kb + 1 == ku) ? 0 : kb + 1) {
+          const bool seg_start = (u == u0) || (kb == 0);
+          const bool seg_end = (u == u1 - 1) || (kb == ku - 1);
+          if (seg_start) {
+            buf = acc_it % C::NACCBUF;
+            wait(&accempty[buf], ((acc_it / C::NACCBUF) & 1) ^ 1, kWhereMma, p);
           }
-          acc0 = 1u;
-          tc_commit_warp(&aempty[slot]);
-        }
-        tc_commit_warp(&xfree[xs]);
-        if (seg_end) {
-          tc_commit_warp(&accfull[buf]);
-          ++acc_it;
+          const uint32_t d_tmem =
+              tmem_base + C::ACC_COL0 + buf * C::ACC_COLS + a_idx * MT + sl * C::SLICE_N;
+          uint32_t acc0 = seg_start ? 0u : 1u;
+#pragma unroll
+          for (int ch = 0; ch < C::NCH; ++ch) {
+            const int xseq = it * C::NCH + ch;
+            const int xs = xseq % C::XS;
+            wait(&xfull[xs], (xseq / C::XS) & 1, kWhereMma, p);
+            const uint64_t chunk_desc = ring_desc + kChunkDesc * xs;
+#pragma unroll
+            for (int i = 0; i < C::XCH / C::NACC; ++i) {
+              const int sbc = a_idx + i * C::NACC;       // sub-block within the chunk
+              const int g = it * NSUB + ch * C::XCH + sbc;
+              const int slot = g % C::NASLOT;
+              wait(&afull[slot], (g / C::NASLOT) & 1, kWhereMma, p);
+              tc_fence_after();
+              if (!*abort_word) {
+                const uint32_t a_tmem = tmem_base + slot * A_COLS;
+                const uint64_t bdesc = chunk_desc + kBlkDesc * sbc;
+                mma_bf16_ts_warp(d_tmem, a_tmem, bdesc, idesc, acc0);
+                mma_bf16_ts_warp(d_tmem, a_tmem + 8, bdesc + 2, idesc, 1u);
+                mma_bf16_ts_warp(d_tmem, a_tmem + 16, bdesc + 4, idesc, 1u);
+                mma_bf16_ts_warp(d_tmem, a_tmem + 24, bdesc + 6, idesc, 1u);
+              }
+              acc0 = 1u;
+              tc_commit_warp(&aempty[slot]);
+            }
+            if constexpr (!C::kXReleaseByA) tc_commit_warp(&xfree[xs]);
+          }
+          if (seg_end) {
+            tc_commit_warp(&accfull[buf]);
+            ++acc_it;
+          }
         }
       }
     }
@@ -498,8 +548,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
       }
       const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
       for (int u = u0; u < u1; ++u, ++it) {
-        const int s = it % NSTAGE;
-        wait(&full[s], (it / NSTAGE) & 1, kWhereDequant, p);
+        const int s = it % C::NSTAGE;
+        wait(&full[s], (it / C::NSTAGE) & 1, kWhereDequant, p);
         const uint32_t st = smem_u32(smem + s * BLK_BYTES);
         // this thread's packed words (SPG sub-blocks x 8 words) and its
         // scales / biases, then the stage goes back to the producer.  Group
@@ -563,11 +613,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
     }
   } else if (warp == WARP_X) {
     // ------------------------------------------------------------ x loads
-    // x for every unit of this CTA, in order, into the XS-slot ring: waits
-    // only for the MMAs to free a slot and, for a phase with a dependency,
-    // for every CTA to have signalled that phase complete (this CTA's own
-    // epilogues of it need no x beyond what is already loaded, so the wait
-    // always ends).
+    // x for every unit of this CTA, in order, in NCH chunks per unit into the
+    // XS-slot ring: waits only for the MMAs to free a slot and, for a phase
+    // with a dependency, for every CTA to have signalled that phase complete
+    // (this CTA's own epilogues of it need no x beyond what is already
+    // loaded, so the wait always ends).
     if (lane == 0) {
       int seq = 0;
       bool ok = true;
@@ -589,18 +639,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
           if (!wait_counter(rp.words + dep, G, abort_word, plan_abort, words, kWhereDep, p, 2 * limit_ns)) break;
           fence_proxy_async_global();   // x rows written by other CTAs' stores
         }
-        for (int u = u0; u < u1; ++u, ++seq) {
-          const int xs = seq % C::XS;
-          if (seq >= C::XS && !wait(&xfree[xs], ((seq / C::XS) - 1) & 1, kWhereXFree, p)) {
-            ok = false;
-            break;
-          }
+        for (int u = u0; ok && u < u1; ++u) {
           const int k0 = (u % ku) * UNIT_K;
-          uint8_t* dst = smem + C::OFF_XRING + xs * C::XSLOT_BYTES;
-          mbar_arrive_expect_tx(&xfull[xs], C::XSLOT_BYTES);
+#pragma unroll 1
+          for (int ch = 0; ch < C::NCH; ++ch, ++seq) {
+            const int xs = seq % C::XS;
+            if (seq >= C::XS) {
+              bool freed;
+              if constexpr (C::kXReleaseByA) {
+                // the slot's previous chunk: its last sub-block's A slot released
+                const int qq = seq - C::XS;
+                const int g = (qq / C::NCH) * NSUB + (qq % C::NCH) * C::XCH + C::XCH - 1;
+                freed = wait(&aempty[g % C::NASLOT], (g / C::NASLOT) & 1, kWhereXFree, p);
+              } else {
+                freed = wait(&xfree[xs], ((seq / C::XS) - 1) & 1, kWhereXFree, p);
+              }
+              if (!freed) {
+                ok = false;
+                break;
+              }
+            }
+            uint8_t* dst = smem + C::OFF_XRING + xs * C::XCHUNK_BYTES;
+            mbar_arrive_expect_tx(&xfull[xs], C::XCHUNK_BYTES);
 #pragma unroll
-          for (int b = 0; b < NSUB; ++b)
-            tma_load_2d(dst + b * C::XBLK_BYTES, &ph.tm_x, &xfull[xs], k0 + b * GS, 0);
+            for (int b = 0; b < C::XCH; ++b)
+              tma_load_2d(dst + b * C::XBLK_BYTES, &ph.tm_x, &xfull[xs], k0 + (ch * C::XCH + b) * GS, 0);
+          }
         }
       }
     }
@@ -637,35 +701,51 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
           const int kb1 = (t == t_last) ? (u1 - t * ku) : ku;
           const bool full_tile = (kb0 == 0 && kb1 == ku);
           const int c_lo = full_tile ? cta : owner_of(t * ku, total, G);
-          // a contributor checks (before its accumulator is ready) that the
-          // consumer of its previous partial in this slot has read it
-          int cons_seen = 0x7fffffff;
-          if (cta != c_lo && et == 0 && lastw[par] > 0) cons_seen = ld_acquire(consumed + 2 * cta + par);
+          const bool collect = !full_tile && cta == c_lo;
+          const int c_hi = collect ? owner_of(t * ku + ku - 1, total, G) : c_lo;
+          if (!full_tile && cta != c_lo) {
+            // contributor: the consumer of its previous partial in this slot
+            // must have read it before the slot is refilled (almost always
+            // already true)
+            bool gok = true;
+            if (et == 0 && lastw[par] > 0 && ld_acquire(consumed + 2 * cta + par) < lastw[par])
+              gok = wait_counter(consumed + 2 * cta + par, lastw[par], abort_word, plan_abort, words,
+                                 kWhereGuard, p, limit_ns);
+            if (!epi_all(gok && !*abort_word)) {
+              ok = false;
+              break;
+            }
+          }
           // c_lo: the contributors computed this tile's other parts first in
-          // their ranges, so their partials are collected (summed in CTA
-          // order) while this CTA's own MMAs for the tile still run; each slot
-          // is marked read at once
-          float psum[MT];
-          if (!full_tile && cta == c_lo) {
+          // their ranges, so their partials are ready (or nearly) while this
+          // CTA's own MMAs for the tile still run.  They are summed in CTA
+          // order; with one epilogue pass (MT <= 32) that happens here and
+          // each slot is marked read at once, otherwise pass by pass below.
+          float psum[C::kEarlyPartials ? MT : 1];
+          if (collect) {
+            if constexpr (C::kEarlyPartials) {
 #pragma unroll
-            for (int m = 0; m < MT; ++m) psum[m] = 0.f;
-            const int c_hi = owner_of(t * ku + ku - 1, total, G);
+              for (int m = 0; m < MT; ++m) psum[m] = 0.f;
+            }
             for (int c = c_lo + 1; ok && c <= c_hi; ++c) {
               if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
               const bool pok = wait_counter(ready + 2 * c + par, p + 1, abort_word, plan_abort, words,
                                             kWherePartial, p, limit_ns);
-              if (pok) {
-                const uint32_t* slot =
-                    reinterpret_cast<const uint32_t*>(rp.partials) + size_t(2 * c + par) * MT * BN;
+              if constexpr (C::kEarlyPartials) {
+                if (pok) {
+                  const uint32_t* slot =
+                      reinterpret_cast<const uint32_t*>(rp.partials) + size_t(2 * c + par) * MT * BN;
 #pragma unroll
-                for (int m = 0; m < MT; ++m) psum[m] += __uint_as_float(ld_relaxed_u32(slot + m * BN + r));
+                  for (int m = 0; m < MT; ++m) psum[m] += __uint_as_float(ld_relaxed_u32(slot + m * BN + r));
+                }
               }
-              // every thread has read the slot: its contributor may refill it
+              // every thread has read the slot (or, with several passes, seen
+              // its stamp): with one pass its contributor may refill it now
               if (!epi_all(pok && !*abort_word)) {
                 ok = false;
                 break;
               }
-              if (et == 0) st_release(consumed + 2 * c + par, p + 1);
+              if (C::kEarlyPartials && et == 0) st_release(consumed + 2 * c + par, p + 1);
             }
             if (!ok) break;
           }
@@ -676,66 +756,97 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             break;
           }
           tc_fence_after();
-          float acc[MT];
-          {
-            uint32_t rr[16];
+          const int n = t * BN + r;
+          uint32_t* const mine = reinterpret_cast<uint32_t*>(rp.partials) + size_t(2 * cta + par) * MT * BN;
+#pragma unroll 1
+          for (int c0 = 0; c0 < MT; c0 += C::EC) {
+            // c_lo with several passes: the contributors' partials of this
+            // pass, summed in CTA order (two contributors' loads in flight
+            // at a time), before the accumulator columns are read
+            float ps[C::EC];
+            if constexpr (!C::kEarlyPartials) {
+              if (collect) {
 #pragma unroll
-            for (int c = 0; c < MT; c += 16) {
+                for (int m = 0; m < C::EC; ++m) ps[m] = 0.f;
+                for (int c = c_lo + 1; c <= c_hi; ++c) {
+                  if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
+                  const uint32_t* sa = reinterpret_cast<const uint32_t*>(rp.partials) +
+                                       size_t(2 * c + par) * MT * BN + size_t(c0) * BN + r;
 #pragma unroll
-              for (int a = 0; a < NUM_MMA_WARPS; ++a) {
-                tmem_ld_32x32b_x16(lane_base + C::ACC_COL0 + buf * C::ACC_COLS + a * MT + c, rr);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                  acc[c + i] = (a == 0) ? __uint_as_float(rr[i]) : acc[c + i] + __uint_as_float(rr[i]);
+                  for (int m = 0; m < C::EC; ++m) ps[m] += __uint_as_float(ld_relaxed_u32(sa + m * BN));
+                }
               }
             }
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&accempty[buf]);
-          ++acc_it;
-
-          const int n = t * BN + r;
-          auto store_final = [&](const float (&v)[MT]) {
-            if (n >= N) return;
+            float acc[C::EC];
+            {
+              uint32_t rr[16];
+#pragma unroll
+              for (int c = 0; c < C::EC; c += 16) {
+#pragma unroll
+                for (int a = 0; a < C::NACC; ++a) {
+                  tmem_ld_32x32b_x16(lane_base + C::ACC_COL0 + buf * C::ACC_COLS + a * MT + c0 + c, rr);
+                  tmem_ld_wait();
+#pragma unroll
+                  for (int i = 0; i < 16; ++i)
+                    acc[c + i] = (a == 0) ? __uint_as_float(rr[i]) : acc[c + i] + __uint_as_float(rr[i]);
+                }
+              }
+            }
+            if (c0 + C::EC == MT) {
+              // the accumulator buffer is read: the MMAs may reuse it
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&accempty[buf]);
+            }
+            if (!full_tile && cta != c_lo) {
+              // contributor: this pass of its partial into its own slot
+#pragma unroll
+              for (int m = 0; m < C::EC; ++m)
+                st_relaxed_u32(mine + (c0 + m) * BN + r, __float_as_uint(acc[m]));
+              continue;
+            }
+            if (collect) {
+              // c_lo: its own accumulator plus the contributors' partial sum
+              if constexpr (C::kEarlyPartials) {
+#pragma unroll
+                for (int m = 0; m < C::EC; ++m) acc[m] += psum[m];
+              } else {
+#pragma unroll
+                for (int m = 0; m < C::EC; ++m) acc[m] += ps[m];
+              }
+            }
+            if (n >= N) continue;
             if (silu) {
               // rows interleaved in blocks of 32 (16 gate, then the 16 up rows
-              // of the same outputs): lanes 0-15 gate, 16-31 up
+              // of the same outputs): lanes 0-15 hold gate, 16-31 up.  Each
+              // lane swaps its rounded values with its partner (lane ^ 16);
+              // lanes 0-15 then finish the even tokens and 16-31 the odd ones,
+              // so all 32 lanes run the SiLU and its steps overlap across tokens.
               const int hcol = (n >> 5) * 16 + (lane & 15);
+              const bool lo = lane < 16;
+              uint32_t own[C::EC], oth[C::EC];
 #pragma unroll
-              for (int m = 0; m < MT; ++m) {
-                const uint32_t mine = __bfloat16_as_ushort(__float2bfloat16_rn(v[m]));
-                const uint32_t up = __shfl_down_sync(0xffffffffu, mine, 16);
-                if (lane < 16 && m < M)
-                  y[(size_t)m * ldy + hcol] = silu_mul_bits<false>(uint16_t(mine), uint16_t(up));
+              for (int m = 0; m < C::EC; ++m) own[m] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[m]));
+#pragma unroll
+              for (int m = 0; m < C::EC; ++m) oth[m] = __shfl_xor_sync(0xffffffffu, own[m], 16);
+#pragma unroll
+              for (int mp = 0; mp < C::EC / 2; ++mp) {
+                const int m = 2 * mp + (lo ? 0 : 1);
+                const uint32_t gbits = lo ? own[2 * mp] : oth[2 * mp + 1];
+                const uint32_t ubits = lo ? oth[2 * mp] : own[2 * mp + 1];
+                const uint16_t h = silu_mul_bits<false>(uint16_t(gbits), uint16_t(ubits));
+                if (c0 + m < M) y[(size_t)(c0 + m) * ldy + hcol] = h;
               }
             } else {
-              uint16_t* yp = y + n;
+              uint16_t* yp = y + (size_t)c0 * ldy + n;
 #pragma unroll
-              for (int m = 0; m < MT; ++m, yp += ldy)
-                if (m < M) *yp = __bfloat16_as_ushort(__float2bfloat16_rn(v[m]));
+              for (int m = 0; m < C::EC; ++m, yp += ldy)
+                if (c0 + m < M) *yp = __bfloat16_as_ushort(__float2bfloat16_rn(acc[m]));
             }
-          };
-          if (full_tile) {
-            store_final(acc);
-            continue;
           }
+          ++acc_it;
+          if (full_tile) continue;
           if (cta != c_lo) {
-            // contributor: its partial goes to its own slot once the slot's
-            // previous partial was read (almost always already true), then
-            // the slot is stamped with this phase
-            bool gok = true;
-            if (et == 0 && lastw[par] > 0 && cons_seen < lastw[par])
-              gok = wait_counter(consumed + 2 * cta + par, lastw[par], abort_word, plan_abort, words,
-                                 kWhereGuard, p, limit_ns);
-            if (!epi_all(gok && !*abort_word)) {
-              ok = false;
-              break;
-            }
-            uint32_t* mine = reinterpret_cast<uint32_t*>(rp.partials) + size_t(2 * cta + par) * MT * BN;
-#pragma unroll
-            for (int m = 0; m < MT; ++m) st_relaxed_u32(mine + m * BN + r, __float_as_uint(acc[m]));
             // the barrier orders every thread's partial stores before the
             // stamp's release (cumulativity)
             if (!epi_all(!*abort_word)) {
@@ -748,10 +859,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             lastw[par] = p + 1;
             continue;
           }
-          // c_lo: its own accumulator plus the contributors' partial sum
-#pragma unroll
-          for (int m = 0; m < MT; ++m) acc[m] += psum[m];
-          store_final(acc);
+          if constexpr (!C::kEarlyPartials) {
+            // every thread has read every contributor's slot: mark them read
+            if (!epi_all(!*abort_word)) {
+              ok = false;
+              break;
+            }
+            if (et == 0)
+              for (int c = c_lo + 1; c <= c_hi; ++c)
+                if (unit_begin(c, total, G) != unit_begin(c + 1, total, G))
+                  st_release(consumed + 2 * c + par, p + 1);
+          }
         }
       }
       if (!ok) break;
@@ -915,7 +1033,8 @@ inline int check_header(const void* plan_host, Header* out) {
   if (!plan_host) return DFL_ERR_NULL_POINTER;
   std::memcpy(out, plan_host, sizeof(Header));
   if (out->magic != kPlanMagic || out->version != kPlanVersion || out->n_phases < 1 ||
-      out->n_phases > kMaxPhases || (out->mt != 16 && out->mt != 32) || out->grid < 1 ||
+      out->n_phases > kMaxPhases ||
+      (out->mt != 16 && out->mt != 32 && out->mt != 64 && out->mt != 128) || out->grid < 1 ||
       out->grid > kMaxGrid || out->wait_limit_ns == 0 || out->wait_limit_ns > kWaitLimitNs)
     return DFL_ERR_BAD_SHAPE;
   return DFL_OK;
@@ -970,7 +1089,7 @@ extern "C" int dfl_qmm_plan_encode(const dfl_qmm_phase* phases, int n_phases, vo
   int max_m = 0, flags_or = 0;
   for (int p = 0; p < n_phases; ++p) {
     const dfl_qmm_phase& q = phases[p];
-    if (q.M < 1 || q.M > 32 || q.K < 64 || q.K % 64 != 0 || q.N < 1 || q.N > (1 << 24))
+    if (q.M < 1 || q.M > kMaxRows || q.K < 64 || q.K % 64 != 0 || q.N < 1 || q.N > (1 << 24))
       return DFL_ERR_BAD_SHAPE;
     if ((q.flags & ~(kPhaseSilu | kPhaseSubnormal)) != 0) return DFL_ERR_BAD_SHAPE;
     const bool silu = (q.flags & kPhaseSilu) != 0;
@@ -986,7 +1105,7 @@ extern "C" int dfl_qmm_plan_encode(const dfl_qmm_phase* phases, int n_phases, vo
     max_m = q.M > max_m ? q.M : max_m;
     flags_or |= q.flags;
   }
-  const int mt = max_m <= 16 ? 16 : 32;
+  const int mt = max_m <= 16 ? 16 : max_m <= 32 ? 32 : max_m <= 64 ? 64 : 128;
   uint8_t* out = static_cast<uint8_t*>(plan_host);
   Header h;
   std::memset(&h, 0, sizeof(h));
@@ -1045,8 +1164,12 @@ extern "C" int dfl_qmm_plan_run(const void* plan_host, const void* plan_dev, voi
   if (st != DFL_OK) return st;
   if (h.grid > sms) return DFL_ERR_UNSUPPORTED;   // encoded for a larger device
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (h.mt == 16) return plan::launch<16>(h, plan_dev, workspace, dev, s);
-  return plan::launch<32>(h, plan_dev, workspace, dev, s);
+  switch (h.mt) {
+    case 16: return plan::launch<16>(h, plan_dev, workspace, dev, s);
+    case 32: return plan::launch<32>(h, plan_dev, workspace, dev, s);
+    case 64: return plan::launch<64>(h, plan_dev, workspace, dev, s);
+    default: return plan::launch<128>(h, plan_dev, workspace, dev, s);
+  }
 }
 
 extern "C" int dfl_qmm_plan_set_test_fault(void* plan_host, int skip_partial_cta,

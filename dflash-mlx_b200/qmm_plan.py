@@ -29,6 +29,7 @@ from ._runtime import as_u32_bits, require_cuda, stream_ptr
 
 PHASE_SILU = 1
 PHASE_SUBNORMAL = 2
+MAX_ROWS = 128          # token rows per phase (one token tile of the plan kernel)
 SUBNORMAL_SCALE_LIMIT = 2.0 ** -5
 
 
@@ -125,8 +126,9 @@ class ProjectionPlan:
                     raise ValueError("every tensor of a plan must be on one device")
             w = ph.weight
             m = int(ph.x.shape[0])
-            if not 1 <= m <= 32:
-                raise ValueError(f"phase {i}: {m} rows (a plan takes 1..32 rows per phase)")
+            if not 1 <= m <= MAX_ROWS:
+                raise ValueError(f"phase {i}: {m} rows (a plan takes 1..{MAX_ROWS} rows per phase; "
+                                 "split more rows into one phase per token tile)")
             ldx = _check_rows(ph.x, f"phase {i} x", w.k)
             n_out = w.n // 2 if ph.silu else w.n
             ldy = _check_rows(ph.y, f"phase {i} y", n_out)
@@ -188,7 +190,8 @@ class ProjectionPlan:
 
 def qmm_tiled(x: torch.Tensor, weight: TiledWeight, out: Optional[torch.Tensor] = None, *,
               silu: bool = False) -> torch.Tensor:
-    """``x [M, K] @ W.T`` (or the fused SiLU*up) through a one-phase plan, M <= 32."""
+    """``x [M, K] @ W.T`` (or the fused SiLU*up) through a plan with one
+    phase per token tile of up to 128 rows."""
     require_cuda(x, "x")
     if x.dtype != torch.bfloat16:
         raise NotImplementedError("the plan kernel takes bfloat16 activations")
@@ -199,5 +202,6 @@ def qmm_tiled(x: torch.Tensor, weight: TiledWeight, out: Optional[torch.Tensor] 
         out = torch.empty((m, n_out), dtype=torch.bfloat16, device=x.device)
     # the plan's device buffers are freed to torch's stream-ordered allocator
     # after the launch is queued, so they are not reused before it ran
-    ProjectionPlan([PlanPhase(x, weight, out, silu=silu)]).run()
+    ProjectionPlan([PlanPhase(x[r0:r0 + MAX_ROWS], weight, out[r0:r0 + MAX_ROWS], silu=silu)
+                    for r0 in range(0, m, MAX_ROWS)]).run()
     return out

@@ -37,7 +37,7 @@ import torch
 from . import lm_head as _lm
 from .kernels import gated_delta_kernel_with_tape, tape_replay_
 from .moe import QuantWeight, silu_mul
-from .qmm_plan import PlanPhase, ProjectionPlan, tile_weight
+from .qmm_plan import MAX_ROWS, PlanPhase, ProjectionPlan, tile_weight
 from .verify_qmm import gate_up_silu, qmm_w4g64, repack_pairs
 
 
@@ -93,12 +93,13 @@ class StackShape:
         return [("qkv", self.q_out + 2 * self.kv_out, h), ("o", h, self.q_out),
                 ("gate_up", 2 * self.inter, h), ("down", h, self.inter)]
 
-    def qmm_bytes_per_step(self, requests: int, packed: bool, silu_fused: bool = False) -> int:
+    def qmm_bytes_per_step(self, requests: int, per_launch: int = 1, silu_fused: bool = False) -> int:
         """Algorithmic bytes of the projection stack for ``requests`` requests on
-        one GPU: weights (+ scales, biases) once per launch, i.e. once per pair
-        of requests when their rows share launches (32 rows per launch), and
-        each request's activations."""
-        launches = (requests + 1) // 2 if packed else requests
+        one GPU: weights (+ scales, biases) once per group of ``per_launch``
+        requests whose rows share each launch or plan phase (2 for the
+        per-call kernel's 32-row tile, 8 for the plan kernel's 128-row tile),
+        and each request's activations."""
+        launches = (requests + per_launch - 1) // per_launch
         total = 0
         for name, n, k in self.launches():
             n_out = n // 2 if (silu_fused and name == "gate_up") else n
@@ -116,6 +117,7 @@ class StackShape:
         return total * self.layers
 
     def qmm_flops_per_request(self) -> int:
+        """Multiply-add FLOPs of one request's projection stack (16 rows)."""
         return 2 * self.block * sum(n * k for _, n, k in self.projections()) * self.layers
 
 
@@ -147,6 +149,9 @@ class VerifyStep:
         # writes silu(gate) * up
         self.fuse_silu = bool(fuse_silu)
         self.pack_requests = bool(pack_requests)
+        # requests whose rows share one read of every weight
+        self.requests_per_launch = (MAX_ROWS // (shape or StackShape()).block if weight_layout == "tiled"
+                                    else 2 if self.pack_requests else 1)
         self.shape = shape or StackShape()
         self.requests = int(requests)
         self.rank, self.world, self.group = rank, world, group
@@ -211,8 +216,10 @@ class VerifyStep:
         self.plan = self._build_plan(qmm_deps) if weight_layout == "tiled" else None
 
     def _build_plan(self, deps: str = "dataflow") -> ProjectionPlan:
-        """The whole projection stack as one plan, requests in groups of two
-        (32 rows per phase).  Every layer writes its own output buffers.
+        """The whole projection stack as one plan, requests in groups of up to
+        eight (128 rows per phase: one token tile, so the group's requests
+        share one read of every weight).  Every layer writes its own output
+        buffers.
 
         ``deps="dataflow"``: a projection waits on the device for exactly the
         projections whose outputs it reads -- down for gate|up's SiLU output,
@@ -226,7 +233,7 @@ class VerifyStep:
             raise ValueError(f"unknown dependency mode {deps!r}")
         sh = self.shape
         rows = self.requests * sh.block
-        groups = [(g0, min(rows, g0 + 2 * sh.block)) for g0 in range(0, rows, 2 * sh.block)]
+        groups = [(g0, min(rows, g0 + MAX_ROWS)) for g0 in range(0, rows, MAX_ROWS)]
 
         def buf(m, n):
             return torch.empty((m, n), dtype=torch.bfloat16, device=self.dev)

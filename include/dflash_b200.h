@@ -185,7 +185,7 @@ int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q, const u
  * projections, it is done once per weight.
  *
  * A plan is an array of phases run in order.  Phase p computes
- * y = x @ dequant(W)^T for M <= 32 rows (bf16 x [M, K] with row stride ldx,
+ * y = x @ dequant(W)^T for M <= 128 rows (bf16 x [M, K] with row stride ldx,
  * ldx % 8 == 0, x 16-byte aligned; y [M, N] with row stride ldy) or, with
  * DFL_PHASE_SILU, h [M, N/2] = silu(gate) * up over gate/up rows
  * interleaved in blocks of 16 (N % 32 == 0, as dfl_verify_qmm_w4g64_silu).
@@ -193,8 +193,11 @@ int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q, const u
  * dep = q (an earlier phase) makes the phase read x only after every output
  * of phase q is written (x may be phase q's y); dep = -1 reads x at once.
  * Results equal dfl_verify_qmm_w4g64 on the same weights up to fp32
- * summation order; each phase's split over the SMs depends only on its own
- * shape, so a phase gives the same bits in any plan.
+ * summation order.  The plan's token tile (16, 32, 64 or 128 rows) follows
+ * its largest M, and every phase runs at that tile, so all rows of a phase
+ * share one read of its weights; more rows than 128 take one phase per
+ * 128-row slice.  Each phase's split over the SMs depends only on its own
+ * shape, so a phase gives the same bits in any plan with the same tile.
  *
  * dfl_qmm_plan_encode writes the plan for the current device into a host
  * buffer of dfl_qmm_plan_bytes(n_phases) bytes; copy those bytes to a
@@ -209,7 +212,7 @@ int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q, const u
  * workspace must not be shared by runs that may overlap.  No counterpart in
  * the reference (it launches one Metal kernel per projection through
  * VerifyQuantizedLinear, dflash_mlx/verify_linear.py:266-286); it replaces
- * that sequence of calls for a block of 16 or 32 verify rows.
+ * that sequence of calls for the verify rows of one or more requests.
  * ---------------------------------------------------------------------- */
 #define DFL_PHASE_SILU 1
 #define DFL_PHASE_SUBNORMAL 2

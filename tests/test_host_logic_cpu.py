@@ -268,14 +268,16 @@ def test_stack_bytes_per_layer_match_launch_shapes(pkg):
     assert expect == 193_921_024
     one = StackShape(layers=1)
     assert one.qmm_bytes_per_request(silu_fused=True) == expect
-    assert one.qmm_bytes_per_step(1, packed=True, silu_fused=True) == expect
-    assert StackShape().qmm_bytes_per_step(1, packed=True, silu_fused=True) == 64 * expect
+    assert one.qmm_bytes_per_step(1, 2, silu_fused=True) == expect
+    assert StackShape().qmm_bytes_per_step(1, 8, silu_fused=True) == 64 * expect
 
 
-@pytest.mark.parametrize("requests", [1, 2, 3, 8])
+@pytest.mark.parametrize("requests", [1, 2, 3, 8, 9, 64])
 def test_stack_bytes_count_weights_once_per_shared_launch(pkg, requests):
-    """Two requests' rows share each launch when packed, so weights are read
-    ceil(requests / 2) times; activations are per request either way."""
+    """Requests whose rows share each launch read the weights once per group:
+    ceil(requests / 2) times with the per-call kernel's 32-row tile, ceil(
+    requests / 8) times with the plan's 128-row tile; activations are per
+    request either way."""
     from dflash_mlx_b200.verify_step import StackShape
 
     sh = StackShape(layers=2)
@@ -283,9 +285,10 @@ def test_stack_bytes_count_weights_once_per_shared_launch(pkg, requests):
     acts = sum(2 * sh.block * (k + (n // 2 if name == "gate_up" else n))
                for name, n, k in sh.launches()) * sh.layers
     weights = per_req - acts
-    assert sh.qmm_bytes_per_step(requests, packed=False, silu_fused=True) == requests * per_req
-    assert (sh.qmm_bytes_per_step(requests, packed=True, silu_fused=True)
-            == (requests + 1) // 2 * weights + requests * acts)
+    assert sh.qmm_bytes_per_step(requests, 1, silu_fused=True) == requests * per_req
+    for per_launch in (2, 8):
+        assert (sh.qmm_bytes_per_step(requests, per_launch, silu_fused=True)
+                == -(-requests // per_launch) * weights + requests * acts)
 
 
 def test_device_error_clears_cached_workspaces(pkg, monkeypatch):
@@ -660,8 +663,8 @@ def test_verify_step_host_path(pkg, monkeypatch, layout, fuse_silu, pack):
 def test_verify_step_plan_host_path(pkg, monkeypatch):
     """Tiled layout on CPU, library replaced by a recorder: set-up repacks
     every projection once into the tiled layout and encodes one plan whose
-    phases are the stack's projections per group of two requests, each
-    waiting for the previous phase of its group (q|k|v -> o -> gate|up + SiLU
+    phases are the stack's projections per group of up to eight requests
+    (one 128-row token tile), each waiting for the previous phase of its group (q|k|v -> o -> gate|up + SiLU
     -> down -> next layer's q|k|v); the qmm stack is one plan launch."""
     import contextlib
 
@@ -708,7 +711,7 @@ def test_verify_step_plan_host_path(pkg, monkeypatch):
         verify_step.VerifyStep("cpu", requests=1, shape=shape, weight_layout="tiled", fuse_silu=False)
     calls.clear()
     encoded.clear()
-    step = verify_step.VerifyStep("cpu", requests=3, shape=shape, weight_layout="tiled", fuse_silu=True)
+    step = verify_step.VerifyStep("cpu", requests=10, shape=shape, weight_layout="tiled", fuse_silu=True)
     assert calls.count("dfl_repack_w4_tiled") == 4 * shape.layers
     assert calls.count("dfl_qmm_plan_encode") == 1
     assert step.layers is None and len(step.tiled) == shape.layers
@@ -716,7 +719,7 @@ def test_verify_step_plan_host_path(pkg, monkeypatch):
     want = []
     last = {0: -1, 1: -1}
     for _ in range(shape.layers):
-        for g, m in ((0, 32), (1, 16)):       # 3 requests: rows 0-31 and 32-47
+        for g, m in ((0, 128), (1, 32)):      # 10 requests: rows 0-127 and 128-159
             base = len(want)
             # dataflow: q|k|v waits for the group's previous down (its input),
             # down for gate|up's SiLU output; o and gate|up read stand-ins

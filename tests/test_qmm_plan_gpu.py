@@ -4,8 +4,9 @@
   weights back) with the subnormal and the general dequantiser;
 * one-phase plans against the oracle (``oracle/qmm.py``, the reference's
   ``nib * s + b`` rounded to bf16, fp32 accumulation) on the benchmark's
-  shapes, ragged N and K, 1..32 rows, both dequantisers: elementwise
-  ``|y - ref| <= 1e-2 + 2e-2 |ref|``;
+  shapes, ragged N and K, 1..128 rows (every token tile: 16, 32, 64, 128),
+  both dequantisers: elementwise ``|y - ref| <= 1e-2 + 2e-2 |ref|``; more
+  than 128 rows as one phase per 128-row slice;
 * the fused SiLU phase equals ``silu_mul`` of the plain phase bit for bit;
 * a decoder layer as one plan (q|k|v, o, gate|up + SiLU, down reading the
   SiLU output through a dependency) equals the same phases run as separate
@@ -44,8 +45,9 @@ def _tiled(pkg, dev, w_q, s, b, subnormal=None):
                            subnormal=subnormal)
 
 
+@pytest.mark.parametrize("rows", [32, 128])
 @pytest.mark.parametrize("subnormal", [True, False])
-def test_tiled_dequant_is_exact(pkg, dev, subnormal):
+def test_tiled_dequant_is_exact(pkg, dev, subnormal, rows):
     # one-hot activations select single dequantised weights: y[m, n] = w[n, k_m]
     rng = np.random.default_rng(31)
     k, n = 1536, 320          # 3 K units, 3 tiles (the last one ragged)
@@ -54,9 +56,9 @@ def test_tiled_dequant_is_exact(pkg, dev, subnormal):
     assert tw.subnormal == subnormal
     w = oqmm.dequantize(w_q, s, b)
     for rep in range(2):
-        cols = rng.choice(k, size=32, replace=False)
-        xf = np.zeros((32, k), dtype=np.float32)
-        xf[np.arange(32), cols] = 1.0
+        cols = rng.choice(k, size=rows, replace=False)
+        xf = np.zeros((rows, k), dtype=np.float32)
+        xf[np.arange(rows), cols] = 1.0
         y = pkg.qmm_tiled(to_dev_bf16(obf16.from_f32(xf), dev), tw)
         assert np.array_equal(obf16.to_f32(bf16_to_np_bits(y)), w[:, cols].T)
     from dflash_mlx_b200 import _lib
@@ -80,6 +82,13 @@ SHAPES = [
     ("ragged", 17, 1600, 384),      # K % 512 != 0, N % 128 != 0, 32-row tile
     ("m32", 32, 5120, 1024),
     ("m5", 5, 640, 200),
+    # several requests' rows in one token tile (64 / 128 rows: split-K
+    # partials summed pass by pass, one or two accumulators)
+    ("m48", 48, 5120, 1024),
+    ("m64_qkv", 64, 5120, 8192),
+    ("m100_ragged", 100, 1600, 384),
+    ("m128_o", 128, 6144, 5120),
+    ("m128_down", 128, 17408, 5120),
 ]
 
 
@@ -120,11 +129,12 @@ def _gate_up(rng, inter, k):
     return (gq, gs, gb), (uq, us, ub), (inter16(gq, uq), inter16(gs, us), inter16(gb, ub))
 
 
-def test_silu_phase_equals_silu_of_plain_phase(pkg, dev):
+@pytest.mark.parametrize("m", [16, 128])
+def test_silu_phase_equals_silu_of_plain_phase(pkg, dev, m):
     import torch
 
     rng = np.random.default_rng(9)
-    inter, k, m = 1024, 2048, 16
+    inter, k = 1024, 2048
     g, u, gu = _gate_up(rng, inter, k)
     x = to_dev_bf16(oqmm.synth_x(rng, m, k), dev)
     tw = _tiled(pkg, dev, *gu)
@@ -166,11 +176,12 @@ def _layer_phases(pkg, tw, x, attn, bufs, first=0):
             P(bufs["h"], tw["down"], bufs["down"], dep=first + 2)]
 
 
-def test_layer_plan_equals_separate_plans_and_oracle(pkg, dev):
+@pytest.mark.parametrize("m", [16, 128])
+def test_layer_plan_equals_separate_plans_and_oracle(pkg, dev, m):
     import torch
 
     rng = np.random.default_rng(12)
-    ws, tw, x, attn, bufs = _layer(pkg, dev, rng)
+    ws, tw, x, attn, bufs = _layer(pkg, dev, rng, m=m)
     plan = pkg.ProjectionPlan(_layer_phases(pkg, tw, x, attn, bufs))
     plan.run()
     got = {k: v.clone() for k, v in bufs.items()}
@@ -190,6 +201,16 @@ def test_layer_plan_equals_separate_plans_and_oracle(pkg, dev):
     assert int(plan.workspace[:COUNTER_BYTES].count_nonzero()) == 0
     from dflash_mlx_b200 import _lib
     assert _lib.device_error() == 0
+
+
+def test_rows_beyond_one_tile_run_as_slices(pkg, dev):
+    """200 rows: two phases (128 + 72 rows) of one plan at the 128-row tile."""
+    rng = np.random.default_rng(210)
+    m, k, n = 200, 5120, 1024
+    w_q, s, b = oqmm.synth_weights(rng, n, k)
+    x = oqmm.synth_x(rng, m, k)
+    y = pkg.qmm_tiled(to_dev_bf16(x, dev), _tiled(pkg, dev, w_q, s, b))
+    _assert_close(bf16_to_np_bits(y), oqmm.qmm(x, w_q, s, b, accum=np.float32), "200 rows")
 
 
 def test_chain_reads_previous_outputs(pkg, dev):
@@ -263,8 +284,8 @@ def test_plan_rejects_bad_phases(pkg, dev):
     with pytest.raises(ValueError):
         pkg.ProjectionPlan([pkg.PlanPhase(x, tw, y, dep=0)])            # dep on itself
     with pytest.raises(ValueError):
-        pkg.ProjectionPlan([pkg.PlanPhase(torch.zeros((33, 512), dtype=torch.bfloat16, device=dev),
-                                          tw, torch.zeros((33, 256), dtype=torch.bfloat16, device=dev))])
+        pkg.ProjectionPlan([pkg.PlanPhase(torch.zeros((129, 512), dtype=torch.bfloat16, device=dev),
+                                          tw, torch.zeros((129, 256), dtype=torch.bfloat16, device=dev))])
     with pytest.raises(ValueError):
         pkg.ProjectionPlan([pkg.PlanPhase(x, tw, y[:, :128])])          # wrong output width
     with pytest.raises(ValueError):
