@@ -213,13 +213,15 @@ def test_rows_beyond_one_tile_run_as_slices(pkg, dev):
     _assert_close(bf16_to_np_bits(y), oqmm.qmm(x, w_q, s, b, accum=np.float32), "200 rows")
 
 
-def test_chain_reads_previous_outputs(pkg, dev):
+@pytest.mark.parametrize("dims", [[2048, 1024, 3072, 512, 2048],
+                                  [1024, 1088, 704, 2048]])      # ragged tiles per 512-column group
+def test_chain_reads_previous_outputs(pkg, dev, dims):
     """Phase i reads phase i-1's output; a result is only right if every
-    phase waited for the whole of the previous one."""
+    phase waited for the whole of the previous one (ragged last tiles
+    included)."""
     import torch
 
     rng = np.random.default_rng(44)
-    dims = [2048, 1024, 3072, 512, 2048]
     tws, raw = [], []
     for i in range(len(dims) - 1):
         w_q, s, b = oqmm.synth_weights(rng, dims[i + 1], dims[i])
@@ -240,6 +242,33 @@ def test_chain_reads_previous_outputs(pkg, dev):
         for i, (w_q, s, b) in enumerate(raw):
             _assert_close(bf16_to_np_bits(outs[i]), oqmm.qmm(xb, w_q, s, b, accum=np.float32), f"link {i}")
             xb = bf16_to_np_bits(outs[i])
+        assert int(plan.workspace[:COUNTER_BYTES].count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("m", [16, 128])
+def test_down_waits_for_the_silu_columns_it_reads(pkg, dev, m):
+    """gate|up + SiLU (1088 outputs: 17 tiles, the last one ragged) then
+    down reading its output through a dependency: the SiLU output equals a
+    one-phase plan's bit for bit and down matches the oracle, run twice."""
+    import torch
+
+    rng = np.random.default_rng(515)
+    hidden, inter = 1024, 1088
+    _, _, gu = _gate_up(rng, inter, hidden)
+    down = oqmm.synth_weights(rng, hidden, inter)
+    tgu, tdown = _tiled(pkg, dev, *gu), _tiled(pkg, dev, *down)
+    x = oqmm.synth_x(rng, m, hidden)
+    xd = to_dev_bf16(x, dev)
+    h = torch.empty((m, inter), dtype=torch.bfloat16, device=dev)
+    y = torch.empty((m, hidden), dtype=torch.bfloat16, device=dev)
+    plan = pkg.ProjectionPlan([pkg.PlanPhase(xd, tgu, h, silu=True), pkg.PlanPhase(h, tdown, y, dep=0)])
+    for _ in range(2):
+        h.fill_(float("nan"))
+        y.fill_(float("nan"))
+        plan.run()
+        torch.cuda.synchronize(dev)
+        assert torch.equal(h, pkg.qmm_tiled(xd, tgu, silu=True))
+        _assert_close(bf16_to_np_bits(y), oqmm.qmm(bf16_to_np_bits(h), *down, accum=np.float32), "down")
         assert int(plan.workspace[:COUNTER_BYTES].count_nonzero()) == 0
 
 
