@@ -386,6 +386,11 @@ def run_ours(args):
         t_chain = float(tc[0])
         step.plan = headline_plan
         del chained
+    # batched requests (every rank, same collectives): 8 requests per GPU, and
+    # a fixed global batch of 64 split over the GPUs (strong scaling)
+    batched = None
+    if step.plan is not None and not args.no_batched:
+        batched = measure_batched(step, args, dev, world, rank, group)
     # roofline of the dominant kernel (the int4 verify qmm)
     peak, peak_kind = _peaks()
     plan = step.plan is not None
@@ -460,6 +465,8 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if batched is not None:
+            line["config"].update(batched)
         if world == 1 and not args.no_extra_configs:
             # the other configurations, measured in this process after the
             # timed loop (each in its own CUDA graph, CUDA events)
@@ -472,6 +479,77 @@ def run_ours(args):
         step.graphs = None
         dist.destroy_process_group()
     return 0
+
+
+def measure_batched(step, args, dev, world: int, rank: int, group) -> dict:
+    """Verify steps with several requests per GPU, on every rank (the same
+    collectives in the same order), reusing ``step``'s weights:
+
+    * ``batched_b8``: 8 requests per GPU (one 128-row token tile: the 8
+      requests share one read of every weight), whole-job requests/s;
+    * ``strong_b64``: a fixed global batch of 64 requests split over the
+      GPUs (64 / N per GPU), requests/s -- v_N / (N v_1) is the strong-scaling
+      efficiency.
+
+    Each: its own CUDA graphs, P = 0.88 verify ids from its own posterior,
+    3 warm-up steps, then min(steps, 5) steps between CUDA events; the step
+    time and the qmm stack's time are maxima over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from dflash_mlx_b200.verify_step import VerifyStep
+
+    sh = step.shape
+    cases = [("batched_b8", 8)]
+    if args.strong_batch % world == 0:
+        cases.append((f"strong_b{args.strong_batch}", args.strong_batch // world))
+    steps = max(1, min(args.steps, 5))
+    tflops = _peak_tflops()
+    peak, _ = _peaks()
+    out = {}
+    for name, b in cases:
+        s2 = VerifyStep(dev, requests=b, shape=sh, rank=rank, world=world, group=group,
+                        weight_layout=step.weight_layout, fuse_silu=step.fuse_silu,
+                        qmm_deps=step.qmm_deps, share_weights=step)
+        gen = torch.Generator(device=dev).manual_seed(300 + rank)
+        s2.x.copy_(torch.randn(s2.x.shape, generator=gen, device=dev).to(torch.bfloat16))
+        s2.verify_ids.copy_(torch.randint(0, sh.vocab, s2.verify_ids.shape, generator=gen, device=dev,
+                                          dtype=torch.int64).to(torch.int32))
+        s2.capture()
+        s2.run_step()
+        torch.cuda.synchronize(dev)
+        s2.verify_ids.copy_(synth_verify_ids(s2.posterior.clone(), sh.vocab, 0.88, gen))
+        for _ in range(3):
+            s2.run_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        evq = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(steps)]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s2.stream)
+        for i in range(steps):
+            s2.run_step(evq[i])
+        e1.record(s2.stream)
+        torch.cuda.synchronize(dev)
+        tt = torch.tensor([e0.elapsed_time(e1) * 1e-3, sum(a.elapsed_time(c) for a, c in evq) * 1e-3],
+                          dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_step, t_qmm = float(tt[0]) / steps, float(tt[1]) / steps
+        by = sh.qmm_bytes_per_step(b, s2.requests_per_launch, silu_fused=s2.fuse_silu)
+        fl = b * sh.qmm_flops_per_request()
+        out[name] = {"requests_per_gpu": b, "global_requests": b * world,
+                     "requests_per_s": world * b / t_step, "ms_per_step": t_step * 1e3,
+                     "qmm_ms_per_step": t_qmm * 1e3, "qmm_tflops": fl / t_qmm / 1e12,
+                     "qmm_tensor_frac": fl / t_qmm / 1e12 / tflops, "qmm_hbm_frac": by / t_qmm / 1e9 / peak,
+                     "mean_acceptance": float(s2.acceptance.float().mean()), "steps": steps}
+        s2.graphs = None
+        del s2
+        torch.cuda.empty_cache()
+    out["batched_note"] = ("measured after the timed loop on every rank; requests_per_s is whole-job "
+                           "(all GPUs); fractions of the measured cuBLAS bf16 burst / HBM copy peaks")
+    return out
 
 
 def synth_verify_ids(posterior, vocab: int, p_match: float, gen):
@@ -773,6 +851,11 @@ def main():
     ap.add_argument("--no-fuse-silu", action="store_true",
                     help="run SiLU*up as its own launch after the gate|up projection")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true",
+                    help="skip the batched-request measurements (8 per GPU, and a fixed global "
+                         "batch split over the GPUs) carried in the line's config")
+    ap.add_argument("--strong-batch", type=int, default=64,
+                    help="global batch of the strong-scaling measurement (split over the GPUs)")
     ap.add_argument("--no-extra-configs", action="store_true",
                     help="skip the config 0 / 2 / 4 and lm_head B=16/128 measurements that the "
                          "one-GPU line carries in its config")

@@ -135,7 +135,10 @@ class VerifyStep:
     def __init__(self, device: torch.device, *, requests: int = 1, shape: Optional[StackShape] = None,
                  rank: int = 0, world: int = 1, group=None, seed: int = 0,
                  weight_layout: str = "mlx", fuse_silu: bool = False, pack_requests: bool = True,
-                 qmm_deps: str = "dataflow"):
+                 qmm_deps: str = "dataflow", share_weights: Optional["VerifyStep"] = None):
+        """``share_weights``: another step on the same device, rank and shape
+        whose decoder and lm_head weights this one reuses (a different number
+        of requests over the same model)."""
         self.dev = torch.device(device)
         if weight_layout not in ("mlx", "pairs", "tiled"):
             raise ValueError(f"unknown weight layout {weight_layout!r}")
@@ -156,12 +159,21 @@ class VerifyStep:
         self.requests = int(requests)
         self.rank, self.world, self.group = rank, world, group
         sh = self.shape
-        gen = torch.Generator(device=self.dev).manual_seed(seed)
-        # replicated decoder weights (identical on every rank: same seed), in
-        # the fused launch layout (q|k|v and gate|up concatenated along N)
-        self.layers = [{name: _quant_weight(gen, self.dev, n, k) for name, n, k in sh.launches()}
-                       for _ in range(sh.layers)]
-        if weight_layout == "pairs":
+        if share_weights is not None:
+            o = share_weights
+            if (o.dev != self.dev or o.shape != sh or o.weight_layout != weight_layout or o.rank != rank
+                    or o.world != world):
+                raise ValueError("share_weights needs a step on the same device, shape, layout and rank")
+            self.layers, self.tiled = o.layers, getattr(o, "tiled", None)
+        else:
+            gen = torch.Generator(device=self.dev).manual_seed(seed)
+            # replicated decoder weights (identical on every rank: same seed), in
+            # the fused launch layout (q|k|v and gate|up concatenated along N)
+            self.layers = [{name: _quant_weight(gen, self.dev, n, k) for name, n, k in sh.launches()}
+                           for _ in range(sh.layers)]
+        if share_weights is not None:
+            pass
+        elif weight_layout == "pairs":
             # load-time repack into the pair-packed nibble order (in place)
             for lw in self.layers:
                 for qw in lw.values():
@@ -177,8 +189,11 @@ class VerifyStep:
             self.layers = None
         # this rank's vocabulary shard of the bf16 lm_head, N(0, 0.02)
         self.v_begin, v_len = _lm.vocab_shard(sh.vocab, rank, world)
-        wgen = torch.Generator(device=self.dev).manual_seed(seed + 1000 + rank)
-        self.lm_w = (torch.randn((v_len, sh.hidden), generator=wgen, device=self.dev) * 0.02).to(torch.bfloat16)
+        if share_weights is not None:
+            self.lm_w = share_weights.lm_w
+        else:
+            wgen = torch.Generator(device=self.dev).manual_seed(seed + 1000 + rank)
+            self.lm_w = (torch.randn((v_len, sh.hidden), generator=wgen, device=self.dev) * 0.02).to(torch.bfloat16)
         # GDN rollback snapshot states [layer, B, Hv, Dv, Dk] fp32 ~ N(0, 0.05)
         # and the tapes of one verify block, recorded by the verify forward
         # (gated_delta_kernel_with_tape) from synthetic inputs:
@@ -241,25 +256,34 @@ class VerifyStep:
         outs = []
         phases = []
         last_down = [None] * len(groups)      # (phase index, tensor) of each group's last down
+        chain = deps == "chain"
         for lt in self.tiled:
-            layer_out = []
+            # projection-major inside a layer (every group's q|k|v, then every
+            # o, gate|up, down), so with several groups a projection's input
+            # was written a few phases earlier and its wait is short
+            layer_out = [{"qkv": buf(g1 - g0, sh.q_out + 2 * sh.kv_out), "o": buf(g1 - g0, sh.hidden),
+                          "h": buf(g1 - g0, sh.inter), "down": buf(g1 - g0, sh.hidden)}
+                         for g0, g1 in groups]
+            idx = {}
             for gi, (g0, g1) in enumerate(groups):
-                m = g1 - g0
-                out = {"qkv": buf(m, sh.q_out + 2 * sh.kv_out), "o": buf(m, sh.hidden),
-                       "h": buf(m, sh.inter), "down": buf(m, sh.hidden)}
-                layer_out.append(out)
                 prev = last_down[gi]
                 x_in = self.x[g0:g1] if prev is None else prev[1]
-                a = self.attn_out[g0:g1]
-                base = len(phases)
-                chain = deps == "chain"
-                dep_qkv = -1 if prev is None else prev[0]
-                phases.append(PlanPhase(x_in, lt["qkv"], out["qkv"], dep=dep_qkv))
-                phases.append(PlanPhase(a, lt["o"], out["o"], dep=base if chain else -1))
-                phases.append(PlanPhase(self.x[g0:g1], lt["gate_up"], out["h"], silu=True,
-                                        dep=base + 1 if chain else -1))
-                phases.append(PlanPhase(out["h"], lt["down"], out["down"], dep=base + 2))
-                last_down[gi] = (base + 3, out["down"])
+                idx["qkv", gi] = len(phases)
+                phases.append(PlanPhase(x_in, lt["qkv"], layer_out[gi]["qkv"],
+                                        dep=-1 if prev is None else prev[0]))
+            for gi, (g0, g1) in enumerate(groups):
+                idx["o", gi] = len(phases)
+                phases.append(PlanPhase(self.attn_out[g0:g1], lt["o"], layer_out[gi]["o"],
+                                        dep=idx["qkv", gi] if chain else -1))
+            for gi, (g0, g1) in enumerate(groups):
+                idx["gate_up", gi] = len(phases)
+                phases.append(PlanPhase(self.x[g0:g1], lt["gate_up"], layer_out[gi]["h"], silu=True,
+                                        dep=idx["o", gi] if chain else -1))
+            for gi in range(len(groups)):
+                idx["down", gi] = len(phases)
+                phases.append(PlanPhase(layer_out[gi]["h"], lt["down"], layer_out[gi]["down"],
+                                        dep=idx["gate_up", gi]))
+                last_down[gi] = (idx["down", gi], layer_out[gi]["down"])
             outs.append(layer_out)
         self.plan_out = outs
         self.last_qkv = outs[-1][0]["qkv"]

@@ -664,8 +664,8 @@ def test_verify_step_plan_host_path(pkg, monkeypatch):
     """Tiled layout on CPU, library replaced by a recorder: set-up repacks
     every projection once into the tiled layout and encodes one plan whose
     phases are the stack's projections per group of up to eight requests
-    (one 128-row token tile), each waiting for the previous phase of its group (q|k|v -> o -> gate|up + SiLU
-    -> down -> next layer's q|k|v); the qmm stack is one plan launch."""
+    (one 128-row token tile), projection-major within a layer (every group's
+    q|k|v, then o, gate|up + SiLU, down); the qmm stack is one plan launch."""
     import contextlib
 
     from dflash_mlx_b200 import _lib, kernels, lm_head, qmm_plan, verify_step
@@ -718,21 +718,24 @@ def test_verify_step_plan_host_path(pkg, monkeypatch):
     h, q_n, inter = shape.hidden, shape.q_out + 2 * shape.kv_out, shape.inter
     want = []
     last = {0: -1, 1: -1}
+    rows = ((0, 128), (1, 32))            # 10 requests: rows 0-127 and 128-159
     for _ in range(shape.layers):
-        for g, m in ((0, 128), (1, 32)):      # 10 requests: rows 0-127 and 128-159
-            base = len(want)
-            # dataflow: q|k|v waits for the group's previous down (its input),
-            # down for gate|up's SiLU output; o and gate|up read stand-ins
-            want += [(m, h, q_n, h, q_n, 2, last[g]),
-                     (m, shape.q_out, h, shape.q_out, h, 2, -1),
-                     (m, h, 2 * inter, h, inter, 3, -1),
-                     (m, inter, h, inter, h, 2, base + 2)]
-            last[g] = base + 3
+        # projection-major inside a layer: every group's q|k|v, o, gate|up, down;
+        # dataflow: q|k|v waits for the group's previous down (its input),
+        # down for the group's gate|up SiLU output; o and gate|up read stand-ins
+        base = len(want)
+        want += [(m, h, q_n, h, q_n, 2, last[g]) for g, m in rows]
+        want += [(m, shape.q_out, h, shape.q_out, h, 2, -1) for g, m in rows]
+        want += [(m, h, 2 * inter, h, inter, 3, -1) for g, m in rows]
+        want += [(m, inter, h, inter, h, 2, base + 4 + g) for g, m in rows]
+        for g, _ in rows:
+            last[g] = base + 6 + g
     assert encoded == want
-    # the chained form: every phase also waits for the one before it
+    # the chained form: o, gate|up and down also wait for the group's previous
+    # projection (two phases back in the projection-major order)
     encoded.clear()
     step._build_plan("chain")
-    assert [e[-1] for e in encoded] == [w[-1] if i % 4 == 0 else i - 1 for i, w in enumerate(want)]
+    assert [e[-1] for e in encoded] == [w[-1] if (i % 8) < 2 else i - 2 for i, w in enumerate(want)]
     calls.clear()
     step._qmm_stack()
     assert calls == ["dfl_qmm_plan_run"]
