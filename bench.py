@@ -673,11 +673,13 @@ def measure_other_configs(dev, args) -> dict:
     return out
 
 
-def measure_moe(dev, layers: int, steps: int, warmup: int, fuse_silu: bool) -> dict:
+def measure_moe(dev, layers: int, steps: int, warmup: int, fuse_silu: bool, plan: bool = True) -> dict:
     """BASELINE config 2 (hidden 2048, 256 experts, top-8, intermediate 512,
     one shared expert, 16 tokens): ``layers`` layers with distinct weights in
     one CUDA graph; HBM GB/s of the bytes of the experts the routing
-    activates + the shared expert + activations."""
+    activates + the shared expert + activations.  ``plan``: each layer's
+    expert projections in one plan launch (MoEPlanLayer: route, sort, plan,
+    combine); otherwise the per-launch path (moe_layer)."""
     import torch
 
     import __graft_entry__
@@ -721,9 +723,17 @@ def measure_moe(dev, layers: int, steps: int, warmup: int, fuse_silu: bool) -> d
     act_bytes = 2 * tok * hid * 2 + 2 * tok * topk * (inter * 2 + hid) + 2 * tok * (3 * inter + hid)
     bytes_total = sum(a * per_expert + per_expert + act_bytes for a in active)
 
-    def body():
-        for experts, shared, logits in lay:
-            M.moe_layer(x, logits, experts, shared, top_k=topk)
+    if plan:
+        runners = [(M.MoEPlanLayer(experts, shared, tokens=tok, top_k=topk), logits)
+                   for experts, shared, logits in lay]
+
+        def body():
+            for layer, logits in runners:
+                layer(x, logits)
+    else:
+        def body():
+            for experts, shared, logits in lay:
+                M.moe_layer(x, logits, experts, shared, top_k=topk)
 
     t = _graph_time(body, dev, reps=steps, warmup=warmup)
     peak, kind = _peaks()
@@ -734,7 +744,8 @@ def measure_moe(dev, layers: int, steps: int, warmup: int, fuse_silu: bool) -> d
         "active_experts_per_layer": active, "bytes_per_layer": bytes_total / layers,
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                      "peak_source": kind},
-        "silu_fused": fuse_silu, "gpu_launches_per_layer": 6 if fuse_silu else 10,
+        "silu_fused": fuse_silu or plan, "path": "plan" if plan else "per-launch",
+        "gpu_launches_per_layer": 4 if plan else (6 if fuse_silu else 10),
         "steps": steps, "warmup": warmup, "dtype": "bf16", "data": "synthetic"}
 
 
@@ -751,7 +762,7 @@ def run_moe(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     print(json.dumps(measure_moe(dev, args.moe_layers, args.steps, args.warmup,
-                                 fuse_silu=not args.no_fuse_silu)))
+                                 fuse_silu=not args.no_fuse_silu, plan=not args.moe_per_launch)))
     return 0
 
 
@@ -863,6 +874,8 @@ def main():
                     help="verify: the benchmark's verify step (default); moe: BASELINE config 2; "
                          "gdn-forward / ddtree: the GDN tape producer and the tree kernel alone")
     ap.add_argument("--moe-layers", type=int, default=4)
+    ap.add_argument("--moe-per-launch", action="store_true",
+                    help="moe workload: one launch per projection instead of one plan per layer")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

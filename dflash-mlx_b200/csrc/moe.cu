@@ -132,6 +132,207 @@ __global__ void combine_kernel(const uint16_t* pair_out, const float* weights, c
   y[i] = __bfloat16_as_ushort(__float2bfloat16_rn(acc));
 }
 
+// Sorted route table of grouped plan phases (qmm_plan.cu) from the top-k
+// expert ids, plus the x rows in sorted order.  Sorted rows are the (token,
+// slot) pairs ordered by expert id, then pair index (= token order, then
+// slot, as route_kernel numbers a problem's rows).  Every CTA ranks all
+// pairs in shared memory (pairs <= 256); CTA 0 writes the table, and the
+// CTAs share the row copies.
+//   route[0] = P (active experts); route[1 + 2i] = first sorted row of
+//   problem i (i <= P, route[1 + 2P] = pairs); route[2 + 2i] = its expert;
+//   route[kRouteRowMap + r] = pair row of sorted row r.
+// ex[] holds the pairs' expert ids (validated by the caller), first[] and
+// pos[] are shared scratch of the same length.
+__device__ void rank_and_gather(const int* ex, int* first, int* pos, int pairs, int top_k,
+                                const uint16_t* x, int ldx, int H, int32_t* route,
+                                uint16_t* x_sorted, uint16_t* x_copy, int T) {
+  const int tid = threadIdx.x;
+  for (int p = tid; p < pairs; p += blockDim.x) {
+    int f = 1;
+    for (int q = 0; q < p; ++q) f &= (ex[q] != ex[p]);
+    first[p] = f;
+  }
+  __syncthreads();
+  // rank of pair p: pairs with a smaller expert id, plus earlier pairs with
+  // the same one; problem index of its expert: distinct smaller expert ids
+  for (int p = tid; p < pairs; p += blockDim.x) {
+    const int e = ex[p];
+    int below = 0, same_before = 0, distinct_below = 0;
+    for (int q = 0; q < pairs; ++q) {
+      const int eq = ex[q];
+      below += (eq < e);
+      same_before += (eq == e && q < p);
+      distinct_below += (eq < e) & first[q];
+    }
+    pos[p] = below + same_before;
+    if (blockIdx.x == 0) {
+      route[plan::kRouteRowMap + below + same_before] = p;
+      if (first[p]) {
+        route[1 + 2 * distinct_below] = below;
+        route[2 + 2 * distinct_below] = e;
+      }
+    }
+  }
+  __syncthreads();
+  if (blockIdx.x == 0 && tid == 0) {
+    int P = 0;
+    for (int p = 0; p < pairs; ++p) P += first[p];
+    route[0] = P;
+    route[1 + 2 * P] = pairs;
+  }
+  // rows: x_sorted[pos[p]] = x[p / top_k] (16-byte words); the caller's x
+  // copied whole into x_copy by the same CTAs
+  const int words = H / 8;
+  const int jobs = pairs + (x_copy ? T : 0);
+  for (int j = blockIdx.x; j < jobs; j += gridDim.x) {
+    const uint4* src;
+    uint4* dst;
+    if (j < pairs) {
+      src = reinterpret_cast<const uint4*>(x + size_t(j / top_k) * ldx);
+      dst = reinterpret_cast<uint4*>(x_sorted + size_t(pos[j]) * H);
+    } else {
+      src = reinterpret_cast<const uint4*>(x + size_t(j - pairs) * ldx);
+      dst = reinterpret_cast<uint4*>(x_copy + size_t(j - pairs) * H);
+    }
+    for (int i = tid; i < words; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
+// An expert id outside [0, E) sets the device error word and the table gets
+// P = 0 (grouped phases then do nothing).
+__global__ void sort_pairs_kernel(const int32_t* topk_ids, int pairs, int top_k, int E,
+                                  const uint16_t* x, int ldx, int H, int32_t* route,
+                                  uint16_t* x_sorted, uint16_t* x_copy, int T) {
+  __shared__ int ex[plan::kRouteMaxRows];
+  __shared__ int first[plan::kRouteMaxRows];   // pair p is its expert's first pair
+  __shared__ int pos[plan::kRouteMaxRows];
+  __shared__ int bad;
+  const int tid = threadIdx.x;
+  if (tid == 0) bad = 0;
+  __syncthreads();
+  for (int p = tid; p < pairs; p += blockDim.x) {
+    const int e = topk_ids[p];
+    ex[p] = e;
+    if (e < 0 || e >= E) bad = 1;
+  }
+  __syncthreads();
+  if (bad) {
+    if (blockIdx.x == 0 && tid == 0) {
+      atomicExch(&g_device_error, kDevBadInput);
+      route[0] = 0;
+      route[1] = 0;
+    }
+    return;
+  }
+  rank_and_gather(ex, first, pos, pairs, top_k, x, ldx, H, route, x_sorted, x_copy, T);
+}
+
+constexpr int kRouteSortMaxExperts = 4096;
+
+// (value desc, id asc): the order in which experts are picked
+__device__ __forceinline__ bool beats(float v, int e, float w, int f) {
+  return v > w || (v == w && e < f);
+}
+
+// Routing and sorting in one launch (MoEPlanLayer): warp t takes token t's
+// top-k by router logit (largest first, ties to the lower id: each lane
+// keeps a best-first list of its own experts e = lane + 32 i in registers,
+// then k rounds of a warp argmax over the lanes' heads pick the experts in
+// route_kernel's order) and its softmax over the kept logits in double
+// precision (the same operations as route_kernel, so the same weights bit
+// for bit); CTA 0 stores weights and ids; then every CTA ranks the pairs and
+// copies its share of the rows (rank_and_gather).  A top-k with no winner
+// (NaN logits) sets the device error word and the table gets P = 0.
+__global__ void route_sort_kernel(const float* logits, int T, int E, int k, const uint16_t* x,
+                                  int ldx, int H, int32_t* route, float* weights, int32_t* topk,
+                                  uint16_t* x_sorted, uint16_t* x_copy) {
+  __shared__ int ex[plan::kRouteMaxRows];
+  __shared__ int first[plan::kRouteMaxRows];
+  __shared__ int pos[plan::kRouteMaxRows];
+  __shared__ int bad;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) bad = 0;
+  __syncthreads();
+  if (warp < T) {
+    const int t = warp;
+    const float* row = logits + (size_t)t * E;
+    float lv[MAX_K];
+    int li[MAX_K];
+#pragma unroll
+    for (int i = 0; i < MAX_K; ++i) {
+      lv[i] = -INFINITY;
+      li[i] = 0x7fffffff;
+    }
+    for (int e = lane; e < E; e += 32) {
+      const float v = row[e];
+      if (!beats(v, e, lv[MAX_K - 1], li[MAX_K - 1])) continue;
+      // insertion from the tail: entries (v, e) beats move down one place
+#pragma unroll
+      for (int i = MAX_K - 1; i >= 1; --i) {
+        if (beats(v, e, lv[i], li[i])) {
+          const bool above = beats(v, e, lv[i - 1], li[i - 1]);
+          lv[i] = above ? lv[i - 1] : v;
+          li[i] = above ? li[i - 1] : e;
+        }
+      }
+      if (beats(v, e, lv[0], li[0])) {
+        lv[0] = v;
+        li[0] = e;
+      }
+    }
+    float myv = 0.f;
+    int myid = 0;
+    for (int j = 0; j < k; ++j) {
+      float bv = lv[0];
+      int bi = li[0];
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (beats(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == j) {
+        myv = bv;
+        myid = bi;
+      }
+      if (bi < 0 || bi >= E) {
+        if (lane == 0) bad = 1;
+        break;
+      }
+      if (li[0] == bi) {
+        // this lane's head was picked: pop it
+#pragma unroll
+        for (int i = 0; i < MAX_K - 1; ++i) {
+          lv[i] = lv[i + 1];
+          li[i] = li[i + 1];
+        }
+        lv[MAX_K - 1] = -INFINITY;
+        li[MAX_K - 1] = 0x7fffffff;
+      }
+    }
+    const float mx = __shfl_sync(0xffffffffu, myv, 0);
+    const double v = (lane < k) ? exp((double)myv - mx) : 0.0;
+    double den = 0.0;
+    for (int j = 0; j < k; ++j) den += __shfl_sync(0xffffffffu, v, j);
+    if (lane < k) {
+      ex[t * k + lane] = myid;
+      if (blockIdx.x == 0) {
+        weights[t * k + lane] = float(v / den);
+        topk[t * k + lane] = myid;
+      }
+    }
+  }
+  __syncthreads();
+  if (bad) {
+    if (blockIdx.x == 0 && tid == 0) {
+      atomicExch(&g_device_error, kDevBadInput);
+      route[0] = 0;
+      route[1] = 0;
+    }
+    return;
+  }
+  rank_and_gather(ex, first, pos, T * k, k, x, ldx, H, route, x_sorted, x_copy, T);
+}
+
 }  // namespace moe
 }  // namespace dfl
 
@@ -186,5 +387,46 @@ extern "C" int dfl_moe_combine(const uint16_t* pair_out, const float* weights,
   const int n = T * H;
   moe::combine_kernel<<<(n + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       pair_out, weights, shared, y, T, top_k, H);
+  return host::launch_status();
+}
+
+extern "C" size_t dfl_moe_sorted_route_ints(void) { return size_t(dfl::plan::kRouteInts); }
+
+extern "C" int dfl_moe_sort_pairs(const int32_t* topk_ids, int T, int top_k, int E,
+                                  const uint16_t* x, int ldx, int H, int32_t* route,
+                                  uint16_t* x_sorted, uint16_t* x_copy, void* stream) {
+  using namespace dfl;
+  if (T < 1 || top_k < 1 || (long long)T * top_k > plan::kRouteMaxRows || E < 1 || E > (1 << 20) ||
+      H < 8 || H % 8 != 0 || ldx < H || ldx % 8 != 0)
+    return DFL_ERR_BAD_SHAPE;
+  if (!topk_ids || !x || !route || !x_sorted) return DFL_ERR_NULL_POINTER;
+  if (!host::aligned(topk_ids, 4) || !host::aligned(route, 4) || !host::aligned(x, 16) ||
+      !host::aligned(x_sorted, 16) || (x_copy && !host::aligned(x_copy, 16)))
+    return DFL_ERR_MISALIGNED;
+  const int pairs = T * top_k;
+  const int blocks = pairs + (x_copy ? T : 0) < 64 ? pairs + (x_copy ? T : 0) : 64;
+  moe::sort_pairs_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      topk_ids, pairs, top_k, E, x, ldx, H, route, x_sorted, x_copy, T);
+  return host::launch_status();
+}
+
+extern "C" int dfl_moe_route_sorted(const float* logits, int T, int E, int top_k, const uint16_t* x,
+                                    int ldx, int H, int32_t* route, float* weights,
+                                    int32_t* topk_ids, uint16_t* x_sorted, uint16_t* x_copy,
+                                    void* stream) {
+  using namespace dfl;
+  if (T < 1 || T > moe::MAX_TOKENS || E < 1 || E > moe::kRouteSortMaxExperts || top_k < 1 ||
+      top_k > moe::MAX_K || top_k > E || T * top_k > plan::kRouteMaxRows || H < 8 || H % 8 != 0 ||
+      ldx < H || ldx % 8 != 0)
+    return DFL_ERR_BAD_SHAPE;
+  if (!logits || !x || !route || !weights || !topk_ids || !x_sorted) return DFL_ERR_NULL_POINTER;
+  if (!host::aligned(logits, 4) || !host::aligned(route, 4) || !host::aligned(weights, 4) ||
+      !host::aligned(topk_ids, 4) || !host::aligned(x, 16) || !host::aligned(x_sorted, 16) ||
+      (x_copy && !host::aligned(x_copy, 16)))
+    return DFL_ERR_MISALIGNED;
+  const int jobs = T * top_k + (x_copy ? T : 0);
+  const int blocks = jobs < 64 ? jobs : 64;
+  moe::route_sort_kernel<<<blocks, 512, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      logits, T, E, top_k, x, ldx, H, route, weights, topk_ids, x_sorted, x_copy);
   return host::launch_status();
 }

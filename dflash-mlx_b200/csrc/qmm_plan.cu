@@ -57,6 +57,8 @@
 #include "common.cuh"
 #include "host_common.cuh"
 
+#include <vector>
+
 namespace dfl {
 namespace plan {
 
@@ -91,6 +93,17 @@ constexpr int kPlanVersion = 1;
 constexpr int kHeaderBytes = 256;
 constexpr int kPhaseSilu = 1;                          // DFL_PHASE_SILU
 constexpr int kPhaseSubnormal = 2;                     // DFL_PHASE_SUBNORMAL
+constexpr int kPhaseGrouped = 4;                       // DFL_PHASE_GROUPED
+constexpr int kPhaseScatter = 8;                       // DFL_PHASE_SCATTER
+// sorted route table of grouped phases (dfl_moe_sort_pairs): [0] problems P;
+// [1 + 2i] first sorted row of problem i (i <= P); [2 + 2i] its expert;
+// [kRowMap + r] the pair row (token * top_k + slot) of sorted row r
+constexpr int kRouteMaxProblems = 256;
+constexpr int kRouteRowMap = 2 + 2 * kRouteMaxProblems;
+constexpr int kRouteMaxRows = 256;
+constexpr int kMaxGroupedRows = 32;                    // token tile of plans with grouped phases
+constexpr int kRouteInts = kRouteRowMap + kRouteMaxRows;
+static_assert(kRouteRowMap == 514, "route table layout documented in dflash_b200.h");
 // workspace: 64 KB of counter words, then the split-K partial slots
 constexpr size_t kCounterBytes = host::kWorkspaceCounterBytes;
 constexpr int kWordExit = kMaxPhases;                  // CTAs that finished the launch
@@ -102,7 +115,18 @@ constexpr int kWordDiag = kMaxPhases + 4;              // [8] details of the fir
 // the phase (+1) whose partial its consumer has read
 constexpr int kWordReady = kMaxPhases + 16;            // [kMaxGrid][2]
 constexpr int kWordConsumed = kWordReady + 2 * kMaxGrid;  // [kMaxGrid][2]
-static_assert((kWordConsumed + 2 * kMaxGrid) * 4 <= int(kCounterBytes), "counter region");
+// per-problem tile counters of grouped phases that a later grouped phase
+// reads per problem: [slot][kRouteMaxProblems]
+constexpr int kWordProblem = 8704;
+constexpr int kMaxProblemSlots = 16;
+static_assert(kWordConsumed + 2 * kMaxGrid <= kWordProblem, "counter region layout");
+static_assert((kWordProblem + kMaxProblemSlots * kRouteMaxProblems) * 4 <= int(kCounterBytes),
+              "counter region");
+// internal phase flag fields (set by the encoder): the problem-counter slot
+// (+1) a grouped phase signals per stored tile, and the one it waits on
+constexpr int kSignalShift = 8;
+constexpr int kWaitShift = 16;
+constexpr int kPublicFlags = 0xFF;
 static_assert(BLK_BYTES % 1024 == 0, "stage alignment");
 
 template <int MT>
@@ -165,8 +189,10 @@ struct alignas(64) Phase {
   const uint8_t* w;      // tiled blob: n_tiles * ku blocks of BLK_BYTES, tile-major
   uint16_t* y;           // [M, N] (SiLU: [M, N/2]), row stride ldy
   int M, K, N, ldy;
-  int n_tiles, ku, total;
+  int n_tiles, ku, total;   // grouped: n_tiles per expert; total from the route table
   int flags, dep;
+  int experts;              // grouped phases: experts stacked in w
+  const int* route;         // grouped phases: sorted route table
 };
 static_assert(sizeof(Phase) == 192, "phase record size");
 
@@ -176,7 +202,7 @@ struct Header {
   // fault injection for tests (dfl_qmm_plan_set_test_fault): a CTA that
   // withholds its split-K partials, and the bound on every wait
   int test_skip_partial_cta;
-  int pad0;
+  int prob_slots;               // problem-counter slots in use
   unsigned long long wait_limit_ns;
   int pad[54];
 };
@@ -186,6 +212,7 @@ struct RunParams {
   const Phase* phases;
   int n_phases;
   int skip_partial_cta;        // -1 normally
+  int prob_slots;
   unsigned long long wait_limit_ns;
   int* words;           // workspace counter words
   float* partials;      // workspace [grid][2][MT][BN]
@@ -276,6 +303,34 @@ __device__ __forceinline__ const void* ld_field_ptr(const void* const* p) {
   return reinterpret_cast<const void*>(v);
 }
 
+// Problems of a grouped phase's route table (the table is complete before
+// the launch), clamped to the table's capacity.
+__device__ __forceinline__ int route_problems(const int* route) {
+  const int P = ld_field(route);
+  return P < 0 ? 0 : (P > kRouteMaxProblems ? kRouteMaxProblems : P);
+}
+
+// Units of phase p: tiles x K units, times the problems of its route table
+// for a grouped phase.
+template <bool GROUPED>
+__device__ __forceinline__ int phase_total(const Phase* phases, int p) {
+  if (!GROUPED || !(ld_field(&phases[p].flags) & kPhaseGrouped)) return ld_field(&phases[p].total);
+  const int* route = static_cast<const int*>(ld_field_ptr(reinterpret_cast<const void* const*>(&phases[p].route)));
+  return route_problems(route) * ld_field(&phases[p].n_tiles) * ld_field(&phases[p].ku);
+}
+
+// Expert of problem pi; an id outside [0, experts) sets the device error
+// word and reads expert 0 instead (the table comes from device memory and
+// must never steer a weight read outside the stacked experts).
+__device__ __forceinline__ int route_expert(const int* route, int pi, int experts) {
+  const int e = ld_field(route + 2 + 2 * pi);
+  if (e < 0 || e >= experts) {
+    atomicExch(&g_device_error, kDevBadInput);
+    return 0;
+  }
+  return e;
+}
+
 // CTA c's share of a phase of `total` units on a grid of G CTAs:
 // [floor(c * total / G), floor((c + 1) * total / G)).
 __device__ __forceinline__ int unit_begin(int c, int total, int grid) {
@@ -364,7 +419,7 @@ __device__ __forceinline__ bool wait_counter(const int* addr, int target, volati
 // first: lanes may arrive from different iterations of their own waits).
 __device__ __forceinline__ bool epi_all(bool pred) { return named_bar_and(BAR_ID_EPI, 128, pred); }
 
-template <int MT>
+template <int MT, bool GROUPED>
 __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_constant__ RunParams rp) {
   using C = Cfg<MT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -436,18 +491,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       int it = 0;
-      int n_total = ld_field(&phases[0].total);
+      int n_total = phase_total<GROUPED>(phases, 0);
       const uint8_t* n_w = static_cast<const uint8_t*>(ld_field_ptr(reinterpret_cast<const void* const*>(&phases[0].w)));
       for (int p = 0; p < P && !*abort_word; ++p) {
         const int total = n_total;
         const uint8_t* w = n_w;
         if (p + 1 < P) {
-          n_total = ld_field(&phases[p + 1].total);
+          n_total = phase_total<GROUPED>(phases, p + 1);
           n_w = static_cast<const uint8_t*>(ld_field_ptr(reinterpret_cast<const void* const*>(&phases[p + 1].w)));
         }
         const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
+        const bool grouped = GROUPED && (ld_field(&phases[p].flags) & kPhaseGrouped) != 0;
+        int g_nt = 0, g_ku = 1, g_ex = 1, last_pi = -1, e = 0;
+        const int* route = nullptr;
+        if (grouped) {
+          g_nt = ld_field(&phases[p].n_tiles);
+          g_ku = ld_field(&phases[p].ku);
+          g_ex = ld_field(&phases[p].experts);
+          route = static_cast<const int*>(ld_field_ptr(reinterpret_cast<const void* const*>(&phases[p].route)));
+        }
         const uint8_t* src = w + size_t(u0) * BLK_BYTES;
         for (int u = u0; u < u1; ++u, ++it, src += BLK_BYTES) {
+          if (grouped) {
+            // unit u = (problem, tile, K unit): the problem's expert's block
+            const int tt = u / g_ku, pi = tt / g_nt;
+            if (pi != last_pi) {
+              e = route_expert(route, pi, g_ex);
+              last_pi = pi;
+            }
+            src = w + (size_t(e) * g_nt + (tt - pi * g_nt)) * g_ku * BLK_BYTES + size_t(u - tt * g_ku) * BLK_BYTES;
+          }
           const int s = it % C::NSTAGE;
           if (!wait(&empty[s], ((it / C::NSTAGE) & 1) ^ 1, kWhereProducer, p)) break;
           mbar_arrive_expect_tx(&full[s], BLK_BYTES);
@@ -473,11 +546,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
     {
       int it = 0, acc_it = 0;
       uint32_t buf = 0;
-      int n_total = ld_field(&phases[0].total), n_ku = ld_field(&phases[0].ku);
+      int n_total = phase_total<GROUPED>(phases, 0), n_ku = ld_field(&phases[0].ku);
       for (int p = 0; p < P; ++p) {
         const int total = n_total, ku = n_ku;
         if (p + 1 < P) {
-          n_total = ld_field(&phases[p + 1].total);
+          n_total = phase_total<GROUPED>(phases, p + 1);
           n_ku = ld_field(&phases[p + 1].ku);
         }
         const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
@@ -538,12 +611,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
     const int r = quad * 32 + lane;        // output row within the tile
     const uint32_t lane_base = tmem_base + (uint32_t(quad * 32) << 16);
     int it = 0;
-    int n_total = ld_field(&phases[0].total), n_flags = ld_field(&phases[0].flags);
+    int n_total = phase_total<GROUPED>(phases, 0), n_flags = ld_field(&phases[0].flags);
     for (int p = 0; p < P; ++p) {
       const int total = n_total;
       const bool subn = (n_flags & kPhaseSubnormal) != 0;
       if (p + 1 < P) {
-        n_total = ld_field(&phases[p + 1].total);
+        n_total = phase_total<GROUPED>(phases, p + 1);
         n_flags = ld_field(&phases[p + 1].flags);
       }
       const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
@@ -623,15 +696,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
       bool ok = true;
       for (int p = 0; ok && p < P; ++p) {
         const Phase& ph = phases[p];
-        const int total = ld_field(&ph.total), ku = ld_field(&ph.ku), dep = ld_field(&ph.dep);
+        const int total = phase_total<GROUPED>(phases, p), ku = ld_field(&ph.ku), dep = ld_field(&ph.dep);
         const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
         if (u0 == u1) continue;
+        const bool grouped = GROUPED && (ld_field(&ph.flags) & kPhaseGrouped) != 0;
+        const int g_nt = ld_field(&ph.n_tiles);
+        const int* route =
+            grouped ? static_cast<const int*>(ld_field_ptr(reinterpret_cast<const void* const*>(&ph.route))) : nullptr;
         // the x tensor map was written into global memory by a host copy:
         // order that write before the TMA unit's reads of the map
         asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(
                          reinterpret_cast<uint64_t>(&ph.tm_x))
                      : "memory");
-        if (dep >= 0) {
+        // a grouped phase reading an earlier grouped phase's rows waits per
+        // problem (that problem's tiles of the earlier phase stored)
+        const int wslot = grouped ? (ld_field(&ph.flags) >> kWaitShift) & 0xFF : 0;
+        const int dep_nt = wslot ? ld_field(&phases[dep].n_tiles) : 0;
+        if (dep >= 0 && wslot == 0) {
           // a dependency wait spans the whole earlier phase, so it runs twice
           // the limit: a stall inside that phase is then reported by the wait
           // that sees it first-hand (split-K partial, guard, pipeline) rather
@@ -639,8 +720,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
           if (!wait_counter(rp.words + dep, G, abort_word, plan_abort, words, kWhereDep, p, 2 * limit_ns)) break;
           fence_proxy_async_global();   // x rows written by other CTAs' stores
         }
+        int last_pi = -1, row0 = 0;
         for (int u = u0; ok && u < u1; ++u) {
           const int k0 = (u % ku) * UNIT_K;
+          // x rows of a grouped phase: the unit's problem's sorted rows
+          if (grouped && (u / ku) / g_nt != last_pi) {
+            last_pi = (u / ku) / g_nt;
+            row0 = ld_field(route + 1 + 2 * last_pi);
+            if (wslot) {
+              if (!wait_counter(rp.words + kWordProblem + (wslot - 1) * kRouteMaxProblems + last_pi, dep_nt,
+                                abort_word, plan_abort, words, kWhereDep, p, 2 * limit_ns)) {
+                ok = false;
+                break;
+              }
+              fence_proxy_async_global();   // x rows written by other CTAs' stores
+            }
+          }
 #pragma unroll 1
           for (int ch = 0; ch < C::NCH; ++ch, ++seq) {
             const int xs = seq % C::XS;
@@ -663,7 +758,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             mbar_arrive_expect_tx(&xfull[xs], C::XCHUNK_BYTES);
 #pragma unroll
             for (int b = 0; b < C::XCH; ++b)
-              tma_load_2d(dst + b * C::XBLK_BYTES, &ph.tm_x, &xfull[xs], k0 + (ch * C::XCH + b) * GS, 0);
+              tma_load_2d(dst + b * C::XBLK_BYTES, &ph.tm_x, &xfull[xs], k0 + (ch * C::XCH + b) * GS, row0);
           }
         }
       }
@@ -681,12 +776,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
     int acc_it = 0;
     int lastw[2] = {0, 0};  // phase + 1 of this CTA's last partial per slot parity
     bool ok = true;
-    int n_total = ld_field(&phases[0].total), n_ku = ld_field(&phases[0].ku);
+    int n_total = phase_total<GROUPED>(phases, 0), n_ku = ld_field(&phases[0].ku);
     for (int p = 0; ok && p < P; ++p) {
       const Phase& ph = phases[p];
       const int total = n_total, ku = n_ku;
       if (p + 1 < P) {
-        n_total = ld_field(&phases[p + 1].total);
+        n_total = phase_total<GROUPED>(phases, p + 1);
         n_ku = ld_field(&phases[p + 1].ku);
       }
       const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
@@ -694,6 +789,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
       if (u0 < u1) {
         const int M = ph.M, N = ph.N, ldy = ph.ldy;
         const bool silu = (ph.flags & kPhaseSilu) != 0;
+        const bool grouped = GROUPED && (ph.flags & kPhaseGrouped) != 0;
+        const bool scatter = GROUPED && (ph.flags & kPhaseScatter) != 0;
+        const int g_nt = ph.n_tiles;
+        const int* const route = ph.route;
+        const int sig_slot = grouped ? (ph.flags >> kSignalShift) & 0xFF : 0;
         uint16_t* const y = ph.y;
         const int t_first = u0 / ku, t_last = (u1 - 1) / ku;
         for (int t = t_first; t <= t_last; ++t) {
@@ -756,7 +856,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             break;
           }
           tc_fence_after();
-          const int n = t * BN + r;
+          // output columns of the tile; a grouped phase's tile t is tile
+          // t % n_tiles of problem t / n_tiles, whose rows are the problem's
+          // sorted rows (scattered to pair rows through the route table)
+          int t_loc = t, row0 = 0, rows = M;
+          if (grouped) {
+            // rows [row0, row0 + rows) of the phase's M rows, at most one tile
+            const int pi = t / g_nt;
+            t_loc = t - pi * g_nt;
+            row0 = ld_field(route + 1 + 2 * pi);
+            rows = ld_field(route + 3 + 2 * pi) - row0;
+            if (row0 < 0 || row0 >= M) rows = 0;
+            rows = rows < 0 ? 0 : (rows > MT ? MT : rows);
+            rows = rows > M - row0 ? M - row0 : rows;
+          }
+          // output row of tile row m (< rows): the sorted row, or with a
+          // scatter the pair row the route table maps it to (one past the
+          // phase's rows when the table holds an out-of-range row: skipped)
+          auto out_row = [&](int m) -> size_t {
+            if (!scatter) return size_t(row0 + m);
+            const int o = ld_field(route + kRouteRowMap + row0 + m);
+            return size_t(o >= 0 && o < M ? o : M);
+          };
+          const int n = t_loc * BN + r;
           uint32_t* const mine = reinterpret_cast<uint32_t*>(rp.partials) + size_t(2 * cta + par) * MT * BN;
 #pragma unroll 1
           for (int c0 = 0; c0 < MT; c0 += C::EC) {
@@ -835,18 +957,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                 const uint32_t gbits = lo ? own[2 * mp] : oth[2 * mp + 1];
                 const uint32_t ubits = lo ? oth[2 * mp] : own[2 * mp + 1];
                 const uint16_t h = silu_mul_bits<false>(uint16_t(gbits), uint16_t(ubits));
-                if (c0 + m < M) y[(size_t)(c0 + m) * ldy + hcol] = h;
+                if (c0 + m < rows) {
+                  const size_t orow = out_row(c0 + m);
+                  if (orow < size_t(M)) y[orow * ldy + hcol] = h;
+                }
               }
             } else {
-              uint16_t* yp = y + (size_t)c0 * ldy + n;
 #pragma unroll
-              for (int m = 0; m < C::EC; ++m, yp += ldy)
-                if (c0 + m < M) *yp = __bfloat16_as_ushort(__float2bfloat16_rn(acc[m]));
+              for (int m = 0; m < C::EC; ++m) {
+                if (c0 + m < rows) {
+                  const size_t orow = out_row(c0 + m);
+                  if (orow < size_t(M)) y[orow * ldy + n] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[m]));
+                }
+              }
             }
           }
           ++acc_it;
-          if (full_tile) continue;
-          if (cta != c_lo) {
+          if (!full_tile && cta != c_lo) {
             // the barrier orders every thread's partial stores before the
             // stamp's release (cumulativity)
             if (!epi_all(!*abort_word)) {
@@ -859,7 +986,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             lastw[par] = p + 1;
             continue;
           }
-          if constexpr (!C::kEarlyPartials) {
+          if (!C::kEarlyPartials && !full_tile) {
             // every thread has read every contributor's slot: mark them read
             if (!epi_all(!*abort_word)) {
               ok = false;
@@ -869,6 +996,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
               for (int c = c_lo + 1; c <= c_hi; ++c)
                 if (unit_begin(c, total, G) != unit_begin(c + 1, total, G))
                   st_release(consumed + 2 * c + par, p + 1);
+          }
+          if (sig_slot > 0) {
+            // the tile's final values are stored (the barrier orders every
+            // thread's stores before the release): count it for its problem
+            if (!epi_all(!*abort_word)) {
+              ok = false;
+              break;
+            }
+            if (et == 0)
+              red_release_add(rp.words + kWordProblem + (sig_slot - 1) * kRouteMaxProblems + t / g_nt, 1);
           }
         }
       }
@@ -898,6 +1035,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
     __threadfence();
     for (int i = threadIdx.x; i < P; i += NUM_THREADS) rp.words[i] = 0;
     for (int i = threadIdx.x; i < 4 * kMaxGrid; i += NUM_THREADS) rp.words[kWordReady + i] = 0;
+    for (int i = threadIdx.x; i < rp.prob_slots * kRouteMaxProblems; i += NUM_THREADS)
+      rp.words[kWordProblem + i] = 0;
     if (threadIdx.x == 0) {
       rp.words[kWordAbort] = 0;
       rp.words[kWordExit] = 0;
@@ -996,16 +1135,19 @@ inline size_t workspace_bytes(int mt, int grid) {
   return kCounterBytes + size_t(grid) * 2 * mt * BN * sizeof(float);
 }
 
-template <int MT>
+// GROUPED: the plan has grouped phases (route tables); plans without any run
+// the variant compiled without that code.
+template <int MT, bool GROUPED>
 int launch(const Header& h, const void* plan_dev, void* ws, int dev, cudaStream_t stream) {
   using C = Cfg<MT>;
   static std::atomic<uint64_t> smem_done{0};
-  int st = host::ensure_smem(qmm_plan_kernel<MT>, C::SMEM_BYTES, dev, smem_done);
+  int st = host::ensure_smem(qmm_plan_kernel<MT, GROUPED>, C::SMEM_BYTES, dev, smem_done);
   if (st != DFL_OK) return st;
   RunParams rp;
   rp.phases = reinterpret_cast<const Phase*>(static_cast<const uint8_t*>(plan_dev) + kHeaderBytes);
   rp.n_phases = h.n_phases;
   rp.skip_partial_cta = h.test_skip_partial_cta;
+  rp.prob_slots = h.prob_slots;
   rp.wait_limit_ns = h.wait_limit_ns;
   rp.words = static_cast<int*>(ws);
   rp.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
@@ -1022,7 +1164,7 @@ int launch(const Header& h, const void* plan_dev, void* ws, int dev, cudaStream_
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, qmm_plan_kernel<MT>, rp) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, qmm_plan_kernel<MT, GROUPED>, rp) != cudaSuccess) {
     cudaGetLastError();
     return DFL_ERR_CUDA;
   }
@@ -1035,7 +1177,8 @@ inline int check_header(const void* plan_host, Header* out) {
   if (out->magic != kPlanMagic || out->version != kPlanVersion || out->n_phases < 1 ||
       out->n_phases > kMaxPhases ||
       (out->mt != 16 && out->mt != 32 && out->mt != 64 && out->mt != 128) || out->grid < 1 ||
-      out->grid > kMaxGrid || out->wait_limit_ns == 0 || out->wait_limit_ns > kWaitLimitNs)
+      out->grid > kMaxGrid || out->wait_limit_ns == 0 || out->wait_limit_ns > kWaitLimitNs ||
+      out->prob_slots < 0 || out->prob_slots > kMaxProblemSlots)
     return DFL_ERR_BAD_SHAPE;
   return DFL_OK;
 }
@@ -1089,9 +1232,23 @@ extern "C" int dfl_qmm_plan_encode(const dfl_qmm_phase* phases, int n_phases, vo
   int max_m = 0, flags_or = 0;
   for (int p = 0; p < n_phases; ++p) {
     const dfl_qmm_phase& q = phases[p];
-    if (q.M < 1 || q.M > kMaxRows || q.K < 64 || q.K % 64 != 0 || q.N < 1 || q.N > (1 << 24))
+    const bool grouped = (q.flags & kPhaseGrouped) != 0;
+    if (q.M < 1 || q.M > (grouped ? kRouteMaxRows : kMaxRows) || q.K < 64 || q.K % 64 != 0 || q.N < 1 ||
+        q.N > (1 << 24))
       return DFL_ERR_BAD_SHAPE;
-    if ((q.flags & ~(kPhaseSilu | kPhaseSubnormal)) != 0) return DFL_ERR_BAD_SHAPE;
+    if ((q.flags & ~(kPhaseSilu | kPhaseSubnormal | kPhaseGrouped | kPhaseScatter)) != 0)
+      return DFL_ERR_BAD_SHAPE;
+    if ((q.flags & kPhaseScatter) && !grouped) return DFL_ERR_BAD_SHAPE;
+    if (grouped) {
+      // experts stacked whole tiles apart; at most kRouteMaxProblems problems
+      // of at most problem_rows rows each, found in the sorted route table
+      if (q.N % BN != 0 || q.experts < 1 || q.problem_rows < 1 || q.problem_rows > kMaxGroupedRows)
+        return DFL_ERR_BAD_SHAPE;
+      if (!q.route) return DFL_ERR_NULL_POINTER;
+      if (!host::aligned(q.route, 4)) return DFL_ERR_MISALIGNED;
+      const long long units = (long long)kRouteMaxProblems * (q.N / BN) * ((q.K + UNIT_K - 1) / UNIT_K);
+      if (units > (1LL << 31) / (kMaxGrid + 1)) return DFL_ERR_BAD_SHAPE;
+    }
     const bool silu = (q.flags & kPhaseSilu) != 0;
     if (silu && q.N % 32 != 0) return DFL_ERR_BAD_SHAPE;
     if (q.ldx < q.K || q.ldy < (silu ? q.N / 2 : q.N)) return DFL_ERR_BAD_SHAPE;
@@ -1102,10 +1259,26 @@ extern "C" int dfl_qmm_plan_encode(const dfl_qmm_phase* phases, int n_phases, vo
       return DFL_ERR_MISALIGNED;
     const long long tiles = (q.N + BN - 1) / BN, ku = (q.K + UNIT_K - 1) / UNIT_K;
     if (tiles * ku > (1LL << 31) / (kMaxGrid + 1)) return DFL_ERR_BAD_SHAPE;
-    max_m = q.M > max_m ? q.M : max_m;
+    const int rows = grouped ? q.problem_rows : q.M;   // rows one token tile holds
+    max_m = rows > max_m ? rows : max_m;
     flags_or |= q.flags;
   }
   const int mt = max_m <= 16 ? 16 : max_m <= 32 ? 32 : max_m <= 64 ? 64 : 128;
+  if ((flags_or & kPhaseGrouped) && mt > kMaxGroupedRows) return DFL_ERR_BAD_SHAPE;
+  // a grouped phase whose dep is a grouped phase over the same route table
+  // waits per problem: the dep counts its stored tiles per problem in a
+  // counter slot (at most kMaxProblemSlots; later pairs wait for the whole
+  // phase as other dependencies do)
+  std::vector<int> sig_slot(n_phases, 0), wait_slot(n_phases, 0);
+  int slots = 0;
+  for (int p = 0; p < n_phases; ++p) {
+    const dfl_qmm_phase& q = phases[p];
+    if (!(q.flags & kPhaseGrouped) || q.dep < 0) continue;
+    const dfl_qmm_phase& d = phases[q.dep];
+    if (!(d.flags & kPhaseGrouped) || d.route != q.route) continue;
+    if (!sig_slot[q.dep] && slots < kMaxProblemSlots) sig_slot[q.dep] = ++slots;
+    wait_slot[p] = sig_slot[q.dep];
+  }
   uint8_t* out = static_cast<uint8_t*>(plan_host);
   Header h;
   std::memset(&h, 0, sizeof(h));
@@ -1116,6 +1289,7 @@ extern "C" int dfl_qmm_plan_encode(const dfl_qmm_phase* phases, int n_phases, vo
   h.grid = sms < kMaxGrid ? sms : kMaxGrid;
   h.flags_or = flags_or;
   h.test_skip_partial_cta = -1;
+  h.prob_slots = slots;
   h.wait_limit_ns = kWaitLimitNs;
   std::memcpy(out, &h, sizeof(h));
   for (int p = 0; p < n_phases; ++p) {
@@ -1133,9 +1307,11 @@ extern "C" int dfl_qmm_plan_encode(const dfl_qmm_phase* phases, int n_phases, vo
     ph.ldy = q.ldy;
     ph.n_tiles = (q.N + BN - 1) / BN;
     ph.ku = (q.K + UNIT_K - 1) / UNIT_K;
-    ph.total = ph.n_tiles * ph.ku;
-    ph.flags = q.flags;
+    ph.total = (q.flags & kPhaseGrouped) ? 0 : ph.n_tiles * ph.ku;   // grouped: from the route table
+    ph.flags = q.flags | (sig_slot[p] << kSignalShift) | (wait_slot[p] << kWaitShift);
     ph.dep = q.dep;
+    ph.route = (q.flags & kPhaseGrouped) ? q.route : nullptr;
+    ph.experts = (q.flags & kPhaseGrouped) ? q.experts : 0;
     std::memcpy(out + kHeaderBytes + size_t(p) * sizeof(Phase), &ph, sizeof(Phase));
   }
   return DFL_OK;
@@ -1165,10 +1341,14 @@ extern "C" int dfl_qmm_plan_run(const void* plan_host, const void* plan_dev, voi
   if (h.grid > sms) return DFL_ERR_UNSUPPORTED;   // encoded for a larger device
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (h.mt) {
-    case 16: return plan::launch<16>(h, plan_dev, workspace, dev, s);
-    case 32: return plan::launch<32>(h, plan_dev, workspace, dev, s);
-    case 64: return plan::launch<64>(h, plan_dev, workspace, dev, s);
-    default: return plan::launch<128>(h, plan_dev, workspace, dev, s);
+    case 16:
+      return (h.flags_or & plan::kPhaseGrouped) ? plan::launch<16, true>(h, plan_dev, workspace, dev, s)
+                                                : plan::launch<16, false>(h, plan_dev, workspace, dev, s);
+    case 32:
+      return (h.flags_or & plan::kPhaseGrouped) ? plan::launch<32, true>(h, plan_dev, workspace, dev, s)
+                                                : plan::launch<32, false>(h, plan_dev, workspace, dev, s);
+    case 64: return plan::launch<64, false>(h, plan_dev, workspace, dev, s);
+    default: return plan::launch<128, false>(h, plan_dev, workspace, dev, s);
   }
 }
 

@@ -241,3 +241,169 @@ def moe_layer(x: torch.Tensor, router_logits: torch.Tensor, experts: dict, share
     d = gather_qmm(h, experts["down"], table, rows_out=t * top_k, gather_by_pair=True, max_problems=mp,
                    table_ready=True)
     return combine(d, w, so)
+
+
+def sort_pairs(topk_ids: torch.Tensor, x: torch.Tensor, n_experts: int, *,
+               route_out: Optional[torch.Tensor] = None, x_sorted: Optional[torch.Tensor] = None,
+               x_copy: Optional[torch.Tensor] = None):
+    """Sorted route table of grouped plan phases + the x rows in sorted order.
+
+    ``topk_ids`` int32 ``[T, k]`` (from :func:`route`), ``x`` bf16 ``[T, H]``
+    -> (``route`` int32, ``x_sorted`` bf16 ``[T*k, H]``): pairs (token, slot)
+    ordered by expert, then pair index; ``route[0]`` active experts P,
+    ``route[1 + 2i]`` first sorted row of problem i, ``route[2 + 2i]`` its
+    expert, ``route[514 + r]`` the pair row of sorted row r.  ``x_copy``
+    (optional, bf16 ``[T, H]``) receives ``x`` in the same launch."""
+    from .qmm_plan import sorted_route_ints
+
+    require_cuda(topk_ids, "topk_ids")
+    require_cuda(x, "x")
+    if topk_ids.dtype != torch.int32 or topk_ids.dim() != 2 or not topk_ids.is_contiguous():
+        raise ValueError("topk_ids must be a contiguous int32 [T, k] tensor")
+    t, k = (int(v) for v in topk_ids.shape)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[0] != t or x.stride(1) != 1:
+        raise ValueError(f"x must be bf16 [{t}, H] with unit column stride")
+    h = int(x.shape[1])
+    dev = x.device
+    if route_out is None:
+        route_out = torch.empty(sorted_route_ints(), dtype=torch.int32, device=dev)
+    elif route_out.dtype != torch.int32 or route_out.numel() < sorted_route_ints():
+        raise ValueError("route_out must be int32 with dfl_moe_sorted_route_ints() entries")
+    if x_sorted is None:
+        x_sorted = torch.empty((t * k, h), dtype=torch.bfloat16, device=dev)
+    elif x_sorted.dtype != torch.bfloat16 or tuple(x_sorted.shape) != (t * k, h) or not x_sorted.is_contiguous():
+        raise ValueError(f"x_sorted must be contiguous bf16 {(t * k, h)}")
+    if x_copy is not None and (x_copy.dtype != torch.bfloat16 or tuple(x_copy.shape) != (t, h)
+                               or not x_copy.is_contiguous()):
+        raise ValueError(f"x_copy must be contiguous bf16 {(t, h)}")
+    with torch.cuda.device(dev):
+        st = _lib.load().dfl_moe_sort_pairs(topk_ids.data_ptr(), t, k, int(n_experts), x.data_ptr(),
+                                            int(x.stride(0)), h, route_out.data_ptr(), x_sorted.data_ptr(),
+                                            None if x_copy is None else x_copy.data_ptr(), stream_ptr(dev))
+    _lib.check("dfl_moe_sort_pairs", st)
+    return route_out, x_sorted
+
+
+def route_sorted(router_logits: torch.Tensor, x: torch.Tensor, top_k: int, *,
+                 route_out: torch.Tensor, x_sorted: torch.Tensor, x_copy: Optional[torch.Tensor] = None,
+                 weights_out: Optional[torch.Tensor] = None, ids_out: Optional[torch.Tensor] = None):
+    """:func:`route` and :func:`sort_pairs` in one launch -> (weights fp32
+    ``[T, k]``, topk_ids int32 ``[T, k]``); the sorted route table, rows and
+    x copy go to ``route_out`` / ``x_sorted`` / ``x_copy``."""
+    from .qmm_plan import sorted_route_ints
+
+    require_cuda(router_logits, "router_logits")
+    require_cuda(x, "x")
+    lg = router_logits.to(torch.float32).contiguous()
+    t, e = (int(v) for v in lg.shape)
+    k = int(top_k)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[0] != t or x.stride(1) != 1:
+        raise ValueError(f"x must be bf16 [{t}, H] with unit column stride")
+    h = int(x.shape[1])
+    dev = x.device
+    if route_out.dtype != torch.int32 or route_out.numel() < sorted_route_ints():
+        raise ValueError("route_out must be int32 with dfl_moe_sorted_route_ints() entries")
+    if x_sorted.dtype != torch.bfloat16 or tuple(x_sorted.shape) != (t * k, h) or not x_sorted.is_contiguous():
+        raise ValueError(f"x_sorted must be contiguous bf16 {(t * k, h)}")
+    if x_copy is not None and (x_copy.dtype != torch.bfloat16 or tuple(x_copy.shape) != (t, h)
+                               or not x_copy.is_contiguous()):
+        raise ValueError(f"x_copy must be contiguous bf16 {(t, h)}")
+    w = weights_out if weights_out is not None else torch.empty((t, k), dtype=torch.float32, device=dev)
+    ids = ids_out if ids_out is not None else torch.empty((t, k), dtype=torch.int32, device=dev)
+    if w.dtype != torch.float32 or tuple(w.shape) != (t, k) or not w.is_contiguous():
+        raise ValueError(f"weights_out must be contiguous fp32 {(t, k)}")
+    if ids.dtype != torch.int32 or tuple(ids.shape) != (t, k) or not ids.is_contiguous():
+        raise ValueError(f"ids_out must be contiguous int32 {(t, k)}")
+    with torch.cuda.device(dev):
+        st = _lib.load().dfl_moe_route_sorted(lg.data_ptr(), t, e, k, x.data_ptr(), int(x.stride(0)), h,
+                                              route_out.data_ptr(), w.data_ptr(), ids.data_ptr(),
+                                              x_sorted.data_ptr(),
+                                              None if x_copy is None else x_copy.data_ptr(), stream_ptr(dev))
+    _lib.check("dfl_moe_route_sorted", st)
+    return w, ids
+
+
+class MoEPlanLayer:
+    """One MoE verify layer with every expert projection in one plan launch.
+
+    Per call: :func:`route_sorted` (top-k + weights, sorted route table, x
+    rows in sorted order, x into the plan's input buffer: one launch), one
+    :class:`~dflash_mlx_b200.qmm_plan.ProjectionPlan` run -- the shared
+    expert's gate|up + SiLU and down as dense phases, the routed experts'
+    gate|up + SiLU and down as grouped phases (down scattered to pair rows;
+    each active expert's weights read once, problems of one phase spread over
+    all SMs) -- and :func:`combine`.  No host synchronisation, CUDA-graph
+    capturable.  Same results as :func:`moe_layer` up to fp32
+    summation order.  Three launches per call.
+
+    ``experts``: QuantWeight stacks ``gate`` / ``up`` ``[E, I, H/8]`` or an
+    interleaved ``gate_up`` (:func:`fuse_expert_gate_up`) and ``down``
+    ``[E, H, I/8]``; ``shared``: QuantWeights ``gate`` / ``up`` (or
+    ``gate_up``) and ``down``, or None.  Needs I % 64 == 0, H % 128 == 0 and
+    ``tokens * top_k`` <= 256.
+    """
+
+    def __init__(self, experts: dict, shared: Optional[dict], tokens: int, top_k: int = 8):
+        from .qmm_plan import PlanPhase, ProjectionPlan, tile_expert_stack, tile_weight
+        from .verify_qmm import interleave_gate_up
+
+        gu = experts["gate_up"] if "gate_up" in experts else fuse_expert_gate_up(experts["gate"], experts["up"])
+        down = experts["down"]
+        _check_stack(gu, "gate_up")
+        _check_stack(down, "down")
+        e, h = int(gu.q.shape[0]), gu.k
+        inter = gu.n // 2
+        if down.k != inter or down.n != h or int(down.q.shape[0]) != e:
+            raise ValueError("down must be [E, H, I/8] for gate_up [E, 2I, H/8]")
+        t, k = int(tokens), int(top_k)
+        if not 1 <= t * k <= 256 or t > 16:
+            raise ValueError(f"{t} tokens x top-{k}: the route kernels take <= 16 tokens, <= 256 pairs")
+        dev = gu.q.device
+        self.tokens, self.top_k, self.experts, self.hidden, self.inter = t, k, e, h, inter
+        self.gate_up = tile_expert_stack(gu.q, gu.s, gu.b)
+        self.down = tile_expert_stack(down.q, down.s, down.b)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.x_in = torch.zeros((t, h), **bf)
+        self.x_sorted = torch.zeros((t * k, h), **bf)
+        self.h_sorted = torch.zeros((t * k, inter), **bf)
+        self.pair_out = torch.zeros((t * k, h), **bf)
+        from .qmm_plan import sorted_route_ints
+        self.route = torch.zeros(sorted_route_ints(), dtype=torch.int32, device=dev)
+        self.weights = torch.zeros((t, k), dtype=torch.float32, device=dev)
+        self.ids = torch.zeros((t, k), dtype=torch.int32, device=dev)
+        phases = []
+        self.shared_out = None
+        if shared is not None:
+            if "gate_up" in shared:
+                sgu = shared["gate_up"]
+            else:
+                g, u = shared["gate"], shared["up"]
+                sgu = QuantWeight(interleave_gate_up(g.q, u.q).contiguous(),
+                                  interleave_gate_up(g.s, u.s).contiguous(),
+                                  interleave_gate_up(g.b, u.b).contiguous())
+            sdown = shared["down"]
+            s_inter = sgu.n // 2
+            self.shared_gate_up = tile_weight(sgu.q, sgu.s, sgu.b)
+            self.shared_down = tile_weight(sdown.q, sdown.s, sdown.b)
+            self.h_shared = torch.zeros((t, s_inter), **bf)
+            self.shared_out = torch.zeros((t, h), **bf)
+            phases.append(PlanPhase(self.x_in, self.shared_gate_up, self.h_shared, silu=True))
+        g_idx = len(phases)
+        phases.append(PlanPhase(self.x_sorted, self.gate_up, self.h_sorted, silu=True, route=self.route,
+                                problem_rows=t))
+        if shared is not None:
+            phases.append(PlanPhase(self.h_shared, self.shared_down, self.shared_out, dep=0))
+        phases.append(PlanPhase(self.h_sorted, self.down, self.pair_out, dep=g_idx, route=self.route,
+                                problem_rows=t, scatter=True))
+        self.plan = ProjectionPlan(phases)
+
+    def __call__(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        require_cuda(x, "x")
+        if x.dtype != torch.bfloat16 or tuple(x.shape) != (self.tokens, self.hidden):
+            raise ValueError(f"x must be bf16 {(self.tokens, self.hidden)}")
+        if tuple(router_logits.shape) != (self.tokens, self.experts):
+            raise ValueError(f"router_logits must be {(self.tokens, self.experts)}")
+        w, _ = route_sorted(router_logits, x, self.top_k, route_out=self.route, x_sorted=self.x_sorted,
+                            x_copy=self.x_in, weights_out=self.weights, ids_out=self.ids)
+        self.plan.run()
+        return combine(self.pair_out, w, self.shared_out)

@@ -29,7 +29,11 @@ from ._runtime import as_u32_bits, require_cuda, stream_ptr
 
 PHASE_SILU = 1
 PHASE_SUBNORMAL = 2
+PHASE_GROUPED = 4
+PHASE_SCATTER = 8
 MAX_ROWS = 128          # token rows per phase (one token tile of the plan kernel)
+MAX_GROUPED_ROWS = 256  # sorted rows of a grouped phase (all problems together)
+MAX_PROBLEM_ROWS = 32   # rows of one problem (plans with grouped phases use <= 32-row tiles)
 SUBNORMAL_SCALE_LIMIT = 2.0 ** -5
 
 
@@ -37,16 +41,20 @@ class _Phase(ctypes.Structure):
     _fields_ = [("x", ctypes.c_void_p), ("y", ctypes.c_void_p), ("w_tiled", ctypes.c_void_p),
                 ("M", ctypes.c_int), ("K", ctypes.c_int), ("N", ctypes.c_int),
                 ("ldx", ctypes.c_int), ("ldy", ctypes.c_int), ("flags", ctypes.c_int),
-                ("dep", ctypes.c_int)]
+                ("dep", ctypes.c_int), ("route", ctypes.c_void_p), ("experts", ctypes.c_int),
+                ("problem_rows", ctypes.c_int)]
 
 
 @dataclass
 class TiledWeight:
-    """A weight [N, K] in the plan kernel's tiled layout (``blob`` uint8)."""
+    """A weight [N, K] in the plan kernel's tiled layout (``blob`` uint8);
+    ``experts`` > 1: that many [N, K] weights tiled one after the other (the
+    stacked experts of a grouped phase)."""
     blob: torch.Tensor
     n: int
     k: int
     subnormal: bool
+    experts: int = 1
 
 
 def scales_fit_subnormal(scales: torch.Tensor) -> bool:
@@ -58,6 +66,11 @@ def scales_fit_subnormal(scales: torch.Tensor) -> bool:
 
 def tiled_bytes(n: int, k: int) -> int:
     return int(_lib.load().dfl_w4_tiled_bytes(int(n), int(k)))
+
+
+def sorted_route_ints() -> int:
+    """int32 entries of a sorted route table (dfl_moe_sorted_route_ints)."""
+    return int(_lib.load().dfl_moe_sorted_route_ints())
 
 
 def tile_weight(w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *,
@@ -87,16 +100,59 @@ def tile_weight(w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *
     return TiledWeight(blob, n, k, bool(subnormal))
 
 
+def tile_expert_stack(w_q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *,
+                      subnormal: Optional[bool] = None) -> TiledWeight:
+    """Stacked experts ``w_q`` [E, N, K/8] + bf16 ``scales`` / ``biases``
+    [E, N, K/64] (N % 128 == 0) -> one :class:`TiledWeight` with the experts'
+    tiled blocks one after the other (the weight of a grouped phase)."""
+    for t, name in ((w_q, "w"), (scales, "scales"), (biases, "biases")):
+        require_cuda(t, name)
+    if w_q.dim() != 3:
+        raise ValueError(f"expert weights must be [E, N, K/8], got {tuple(w_q.shape)}")
+    e, n, k = int(w_q.shape[0]), int(w_q.shape[1]), int(w_q.shape[2]) * 8
+    if n % 128 != 0:
+        raise ValueError(f"grouped phases need N % 128 == 0 (whole tiles per expert), got N={n}")
+    if subnormal is None:
+        subnormal = scales_fit_subnormal(scales)
+    per = tiled_bytes(n, k)
+    blob = torch.empty(e * per, dtype=torch.uint8, device=w_q.device)
+    lib = _lib.load()
+    w_q = as_u32_bits(w_q)
+    scales, biases = scales.contiguous(), biases.contiguous()
+    if tuple(scales.shape) != (e, n, k // 64) or tuple(biases.shape) != (e, n, k // 64):
+        raise ValueError("scales/biases must be [E, N, K/64]")
+    if scales.dtype != torch.bfloat16 or biases.dtype != torch.bfloat16:
+        raise NotImplementedError("the tiled layout takes bfloat16 scales and biases")
+    with torch.cuda.device(w_q.device):
+        for i in range(e):
+            st = lib.dfl_repack_w4_tiled(w_q[i].data_ptr(), scales[i].data_ptr(), biases[i].data_ptr(),
+                                         n, k, 1 if subnormal else 0, blob[i * per:].data_ptr(), per,
+                                         stream_ptr(w_q.device))
+            _lib.check("dfl_repack_w4_tiled", st)
+    return TiledWeight(blob, n, k, bool(subnormal), experts=e)
+
+
 @dataclass
 class PlanPhase:
     """One projection of a plan: ``y = x @ W.T`` (or ``silu(gate) * up`` with
     ``silu`` over gate/up rows interleaved by ``interleave_gate_up``); ``dep``
-    = index of an earlier phase whose outputs ``x`` reads (-1: none)."""
+    = index of an earlier phase whose outputs ``x`` reads (-1: none).
+
+    Grouped phase (``route`` given, the int32 table of
+    :func:`dflash_mlx_b200.moe.sort_pairs`): ``x`` / ``y`` are the sorted
+    rows of every problem (up to 256), ``weight`` a stack of experts
+    (:func:`tile_expert_stack`) and problem i multiplies its rows by its
+    expert's weight; ``problem_rows`` bounds the rows of one problem (<= 32,
+    and a plan with grouped phases takes at most 32 rows in its dense ones);
+    ``scatter`` writes sorted row r to ``y`` row ``route[514 + r]``."""
     x: torch.Tensor
     weight: TiledWeight
     y: torch.Tensor
     silu: bool = False
     dep: int = -1
+    route: Optional[torch.Tensor] = None
+    problem_rows: int = 0
+    scatter: bool = False
 
 
 def _check_rows(t: torch.Tensor, name: str, cols: int) -> int:
@@ -126,7 +182,20 @@ class ProjectionPlan:
                     raise ValueError("every tensor of a plan must be on one device")
             w = ph.weight
             m = int(ph.x.shape[0])
-            if not 1 <= m <= MAX_ROWS:
+            grouped = ph.route is not None
+            if grouped:
+                require_cuda(ph.route, "route")
+                if ph.route.dtype != torch.int32 or ph.route.numel() < sorted_route_ints():
+                    raise ValueError(f"phase {i}: route must be the int32 table of sort_pairs")
+                if not 1 <= m <= MAX_GROUPED_ROWS:
+                    raise ValueError(f"phase {i}: {m} sorted rows (1..{MAX_GROUPED_ROWS})")
+                if not 1 <= ph.problem_rows <= MAX_PROBLEM_ROWS:
+                    raise ValueError(f"phase {i}: problem_rows must be 1..{MAX_PROBLEM_ROWS}")
+                if w.n % 128 != 0:
+                    raise ValueError(f"phase {i}: grouped phases need N % 128 == 0")
+            elif ph.scatter:
+                raise ValueError(f"phase {i}: scatter needs a route table (grouped phase)")
+            elif not 1 <= m <= MAX_ROWS:
                 raise ValueError(f"phase {i}: {m} rows (a plan takes 1..{MAX_ROWS} rows per phase; "
                                  "split more rows into one phase per token tile)")
             ldx = _check_rows(ph.x, f"phase {i} x", w.k)
@@ -139,8 +208,12 @@ class ProjectionPlan:
             if not -1 <= ph.dep < i:
                 raise ValueError(f"phase {i}: dep {ph.dep} must name an earlier phase or be -1")
             flags = (PHASE_SILU if ph.silu else 0) | (PHASE_SUBNORMAL if w.subnormal else 0)
+            if grouped:
+                flags |= PHASE_GROUPED | (PHASE_SCATTER if ph.scatter else 0)
             arr[i] = _Phase(ph.x.data_ptr(), ph.y.data_ptr(), w.blob.data_ptr(), m, w.k, w.n,
-                            ldx, ldy, flags, int(ph.dep))
+                            ldx, ldy, flags, int(ph.dep),
+                            ph.route.data_ptr() if grouped else None, w.experts if grouped else 0,
+                            int(ph.problem_rows) if grouped else 0)
         nbytes = int(lib.dfl_qmm_plan_bytes(len(phases)))
         if nbytes == 0:
             raise ValueError(f"{len(phases)} phases is outside the plan limit")

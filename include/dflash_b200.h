@@ -192,6 +192,17 @@ int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q, const u
  * DFL_PHASE_SUBNORMAL must match the subnormal flag of the phase's repack.
  * dep = q (an earlier phase) makes the phase read x only after every output
  * of phase q is written (x may be phase q's y); dep = -1 reads x at once.
+ * DFL_PHASE_GROUPED runs one projection per problem of a sorted route
+ * table (dfl_moe_sort_pairs; route, read on the device when the plan runs):
+ * w_tiled holds `experts` weights [N, K] (N % 128 == 0) tiled one after the
+ * other, x and y have M <= 256 rows (the sorted rows), and problem i
+ * multiplies its rows [route[1+2i], route[3+2i]) (at most problem_rows of
+ * them; a plan with grouped phases runs at a 16- or 32-row token tile, so
+ * problem_rows <= 32 and every dense phase of it has M <= 32) by expert
+ * route[2+2i]'s weight.  With DFL_PHASE_SCATTER
+ * (grouped only) output row r goes to row route[514 + r] of y instead of r.
+ * Expert ids and rows outside the phase's bounds set the device error word
+ * and read expert 0 / store nothing.
  * Results equal dfl_verify_qmm_w4g64 on the same weights up to fp32
  * summation order.  The plan's token tile (16, 32, 64 or 128 rows) follows
  * its largest M, and every phase runs at that tile, so all rows of a phase
@@ -216,6 +227,8 @@ int dfl_verify_qmm_w4g64_noalloc(const uint16_t* x, const uint32_t* w_q, const u
  * ---------------------------------------------------------------------- */
 #define DFL_PHASE_SILU 1
 #define DFL_PHASE_SUBNORMAL 2
+#define DFL_PHASE_GROUPED 4
+#define DFL_PHASE_SCATTER 8
 
 typedef struct dfl_qmm_phase {
   const void* x;        /* bf16 [M, K], row stride ldx elements */
@@ -223,8 +236,11 @@ typedef struct dfl_qmm_phase {
   const void* w_tiled;  /* dfl_repack_w4_tiled output for this [N, K] weight */
   int M, K, N;
   int ldx, ldy;
-  int flags;            /* DFL_PHASE_SILU | DFL_PHASE_SUBNORMAL */
+  int flags;            /* DFL_PHASE_SILU | DFL_PHASE_SUBNORMAL | DFL_PHASE_GROUPED | DFL_PHASE_SCATTER */
   int dep;              /* -1, or an earlier phase whose outputs x reads */
+  const int32_t* route; /* DFL_PHASE_GROUPED: sorted route table (dfl_moe_sort_pairs), else NULL */
+  int experts;          /* DFL_PHASE_GROUPED: experts stacked in w_tiled */
+  int problem_rows;     /* DFL_PHASE_GROUPED: rows of the largest problem (tokens per expert) */
 } dfl_qmm_phase;
 
 size_t dfl_w4_tiled_bytes(int N, int K);
@@ -436,6 +452,37 @@ int dfl_silu_mul_rows_bf16(const uint16_t* gate, const uint16_t* up, int ld, uin
                            int rows, int cols, void* stream);
 int dfl_moe_combine(const uint16_t* pair_out, const float* weights, const uint16_t* shared,
                     uint16_t* y, int T, int top_k, int H, void* stream);
+
+/* Sorted route table for grouped plan phases (DFL_PHASE_GROUPED).
+ * dfl_moe_sort_pairs orders the T * top_k (token, slot) pairs of topk_ids
+ * (int32 [T, top_k], ids in [0, E); T * top_k <= 256) by expert id, then by
+ * pair index (token, then slot), and writes, on the device:
+ *   route (dfl_moe_sorted_route_ints() int32): [0] number P of active
+ *     experts; [1 + 2i] first sorted row of problem i for i <= P
+ *     ([1 + 2P] = T * top_k); [2 + 2i] expert of problem i (ascending);
+ *     [514 + r] pair row (t * top_k + j) of sorted row r;
+ *   x_sorted bf16 [T * top_k, H]: row r = x[pair row r / top_k];
+ *   x_copy (optional, NULL to skip) bf16 [T, H] = x, the input buffer of a
+ *     plan's dense phases (the shared expert), filled by the same launch.
+ * x is bf16 [T, H] with row stride ldx (H % 8 == 0, ldx % 8 == 0, 16-byte
+ * aligned).  An id outside [0, E) sets the device error word and the table
+ * gets P = 0.  The grouped gate/up phase reads x_sorted and writes its rows
+ * in sorted order; the grouped down phase (DFL_PHASE_SCATTER) writes row r
+ * to pair row route[514 + r], so pair_out is ready for dfl_moe_combine.
+ * Replaces the gather/sort inside mlx-lm's SwitchGLU -> mx.gather_qmm
+ * (sort_indices; third party), reached from
+ * dflash_mlx/engine/target_qwen_gdn.py:863-865. */
+size_t dfl_moe_sorted_route_ints(void);
+int dfl_moe_sort_pairs(const int32_t* topk_ids, int T, int top_k, int E, const uint16_t* x,
+                       int ldx, int H, int32_t* route, uint16_t* x_sorted, uint16_t* x_copy,
+                       void* stream);
+/* dfl_moe_route_sorted: dfl_moe_route's top-k ids and weights (same values
+ * bit for bit; T <= 16, E <= 4096) and dfl_moe_sort_pairs' table, sorted rows
+ * and x copy, in one launch (no dfl_moe_route table).  A token whose top-k
+ * finds no finite logit sets the device error word and the table gets P = 0. */
+int dfl_moe_route_sorted(const float* logits, int T, int E, int top_k, const uint16_t* x, int ldx,
+                         int H, int32_t* route, float* weights, int32_t* topk_ids,
+                         uint16_t* x_sorted, uint16_t* x_copy, void* stream);
 
 #ifdef __cplusplus
 }
