@@ -127,6 +127,9 @@ static_assert((kWordProblem + kMaxProblemSlots * kRouteMaxProblems) * 4 <= int(k
 constexpr int kSignalShift = 8;
 constexpr int kWaitShift = 16;
 constexpr int kPublicFlags = 0xFF;
+// internal phase flag (set by the encoder): y takes 16-byte row stores (y
+// 16-byte aligned, ldy and the output width multiples of 8)
+constexpr int kVecStore = 1 << 24;
 static_assert(BLK_BYTES % 1024 == 0, "stage alignment");
 
 template <int MT>
@@ -151,7 +154,12 @@ struct Cfg {
   static constexpr int XS = (MT <= 16) ? 4 : (MT == 128 ? 3 : 2);   // x ring depth (chunks)
   static constexpr int OFF_XRING = NSTAGE * BLK_BYTES;
   static constexpr int OFF_BARS = OFF_XRING + XS * XCHUNK_BYTES;
-  static constexpr int SMEM_BYTES = OFF_BARS + 512 + 1024;
+  // epilogue staging: per epilogue warp one 16-token pass of its 32 output
+  // columns, transposed to token rows (rows padded to 80 bytes)
+  static constexpr int STAGE_ROW_BYTES = 80;
+  static constexpr int STAGE_WARP_BYTES = 16 * STAGE_ROW_BYTES;
+  static constexpr int OFF_STAGE = OFF_BARS + 512;
+  static constexpr int SMEM_BYTES = OFF_STAGE + 4 * STAGE_WARP_BYTES + 1024;
   static constexpr int NASLOT = 8;                     // TMEM A slots (one unit)
   static constexpr int ACC_COL0 = NASLOT * A_COLS;
   static constexpr int ACC_COLS = NACC * MT;           // one accumulator buffer
@@ -171,6 +179,11 @@ struct Cfg {
   static constexpr bool kXReleaseByA = (NSLICE == NUM_MMA_WARPS) && (NCH >= XS);
   static constexpr int EC = 16;
   static constexpr bool kEarlyPartials = (EC == MT);
+  // epilogue: at 32+ token rows the accumulator is read in the MMA fragment
+  // layout and leaves through stmatrix.trans staging in 16-byte row stores
+  // (8x fewer store instructions); 16-row tiles keep one thread per output
+  // column and one store per value (fewer live registers in that variant)
+  static constexpr bool kFragEpi = (MT >= 32);
   static_assert(ACC_COL0 + NACCBUF * ACC_COLS <= TMEM_COLS, "TMEM budget");
   static constexpr int NUM_BARS = 2 * NSTAGE + 2 * NASLOT + 2 * XS + 2 * NACCBUF + NUM_MMA_WARPS;
   static_assert(NUM_BARS * 8 + 16 <= 512, "barrier area");
@@ -280,6 +293,47 @@ __device__ __forceinline__ void dequant8_magic(uint32_t q, uint32_t s, uint32_t 
       "fma.rn.bf16x2 %3, t3, %5, %6;\n\t}"
       : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
       : "r"(q), "r"(s), "r"(b), "r"(0x3F803F80u), "r"(0xC300C300u));
+}
+
+// 16 TMEM lanes x 16 columns of 32-bit: thread t gets lanes t/4 and t/4 + 8,
+// columns 2(t%4) + {0, 1} and 8 + 2(t%4) + {0, 1} (registers: {lane t/4: c,
+// c+1}, {lane t/4+8: c, c+1}, then the same 8 columns further on).
+__device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                 "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+
+// Four 8x8 bf16 matrices from the fragment layout (thread t: row t/4, columns
+// 2(t%4), 2(t%4)+1 of each) stored transposed; thread 8i + j gives the
+// shared address of row j of matrix i.
+__device__ __forceinline__ void stmatrix_x4_trans(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                                  uint32_t d) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr),
+               "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_relaxed_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("st.relaxed.gpu.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ float4 ld_relaxed_v4(const float* p) {
+  float4 v;
+  asm volatile("ld.relaxed.gpu.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  return uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(lo))) |
+         (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(hi))) << 16);
 }
 
 __device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
@@ -794,6 +848,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
         const int g_nt = ph.n_tiles;
         const int* const route = ph.route;
         const int sig_slot = grouped ? (ph.flags >> kSignalShift) & 0xFF : 0;
+        const bool vec = (ph.flags & kVecStore) != 0;
         uint16_t* const y = ph.y;
         const int t_first = u0 / ku, t_last = (u1 - 1) / ku;
         for (int t = t_first; t <= t_last; ++t) {
@@ -833,10 +888,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                                             kWherePartial, p, limit_ns);
               if constexpr (C::kEarlyPartials) {
                 if (pok) {
-                  const uint32_t* slot =
-                      reinterpret_cast<const uint32_t*>(rp.partials) + size_t(2 * c + par) * MT * BN;
+                  if constexpr (C::kFragEpi) {
+                    const float* slot = rp.partials + size_t(2 * c + par) * MT * BN + et * 16;
 #pragma unroll
-                  for (int m = 0; m < MT; ++m) psum[m] += __uint_as_float(ld_relaxed_u32(slot + m * BN + r));
+                    for (int v = 0; v < 4; ++v) {
+                      const float4 q4 = ld_relaxed_v4(slot + 4 * v);
+                      psum[4 * v] += q4.x;
+                      psum[4 * v + 1] += q4.y;
+                      psum[4 * v + 2] += q4.z;
+                      psum[4 * v + 3] += q4.w;
+                    }
+                  } else {
+                    const uint32_t* slot =
+                        reinterpret_cast<const uint32_t*>(rp.partials) + size_t(2 * c + par) * MT * BN;
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) psum[m] += __uint_as_float(ld_relaxed_u32(slot + m * BN + r));
+                  }
                 }
               }
               // every thread has read the slot (or, with several passes, seen
@@ -878,6 +945,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             const int o = ld_field(route + kRouteRowMap + row0 + m);
             return size_t(o >= 0 && o < M ? o : M);
           };
+          if constexpr (!C::kFragEpi) {
+          // 16-token tiles: one thread per output column, one store per value
           const int n = t_loc * BN + r;
           uint32_t* const mine = reinterpret_cast<uint32_t*>(rp.partials) + size_t(2 * cta + par) * MT * BN;
 #pragma unroll 1
@@ -971,6 +1040,153 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                 }
               }
             }
+          }
+          } else {
+          // Pass layout (16 tokens): accumulator lanes are output columns,
+          // TMEM columns tokens.  Thread t of quadrant warp q holds acc[8h + j]
+          // = column 32q + 16h + fa + 8((j >> 1) & 1), token tb + (j & 1) +
+          // 8(j >> 2) of the pass (fa = t / 4, tb = 2(t % 4)): the fragment
+          // layout of the 16x256b TMEM loads, which stmatrix.trans turns into
+          // token rows for 16-byte stores.  Split-K partials keep the same
+          // per-thread assignment: 16 contiguous floats per thread and pass.
+          const int fa = lane >> 2, tb = 2 * (lane & 3);
+          const int n_q = t_loc * BN + 32 * quad;    // first output column of this warp
+          float* const mine = rp.partials + size_t(2 * cta + par) * MT * BN + et * 16;
+          const uint32_t stage_w = smem_u32(smem + C::OFF_STAGE) + uint32_t(quad * C::STAGE_WARP_BYTES);
+#pragma unroll 1
+          for (int c0 = 0; c0 < MT; c0 += C::EC) {
+            // c_lo with several passes: the contributors' partials of this
+            // pass, summed in CTA order, before the accumulator is read
+            float ps[C::EC];
+            if constexpr (!C::kEarlyPartials) {
+              if (collect) {
+#pragma unroll
+                for (int m = 0; m < C::EC; ++m) ps[m] = 0.f;
+                for (int c = c_lo + 1; c <= c_hi; ++c) {
+                  if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
+                  const float* sa = rp.partials + size_t(2 * c + par) * MT * BN + size_t(c0) * BN + et * 16;
+#pragma unroll
+                  for (int v = 0; v < 4; ++v) {
+                    const float4 q4 = ld_relaxed_v4(sa + 4 * v);
+                    ps[4 * v] += q4.x;
+                    ps[4 * v + 1] += q4.y;
+                    ps[4 * v + 2] += q4.z;
+                    ps[4 * v + 3] += q4.w;
+                  }
+                }
+              }
+            }
+            float acc[C::EC];
+            {
+              uint32_t ra[8], rb[8];
+#pragma unroll
+              for (int a = 0; a < C::NACC; ++a) {
+                const uint32_t col = uint32_t(C::ACC_COL0 + buf * C::ACC_COLS + a * MT + c0);
+                tmem_ld_16x256b_x2(lane_base + col, ra);
+                tmem_ld_16x256b_x2(lane_base + (16u << 16) + col, rb);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  acc[i] = (a == 0) ? __uint_as_float(ra[i]) : acc[i] + __uint_as_float(ra[i]);
+                  acc[8 + i] = (a == 0) ? __uint_as_float(rb[i]) : acc[8 + i] + __uint_as_float(rb[i]);
+                }
+              }
+            }
+            if (c0 + C::EC == MT) {
+              // the accumulator buffer is read: the MMAs may reuse it
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&accempty[buf]);
+            }
+            if (!full_tile && cta != c_lo) {
+              // contributor: this pass of its partial into its own slot
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                st_relaxed_v4(mine + size_t(c0) * BN + 4 * v, acc[4 * v], acc[4 * v + 1], acc[4 * v + 2],
+                              acc[4 * v + 3]);
+              continue;
+            }
+            if (collect) {
+              // c_lo: its own accumulator plus the contributors' partial sum
+              if constexpr (C::kEarlyPartials) {
+#pragma unroll
+                for (int m = 0; m < C::EC; ++m) acc[m] += psum[m];
+              } else {
+#pragma unroll
+                for (int m = 0; m < C::EC; ++m) acc[m] += ps[m];
+              }
+            }
+            const int nrows = min(C::EC, rows - c0);
+            if (silu) {
+              // columns in blocks of 32 (16 gate, then the 16 up columns of
+              // the same outputs): this warp's block is quadrant q, so each
+              // thread holds the gate (h = 0) and up (h = 1) values of its
+              // outputs fa, fa + 8 for its four tokens
+              const int hq = (t_loc * 4 + quad) * 16;   // first output of this warp
+              uint32_t hv[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                hv[j] = silu_mul_bits<false>(__bfloat16_as_ushort(__float2bfloat16_rn(acc[j])),
+                                             __bfloat16_as_ushort(__float2bfloat16_rn(acc[8 + j])));
+              if (vec) {
+                const int i = lane >> 3, rho = lane & 7;
+                stmatrix_x4_trans(stage_w + uint32_t(((i >> 1) * 8 + rho) * C::STAGE_ROW_BYTES + (i & 1) * 16),
+                                  hv[0] | (hv[1] << 16), hv[2] | (hv[3] << 16), hv[4] | (hv[5] << 16),
+                                  hv[6] | (hv[7] << 16));
+                __syncwarp();
+                const int m = lane >> 1, ch = lane & 1;
+                if (m < nrows && n_q < N) {
+                  const size_t orow = out_row(c0 + m);
+                  if (orow < size_t(M))
+                    *reinterpret_cast<uint4*>(y + orow * ldy + hq + ch * 8) =
+                        ld_shared_v4(stage_w + uint32_t(m * C::STAGE_ROW_BYTES + ch * 16));
+                }
+                __syncwarp();
+              } else if (n_q < N) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const int k = tb + (j & 1) + 8 * (j >> 2);
+                  if (k < nrows) {
+                    const size_t orow = out_row(c0 + k);
+                    if (orow < size_t(M)) y[orow * ldy + hq + fa + 8 * ((j >> 1) & 1)] = uint16_t(hv[j]);
+                  }
+                }
+              }
+            } else if (vec) {
+              const int i = lane >> 3, rho = lane & 7;
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                stmatrix_x4_trans(
+                    stage_w + uint32_t(((i >> 1) * 8 + rho) * C::STAGE_ROW_BYTES + (2 * h + (i & 1)) * 16),
+                    pack_bf16(acc[8 * h], acc[8 * h + 1]), pack_bf16(acc[8 * h + 2], acc[8 * h + 3]),
+                    pack_bf16(acc[8 * h + 4], acc[8 * h + 5]), pack_bf16(acc[8 * h + 6], acc[8 * h + 7]));
+              __syncwarp();
+              const int ch = lane & 3;
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                const int m = hh * 8 + (lane >> 2);
+                if (m < nrows && n_q + ch * 8 < N) {
+                  const size_t orow = out_row(c0 + m);
+                  if (orow < size_t(M))
+                    *reinterpret_cast<uint4*>(y + orow * ldy + n_q + ch * 8) =
+                        ld_shared_v4(stage_w + uint32_t(m * C::STAGE_ROW_BYTES + ch * 16));
+                }
+              }
+              __syncwarp();
+            } else {
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const int k = tb + (j & 1) + 8 * (j >> 2);
+                  const int nn = n_q + 16 * h + fa + 8 * ((j >> 1) & 1);
+                  if (k < nrows && nn < N) {
+                    const size_t orow = out_row(c0 + k);
+                    if (orow < size_t(M)) y[orow * ldy + nn] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[8 * h + j]));
+                  }
+                }
+            }
+          }
           }
           ++acc_it;
           if (!full_tile && cta != c_lo) {
@@ -1308,7 +1524,9 @@ extern "C" int dfl_qmm_plan_encode(const dfl_qmm_phase* phases, int n_phases, vo
     ph.n_tiles = (q.N + BN - 1) / BN;
     ph.ku = (q.K + UNIT_K - 1) / UNIT_K;
     ph.total = (q.flags & kPhaseGrouped) ? 0 : ph.n_tiles * ph.ku;   // grouped: from the route table
-    ph.flags = q.flags | (sig_slot[p] << kSignalShift) | (wait_slot[p] << kWaitShift);
+    const int n_out = (q.flags & kPhaseSilu) ? q.N / 2 : q.N;
+    const bool vec = host::aligned(q.y, 16) && q.ldy % 8 == 0 && n_out % 8 == 0;
+    ph.flags = q.flags | (sig_slot[p] << kSignalShift) | (wait_slot[p] << kWaitShift) | (vec ? kVecStore : 0);
     ph.dep = q.dep;
     ph.route = (q.flags & kPhaseGrouped) ? q.route : nullptr;
     ph.experts = (q.flags & kPhaseGrouped) ? q.experts : 0;
