@@ -291,7 +291,7 @@ def run_ours(args):
     step = VerifyStep(dev, requests=args.requests_per_gpu, shape=shape, rank=rank, world=world,
                       group=group, weight_layout=args.weight_layout,
                       fuse_silu=args.weight_layout != "mlx" and not args.no_fuse_silu,
-                      qmm_deps=args.qmm_deps)
+                      qmm_deps=args.qmm_deps, collectives_in_graph=not args.collectives_eager)
     sh = step.shape
     b = args.requests_per_gpu
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -437,6 +437,9 @@ def run_ours(args):
                 "qmm_ms_per_step_chained": t_chain,
                 "mlp_silu_fused": step.fuse_silu,
                 "parallelism": f"request-DP x{world}, lm_head vocab split x{world}",
+                "collectives": ("all-gathers captured in the step's second CUDA graph"
+                                if world > 1 and step.collectives_in_graph else
+                                "host-issued between CUDA graphs" if world > 1 else "none"),
                 "l2": "inputs larger than L2 (12.4 GB of packed weights per step)",
                 "qmm_ms_per_step": t_qmm / args.steps * 1e3,
                 "qmm_gbs": achieved,
@@ -510,7 +513,8 @@ def measure_batched(step, args, dev, world: int, rank: int, group) -> dict:
     for name, b in cases:
         s2 = VerifyStep(dev, requests=b, shape=sh, rank=rank, world=world, group=group,
                         weight_layout=step.weight_layout, fuse_silu=step.fuse_silu,
-                        qmm_deps=step.qmm_deps, share_weights=step)
+                        qmm_deps=step.qmm_deps, share_weights=step,
+                        collectives_in_graph=step.collectives_in_graph)
         gen = torch.Generator(device=dev).manual_seed(300 + rank)
         s2.x.copy_(torch.randn(s2.x.shape, generator=gen, device=dev).to(torch.bfloat16))
         s2.verify_ids.copy_(torch.randint(0, sh.vocab, s2.verify_ids.shape, generator=gen, device=dev,
@@ -595,6 +599,7 @@ def measure_other_configs(dev, args) -> dict:
 
     * config0: 16 x 4096 x 4096 int4 verify qmm (MLX packing, the drop-in
       entry), 64 calls over 64 distinct weight copies (621 MB > L2) per graph;
+      config0_plan: the same 64 products as one 64-phase projection plan;
     * moe: the config-2 MoE layer (4 layers with distinct weights per graph);
     * rollback_config4: tape replay of 64 sequences x 48 layers (a ~ U{0..16}
       per sequence, Hk = Hv = 48), in place, one launch;
@@ -632,7 +637,18 @@ def measure_other_configs(dev, args) -> dict:
     out["config0_qmm_us"] = t * 1e6
     out["config0_qmm_gbs"] = b0 / t / 1e9
     out["config0_qmm_frac"] = b0 / t / 1e9 / peak
+    # the same 64 calls as one projection plan (tiled copies of the weights,
+    # 64 independent phases in one launch)
+    from dflash_mlx_b200 import qmm_plan as QP
+    tiled = [QP.tile_weight(q, sc, bi) for q, sc, bi in ws]
     del ws
+    ys = [torch.empty((m, n), dtype=torch.bfloat16, device=dev) for _ in tiled]
+    plan0 = QP.ProjectionPlan([QP.PlanPhase(x0, w, yy) for w, yy in zip(tiled, ys)])
+    t = _graph_time(plan0.run, dev, reps=10) / copies
+    out["config0_plan_us"] = t * 1e6
+    out["config0_plan_gbs"] = b0 / t / 1e9
+    out["config0_plan_frac"] = b0 / t / 1e9 / peak
+    del tiled, plan0, ys
     # config 2
     moe = measure_moe(dev, layers=4, steps=10, warmup=3, fuse_silu=True)
     out["moe_layer_us"] = moe["us_per_layer"]
@@ -862,6 +878,9 @@ def main():
     ap.add_argument("--no-fuse-silu", action="store_true",
                     help="run SiLU*up as its own launch after the gate|up projection")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--collectives-eager", action="store_true",
+                    help="N > 1: issue the lm_head all-gathers from the host between CUDA graphs "
+                         "instead of capturing them in the step graph")
     ap.add_argument("--no-batched", action="store_true",
                     help="skip the batched-request measurements (8 per GPU, and a fixed global "
                          "batch split over the GPUs) carried in the line's config")

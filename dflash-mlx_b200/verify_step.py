@@ -135,10 +135,14 @@ class VerifyStep:
     def __init__(self, device: torch.device, *, requests: int = 1, shape: Optional[StackShape] = None,
                  rank: int = 0, world: int = 1, group=None, seed: int = 0,
                  weight_layout: str = "mlx", fuse_silu: bool = False, pack_requests: bool = True,
-                 qmm_deps: str = "dataflow", share_weights: Optional["VerifyStep"] = None):
+                 qmm_deps: str = "dataflow", share_weights: Optional["VerifyStep"] = None,
+                 collectives_in_graph: bool = True):
         """``share_weights``: another step on the same device, rank and shape
         whose decoder and lm_head weights this one reuses (a different number
-        of requests over the same model)."""
+        of requests over the same model).  ``collectives_in_graph``: with
+        several ranks, capture the all-gathers of the vocabulary-split lm_head
+        in the same CUDA graph as the keys, acceptance and rollback (False:
+        issue them from the host between graphs)."""
         self.dev = torch.device(device)
         if weight_layout not in ("mlx", "pairs", "tiled"):
             raise ValueError(f"unknown weight layout {weight_layout!r}")
@@ -228,6 +232,7 @@ class VerifyStep:
         self.graphs = None
         self.ev = None
         self.qmm_deps = qmm_deps
+        self.collectives_in_graph = collectives_in_graph
         self.plan = self._build_plan(qmm_deps) if weight_layout == "tiled" else None
 
     def _build_plan(self, deps: str = "dataflow") -> ProjectionPlan:
@@ -335,12 +340,31 @@ class VerifyStep:
                      self.tape_g.view(lb, *self.tape_g.shape[2:]),
                      steps.repeat(sh.gdn_layers))
 
+    def _exchange(self, with_collectives: bool = True):
+        """lm_head keys and acceptance + rollback; with several ranks the
+        hidden rows and verify ids are all-gathered before the keys and the
+        8-byte row keys after them (vocabulary split)."""
+        if self.world > 1:
+            import torch.distributed as dist
+
+            if with_collectives:
+                dist.all_gather_into_tensor(self.x_all, self.x, group=self.group)
+                dist.all_gather_into_tensor(self.ids_all, self.verify_ids, group=self.group)
+            self._keys(self.x_all)
+            if with_collectives:
+                dist.all_gather_into_tensor(self.keys_all.view(-1), self.keys, group=self.group)
+        else:
+            self._keys(self.x_all)
+            self.keys_all.view(-1).copy_(self.keys)
+        self._accept_and_rollback(self.keys_all, self.ids_all)
+
     # -------------------------------------------------------------- driving
     def capture(self):
-        """Warm up once eagerly, then capture the three device parts in CUDA
-        graphs: A = qmm stack, B = lm_head keys, C = accept + rollback.  With
-        several ranks the hidden rows, verify ids and keys are all-gathered
-        between the graphs."""
+        """Warm up once eagerly, then capture the device parts in CUDA graphs:
+        A = qmm stack, B = lm_head keys + acceptance + rollback, with the
+        all-gathers of several ranks inside B (``collectives_in_graph``; the
+        eager warm-up creates the communicator first) or issued from the host
+        between the lm_head keys and the rest."""
         sh = self.shape
         rows = self.requests * sh.block
         with torch.cuda.device(self.dev), torch.cuda.stream(self.stream):
@@ -354,17 +378,24 @@ class VerifyStep:
             self.keys_all = torch.empty((self.world, self.world * rows), dtype=torch.int64,
                                         device=self.dev)
             self._qmm_stack()
-            self._keys(self.x_all)
-            self._accept_and_rollback(self.keys_all, self.ids_all)
+            in_graph = self.world == 1 or self.collectives_in_graph
+            self._exchange(with_collectives=in_graph)
             self.stream.synchronize()
-            ga, gb, gc = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            ga = torch.cuda.CUDAGraph()
             with torch.cuda.graph(ga, stream=self.stream):
                 self._qmm_stack()
-            with torch.cuda.graph(gb, stream=self.stream):
-                self._keys(self.x_all)
-            with torch.cuda.graph(gc, stream=self.stream):
-                self._accept_and_rollback(self.keys_all, self.ids_all)
-            self.graphs = [ga, gb, gc]
+            if in_graph:
+                gb = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gb, stream=self.stream):
+                    self._exchange()
+                self.graphs = [ga, gb]
+            else:
+                gb, gc = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gb, stream=self.stream):
+                    self._keys(self.x_all)
+                with torch.cuda.graph(gc, stream=self.stream):
+                    self._accept_and_rollback(self.keys_all, self.ids_all)
+                self.graphs = [ga, gb, gc]
         torch.cuda.synchronize(self.dev)
 
     def run_step(self, ev_qmm: Optional[tuple] = None):
@@ -376,17 +407,17 @@ class VerifyStep:
             self.graphs[0].replay()
             if ev_qmm is not None:
                 ev_qmm[1].record(self.stream)
-            if self.world > 1:
+            if len(self.graphs) == 2:
+                self.graphs[1].replay()
+            else:
+                # several ranks, collectives issued from the host between graphs
                 import torch.distributed as dist
 
                 dist.all_gather_into_tensor(self.x_all, self.x, group=self.group)
                 dist.all_gather_into_tensor(self.ids_all, self.verify_ids, group=self.group)
                 self.graphs[1].replay()
                 dist.all_gather_into_tensor(self.keys_all.view(-1), self.keys, group=self.group)
-            else:
-                self.graphs[1].replay()
-                self.keys_all.view(-1).copy_(self.keys)
-            self.graphs[2].replay()
+                self.graphs[2].replay()
 
     def verify(self, x_host: torch.Tensor, verify_ids_host: torch.Tensor):
         """End-to-end call: copy this rank's inputs from (pinned) host memory,

@@ -167,8 +167,9 @@ def test_key_packing_orders_like_argmax():
 
 def _step_rank_main(rank: int, world: int, port: int, q):
     """One rank of the benchmark step's multi-rank host path on gloo: the
-    library is a recorder (no kernel runs), the three CUDA graphs are the
-    step's parts called directly, the all-gathers between them are real."""
+    library is a recorder (no kernel runs), the two CUDA graphs are the
+    step's parts called directly (the second holds the all-gathers, which are
+    real)."""
     import contextlib
     import types
 
@@ -214,8 +215,7 @@ def _step_rank_main(rank: int, world: int, port: int, q):
         step.keys_all = torch.empty((world, world * rows), dtype=torch.int64)
         step.x.fill_(rank + 1)
         step.verify_ids.fill_(10 * (rank + 1))
-        parts = (step._qmm_stack, lambda: step._keys(step.x_all),
-                 lambda: step._accept_and_rollback(step.keys_all, step.ids_all))
+        parts = (step._qmm_stack, step._exchange)
         step.graphs = [types.SimpleNamespace(replay=f) for f in parts]
         calls.clear()
         step.run_step()
