@@ -173,10 +173,8 @@ __device__ void rank_and_gather(const int* ex, int* first, int* pos, int pairs, 
       }
     }
   }
-  __syncthreads();
+  const int P = __syncthreads_count(tid < pairs && first[tid]);
   if (blockIdx.x == 0 && tid == 0) {
-    int P = 0;
-    for (int p = 0; p < pairs; ++p) P += first[p];
     route[0] = P;
     route[1 + 2 * P] = pairs;
   }
@@ -263,21 +261,29 @@ __global__ void route_sort_kernel(const float* logits, int T, int E, int k, cons
       lv[i] = -INFINITY;
       li[i] = 0x7fffffff;
     }
-    for (int e = lane; e < E; e += 32) {
-      const float v = row[e];
-      if (!beats(v, e, lv[MAX_K - 1], li[MAX_K - 1])) continue;
-      // insertion from the tail: entries (v, e) beats move down one place
+    // this lane's logits, 8 loads in flight at a time
+    for (int e0 = lane; e0 < E; e0 += 32 * 8) {
+      float vb[8];
 #pragma unroll
-      for (int i = MAX_K - 1; i >= 1; --i) {
-        if (beats(v, e, lv[i], li[i])) {
-          const bool above = beats(v, e, lv[i - 1], li[i - 1]);
-          lv[i] = above ? lv[i - 1] : v;
-          li[i] = above ? li[i - 1] : e;
+      for (int u = 0; u < 8; ++u) vb[u] = (e0 + 32 * u < E) ? row[e0 + 32 * u] : -INFINITY;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = e0 + 32 * u;
+        const float v = vb[u];
+        if (e >= E || !beats(v, e, lv[MAX_K - 1], li[MAX_K - 1])) continue;
+        // insertion from the tail: entries (v, e) beats move down one place
+#pragma unroll
+        for (int i = MAX_K - 1; i >= 1; --i) {
+          if (beats(v, e, lv[i], li[i])) {
+            const bool above = beats(v, e, lv[i - 1], li[i - 1]);
+            lv[i] = above ? lv[i - 1] : v;
+            li[i] = above ? li[i - 1] : e;
+          }
         }
-      }
-      if (beats(v, e, lv[0], li[0])) {
-        lv[0] = v;
-        li[0] = e;
+        if (beats(v, e, lv[0], li[0])) {
+          lv[0] = v;
+          li[0] = e;
+        }
       }
     }
     float myv = 0.f;
@@ -425,7 +431,7 @@ extern "C" int dfl_moe_route_sorted(const float* logits, int T, int E, int top_k
       (x_copy && !host::aligned(x_copy, 16)))
     return DFL_ERR_MISALIGNED;
   const int jobs = T * top_k + (x_copy ? T : 0);
-  const int blocks = jobs < 64 ? jobs : 64;
+  const int blocks = jobs < 148 ? jobs : 148;
   moe::route_sort_kernel<<<blocks, 512, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       logits, T, E, top_k, x, ldx, H, route, weights, topk_ids, x_sorted, x_copy);
   return host::launch_status();

@@ -89,6 +89,8 @@ SHAPES = [
     ("m100_ragged", 100, 1600, 384),
     ("m128_o", 128, 6144, 5120),
     ("m128_down", 128, 17408, 5120),
+    # N % 8 != 0 at a 64-row tile: one store per value instead of 16-byte rows
+    ("m40_n196", 40, 1024, 196),
 ]
 
 
@@ -129,7 +131,7 @@ def _gate_up(rng, inter, k):
     return (gq, gs, gb), (uq, us, ub), (inter16(gq, uq), inter16(gs, us), inter16(gb, ub))
 
 
-@pytest.mark.parametrize("m", [16, 128])
+@pytest.mark.parametrize("m", [16, 32, 64, 128])
 def test_silu_phase_equals_silu_of_plain_phase(pkg, dev, m):
     import torch
 
@@ -365,3 +367,70 @@ def test_withheld_partial_times_out_and_the_plan_recovers(pkg, dev):
     _assert_close(bf16_to_np_bits(y0), ref0, "phase 0 after recovery")
     _assert_close(bf16_to_np_bits(y1), oqmm.qmm(bf16_to_np_bits(y0), *w1, accum=np.float32),
                   "phase 1 after recovery")
+
+
+def test_strided_output_rows(pkg, dev):
+    """y rows with a stride that is not a multiple of 8 (a view into a wider
+    buffer) at a 64-row tile: same values as a contiguous y, columns outside
+    the view untouched."""
+    import torch
+
+    rng = np.random.default_rng(21)
+    m, k, n = 48, 1024, 512
+    w_q, s_, b_ = oqmm.synth_weights(rng, n, k)
+    tw = _tiled(pkg, dev, w_q, s_, b_)
+    x = to_dev_bf16(oqmm.synth_x(rng, m, k), dev)
+    wide = torch.full((m, n + 4), 7.0, dtype=torch.bfloat16, device=dev)
+    y = wide[:, 2:2 + n]
+    pkg.ProjectionPlan([pkg.PlanPhase(x, tw, y)]).run()
+    ref = pkg.qmm_tiled(x, tw)
+    assert torch.equal(y, ref)
+    assert torch.all(wide[:, :2] == 7.0) and torch.all(wide[:, 2 + n:] == 7.0)
+
+
+def test_grouped_phases_at_32_rows(pkg, dev):
+    """Grouped gate|up + SiLU and scattered down phases over a sorted route
+    table of 32 tokens x top-2 of 8 experts (problems of up to 32 rows: a
+    32-row token tile), with the shared expert as dense phases, then the
+    combine: equals the MoE oracle."""
+    import torch
+
+    from oracle import moe as omoe
+    from test_moe_gpu import _assert_close, _layer, _oracle
+
+    t, e, h, inter, k = 32, 8, 512, 256, 2
+    x, logits, experts, sh = _layer(pkg, dev, 7, t, e, h, inter, k)
+    logits[:, 1] += 3.0          # expert 1 takes most tokens: a problem of > 16 rows
+    ids_np, w_np = omoe.route_topk(logits.cpu().numpy(), k)
+    counts = np.bincount(ids_np.reshape(-1), minlength=e)
+    assert counts.max() > 16
+    ids = torch.as_tensor(ids_np, device=dev)
+    w = torch.as_tensor(w_np, device=dev)
+    M = pkg.moe
+    gu = M.fuse_expert_gate_up(experts["gate"], experts["up"])
+    tgu = pkg.qmm_plan.tile_expert_stack(gu.q, gu.s, gu.b)
+    tdn = pkg.qmm_plan.tile_expert_stack(experts["down"].q, experts["down"].s, experts["down"].b)
+    from dflash_mlx_b200.verify_qmm import interleave_gate_up
+    sgu = M.QuantWeight(interleave_gate_up(sh["gate"].q, sh["up"].q).contiguous(),
+                        interleave_gate_up(sh["gate"].s, sh["up"].s).contiguous(),
+                        interleave_gate_up(sh["gate"].b, sh["up"].b).contiguous())
+    tsgu = pkg.qmm_plan.tile_weight(sgu.q, sgu.s, sgu.b)
+    tsdn = pkg.qmm_plan.tile_weight(sh["down"].q, sh["down"].s, sh["down"].b)
+    bf = dict(dtype=torch.bfloat16, device=dev)
+    x_in = torch.empty((t, h), **bf)
+    route, xs = M.sort_pairs(ids, x, e, x_copy=x_in)
+    hs = torch.empty((t * k, inter), **bf)
+    pair_out = torch.empty((t * k, h), **bf)
+    hsh = torch.empty((t, inter), **bf)
+    so = torch.empty((t, h), **bf)
+    P = pkg.PlanPhase
+    plan = pkg.ProjectionPlan([
+        P(x_in, tsgu, hsh, silu=True),
+        P(xs, tgu, hs, silu=True, route=route, problem_rows=32),
+        P(hsh, tsdn, so, dep=0),
+        P(hs, tdn, pair_out, dep=1, route=route, problem_rows=32, scatter=True)])
+    plan.run()
+    y = M.combine(pair_out, w, so)
+    _assert_close(bf16_to_np_bits(y), _oracle(x, logits, experts, sh, k))
+    from dflash_mlx_b200 import _lib
+    assert _lib.device_error() == 0
