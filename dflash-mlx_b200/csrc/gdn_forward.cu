@@ -192,8 +192,169 @@ __global__ void __launch_bounds__(THREADS) gdn_forward_tape_kernel(const FwdPara
     store_row<NPL>(p.state_out + head_off + (size_t)(row0 + warp * ROWS_PER_WARP + j) * DK + c0, s[j]);
 }
 
+// Dk = 128 variant: a CTA of 128 threads owns 64 value rows of one head;
+// four consecutive lanes share a pair of rows and lane quad q holds columns
+// 16 i + 4 q + e (i < 8, e < 4) of both, so each step is 10 FP32 operations
+// per shared-memory load or shuffle (k / q chunks are broadcast loads: the
+// lanes of a row pair read 64 contiguous bytes), a dot product ends in two
+// butterfly shuffles inside the four lanes (each lane gets the same sum),
+// and state rows load and store as 64-byte pieces.  Same operations and
+// update order as the general kernel (the tape replays exactly).  The
+// kernel is bound by FP32 issue: 5 operations per state element and step
+// (decay, two for the rank-1 update, two dot-product FMAs).
+constexpr int K128_THREADS = 128;
+constexpr int K128_ROWS = 64;
+
+__host__ __device__ constexpr size_t smem_bytes_k128(int T, int g_vec) {
+  return size_t(T) * 128 * 4 * 2 + size_t(T) * (g_vec ? 128 : 1) * 4 + size_t(T) * 4 +
+         size_t(T) * K128_ROWS * 4 + size_t(T) * 4;
+}
+
+__device__ __forceinline__ float4 lds_f4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+__global__ void __launch_bounds__(K128_THREADS, 4) gdn_forward_tape_k128(const FwdParams p) {
+  constexpr int DK = 128;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int T = p.T;
+  float* k_s = reinterpret_cast<float*>(smem_raw);          // [T][128]
+  float* q_s = k_s + T * DK;                                // [T][128]
+  float* g_s = q_s + T * DK;                                // [T][128] or [T]
+  float* b_s = g_s + T * (p.g_vec ? DK : 1);                // [T]
+  float* v_s = b_s + T;                                     // [T][64]
+  int* m_s = reinterpret_cast<int*>(v_s + T * K128_ROWS);   // [T]
+
+  const int blocks_per_head = p.Dv / K128_ROWS;
+  const int n = blockIdx.x / blocks_per_head;  // b * Hv + hv
+  const int row0 = (blockIdx.x - n * blocks_per_head) * K128_ROWS;
+  const int b = n / p.Hv;
+  const int hv = n - b * p.Hv;
+  const int hk = hv / (p.Hv / p.Hk);
+
+  for (int i = threadIdx.x; i < T * DK; i += K128_THREADS) {
+    const int t = i / DK, d = i - t * DK;
+    const size_t kq = (((size_t)b * T + t) * p.Hk + hk) * DK + d;
+    k_s[i] = __bfloat162float(p.k[kq]);
+    q_s[i] = __bfloat162float(p.q[kq]);
+    if (p.g_vec) g_s[i] = p.g[(((size_t)b * T + t) * p.Hv + hv) * DK + d];
+  }
+  for (int i = threadIdx.x; i < T * K128_ROWS; i += K128_THREADS) {
+    const int t = i / K128_ROWS, r = i - t * K128_ROWS;
+    v_s[i] = __bfloat162float(p.v[(((size_t)b * T + t) * p.Hv + hv) * p.Dv + row0 + r]);
+  }
+  for (int t = threadIdx.x; t < T; t += K128_THREADS) {
+    const size_t bt = ((size_t)b * T + t) * p.Hv + hv;
+    if (!p.g_vec) g_s[t] = p.g[bt];
+    b_s[t] = p.beta[bt];
+    m_s[t] = p.mask ? (p.mask[(size_t)b * T + t] != 0) : 1;
+  }
+
+  const int quad = threadIdx.x & 3;
+  const int pr = threadIdx.x >> 2;             // row pair
+  const int ra = row0 + 2 * pr;                // rows ra, ra + 1
+  const size_t head_off = (size_t)n * p.Dv * DK;
+  const float* src0 = p.state_in + head_off + (size_t)ra * DK + 4 * quad;
+  float s0[32], s1[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 a = *reinterpret_cast<const float4*>(src0 + 16 * i);
+    const float4 c = *reinterpret_cast<const float4*>(src0 + DK + 16 * i);
+    s0[4 * i] = a.x; s0[4 * i + 1] = a.y; s0[4 * i + 2] = a.z; s0[4 * i + 3] = a.w;
+    s1[4 * i] = c.x; s1[4 * i + 1] = c.y; s1[4 * i + 2] = c.z; s1[4 * i + 3] = c.w;
+  }
+  __syncthreads();
+
+  for (int t = 0; t < T; ++t) {
+    const size_t out_off = (((size_t)b * T + t) * p.Hv + hv) * p.Dv + ra;
+    if (!m_s[t]) {
+      if (quad == 0) {
+        p.tape[out_off] = 0.f;
+        p.tape[out_off + 1] = 0.f;
+        p.y[out_off] = __float2bfloat16_rn(0.f);
+        p.y[out_off + 1] = __float2bfloat16_rn(0.f);
+      }
+      continue;
+    }
+    const float* kt = k_s + t * DK + 4 * quad;
+    const float* qt = q_s + t * DK + 4 * quad;
+    const float* gt = g_s + (p.g_vec ? t * DK + 4 * quad : t);
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 k4 = lds_f4(kt + 16 * i);
+      float4 g4;
+      if (p.g_vec) {
+        g4 = lds_f4(gt + 16 * i);
+      } else {
+        g4.x = g4.y = g4.z = g4.w = *gt;
+      }
+      const float kk[4] = {k4.x, k4.y, k4.z, k4.w};
+      const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s0[4 * i + e] = __fmul_rn(s0[4 * i + e], gg[e]);
+        s1[4 * i + e] = __fmul_rn(s1[4 * i + e], gg[e]);
+        a0 = __fmaf_rn(s0[4 * i + e], kk[e], a0);
+        a1 = __fmaf_rn(s1[4 * i + e], kk[e], a1);
+      }
+    }
+    a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 1));
+    a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
+    a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 2));
+    a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 2));
+    const float d0 = __fmul_rn(__fsub_rn(v_s[t * K128_ROWS + 2 * pr], a0), b_s[t]);
+    const float d1 = __fmul_rn(__fsub_rn(v_s[t * K128_ROWS + 2 * pr + 1], a1), b_s[t]);
+    float y0 = 0.f, y1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 k4 = lds_f4(kt + 16 * i);
+      const float4 q4 = lds_f4(qt + 16 * i);
+      const float kk[4] = {k4.x, k4.y, k4.z, k4.w};
+      const float qq[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s0[4 * i + e] = __fadd_rn(s0[4 * i + e], __fmul_rn(kk[e], d0));
+        s1[4 * i + e] = __fadd_rn(s1[4 * i + e], __fmul_rn(kk[e], d1));
+        y0 = __fmaf_rn(s0[4 * i + e], qq[e], y0);
+        y1 = __fmaf_rn(s1[4 * i + e], qq[e], y1);
+      }
+    }
+    y0 = __fadd_rn(y0, __shfl_xor_sync(0xffffffffu, y0, 1));
+    y1 = __fadd_rn(y1, __shfl_xor_sync(0xffffffffu, y1, 1));
+    y0 = __fadd_rn(y0, __shfl_xor_sync(0xffffffffu, y0, 2));
+    y1 = __fadd_rn(y1, __shfl_xor_sync(0xffffffffu, y1, 2));
+    if (quad == 0) {
+      p.tape[out_off] = d0;
+      p.tape[out_off + 1] = d1;
+      p.y[out_off] = __float2bfloat16_rn(y0);
+      p.y[out_off + 1] = __float2bfloat16_rn(y1);
+    }
+  }
+
+  float* dst0 = p.state_out + head_off + (size_t)ra * DK + 4 * quad;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    *reinterpret_cast<float4*>(dst0 + 16 * i) =
+        make_float4(s0[4 * i], s0[4 * i + 1], s0[4 * i + 2], s0[4 * i + 3]);
+    *reinterpret_cast<float4*>(dst0 + DK + 16 * i) =
+        make_float4(s1[4 * i], s1[4 * i + 1], s1[4 * i + 2], s1[4 * i + 3]);
+  }
+}
+
+inline int launch_forward_k128(const FwdParams& p, cudaStream_t stream) {
+  static std::atomic<uint64_t> smem_done{0};
+  int dev, sms;
+  int st = host::current_device(&dev, &sms);
+  if (st != DFL_OK) return st;
+  st = host::ensure_smem(gdn_forward_tape_k128, int(smem_bytes_k128(MAX_STEPS, 1)), dev, smem_done);
+  if (st != DFL_OK) return st;
+  const int grid = p.B * p.Hv * (p.Dv / K128_ROWS);
+  gdn_forward_tape_k128<<<grid, K128_THREADS, smem_bytes_k128(p.T, p.g_vec), stream>>>(p);
+  return host::launch_status();
+}
+
 template <int DK>
 int launch_forward(const FwdParams& p, cudaStream_t stream) {
+  if (DK == 128 && p.Dv % K128_ROWS == 0) return launch_forward_k128(p, stream);
   static std::atomic<uint64_t> smem_done{0};
   const size_t smem = smem_bytes(p.T, DK, p.g_vec);
   int dev, sms;

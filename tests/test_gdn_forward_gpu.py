@@ -67,6 +67,7 @@ def _check(got, ref):
     (1, 7, 1, 2, 64, 32, False),        # ragged T, Dk 64
     (1, 5, 2, 2, 256, 32, True),        # Dk 256
     (3, 16, 1, 1, 32, 32, False),       # Dk 32
+    (1, 9, 2, 2, 128, 96, True),        # Dk 128 with Dv % 64 != 0 (general kernel)
 ])
 def test_forward_tape_matches_oracle(pkg, dev, b, t, hk, hv, dk, dv, vec):
     q, k, v, g, beta, s0 = _inputs(b * 100 + t + dk, b, t, hk, hv, dk, dv, vec)
