@@ -46,6 +46,7 @@ struct ReplayParams {
   int B, T, Hv, Hk, Dv, Dk;
   int g_vec;
   int vec;                // tape, k, g 16-byte aligned and Dv % 4 == 0: stage by cp.async
+  int parts;              // CTAs per head (row slices of Dv / parts rows)
 };
 
 // Four consecutive k values from shared memory as floats (bf16 -> fp32 is exact).
@@ -74,11 +75,19 @@ __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint8_t* src, int
   }
 }
 
-template <typename KT, int DK>
-__global__ void __launch_bounds__(THREADS)
+// NCH: float4 state chunks per thread (16: a whole head of up to 16384
+// elements per CTA; 8: heads of more than 8192 elements split by rows over
+// `parts` CTAs with half the registers, three CTAs per SM: config 4's
+// 64 x 48 x 48 heads in 5.10 ms instead of 5.44; four per SM spilled and
+// was slower).
+template <typename KT, int DK, int NCH>
+__global__ void __launch_bounds__(THREADS, NCH <= 8 ? 3 : 1)
     tape_replay_kernel(const ReplayParams p) {
   extern __shared__ float sh[];
-  const int head = blockIdx.x;          // b * Hv + hv
+  const int head = blockIdx.x / p.parts;          // b * Hv + hv
+  const int part = blockIdx.x - head * p.parts;
+  const int rows = p.Dv / p.parts;                // value rows of this CTA
+  const int r0 = part * rows;
   const int b = head / p.Hv;
   const int hv = head - b * p.Hv;
   const int hk = hv / (p.Hv / p.Hk);
@@ -92,8 +101,8 @@ __global__ void __launch_bounds__(THREADS)
   for (int t = 0; t < nsteps; ++t)
     if (!p.mask || p.mask[(size_t)b * p.T + t]) active |= (uint64_t(1) << t);
 
-  const int dv_dk = p.Dv * DK;
-  const size_t sbase = (size_t)head * dv_dk;
+  const int dv_dk = rows * DK;
+  const size_t sbase = (size_t)head * p.Dv * DK + (size_t)r0 * DK;
   const float4* src = reinterpret_cast<const float4*>(p.state_in + sbase);
   float4* dst = reinterpret_cast<float4*>(p.state_out + sbase);
   const int n4 = dv_dk / 4;
@@ -108,10 +117,10 @@ __global__ void __launch_bounds__(THREADS)
   // staging copies below are all in flight together.  Thread tid owns float4
   // chunks f = j * THREADS + tid: row dv = 4f / DK, columns dk0..dk0+3 with
   // dk0 = 4f % DK = (4 * tid) % DK (DK divides 1024).
-  float4 st[MAX_CHUNKS];
+  float4 st[NCH];
   const int nchunk = (n4 + THREADS - 1) / THREADS;
 #pragma unroll
-  for (int j = 0; j < MAX_CHUNKS; ++j) {
+  for (int j = 0; j < NCH; ++j) {
     const int f = j * THREADS + tid;
     if (j < nchunk && f < n4) st[j] = __ldcs(src + f);
   }
@@ -135,7 +144,7 @@ __global__ void __launch_bounds__(THREADS)
       stage_rows(reinterpret_cast<uint8_t*>(s_g), reinterpret_cast<const uint8_t*>(p.g + g_row0 * DK),
                  nsteps, DK * 4, (size_t)p.Hv * DK * 4, tid);
     stage_rows(reinterpret_cast<uint8_t*>(s_delta),
-               reinterpret_cast<const uint8_t*>(p.tape + g_row0 * p.Dv), nsteps, p.Dv * 4,
+               reinterpret_cast<const uint8_t*>(p.tape + g_row0 * p.Dv + r0), nsteps, rows * 4,
                (size_t)p.Hv * p.Dv * 4, tid);
   } else {
     for (int i = tid; i < nsteps * DK; i += THREADS) {
@@ -147,9 +156,9 @@ __global__ void __launch_bounds__(THREADS)
         const int t = i / DK, dk = i - t * DK;
         s_g[i] = p.g[(g_row0 + (size_t)t * p.Hv) * DK + dk];
       }
-    for (int i = tid; i < nsteps * p.Dv; i += THREADS) {
-      const int t = i / p.Dv, dv = i - t * p.Dv;
-      s_delta[i] = p.tape[(g_row0 + (size_t)t * p.Hv) * p.Dv + dv];
+    for (int i = tid; i < nsteps * rows; i += THREADS) {
+      const int t = i / rows, dv = i - t * rows;
+      s_delta[i] = p.tape[(g_row0 + (size_t)t * p.Hv) * p.Dv + r0 + dv];
     }
   }
   if (!p.g_vec)
@@ -169,11 +178,11 @@ __global__ void __launch_bounds__(THREADS)
       gv = make_float4(g0, g0, g0, g0);
     }
 #pragma unroll
-    for (int j = 0; j < MAX_CHUNKS; ++j) {
+    for (int j = 0; j < NCH; ++j) {
       const int f = j * THREADS + tid;
       if (j < nchunk && f < n4) {
         const int dv = (4 * f) / DK;
-        const float d = s_delta[t * p.Dv + dv];
+        const float d = s_delta[t * rows + dv];
         float4 s = st[j];
         s.x = __fadd_rn(__fmul_rn(s.x, gv.x), __fmul_rn(d, kv.x));
         s.y = __fadd_rn(__fmul_rn(s.y, gv.y), __fmul_rn(d, kv.y));
@@ -185,26 +194,26 @@ __global__ void __launch_bounds__(THREADS)
   }
 
 #pragma unroll
-  for (int j = 0; j < MAX_CHUNKS; ++j) {
+  for (int j = 0; j < NCH; ++j) {
     const int f = j * THREADS + tid;
     if (j < nchunk && f < n4) __stcs(dst + f, st[j]);
   }
 }
 
-template <typename KT>
+template <typename KT, int NCH>
 int launch_replay(const ReplayParams& p, cudaStream_t stream) {
   const int gw = p.g_vec ? p.Dk : 1;
-  const size_t smem = size_t(p.T) * (p.Dv + p.Dk + gw) * sizeof(float) + 16;
-  const int grid = p.B * p.Hv;
+  const size_t smem = size_t(p.T) * (p.Dv / p.parts + p.Dk + gw) * sizeof(float) + 16;
+  const int grid = p.B * p.Hv * p.parts;
   switch (p.Dk) {
 #define DFL_CASE(D)                                                                        \
   case D: {                                                                                \
     static std::atomic<uint64_t> done{0};                                                  \
     int dev = 0;                                                                           \
     if (cudaGetDevice(&dev) != cudaSuccess) return DFL_ERR_CUDA;                           \
-    int st = host::ensure_smem(tape_replay_kernel<KT, D>, kMaxSmem, dev, done);             \
+    int st = host::ensure_smem(tape_replay_kernel<KT, D, NCH>, kMaxSmem, dev, done);        \
     if (st != DFL_OK) return st;                                                           \
-    tape_replay_kernel<KT, D><<<grid, THREADS, smem, stream>>>(p);                         \
+    tape_replay_kernel<KT, D, NCH><<<grid, THREADS, smem, stream>>>(p);                    \
     break;                                                                                 \
   }
     DFL_CASE(32)
@@ -255,6 +264,12 @@ extern "C" int dfl_gdn_tape_replay(const float* tape, const void* k, int k_is_bf
   p.g_vec = g_vectorized ? 1 : 0;
   p.vec = (Dv % 4 == 0 && host::aligned(tape, 16) && host::aligned(k, 16) && host::aligned(g, 16))
               ? 1 : 0;
+  // heads of more than 8192 state elements: two CTAs of Dv / 2 rows each
+  // (when the half keeps 16-byte rows of the tape: Dv / 2 % 4 == 0)
+  const bool split = (long long)Dv * Dk > 8 * gdn::THREADS * 4 && Dv % 8 == 0;
+  p.parts = split ? 2 : 1;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return k_is_bf16 ? gdn::launch_replay<__nv_bfloat16>(p, s) : gdn::launch_replay<float>(p, s);
+  if (split)
+    return k_is_bf16 ? gdn::launch_replay<__nv_bfloat16, 8>(p, s) : gdn::launch_replay<float, 8>(p, s);
+  return k_is_bf16 ? gdn::launch_replay<__nv_bfloat16, 16>(p, s) : gdn::launch_replay<float, 16>(p, s);
 }
