@@ -30,6 +30,9 @@ def test_reference_arm_prints_one_contract_line():
     assert d["impl"] == "reference"
     assert d["metric"] == bench.METRIC and d["unit"] == bench.UNIT
     assert d["value"] > 0 and d["ms_per_step"] > 0
+    # a step is the bounded sample that ran; value extrapolates it to a whole verify step
+    assert d["extrapolated_ms_per_step"] > d["ms_per_step"]
+    assert abs(d["value"] - 1e3 / d["extrapolated_ms_per_step"]) < 1e-9 * d["value"] + 1e-12
     assert (d["n_gpus"], d["steps"]) == (1, 1)
     assert d["warmup"] == 3  # fewer than 3 warm-up steps are raised to 3
     assert d["higher_is_better"] is True and d["scaling"] == "weak"
