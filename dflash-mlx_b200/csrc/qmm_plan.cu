@@ -113,13 +113,17 @@ constexpr int kWordWhereCta = kMaxPhases + 3;          // first time-out: CTA
 constexpr int kWordDiag = kMaxPhases + 4;              // [8] details of the first time-out
 // per CTA and phase parity: the phase (+1) whose partial the slot holds, and
 // the phase (+1) whose partial its consumer has read
-constexpr int kWordReady = kMaxPhases + 16;            // [kMaxGrid][2]
-constexpr int kWordConsumed = kWordReady + 2 * kMaxGrid;  // [kMaxGrid][2]
+// split-K partial slots per CTA: one per phase modulo kSlotPhases, so a
+// contributor refills a slot only kSlotPhases phases later (its consumer,
+// a neighbouring CTA, may lag that far behind before it holds it up)
+constexpr int kSlotPhases = 4;
+constexpr int kWordReady = kMaxPhases + 16;            // [kMaxGrid][kSlotPhases]
+constexpr int kWordConsumed = kWordReady + kSlotPhases * kMaxGrid;  // [kMaxGrid][kSlotPhases]
 // per-problem tile counters of grouped phases that a later grouped phase
 // reads per problem: [slot][kRouteMaxProblems]
-constexpr int kWordProblem = 8704;
+constexpr int kWordProblem = 9472;
 constexpr int kMaxProblemSlots = 16;
-static_assert(kWordConsumed + 2 * kMaxGrid <= kWordProblem, "counter region layout");
+static_assert(kWordConsumed + kSlotPhases * kMaxGrid <= kWordProblem, "counter region layout");
 static_assert((kWordProblem + kMaxProblemSlots * kRouteMaxProblems) * 4 <= int(kCounterBytes),
               "counter region");
 // internal phase flag fields (set by the encoder): the problem-counter slot
@@ -228,7 +232,7 @@ struct RunParams {
   int prob_slots;
   unsigned long long wait_limit_ns;
   int* words;           // workspace counter words
-  float* partials;      // workspace [grid][2][MT][BN]
+  float* partials;      // workspace [grid][kSlotPhases][MT][BN]
 };
 
 __device__ __forceinline__ uint64_t policy_evict_first() {
@@ -828,7 +832,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
     int* const consumed = rp.words + kWordConsumed;
 
     int acc_it = 0;
-    int lastw[2] = {0, 0};  // phase + 1 of this CTA's last partial per slot parity
+    int lastw[kSlotPhases] = {0, 0, 0, 0};  // phase + 1 of this CTA's last partial per slot
     bool ok = true;
     int n_total = phase_total<GROUPED>(phases, 0), n_ku = ld_field(&phases[0].ku);
     for (int p = 0; ok && p < P; ++p) {
@@ -839,7 +843,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
         n_ku = ld_field(&phases[p + 1].ku);
       }
       const int u0 = unit_begin(cta, total, G), u1 = unit_begin(cta + 1, total, G);
-      const int par = p & 1;
+      const int par = p % kSlotPhases;
       if (u0 < u1) {
         const int M = ph.M, N = ph.N, ldy = ph.ldy;
         const bool silu = (ph.flags & kPhaseSilu) != 0;
@@ -863,8 +867,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             // must have read it before the slot is refilled (almost always
             // already true)
             bool gok = true;
-            if (et == 0 && lastw[par] > 0 && ld_acquire(consumed + 2 * cta + par) < lastw[par])
-              gok = wait_counter(consumed + 2 * cta + par, lastw[par], abort_word, plan_abort, words,
+            if (et == 0 && lastw[par] > 0 && ld_acquire(consumed + kSlotPhases * cta + par) < lastw[par])
+              gok = wait_counter(consumed + kSlotPhases * cta + par, lastw[par], abort_word, plan_abort, words,
                                  kWhereGuard, p, limit_ns);
             if (!epi_all(gok && !*abort_word)) {
               ok = false;
@@ -884,12 +888,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             }
             for (int c = c_lo + 1; ok && c <= c_hi; ++c) {
               if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
-              const bool pok = wait_counter(ready + 2 * c + par, p + 1, abort_word, plan_abort, words,
+              const bool pok = wait_counter(ready + kSlotPhases * c + par, p + 1, abort_word, plan_abort, words,
                                             kWherePartial, p, limit_ns);
               if constexpr (C::kEarlyPartials) {
                 if (pok) {
                   if constexpr (C::kFragEpi) {
-                    const float* slot = rp.partials + size_t(2 * c + par) * MT * BN + et * 16;
+                    const float* slot = rp.partials + size_t(kSlotPhases * c + par) * MT * BN + et * 16;
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
                       const float4 q4 = ld_relaxed_v4(slot + 4 * v);
@@ -900,7 +904,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                     }
                   } else {
                     const uint32_t* slot =
-                        reinterpret_cast<const uint32_t*>(rp.partials) + size_t(2 * c + par) * MT * BN;
+                        reinterpret_cast<const uint32_t*>(rp.partials) + size_t(kSlotPhases * c + par) * MT * BN;
 #pragma unroll
                     for (int m = 0; m < MT; ++m) psum[m] += __uint_as_float(ld_relaxed_u32(slot + m * BN + r));
                   }
@@ -912,7 +916,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                 ok = false;
                 break;
               }
-              if (C::kEarlyPartials && et == 0) st_release(consumed + 2 * c + par, p + 1);
+              if (C::kEarlyPartials && et == 0) st_release(consumed + kSlotPhases * c + par, p + 1);
             }
             if (!ok) break;
           }
@@ -948,7 +952,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
           if constexpr (!C::kFragEpi) {
           // 16-token tiles: one thread per output column, one store per value
           const int n = t_loc * BN + r;
-          uint32_t* const mine = reinterpret_cast<uint32_t*>(rp.partials) + size_t(2 * cta + par) * MT * BN;
+          uint32_t* const mine = reinterpret_cast<uint32_t*>(rp.partials) + size_t(kSlotPhases * cta + par) * MT * BN;
 #pragma unroll 1
           for (int c0 = 0; c0 < MT; c0 += C::EC) {
             // c_lo with several passes: the contributors' partials of this
@@ -962,7 +966,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                 for (int c = c_lo + 1; c <= c_hi; ++c) {
                   if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
                   const uint32_t* sa = reinterpret_cast<const uint32_t*>(rp.partials) +
-                                       size_t(2 * c + par) * MT * BN + size_t(c0) * BN + r;
+                                       size_t(kSlotPhases * c + par) * MT * BN + size_t(c0) * BN + r;
 #pragma unroll
                   for (int m = 0; m < C::EC; ++m) ps[m] += __uint_as_float(ld_relaxed_u32(sa + m * BN));
                 }
@@ -1051,7 +1055,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
           // per-thread assignment: 16 contiguous floats per thread and pass.
           const int fa = lane >> 2, tb = 2 * (lane & 3);
           const int n_q = t_loc * BN + 32 * quad;    // first output column of this warp
-          float* const mine = rp.partials + size_t(2 * cta + par) * MT * BN + et * 16;
+          float* const mine = rp.partials + size_t(kSlotPhases * cta + par) * MT * BN + et * 16;
           const uint32_t stage_w = smem_u32(smem + C::OFF_STAGE) + uint32_t(quad * C::STAGE_WARP_BYTES);
 #pragma unroll 1
           for (int c0 = 0; c0 < MT; c0 += C::EC) {
@@ -1064,7 +1068,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                 for (int m = 0; m < C::EC; ++m) ps[m] = 0.f;
                 for (int c = c_lo + 1; c <= c_hi; ++c) {
                   if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
-                  const float* sa = rp.partials + size_t(2 * c + par) * MT * BN + size_t(c0) * BN + et * 16;
+                  const float* sa = rp.partials + size_t(kSlotPhases * c + par) * MT * BN + size_t(c0) * BN + et * 16;
 #pragma unroll
                   for (int v = 0; v < 4; ++v) {
                     const float4 q4 = ld_relaxed_v4(sa + 4 * v);
@@ -1198,7 +1202,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             }
             // (a test can make one CTA withhold its partials: the consumer's
             // bounded wait then runs out and the plan winds down)
-            if (et == 0 && cta != rp.skip_partial_cta) st_release(ready + 2 * cta + par, p + 1);
+            if (et == 0 && cta != rp.skip_partial_cta) st_release(ready + kSlotPhases * cta + par, p + 1);
             lastw[par] = p + 1;
             continue;
           }
@@ -1211,7 +1215,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
             if (et == 0)
               for (int c = c_lo + 1; c <= c_hi; ++c)
                 if (unit_begin(c, total, G) != unit_begin(c + 1, total, G))
-                  st_release(consumed + 2 * c + par, p + 1);
+                  st_release(consumed + kSlotPhases * c + par, p + 1);
           }
           if (sig_slot > 0) {
             // the tile's final values are stored (the barrier orders every
@@ -1250,7 +1254,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
   if (*last_flag) {
     __threadfence();
     for (int i = threadIdx.x; i < P; i += NUM_THREADS) rp.words[i] = 0;
-    for (int i = threadIdx.x; i < 4 * kMaxGrid; i += NUM_THREADS) rp.words[kWordReady + i] = 0;
+    for (int i = threadIdx.x; i < 2 * kSlotPhases * kMaxGrid; i += NUM_THREADS) rp.words[kWordReady + i] = 0;
     for (int i = threadIdx.x; i < rp.prob_slots * kRouteMaxProblems; i += NUM_THREADS)
       rp.words[kWordProblem + i] = 0;
     if (threadIdx.x == 0) {
@@ -1348,7 +1352,7 @@ inline size_t tiled_bytes(int N, int K) {
 inline size_t plan_bytes(int n) { return kHeaderBytes + size_t(n) * sizeof(Phase); }
 
 inline size_t workspace_bytes(int mt, int grid) {
-  return kCounterBytes + size_t(grid) * 2 * mt * BN * sizeof(float);
+  return kCounterBytes + size_t(grid) * kSlotPhases * mt * BN * sizeof(float);
 }
 
 // GROUPED: the plan has grouped phases (route tables); plans without any run
