@@ -886,11 +886,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
 #pragma unroll
               for (int m = 0; m < MT; ++m) psum[m] = 0.f;
             }
-            for (int c = c_lo + 1; ok && c <= c_hi; ++c) {
-              if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
-              const bool pok = wait_counter(ready + kSlotPhases * c + par, p + 1, abort_word, plan_abort, words,
-                                            kWherePartial, p, limit_ns);
-              if constexpr (C::kEarlyPartials) {
+            if constexpr (C::kEarlyPartials) {
+              // 16-row tiles (one or two contributors, usually): each
+              // contributor's stamp, its partial summed in CTA order, then
+              // its slot released
+              for (int c = c_lo + 1; ok && c <= c_hi; ++c) {
+                if (unit_begin(c, total, G) == unit_begin(c + 1, total, G)) continue;
+                const bool pok = wait_counter(ready + kSlotPhases * c + par, p + 1, abort_word, plan_abort,
+                                              words, kWherePartial, p, limit_ns);
                 if (pok) {
                   if constexpr (C::kFragEpi) {
                     const float* slot = rp.partials + size_t(kSlotPhases * c + par) * MT * BN + et * 16;
@@ -909,14 +912,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) qmm_plan_kernel(const __grid_c
                     for (int m = 0; m < MT; ++m) psum[m] += __uint_as_float(ld_relaxed_u32(slot + m * BN + r));
                   }
                 }
+                // every thread has read the slot: its contributor may refill it
+                if (!epi_all(pok && !*abort_word)) {
+                  ok = false;
+                  break;
+                }
+                if (et == 0) st_release(consumed + kSlotPhases * c + par, p + 1);
               }
-              // every thread has read the slot (or, with several passes, seen
-              // its stamp): with one pass its contributor may refill it now
-              if (!epi_all(pok && !*abort_word)) {
-                ok = false;
-                break;
+            } else {
+              // 32+ rows (partials summed pass by pass below): every
+              // contributor's stamp awaited by its own epilogue thread
+              // (acquire), then one barrier makes all of them visible to
+              // every thread (acquire + bar.sync) instead of one wait and
+              // barrier per contributor in turn
+              bool pok = true;
+              for (int j = et; j < c_hi - c_lo; j += 128) {
+                const int c = c_lo + 1 + j;
+                if (unit_begin(c, total, G) != unit_begin(c + 1, total, G))
+                  pok = pok && wait_counter(ready + kSlotPhases * c + par, p + 1, abort_word, plan_abort, words,
+                                            kWherePartial, p, limit_ns);
               }
-              if (C::kEarlyPartials && et == 0) st_release(consumed + kSlotPhases * c + par, p + 1);
+              if (!epi_all(pok && !*abort_word)) ok = false;
             }
             if (!ok) break;
           }
