@@ -78,8 +78,8 @@ SIGNATURES = {
     "dfl_moe_sorted_route_ints": (_c_size, []),
     "dfl_moe_sort_pairs": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp,
                                     _vp]),
-    "dfl_moe_route_sorted": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp,
-                                      _vp, _vp, _vp]),
+    "dfl_moe_route_sorted": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp,
+                                      _vp, _vp, _vp, _vp]),
     "dfl_w4_tiled_bytes": (_c_size, [_c_int, _c_int]),
     "dfl_repack_w4_tiled": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
     "dfl_qmm_plan_bytes": (_c_size, [_c_int]),

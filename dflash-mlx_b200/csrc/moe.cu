@@ -143,9 +143,12 @@ __global__ void combine_kernel(const uint16_t* pair_out, const float* weights, c
 //   route[kRouteRowMap + r] = pair row of sorted row r.
 // ex[] holds the pairs' expert ids (validated by the caller), first[] and
 // pos[] are shared scratch of the same length.
+// shared >= 0: one more problem after the routed ones, expert `shared`, whose
+// rows are the T tokens themselves (sorted rows pairs .. pairs + T - 1, row
+// map to pair rows pairs + t): a shared expert run as one more grouped problem.
 __device__ void rank_and_gather(const int* ex, int* first, int* pos, int pairs, int top_k,
                                 const uint16_t* x, int ldx, int H, int32_t* route,
-                                uint16_t* x_sorted, uint16_t* x_copy, int T) {
+                                uint16_t* x_sorted, uint16_t* x_copy, int T, int shared) {
   const int tid = threadIdx.x;
   for (int p = tid; p < pairs; p += blockDim.x) {
     int f = 1;
@@ -174,23 +177,38 @@ __device__ void rank_and_gather(const int* ex, int* first, int* pos, int pairs, 
     }
   }
   const int P = __syncthreads_count(tid < pairs && first[tid]);
-  if (blockIdx.x == 0 && tid == 0) {
-    route[0] = P;
-    route[1 + 2 * P] = pairs;
+  if (blockIdx.x == 0) {
+    if (tid == 0) {
+      route[1 + 2 * P] = pairs;
+      if (shared >= 0) {
+        route[0] = P + 1;
+        route[2 + 2 * P] = shared;
+        route[3 + 2 * P] = pairs + T;
+      } else {
+        route[0] = P;
+      }
+    }
+    if (shared >= 0)
+      for (int t = tid; t < T; t += blockDim.x) route[plan::kRouteRowMap + pairs + t] = pairs + t;
   }
-  // rows: x_sorted[pos[p]] = x[p / top_k] (16-byte words); the caller's x
-  // copied whole into x_copy by the same CTAs
+  // rows: x_sorted[pos[p]] = x[p / top_k] (16-byte words), then the shared
+  // expert's rows x_sorted[pairs + t] = x[t], then the caller's x copied
+  // whole into x_copy, by the same CTAs
   const int words = H / 8;
-  const int jobs = pairs + (x_copy ? T : 0);
+  const int n_shared = shared >= 0 ? T : 0;
+  const int jobs = pairs + n_shared + (x_copy ? T : 0);
   for (int j = blockIdx.x; j < jobs; j += gridDim.x) {
     const uint4* src;
     uint4* dst;
     if (j < pairs) {
       src = reinterpret_cast<const uint4*>(x + size_t(j / top_k) * ldx);
       dst = reinterpret_cast<uint4*>(x_sorted + size_t(pos[j]) * H);
-    } else {
+    } else if (j < pairs + n_shared) {
       src = reinterpret_cast<const uint4*>(x + size_t(j - pairs) * ldx);
-      dst = reinterpret_cast<uint4*>(x_copy + size_t(j - pairs) * H);
+      dst = reinterpret_cast<uint4*>(x_sorted + size_t(j) * H);
+    } else {
+      src = reinterpret_cast<const uint4*>(x + size_t(j - pairs - n_shared) * ldx);
+      dst = reinterpret_cast<uint4*>(x_copy + size_t(j - pairs - n_shared) * H);
     }
     for (int i = tid; i < words; i += blockDim.x) dst[i] = src[i];
   }
@@ -222,7 +240,7 @@ __global__ void sort_pairs_kernel(const int32_t* topk_ids, int pairs, int top_k,
     }
     return;
   }
-  rank_and_gather(ex, first, pos, pairs, top_k, x, ldx, H, route, x_sorted, x_copy, T);
+  rank_and_gather(ex, first, pos, pairs, top_k, x, ldx, H, route, x_sorted, x_copy, T, -1);
 }
 
 constexpr int kRouteSortMaxExperts = 4096;
@@ -241,9 +259,9 @@ __device__ __forceinline__ bool beats(float v, int e, float w, int f) {
 // for bit); CTA 0 stores weights and ids; then every CTA ranks the pairs and
 // copies its share of the rows (rank_and_gather).  A top-k with no winner
 // (NaN logits) sets the device error word and the table gets P = 0.
-__global__ void route_sort_kernel(const float* logits, int T, int E, int k, const uint16_t* x,
-                                  int ldx, int H, int32_t* route, float* weights, int32_t* topk,
-                                  uint16_t* x_sorted, uint16_t* x_copy) {
+__global__ void route_sort_kernel(const float* logits, int T, int E, int k, int shared,
+                                  const uint16_t* x, int ldx, int H, int32_t* route, float* weights,
+                                  int32_t* topk, uint16_t* x_sorted, uint16_t* x_copy) {
   __shared__ int ex[plan::kRouteMaxRows];
   __shared__ int first[plan::kRouteMaxRows];
   __shared__ int pos[plan::kRouteMaxRows];
@@ -336,7 +354,7 @@ __global__ void route_sort_kernel(const float* logits, int T, int E, int k, cons
     }
     return;
   }
-  rank_and_gather(ex, first, pos, T * k, k, x, ldx, H, route, x_sorted, x_copy, T);
+  rank_and_gather(ex, first, pos, T * k, k, x, ldx, H, route, x_sorted, x_copy, T, shared);
 }
 
 }  // namespace moe
@@ -416,23 +434,24 @@ extern "C" int dfl_moe_sort_pairs(const int32_t* topk_ids, int T, int top_k, int
   return host::launch_status();
 }
 
-extern "C" int dfl_moe_route_sorted(const float* logits, int T, int E, int top_k, const uint16_t* x,
-                                    int ldx, int H, int32_t* route, float* weights,
+extern "C" int dfl_moe_route_sorted(const float* logits, int T, int E, int top_k, int shared_expert,
+                                    const uint16_t* x, int ldx, int H, int32_t* route, float* weights,
                                     int32_t* topk_ids, uint16_t* x_sorted, uint16_t* x_copy,
                                     void* stream) {
   using namespace dfl;
   if (T < 1 || T > moe::MAX_TOKENS || E < 1 || E > moe::kRouteSortMaxExperts || top_k < 1 ||
-      top_k > moe::MAX_K || top_k > E || T * top_k > plan::kRouteMaxRows || H < 8 || H % 8 != 0 ||
-      ldx < H || ldx % 8 != 0)
+      top_k > moe::MAX_K || top_k > E || T * top_k + (shared_expert ? T : 0) > plan::kRouteMaxRows ||
+      H < 8 || H % 8 != 0 || ldx < H || ldx % 8 != 0 || (shared_expert != 0 && shared_expert != 1))
     return DFL_ERR_BAD_SHAPE;
   if (!logits || !x || !route || !weights || !topk_ids || !x_sorted) return DFL_ERR_NULL_POINTER;
   if (!host::aligned(logits, 4) || !host::aligned(route, 4) || !host::aligned(weights, 4) ||
       !host::aligned(topk_ids, 4) || !host::aligned(x, 16) || !host::aligned(x_sorted, 16) ||
       (x_copy && !host::aligned(x_copy, 16)))
     return DFL_ERR_MISALIGNED;
-  const int jobs = T * top_k + (x_copy ? T : 0);
+  const int jobs = T * top_k + (shared_expert ? T : 0) + (x_copy ? T : 0);
   const int blocks = jobs < 148 ? jobs : 148;
   moe::route_sort_kernel<<<blocks, 512, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      logits, T, E, top_k, x, ldx, H, route, weights, topk_ids, x_sorted, x_copy);
+      logits, T, E, top_k, shared_expert ? E : -1, x, ldx, H, route, weights, topk_ids, x_sorted,
+      x_copy);
   return host::launch_status();
 }

@@ -286,10 +286,14 @@ def sort_pairs(topk_ids: torch.Tensor, x: torch.Tensor, n_experts: int, *,
 
 def route_sorted(router_logits: torch.Tensor, x: torch.Tensor, top_k: int, *,
                  route_out: torch.Tensor, x_sorted: torch.Tensor, x_copy: Optional[torch.Tensor] = None,
-                 weights_out: Optional[torch.Tensor] = None, ids_out: Optional[torch.Tensor] = None):
+                 weights_out: Optional[torch.Tensor] = None, ids_out: Optional[torch.Tensor] = None,
+                 shared_expert: bool = False):
     """:func:`route` and :func:`sort_pairs` in one launch -> (weights fp32
     ``[T, k]``, topk_ids int32 ``[T, k]``); the sorted route table, rows and
-    x copy go to ``route_out`` / ``x_sorted`` / ``x_copy``."""
+    x copy go to ``route_out`` / ``x_sorted`` / ``x_copy``.
+    ``shared_expert``: one more problem, expert E (a shared expert stacked
+    after the routed ones), over the T tokens themselves (``x_sorted`` rows
+    ``T*k .. T*k+T-1``, scattered to pair rows ``T*k + t``)."""
     from .qmm_plan import sorted_route_ints
 
     require_cuda(router_logits, "router_logits")
@@ -303,8 +307,9 @@ def route_sorted(router_logits: torch.Tensor, x: torch.Tensor, top_k: int, *,
     dev = x.device
     if route_out.dtype != torch.int32 or route_out.numel() < sorted_route_ints():
         raise ValueError("route_out must be int32 with dfl_moe_sorted_route_ints() entries")
-    if x_sorted.dtype != torch.bfloat16 or tuple(x_sorted.shape) != (t * k, h) or not x_sorted.is_contiguous():
-        raise ValueError(f"x_sorted must be contiguous bf16 {(t * k, h)}")
+    rows = t * k + (t if shared_expert else 0)
+    if x_sorted.dtype != torch.bfloat16 or tuple(x_sorted.shape) != (rows, h) or not x_sorted.is_contiguous():
+        raise ValueError(f"x_sorted must be contiguous bf16 {(rows, h)}")
     if x_copy is not None and (x_copy.dtype != torch.bfloat16 or tuple(x_copy.shape) != (t, h)
                                or not x_copy.is_contiguous()):
         raise ValueError(f"x_copy must be contiguous bf16 {(t, h)}")
@@ -315,7 +320,8 @@ def route_sorted(router_logits: torch.Tensor, x: torch.Tensor, top_k: int, *,
     if ids.dtype != torch.int32 or tuple(ids.shape) != (t, k) or not ids.is_contiguous():
         raise ValueError(f"ids_out must be contiguous int32 {(t, k)}")
     with torch.cuda.device(dev):
-        st = _lib.load().dfl_moe_route_sorted(lg.data_ptr(), t, e, k, x.data_ptr(), int(x.stride(0)), h,
+        st = _lib.load().dfl_moe_route_sorted(lg.data_ptr(), t, e, k, 1 if shared_expert else 0, x.data_ptr(),
+                                              int(x.stride(0)), h,
                                               route_out.data_ptr(), w.data_ptr(), ids.data_ptr(),
                                               x_sorted.data_ptr(),
                                               None if x_copy is None else x_copy.data_ptr(), stream_ptr(dev))
@@ -327,24 +333,28 @@ class MoEPlanLayer:
     """One MoE verify layer with every expert projection in one plan launch.
 
     Per call: :func:`route_sorted` (top-k + weights, sorted route table, x
-    rows in sorted order, x into the plan's input buffer: one launch), one
-    :class:`~dflash_mlx_b200.qmm_plan.ProjectionPlan` run -- the shared
-    expert's gate|up + SiLU and down as dense phases, the routed experts'
-    gate|up + SiLU and down as grouped phases (down scattered to pair rows;
-    each active expert's weights read once, problems of one phase spread over
-    all SMs) -- and :func:`combine`.  No host synchronisation, CUDA-graph
+    rows in sorted order: one launch), one
+    :class:`~dflash_mlx_b200.qmm_plan.ProjectionPlan` run -- gate|up + SiLU
+    and down as two grouped phases over the active experts (down scattered
+    to pair rows; each active expert's weights read once, the problems of a
+    phase spread over all SMs), with a shared expert of the routed experts'
+    shape stacked after them as one more problem over all tokens (a shared
+    expert of another shape runs as two dense phases of the same plan) --
+    and :func:`combine`.  No host synchronisation, CUDA-graph
     capturable.  Same results as :func:`moe_layer` up to fp32
     summation order.  Three launches per call.
 
     ``experts``: QuantWeight stacks ``gate`` / ``up`` ``[E, I, H/8]`` or an
     interleaved ``gate_up`` (:func:`fuse_expert_gate_up`) and ``down``
     ``[E, H, I/8]``; ``shared``: QuantWeights ``gate`` / ``up`` (or
-    ``gate_up``) and ``down``, or None.  Needs I % 64 == 0, H % 128 == 0 and
-    ``tokens * top_k`` <= 256.
+    ``gate_up``) and ``down``, or None.  ``stack_shared=False`` keeps a
+    same-shaped shared expert in dense phases too.  Needs I % 64 == 0,
+    H % 128 == 0 and ``tokens * top_k`` <= 240.
     """
 
-    def __init__(self, experts: dict, shared: Optional[dict], tokens: int, top_k: int = 8):
-        from .qmm_plan import PlanPhase, ProjectionPlan, tile_expert_stack, tile_weight
+    def __init__(self, experts: dict, shared: Optional[dict], tokens: int, top_k: int = 8,
+                 stack_shared: bool = True):
+        from .qmm_plan import PlanPhase, ProjectionPlan, sorted_route_ints, tile_expert_stack, tile_weight
         from .verify_qmm import interleave_gate_up
 
         gu = experts["gate_up"] if "gate_up" in experts else fuse_expert_gate_up(experts["gate"], experts["up"])
@@ -356,23 +366,13 @@ class MoEPlanLayer:
         if down.k != inter or down.n != h or int(down.q.shape[0]) != e:
             raise ValueError("down must be [E, H, I/8] for gate_up [E, 2I, H/8]")
         t, k = int(tokens), int(top_k)
-        if not 1 <= t * k <= 256 or t > 16:
-            raise ValueError(f"{t} tokens x top-{k}: the route kernels take <= 16 tokens, <= 256 pairs")
+        if not 1 <= t * k <= 240 or t > 16:
+            raise ValueError(f"{t} tokens x top-{k}: the route kernels take <= 16 tokens, <= 240 pairs")
         dev = gu.q.device
         self.tokens, self.top_k, self.experts, self.hidden, self.inter = t, k, e, h, inter
-        self.gate_up = tile_expert_stack(gu.q, gu.s, gu.b)
-        self.down = tile_expert_stack(down.q, down.s, down.b)
         bf = dict(dtype=torch.bfloat16, device=dev)
-        self.x_in = torch.zeros((t, h), **bf)
-        self.x_sorted = torch.zeros((t * k, h), **bf)
-        self.h_sorted = torch.zeros((t * k, inter), **bf)
-        self.pair_out = torch.zeros((t * k, h), **bf)
-        from .qmm_plan import sorted_route_ints
-        self.route = torch.zeros(sorted_route_ints(), dtype=torch.int32, device=dev)
-        self.weights = torch.zeros((t, k), dtype=torch.float32, device=dev)
-        self.ids = torch.zeros((t, k), dtype=torch.int32, device=dev)
-        phases = []
-        self.shared_out = None
+        pairs = t * k
+        sgu = sdown = None
         if shared is not None:
             if "gate_up" in shared:
                 sgu = shared["gate_up"]
@@ -382,16 +382,40 @@ class MoEPlanLayer:
                                   interleave_gate_up(g.s, u.s).contiguous(),
                                   interleave_gate_up(g.b, u.b).contiguous())
             sdown = shared["down"]
-            s_inter = sgu.n // 2
+        # a shared expert of the routed experts' shape is stacked after them
+        # and runs as one more grouped problem over all T tokens (two plan
+        # phases per layer); another shape keeps two dense phases of its own
+        self.shared_stacked = (stack_shared and sgu is not None and tuple(sgu.q.shape) == tuple(gu.q.shape[1:])
+                               and tuple(sdown.q.shape) == tuple(down.q.shape[1:]))
+        if self.shared_stacked:
+            cat = lambda st, one: torch.cat([st, one.unsqueeze(0)]).contiguous()  # noqa: E731
+            self.gate_up = tile_expert_stack(cat(gu.q, sgu.q), cat(gu.s, sgu.s), cat(gu.b, sgu.b))
+            self.down = tile_expert_stack(cat(down.q, sdown.q), cat(down.s, sdown.s), cat(down.b, sdown.b))
+        else:
+            self.gate_up = tile_expert_stack(gu.q, gu.s, gu.b)
+            self.down = tile_expert_stack(down.q, down.s, down.b)
+        rows = pairs + (t if self.shared_stacked else 0)
+        self.x_in = torch.zeros((t, h), **bf)
+        self.x_sorted = torch.zeros((rows, h), **bf)
+        self.h_sorted = torch.zeros((rows, inter), **bf)
+        self.pair_out = torch.zeros((rows, h), **bf)
+        self.route = torch.zeros(sorted_route_ints(), dtype=torch.int32, device=dev)
+        self.weights = torch.zeros((t, k), dtype=torch.float32, device=dev)
+        self.ids = torch.zeros((t, k), dtype=torch.int32, device=dev)
+        phases = []
+        self.shared_out = None
+        if sgu is not None and not self.shared_stacked:
             self.shared_gate_up = tile_weight(sgu.q, sgu.s, sgu.b)
             self.shared_down = tile_weight(sdown.q, sdown.s, sdown.b)
-            self.h_shared = torch.zeros((t, s_inter), **bf)
+            self.h_shared = torch.zeros((t, sgu.n // 2), **bf)
             self.shared_out = torch.zeros((t, h), **bf)
             phases.append(PlanPhase(self.x_in, self.shared_gate_up, self.h_shared, silu=True))
+        elif self.shared_stacked:
+            self.shared_out = self.pair_out[pairs:]
         g_idx = len(phases)
         phases.append(PlanPhase(self.x_sorted, self.gate_up, self.h_sorted, silu=True, route=self.route,
                                 problem_rows=t))
-        if shared is not None:
+        if sgu is not None and not self.shared_stacked:
             phases.append(PlanPhase(self.h_shared, self.shared_down, self.shared_out, dep=0))
         phases.append(PlanPhase(self.h_sorted, self.down, self.pair_out, dep=g_idx, route=self.route,
                                 problem_rows=t, scatter=True))
@@ -403,7 +427,10 @@ class MoEPlanLayer:
             raise ValueError(f"x must be bf16 {(self.tokens, self.hidden)}")
         if tuple(router_logits.shape) != (self.tokens, self.experts):
             raise ValueError(f"router_logits must be {(self.tokens, self.experts)}")
+        dense_shared = self.shared_out is not None and not self.shared_stacked
         w, _ = route_sorted(router_logits, x, self.top_k, route_out=self.route, x_sorted=self.x_sorted,
-                            x_copy=self.x_in, weights_out=self.weights, ids_out=self.ids)
+                            x_copy=self.x_in if dense_shared else None, weights_out=self.weights,
+                            ids_out=self.ids, shared_expert=self.shared_stacked)
         self.plan.run()
-        return combine(self.pair_out, w, self.shared_out)
+        pairs = self.tokens * self.top_k
+        return combine(self.pair_out[:pairs], w, self.shared_out)

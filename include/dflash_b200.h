@@ -478,11 +478,16 @@ int dfl_moe_sort_pairs(const int32_t* topk_ids, int T, int top_k, int E, const u
                        void* stream);
 /* dfl_moe_route_sorted: dfl_moe_route's top-k ids and weights (same values
  * bit for bit; T <= 16, E <= 4096) and dfl_moe_sort_pairs' table, sorted rows
- * and x copy, in one launch (no dfl_moe_route table).  A token whose top-k
- * finds no finite logit sets the device error word and the table gets P = 0. */
-int dfl_moe_route_sorted(const float* logits, int T, int E, int top_k, const uint16_t* x, int ldx,
-                         int H, int32_t* route, float* weights, int32_t* topk_ids,
-                         uint16_t* x_sorted, uint16_t* x_copy, void* stream);
+ * and x copy, in one launch (no dfl_moe_route table).  shared_expert = 1
+ * appends one more problem, expert E (a shared expert stacked after the E
+ * routed ones), whose rows are the T tokens: sorted rows T * top_k + t =
+ * x[t], mapped to pair rows T * top_k + t (x_sorted then has T * top_k + T
+ * rows, at most 256), so a layer's shared expert runs in the same grouped
+ * phases as its routed experts.  A token whose top-k finds no finite logit
+ * sets the device error word and the table gets P = 0. */
+int dfl_moe_route_sorted(const float* logits, int T, int E, int top_k, int shared_expert,
+                         const uint16_t* x, int ldx, int H, int32_t* route, float* weights,
+                         int32_t* topk_ids, uint16_t* x_sorted, uint16_t* x_copy, void* stream);
 
 #ifdef __cplusplus
 }

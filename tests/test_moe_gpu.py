@@ -3,8 +3,10 @@ SiLU*up, weighted combine, shared expert) against the CPU oracle.
 
 The reference has no test for this path (it is mlx-lm's SwitchGLU ->
 mx.gather_qmm, not vendored): parity is against ``oracle/moe.py``'s
-restatement, elementwise within |y - ref| <= 1e-2 + 2e-2 |ref| (bf16 out,
-fp32 accumulate).  Covered: a small configuration with ragged expert loads,
+restatement, elementwise within |y - ref| <= 1e-2 + 2e-2 |ref| plus one
+bf16 step of the row's largest output (2^-7 max_row |ref|: the rounding of
+the intermediate projections, see _assert_close; bf16 out, fp32
+accumulate).  Covered: a small configuration with ragged expert loads,
 BASELINE config 2 (256 experts, top-8, hidden 2048, intermediate 512, one
 shared expert, 16 tokens), the routing table itself, and a layer where one
 expert takes every token (16 rows in one problem).
@@ -76,10 +78,18 @@ def _oracle(x, logits, experts, sh, k):
 
 
 def _assert_close(y_bits, ref_bits):
+    """Layer outputs: |y - ref| <= 1e-2 + 2e-2 |ref| + 2^-7 max_row |ref|.
+    A layer output passes through two bf16-rounded projections and a
+    weighted sum, so a one-step rounding difference in an intermediate
+    (fp32 sums taken in another order) moves it by up to one bf16 step of
+    the row's largest values, which the elementwise bound alone does not
+    allow where outputs cancel to near zero.  A wrong expert, row or split-K
+    partial moves outputs by their own magnitude and still fails."""
     y = obf16.to_f32(y_bits).astype(np.float64)
     r = obf16.to_f32(ref_bits).astype(np.float64)
     err = np.abs(y - r)
-    bad = err > 1e-2 + 2e-2 * np.abs(r)
+    row_scale = np.abs(r).max(axis=-1, keepdims=True)
+    bad = err > 1e-2 + 2e-2 * np.abs(r) + 2.0 ** -7 * row_scale
     assert not bad.any(), f"{int(bad.sum())} of {bad.size} outside tolerance, max err {err.max():.4g}"
 
 
