@@ -323,15 +323,18 @@ def test_plan_rejects_bad_phases(pkg, dev):
         pkg.ProjectionPlan([pkg.PlanPhase(x, tw, y, silu=True)])        # SiLU output is N/2 wide
 
 
-def test_withheld_partial_times_out_and_the_plan_recovers(pkg, dev):
+@pytest.mark.parametrize("rows", [16, 32])
+def test_withheld_partial_times_out_and_the_plan_recovers(pkg, dev, rows):
     """Failure path of a plan, made on the host: CTA 1 is told to withhold its
     split-K partials (its range lies inside tile 0 of a 640-unit phase, so CTA
-    0 must sum its partial) and every wait is bounded by 20 ms.  CTA 0's wait
-    runs out, the plan-wide abort word stops every CTA (the second phase's
-    CTAs were waiting for the first phase to complete), the launch ends in
-    well under a second with the device error word set and the time-out
-    recorded (split-K partial, phase 0, CTA 0).  After the workspace is
-    zeroed, the same plan gives the oracle's results."""
+    0 must sum its partial) and every wait is bounded by 20 ms, at 16-row
+    tiles (partials summed before the accumulator is read) and 32-row tiles
+    (summed pass by pass).  CTA 0's wait runs out, the plan-wide abort word
+    stops every CTA (the second phase's CTAs were waiting for the first phase
+    to complete), the launch ends in well under a second with the device
+    error word set and the time-out recorded (split-K partial, phase 0, CTA
+    0).  After the workspace is zeroed, the same plan gives the oracle's
+    results."""
     import time
 
     import torch
@@ -342,10 +345,10 @@ def test_withheld_partial_times_out_and_the_plan_recovers(pkg, dev):
     w0 = oqmm.synth_weights(rng, 8192, 5120)
     w1 = oqmm.synth_weights(rng, 1024, 8192)
     tw0, tw1 = _tiled(pkg, dev, *w0), _tiled(pkg, dev, *w1)
-    x = oqmm.synth_x(rng, 16, 5120)
+    x = oqmm.synth_x(rng, rows, 5120)
     xd = to_dev_bf16(x, dev)
-    y0 = torch.empty((16, 8192), dtype=torch.bfloat16, device=dev)
-    y1 = torch.empty((16, 1024), dtype=torch.bfloat16, device=dev)
+    y0 = torch.empty((rows, 8192), dtype=torch.bfloat16, device=dev)
+    y1 = torch.empty((rows, 1024), dtype=torch.bfloat16, device=dev)
     plan = pkg.ProjectionPlan([pkg.PlanPhase(xd, tw0, y0), pkg.PlanPhase(y0, tw1, y1, dep=0)])
     torch.cuda.synchronize(dev)
     assert _lib.device_error() == 0
