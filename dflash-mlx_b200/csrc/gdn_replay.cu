@@ -77,9 +77,9 @@ __device__ __forceinline__ void stage_rows(uint8_t* dst, const uint8_t* src, int
 
 // NCH: float4 state chunks per thread (16: a whole head of up to 16384
 // elements per CTA; 8: heads of more than 8192 elements split by rows over
-// `parts` CTAs with half the registers, three CTAs per SM: config 4's
-// 64 x 48 x 48 heads in 5.10 ms instead of 5.44; four per SM spilled and
-// was slower).
+// `parts` CTAs with half the registers, three CTAs per SM: 64 sequences x
+// 48 layers x 48 heads of 128 x 128 in 5.10 ms instead of 5.44; four per SM
+// spilled and was slower).
 template <typename KT, int DK, int NCH>
 __global__ void __launch_bounds__(THREADS, NCH <= 8 ? 3 : 1)
     tape_replay_kernel(const ReplayParams p) {
